@@ -1,0 +1,380 @@
+"""Benchmark of the B200 decode-attention hot path (tinyllama-engine GQA).
+
+Workload (the largest single-GPU decode case):
+256 sequences x 32768 cached positions (pos = 32767, 32768 attended rows),
+TinyLlama attention geometry (32 q heads, 4 KV heads, head_dim 64), fp32
+KV ~ N(0,1), one layer per step (17.18 GB of K+V per step, far larger than
+the 126 MB L2, so no flush is needed).  A step is one fused
+rope + append + GQA decode-attention call for every sequence
+(tle_decode_batch), i.e. attention() of src/ops.cpp:1317 for 256 sequences.
+
+Multi-GPU (torchrun, one process per GPU): sequences are partitioned by
+length (tle_partition_lpt), every rank decodes its shard from its own HBM,
+then the outputs are all-gathered over NCCL; the step time is the max over
+ranks (strong scaling: the 256-sequence total is fixed).
+
+`--impl reference` times the reference's own CPU attention (src/ops.cpp
+compiled unmodified into oracle/_ref) on a bounded sample of the same
+workload on all host cores.
+
+Prints ONE JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tinyllama-engine_b200"))
+
+N_SEQS = 256
+CTX = 32768
+NH, NKV, HD = 32, 4, 64
+QD, KVD = NH * HD, NKV * HD
+ROW_BYTES = 2 * KVD * 4  # K + V bytes per attended row (all 4 KV heads)
+METRIC = "decode-attn KV GB/s"
+WORKLOAD = ("config5: 256 seqs x 32768 cached rows (pos 32767), 32q/4kv heads, hd 64, fp32 KV, "
+            "1 layer per step, fused rope+append+GQA split-K decode")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["tle", "reference"], default="tle")
+    ap.add_argument("--seqs", type=int, default=N_SEQS)
+    ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="target wall time of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1])); smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_reference_run(seqs: int, ctx: int, steps: int, warmup: int, target_s: float):
+    """Times the reference's attention() (oracle/_ref, compiled from its own
+    src/ops.cpp) over a bounded sample of the workload with all host threads.
+    Returns (GB/s, dict describing the sample)."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    kind = "reference" if oracle.have_reference() else "port"
+    lib = oracle.reference() if kind == "reference" else oracle.port()
+    threads = os.cpu_count() or 1
+    n = max(1, min(seqs, threads, 64))
+    g = torch.Generator().manual_seed(1234)
+    kcs = [torch.randn((1, ctx, KVD), generator=g).numpy() for _ in range(n)]
+    vcs = [torch.randn((1, ctx, KVD), generator=g).numpy() for _ in range(n)]
+    q = torch.randn((n, QD), generator=g).numpy()
+    k = torch.randn((n, KVD), generator=g).numpy()
+    v = torch.randn((n, KVD), generator=g).numpy()
+    out = np.zeros((n, QD), np.float32)
+    pos = [ctx - 1] * n
+
+    def one():
+        lib.decode_batch(kcs, vcs, [ctx] * n, pos, q.copy(), k.copy(), v, out, 0, n_threads=n)
+
+    for _ in range(max(0, warmup)):
+        one()
+    times = []
+    t_end = time.perf_counter() + target_s
+    while len(times) < max(1, steps) and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    gbs = n * ctx * ROW_BYTES / med / 1e9
+    desc = {"kind": kind, "cores": n,
+            "sample": f"{n} of {seqs} sequences x {ctx} rows, 1 layer, rope+attention per sequence "
+                      f"on {n} std::threads; median of {len(times)} runs",
+            "seconds": round(sum(times), 2), "cpu_model": cpu_model(), "host_threads": threads}
+    return gbs, med, len(times), desc
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        # Reference arm: rank 0 alone times the reference CPU path.
+        if rank != 0:
+            return
+        gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, args.steps, args.warmup,
+                                                 target_s=max(20.0, args.cpu_seconds))
+        line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
+                "n_gpus": args.gpus, "steps": runs, "warmup": args.warmup,
+                "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+                "config": {"workload": WORKLOAD, "n_seqs": args.seqs, "ctx": args.ctx},
+                "cpu_baseline": dict(desc, value=round(gbs, 3), unit="GB/s"),
+                "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import tle
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+
+    # ---- shard the sequences (LPT by length; all equal here) ----
+    lengths = [args.ctx] * args.seqs
+    owner = tle.partition_lpt(lengths, world)
+    mine = [s for s in range(args.seqs) if owner[s] == rank]
+    counts = [owner.count(r) for r in range(world)]
+    max_local = max(counts)
+    n = len(mine)
+
+    # ---- device-resident state (KV caches of my sequences) ----
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    kc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
+    vc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
+    caches = [(kc[i], vc[i], args.ctx) for i in range(n)]
+    shape = tle.tinyllama_shape(1)
+    batch = tle.DecodeBatch(caches, [args.ctx - 1] * n, shape)
+    hq = torch.randn((max_local, QD), generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
+    hk = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(8 + rank)).pin_memory()
+    hv = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
+    q = hq.to(dev); k = hk.to(dev); v = hv.to(dev)
+    out = torch.zeros((max_local, QD), device=dev)
+    gathered = torch.zeros((world * max_local, QD), device=dev)
+    hout = torch.zeros((args.seqs, QD)).pin_memory()
+    # global sequence order of the gathered rows
+    order = []
+    for r in range(world):
+        rs = [s for s in range(args.seqs) if owner[s] == r]
+        order += rs + [-1] * (max_local - len(rs))
+    inv = torch.empty(args.seqs, dtype=torch.long)
+    for i, s in enumerate(order):
+        if s >= 0:
+            inv[s] = i
+    inv = inv.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def decode_only():
+        batch.run(q, k, v, out, 0, rotate=True, stream=stream)
+
+    def step():
+        decode_only()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            return gathered.index_select(0, inv)
+        return out
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+
+    # ---- device-timed region: K steps (decode + NCCL gather) ----
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    barrier()
+    ev[0].record(stream)
+    for i in range(args.steps):
+        kev[i][0].record(stream)
+        decode_only()
+        kev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            gathered.index_select(0, inv)
+    ev[1].record(stream)
+    barrier()
+    t_ms = ev[0].elapsed_time(ev[1])
+    k_ms = [a.elapsed_time(b) for a, b in kev]
+
+    # ---- end-to-end through the public API with host buffers ----
+    barrier()
+    e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    e2[0].record(stream)
+    for i in range(args.steps):
+        batch.upload(stream)                      # per-step descriptor (positions)
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        res = step()
+        if world > 1:
+            hout.copy_(res, non_blocking=True)
+        else:
+            hout[:n].copy_(res[:n], non_blocking=True)
+    e2[1].record(stream)
+    barrier()
+    e2e_ms = e2[0].elapsed_time(e2[1])
+    clk = clocks.stop()
+    err_code = tle.device_error()
+    if err_code:
+        raise RuntimeError(f"device error word 0x{err_code:x}")
+
+    # ---- max over ranks ----
+    vals = torch.tensor([t_ms, e2e_ms, statistics.mean(k_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, kernel_ms = [float(x) for x in vals.cpu()]
+
+    total_bytes = args.seqs * args.ctx * ROW_BYTES
+    step_s = t_ms / 1e3 / args.steps
+    value = total_bytes / step_s / 1e9
+    e2e_value = total_bytes / (e2e_ms / 1e3 / args.steps) / 1e9
+
+    if rank == 0:
+        peaks = load_peaks()
+        local_bytes = n * args.ctx * ROW_BYTES
+        achieved = local_bytes / (kernel_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1) fp32, seeded (no dataset)",
+            "config": {"workload": WORKLOAD, "n_seqs": args.seqs, "ctx": args.ctx,
+                       "layers_timed": 1, "l2": "inputs larger than L2 (17.2 GB KV per step)",
+                       "parallelism": f"sequence partition over {world} GPU(s) + NCCL all-gather"
+                       if world > 1 else "1 GPU"},
+            "tok_s_attn_22_layers": round(args.seqs / (step_s * 22), 1),
+            "pct_hbm_peak": round(100 * achieved / peaks["hbm_gbs"], 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"],
+                         "traffic": profile_traffic(local_bytes),
+                         "kernel": "tle_decode_batch (decode_kernel + merge_kernel), rank 0",
+                         "algorithmic_bytes_per_launch": local_bytes,
+                         "kernel_ms": round(kernel_ms, 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(hq[:n].numel() * 4 + hk[:n].numel() * 4
+                                              + hv[:n].numel() * 4 + batch.desc_bytes),
+                    "d2h_bytes_per_step": int(args.seqs * QD * 4 if world > 1 else n * QD * 4),
+                    "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "path": "tle.DecodeBatch.run (C ABI tle_decode_batch) with pinned host q/k/v "
+                            "in and host out back every step"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
+            line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(local_bytes):
+    """DRAM bytes per launch from the committed ncu summary (scaled to this
+    launch's rows), or None when no capture has been summarised."""
+    p = os.path.join(ROOT, "profiles", "decode_kernel_traffic.txt")
+    try:
+        for ln in open(p):
+            if ln.startswith("dram_bytes_per_algorithmic_byte:"):
+                return int(float(ln.split(":", 1)[1]) * local_bytes)
+    except OSError:
+        pass
+    return None
+
+
+if __name__ == "__main__":
+    main()

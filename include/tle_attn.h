@@ -1,0 +1,152 @@
+/*
+ * tle_attn.h -- C ABI of the B200 grouped-query-attention hot path of
+ * tinyllama-engine (RoPE on Q/K, KV-cache append, QK^T, causal softmax, PV).
+ *
+ * Plain C: device pointers, sizes, an opaque stream handle (a cudaStream_t
+ * passed as void*; NULL = legacy default stream) and an int status.  No
+ * exceptions cross this boundary; tle_last_error() gives the message of the
+ * last failing call on the calling host thread.  Every kernel is sm_100a
+ * only; there is no CPU fallback -- calls fail with TLE_ERR_CUDA when no
+ * B200 is present.
+ *
+ * Shapes follow llama_config_t (reference src/gguf.h:139-168).  The kernels
+ * are specialised for TinyLlama-1.1B attention: n_head = 32, n_head_kv = 4,
+ * head_dim = 64 (tle_rope accepts any even head_dim).  Other shapes return
+ * TLE_ERR_UNSUPPORTED.
+ *
+ * KV-cache layout is the reference's (run_state.h:100-101, ops.cpp:1350):
+ * one fp32 array per sequence per K/V, [n_layers][n_ctx][n_head_kv*head_dim],
+ * device-resident, 16-byte aligned.
+ */
+#ifndef TLE_ATTN_H
+#define TLE_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TLE_OK = 0,
+    TLE_ERR_INVALID = 1,     /* bad argument (null pointer, range, alignment) */
+    TLE_ERR_UNSUPPORTED = 2, /* shape outside the specialised kernels */
+    TLE_ERR_WORKSPACE = 3,   /* workspace smaller than the *_workspace_bytes() result */
+    TLE_ERR_CUDA = 4,        /* CUDA runtime error (message in tle_last_error) */
+    TLE_ERR_DEVICE = 5       /* a kernel recorded a device-side error (bounded wait expired) */
+};
+
+/* The fields of llama_config_t (gguf.h:139-168) that attention reads. */
+typedef struct {
+    int32_t n_layers;      /* llama.block_count                  (22)    */
+    int32_t n_head;        /* llama.attention.head_count         (32)    */
+    int32_t n_head_kv;     /* llama.attention.head_count_kv      (4)     */
+    int32_t head_dim;      /* n_embd / n_head, gguf.h:165-167    (64)    */
+    float rope_freq_base;  /* llama.rope.freq_base               (10000) */
+} tle_shape_t;
+
+/* One decoding sequence: its device KV cache and the position of the token
+ * being decoded (the call appends row `pos` and attends to rows 0..pos,
+ * exactly like attention(..., layer, pos, cfg) with cfg.n_ctx = n_ctx). */
+typedef struct {
+    float* key_cache;   /* device [n_layers][n_ctx][n_head_kv*head_dim] */
+    float* value_cache; /* device, same layout                           */
+    int32_t n_ctx;      /* rows per layer (RunState capacity)            */
+    int32_t pos;        /* 0 <= pos < n_ctx                              */
+} tle_seq_t;
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* tle_last_error(void);
+
+/* Library version string. */
+const char* tle_version(void);
+
+/* Replaces rope() (reference src/ops.h:175-176, src/ops.cpp:1223-1281):
+ * rotates pairs (2i, 2i+1) of q [n_head*head_dim] and k [n_head_kv*head_dim]
+ * in place by pos * 1/freq_base^(2i/head_dim).  Device pointers. */
+int tle_rope(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv,
+             float freq_base, void* stream);
+
+/* Workspace for tle_attention / tle_rope_attention (split-K partials). */
+size_t tle_attention_workspace_bytes(const tle_shape_t* shape, int n_ctx);
+
+/* Replaces attention() (reference src/ops.h:204-206, src/ops.cpp:1317-1515)
+ * for one sequence: appends k, v at row pos of layer `layer`, then writes
+ * out [n_head*head_dim] = softmax(q.K^T/sqrt(hd)) V over rows 0..pos.  q and
+ * k are already rotated, as in the reference.  The reference's `att` scratch
+ * is replaced by `workspace` (device, tle_attention_workspace_bytes()). */
+int tle_attention(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                  float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* forward.cpp:192-208 in one launch: rope(q, k, pos) then attention().
+ * q and k are the UNROTATED projections and are left unmodified; the rotated
+ * k is what lands in the cache, as in the reference. */
+int tle_rope_attention(float* out, const float* q, const float* k, const float* v,
+                       float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                       const tle_shape_t* shape, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* ---- batched multi-sequence decode (no reference counterpart: the
+ * reference decodes one sequence; this runs its attention() for many
+ * independent sequences in one launch, ops.cpp:1317 per sequence) ---- */
+
+/* Bytes of the batch descriptor for n_seqs sequences and up to max_ctas CTAs. */
+size_t tle_decode_desc_bytes(int n_seqs, int max_ctas);
+
+/* Builds the batch descriptor in HOST memory from host-side sequence
+ * records: copies the records and splits the sum of (pos+1) over the
+ * sequences evenly across *n_ctas CTAs (max_ctas <= 0: one per SM of the
+ * current device).  The caller copies desc_host to device memory unchanged
+ * and passes that copy and *n_ctas to tle_decode_batch. */
+int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs, int max_ctas,
+                    void* desc_host, size_t desc_bytes, int* n_ctas);
+
+/* Workspace for tle_decode_batch. */
+size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ctas);
+
+/* One decode step of layer `layer` for every sequence in the descriptor:
+ * per sequence s, with q [n_seqs][n_head*hd], k/v [n_seqs][n_head_kv*hd]:
+ * if rotate, rope(q_s, k_s, pos_s) (not written back); append k_s, v_s at
+ * row pos_s; out_s = attention over rows 0..pos_s.  desc_dev is the device
+ * copy of the tle_decode_desc() output. */
+int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
+                     const float* q, const float* k, const float* v, float* out, int layer,
+                     int rotate, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- prefill ---- */
+
+/* Workspace for tle_prefill with n_rows = pos0 + n_tokens attended rows. */
+size_t tle_prefill_workspace_bytes(const tle_shape_t* shape, int n_tokens, int pos0);
+
+/* The reference's prefill (generate.cpp:56-59: one forward() per prompt
+ * token, i.e. rope+attention at pos0, pos0+1, ..., pos0+n_tokens-1) as one
+ * causal flash attention on the tcgen05 tensor cores: q [n_tokens][n_head*hd],
+ * k/v [n_tokens][n_head_kv*hd] (unrotated, unmodified); rotated k and v are
+ * appended at rows pos0.. of layer `layer`; out [n_tokens][n_head*hd].
+ * Q, K and V enter the tensor cores as bf16 with fp32 accumulation and an
+ * fp32 softmax; rows < pos0 are read from the fp32 cache. */
+int tle_prefill(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                float* value_cache, int layer, int pos0, int n_tokens, int n_ctx,
+                const tle_shape_t* shape, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- multi-GPU sequence partition ---- */
+
+/* Greedy longest-processing-time assignment of sequences to n_ranks GPUs,
+ * balancing sum(lengths) per rank (KV bytes are proportional to length).
+ * rank_of_seq[s] receives the rank of sequence s; ties keep sequence order.
+ * Host-only; no counterpart in the single-process reference. */
+int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* rank_of_seq);
+
+/* ---- diagnostics ---- */
+
+/* Reads (and clears if clear != 0) the device error word that kernels set
+ * when a bounded wait expires; 0 = no error.  Synchronises the device. */
+int tle_device_error(int clear, uint32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TLE_ATTN_H */

@@ -1,0 +1,126 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, and its host-side logic (argument checks, the decode work plan,
+the multi-GPU partition) behaves as documented.  No kernel is launched."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import tle
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "tle_attn.h")).read()
+    return sorted(set(re.findall(r"\b(tle_[a-z_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    L = tle.lib()
+    declared = header_functions()
+    assert set(declared) == set(tle.EXPORTED), declared
+    for name in declared:
+        assert hasattr(L, name), name
+    assert "sm_100a" in tle.version()
+
+
+def test_header_compiles_as_c():
+    # the boundary is plain C: the header must compile with a C compiler
+    import subprocess
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "t.c")
+        with open(src, "w") as f:
+            f.write('#include "tle_attn.h"\nint main(void){tle_shape_t s; (void)s; return 0;}\n')
+        r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                            src, "-c", "-o", os.path.join(d, "t.o")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
+def parse_desc(buf, n_seqs, n_ctas):
+    b = bytes(buf)
+    magic, ns, nc, _ = np.frombuffer(b[:16], np.int32)
+    total = int(np.frombuffer(b[16:24], np.int64)[0])
+    off = 32 + 24 * n_seqs
+    cs = np.frombuffer(b[off:off + 8 * (n_ctas + 1)], np.int32).reshape(-1, 2)
+    off2 = off + 8 * (n_ctas + 1)
+    sc = np.frombuffer(b[off2:off2 + 8 * n_seqs], np.int32).reshape(-1, 2)
+    return magic, ns, nc, total, cs, sc
+
+
+def build_desc(positions, n_ctx, max_ctas):
+    n = len(positions)
+    shape = tle.tinyllama_shape()
+    seqs = (tle.Seq * n)()
+    for i, p in enumerate(positions):
+        seqs[i] = tle.Seq(0x1000 * (i + 1), 0x100000 * (i + 1), n_ctx[i], p)
+    nbytes = tle.lib().tle_decode_desc_bytes(n, max_ctas)
+    buf = (ctypes.c_uint8 * nbytes)()
+    n_ctas = ctypes.c_int(0)
+    rc = tle.lib().tle_decode_desc(ctypes.byref(shape), seqs, n, max_ctas, buf, nbytes,
+                                   ctypes.byref(n_ctas))
+    return rc, buf, n_ctas.value
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_decode_plan_covers_every_row_once(seed):
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(1, 70))
+    n_ctx = rng.integers(1, 3000, n).astype(int)
+    pos = [int(rng.integers(0, c)) for c in n_ctx]
+    max_ctas = int(rng.integers(1, 300))
+    rc, buf, G = build_desc(pos, list(n_ctx), max_ctas)
+    assert rc == 0, tle.lib().tle_last_error()
+    magic, ns, nc, total, cs, sc = parse_desc(buf, n, G)
+    L = np.array(pos) + 1
+    assert ns == n and nc == G and total == int(L.sum())
+    assert 1 <= G <= max_ctas and G <= max(1, -(-total // 32))
+    prefix = np.concatenate([[0], np.cumsum(L)])
+    # CTA c starts at global row c*total//G, expressed as (seq, offset)
+    covered = np.zeros(total, np.int32)
+    owner = np.full(total, -1)
+    for c in range(G):
+        a = prefix[cs[c, 0]] + cs[c, 1] if cs[c, 0] < n else total
+        b = prefix[cs[c + 1, 0]] + cs[c + 1, 1] if cs[c + 1, 0] < n else total
+        assert a == c * total // G and b == (c + 1) * total // G
+        assert b > a  # no empty CTA
+        covered[a:b] += 1
+        owner[a:b] = c
+    assert np.all(covered == 1)
+    for s in range(n):
+        lo, hi = sc[s]
+        assert lo == owner[prefix[s]] and hi == owner[prefix[s + 1] - 1]
+
+
+def test_decode_plan_rejects_bad_sequences():
+    rc, _, _ = build_desc([5], [5], 8)  # pos == n_ctx
+    assert rc == tle.TLE_ERR_INVALID
+    assert "pos" in tle.lib().tle_last_error().decode()
+    rc, _, _ = build_desc([-1], [5], 8)
+    assert rc == tle.TLE_ERR_INVALID
+
+
+def test_unsupported_shape_is_rejected_without_gpu():
+    shape = tle.Shape(22, 16, 4, 64, 10000.0)
+    seqs = (tle.Seq * 1)(tle.Seq(0x1000, 0x2000, 8, 3))
+    buf = (ctypes.c_uint8 * 4096)()
+    n = ctypes.c_int(0)
+    rc = tle.lib().tle_decode_desc(ctypes.byref(shape), seqs, 1, 4, buf, 4096, ctypes.byref(n))
+    assert rc == tle.TLE_ERR_UNSUPPORTED
+
+
+def test_partition_lpt_balances_and_is_deterministic():
+    rng = np.random.default_rng(3)
+    lengths = rng.integers(128, 2049, 64)
+    for ranks in (1, 2, 4, 8):
+        r = tle.partition_lpt(lengths, ranks)
+        assert r == tle.partition_lpt(lengths, ranks)
+        loads = np.bincount(r, weights=lengths, minlength=ranks)
+        assert len(loads) == ranks
+        # LPT bound: max load <= mean + max item
+        assert loads.max() <= loads.sum() / ranks + lengths.max()
+    # equal lengths: round robin in sequence order
+    assert tle.partition_lpt([7] * 8, 4) == [0, 1, 2, 3, 0, 1, 2, 3]

@@ -1,0 +1,251 @@
+"""GPU parity of the decode path (tle_rope, tle_attention, tle_rope_attention,
+tle_decode_batch) against the reference: golden fixtures made by the
+reference itself, the reference suite's known-answer tests
+(src/test_ops.cpp:295-546) run through the CUDA path, and the C oracle on
+seeded inputs up to the north-star shapes.
+
+Tolerance: max-abs 1e-4 on attention outputs (fp32 accumulation, the
+north-star bound); 1e-5 on rotated q/k and appended cache rows (device
+sincosf vs glibc sinf/cosf).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+NH, NKV, HD = 32, 4, 64
+QD, KVD = NH * HD, NKV * HD
+ATOL = 1e-4
+ROT_ATOL = 1e-5
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def maxabs(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
+
+
+# --------------------------------------------------------------- golden
+@pytest.mark.parametrize("name", ["decode_mid", "decode_pos0", "decode_full"])
+@pytest.mark.parametrize("fused", [True, False])
+def test_golden_decode(cuda, name, fused):
+    import tle
+    g = load_golden(name)
+    layer, pos, n_ctx = int(g["layer"]), int(g["pos"]), int(g["n_ctx"])
+    shape = tle.tinyllama_shape(int(g["n_layers"]))
+    kc, vc = dev(g["key_cache"]), dev(g["value_cache"])
+    q, k, v = dev(g["q"]), dev(g["k"]), dev(g["v"])
+    out = dev(np.full(QD, np.nan, np.float32))
+    if fused:
+        tle.rope_attention(out, q, k, v, kc, vc, layer, pos, n_ctx, shape)
+        assert np.array_equal(host(q), g["q"].astype(np.float32))  # fused call leaves q untouched
+    else:
+        tle.rope(q, k, pos)
+        assert maxabs(host(q), g["q_rot"]) <= ROT_ATOL
+        tle.attention(out, q, k, v, kc, vc, layer, pos, n_ctx, shape)
+    assert maxabs(host(out), g["out"]) <= ATOL
+    kc_h, vc_h = host(kc), host(vc)
+    assert maxabs(kc_h[layer, pos], g["k_rot"]) <= ROT_ATOL
+    assert np.array_equal(vc_h[layer, pos], g["v"].astype(np.float32))
+    # every other row untouched
+    ref_kc = g["key_cache"].astype(np.float32)
+    mask = np.ones(ref_kc.shape[:2], bool); mask[layer, pos] = False
+    assert np.array_equal(kc_h[mask], ref_kc[mask])
+    assert tle.device_error() == 0
+
+
+def test_golden_rope_positions(cuda):
+    import tle
+    g = load_golden("rope_positions")
+    for i, p in enumerate(g["pos"]):
+        q, k = dev(g["q"][i]), dev(g["k"][i])
+        tle.rope(q, k, int(p))
+        assert maxabs(host(q), g["q_out"][i]) <= ROT_ATOL, int(p)
+        assert maxabs(host(k), g["k_out"][i]) <= ROT_ATOL, int(p)
+
+
+def test_golden_batch(cuda):
+    import tle
+    g = load_golden("batch_ragged")
+    n = len(g["pos"])
+    caches = [(dev(g[f"key_cache_{i}"]), dev(g[f"value_cache_{i}"]), int(g["n_ctx"][i]))
+              for i in range(n)]
+    for max_ctas in (1, 3, 0):
+        cs = [(a.clone(), b.clone(), c) for a, b, c in caches]
+        batch = tle.DecodeBatch(cs, g["pos"], tle.tinyllama_shape(int(g["n_layers"])), max_ctas)
+        out = dev(np.full((n, QD), np.nan, np.float32))
+        batch.run(dev(g["q"]), dev(g["k"]), dev(g["v"]), out, int(g["layer"]), rotate=True)
+        assert maxabs(host(out), g["out"]) <= ATOL, max_ctas
+
+
+# ----------------------------------------- reference known-answer tests
+def test_known_answers_through_cuda(cuda):
+    """test_ops.cpp:295-431 with the CUDA attention (q, k pre-rotated = unrotated at pos 0)."""
+    import tle
+    n_ctx = 64
+    shape = tle.tinyllama_shape(2)
+    kc = dev(np.zeros((2, n_ctx, KVD))); vc = dev(np.zeros((2, n_ctx, KVD)))
+    out = dev(np.zeros(QD))
+    q = dev(np.ones(QD)); k = dev(np.ones(KVD))
+    tle.attention(out, q, k, dev(np.arange(KVD) % HD), kc, vc, 0, 0, n_ctx, shape)   # T1
+    assert np.allclose(host(out)[:HD], np.arange(HD), atol=1e-3)
+    kc.zero_(); vc.zero_()
+    tle.attention(out, q, k, dev(np.ones(KVD)), kc, vc, 0, 0, n_ctx, shape)           # T2
+    tle.attention(out, q, k, dev(np.full(KVD, 3.0)), kc, vc, 0, 1, n_ctx, shape)
+    assert abs(host(out)[0] - 2.0) < 0.01
+    kc.zero_(); vc.zero_()
+    for p in range(10):                                                               # T3
+        tle.attention(out, dev((np.arange(QD) + p) % 11 - 5), dev((np.arange(KVD) + 3 * p) % 7 - 3),
+                      dev((np.arange(KVD) + 5 * p) % 9 - 4), kc, vc, 0, p, n_ctx, shape)
+    assert np.all(np.isfinite(host(out)))
+    kc.zero_(); vc.zero_()
+    v = np.zeros(KVD); v[:HD] = 10; v[HD:2 * HD] = 20                                # T4
+    tle.attention(out, q, k, dev(v), kc, vc, 0, 0, n_ctx, shape)
+    o = host(out)
+    assert abs(o[0] - 10) < 0.01 and abs(o[8 * HD] - 20) < 0.01
+
+
+def test_rope_known_answers_through_cuda(cuda):
+    """test_ops.cpp:433-546 with tle_rope."""
+    import tle
+    q, k = dev(np.ones(QD)), dev(np.ones(KVD))
+    tle.rope(q, k, 0)
+    assert np.all(np.abs(host(q) - 1) < 1e-4) and np.all(np.abs(host(k) - 1) < 1e-4)
+    qh = (np.arange(QD) % 7 - 3).astype(np.float32)
+    q, k = dev(qh), dev(np.arange(KVD) % 5 - 2)
+    tle.rope(q, k, 42)
+    assert abs(np.linalg.norm(host(q)[:HD]) - np.linalg.norm(qh[:HD])) < 1e-3
+    q1, k1, q2, k2 = dev(np.ones(QD)), dev(np.ones(KVD)), dev(np.ones(QD)), dev(np.ones(KVD))
+    tle.rope(q1, k1, 5); tle.rope(q2, k2, 100)
+    assert np.any(np.abs(host(q1)[:HD] - host(q2)[:HD]) >= 1e-4)
+    q1, k1 = dev(np.full(QD, 2.5)), dev(np.full(KVD, 2.5))
+    q2, k2 = dev(np.full(QD, 2.5)), dev(np.full(KVD, 2.5))
+    tle.rope(q1, k1, 17); tle.rope(q2, k2, 17)
+    assert np.array_equal(host(q1), host(q2))
+    qz = np.zeros(QD, np.float32); qz[0], qz[1] = 3, 4
+    q, k = dev(qz), dev(np.zeros(KVD))
+    tle.rope(q, k, 1)
+    c, s = np.cos(np.float32(1)), np.sin(np.float32(1))
+    assert abs(host(q)[0] - (3 * c - 4 * s)) < 1e-4 and abs(host(q)[1] - (3 * s + 4 * c)) < 1e-4
+
+
+# ------------------------------------------------- seeded, oracle-checked
+def run_batch_case(lengths, n_layers, layer, max_ctas, seed, check=None):
+    """Random caches/q/k/v for sequences of the given attended lengths; runs the
+    CUDA batch decode and the oracle on the sequences in `check` (all by default)."""
+    import torch
+    import tle
+    rng = np.random.default_rng(seed)
+    n = len(lengths)
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    caches, n_ctx, pos = [], [], []
+    for L in lengths:
+        cap = int(L + rng.integers(0, 5))
+        kc = torch.randn((n_layers, cap, KVD), generator=gen, device="cuda")
+        vc = torch.randn((n_layers, cap, KVD), generator=gen, device="cuda")
+        caches.append((kc, vc, cap)); n_ctx.append(cap); pos.append(int(L) - 1)
+    q = rng.standard_normal((n, QD), dtype=np.float32)
+    k = rng.standard_normal((n, KVD), dtype=np.float32)
+    v = rng.standard_normal((n, KVD), dtype=np.float32)
+    check = list(range(n)) if check is None else list(check)
+    kc_h = [caches[i][0].cpu().numpy() for i in check]
+    vc_h = [caches[i][1].cpu().numpy() for i in check]
+    batch = tle.DecodeBatch(caches, pos, tle.tinyllama_shape(n_layers), max_ctas)
+    out = torch.full((n, QD), float("nan"), device="cuda")
+    batch.run(dev(q), dev(k), dev(v), out, layer, rotate=True)
+    got = host(out)
+    want = np.zeros((len(check), QD), np.float32)
+    oracle.port().decode_batch(kc_h, vc_h, [n_ctx[i] for i in check], [pos[i] for i in check],
+                               q[check].copy(), k[check].copy(), v[check].copy(), want, layer,
+                               n_threads=8)
+    err = maxabs(got[check], want)
+    # appended rows: the oracle appended into its host copies
+    for j, i in enumerate(check):
+        row_dev = caches[i][0][layer, pos[i]].cpu().numpy()
+        assert maxabs(row_dev, kc_h[j][layer, pos[i]]) <= ROT_ATOL
+        assert np.array_equal(caches[i][1][layer, pos[i]].cpu().numpy(), v[i])
+    return err, batch.n_ctas
+
+
+@pytest.mark.parametrize("lengths,max_ctas", [
+    ([1], 0), ([2], 0), ([31], 0), ([32], 0), ([33], 0), ([64], 1), ([1000], 0),
+    ([1, 1, 1, 1, 1], 3),                       # many tiny sequences per CTA
+    ([5, 4097, 33, 1, 640], 0),                 # ragged, split across CTAs
+    ([300, 300, 300, 300], 7),                  # CTA boundaries inside sequences
+    ([2048] * 6, 148),
+])
+def test_batch_decode_matches_oracle(cuda, lengths, max_ctas):
+    err, _ = run_batch_case(lengths, n_layers=2, layer=1, max_ctas=max_ctas, seed=sum(lengths))
+    assert err <= ATOL, err
+
+
+def test_single_long_context_matches_oracle(cuda):
+    """One sequence, 16384 cached rows, split over ~148 CTAs and merged."""
+    import torch
+    import tle
+    rng = np.random.default_rng(11)
+    n_ctx, pos, layer = 16400, 16383, 0
+    kc_h = rng.standard_normal((1, n_ctx, KVD), dtype=np.float32)
+    vc_h = rng.standard_normal((1, n_ctx, KVD), dtype=np.float32)
+    q = rng.standard_normal(QD, dtype=np.float32)
+    k = rng.standard_normal(KVD, dtype=np.float32)
+    v = rng.standard_normal(KVD, dtype=np.float32)
+    kc, vc = dev(kc_h), dev(vc_h)
+    out = dev(np.zeros(QD))
+    tle.rope_attention(out, dev(q), dev(k), dev(v), kc, vc, layer, pos, n_ctx, tle.tinyllama_shape(1))
+    want = np.zeros(QD, np.float32)
+    P = oracle.port()
+    q2, k2 = q.copy(), k.copy()
+    P.rope(q2, k2, pos)
+    P.attention(want, q2, k2, v, kc_h, vc_h, layer, pos, n_ctx)
+    assert maxabs(host(out), want) <= ATOL
+
+
+def test_config4_shapes_all_sequences(cuda):
+    """North-star config 4: 64 sequences, lengths U[128, 2048], 22-layer caches;
+    layer 13 checked for every sequence."""
+    rng = np.random.default_rng(4)
+    lengths = rng.integers(128, 2049, 64)
+    err, n_ctas = run_batch_case(lengths, n_layers=22, layer=13, max_ctas=0, seed=4)
+    assert n_ctas > 1
+    assert err <= ATOL, err
+
+
+def test_repeat_call_is_idempotent(cuda):
+    """Decoding the same token twice rewrites the same row and gives the same output."""
+    import torch
+    import tle
+    rng = np.random.default_rng(5)
+    kc = dev(rng.standard_normal((1, 700, KVD), dtype=np.float32))
+    vc = dev(rng.standard_normal((1, 700, KVD), dtype=np.float32))
+    q, k, v = (dev(rng.standard_normal(n, dtype=np.float32)) for n in (QD, KVD, KVD))
+    o1, o2 = dev(np.zeros(QD)), dev(np.zeros(QD))
+    shape = tle.tinyllama_shape(1)
+    tle.rope_attention(o1, q, k, v, kc, vc, 0, 650, 700, shape)
+    tle.rope_attention(o2, q, k, v, kc, vc, 0, 650, 700, shape)
+    assert np.array_equal(host(o1), host(o2))
+
+
+def test_invalid_arguments_fail_loudly(cuda):
+    import tle
+    shape = tle.tinyllama_shape(1)
+    kc, vc = dev(np.zeros((2, 8, KVD))), dev(np.zeros((2, 8, KVD)))
+    out, q, k, v = dev(np.zeros(QD)), dev(np.zeros(QD)), dev(np.zeros(KVD)), dev(np.zeros(KVD))
+    with pytest.raises(tle.TleError) as e:
+        tle.attention(out, q, k, v, kc, vc, 0, 8, 8, shape)   # pos == n_ctx
+    assert e.value.code == tle.TLE_ERR_INVALID
+    with pytest.raises(tle.TleError) as e:
+        tle.attention(out, q, k, v, kc, vc, 1, 3, 8, shape)   # layer >= shape.n_layers
+    assert e.value.code == tle.TLE_ERR_INVALID

@@ -1,0 +1,349 @@
+// abi.cu -- the extern "C" boundary (include/tle_attn.h): argument checks,
+// the decode work plan and kernel launches.  No exceptions leave this file;
+// every entry point returns a TLE_* status and records a message for
+// tle_last_error().
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "tle_attn.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    return set_error(TLE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int ok() {
+    g_last_error.clear();
+    return TLE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 1/freq_base^(2i/head_dim) with the reference's exact float expression
+// (ops.cpp:1244-1245): std::pow on floats resolves to powf.
+void fill_inv_freq(float* dst, int half, float freq_base) {
+    const int head_dim = 2 * half;
+    for (int i = 0; i < half; ++i)
+        dst[i] = 1.0f / std::pow(freq_base, static_cast<float>(2 * i) / static_cast<float>(head_dim));
+}
+
+int check_shape(const tle_shape_t* shape) {
+    if (!shape) return set_error(TLE_ERR_INVALID, "shape is NULL");
+    if (shape->n_head != tle::kNHead || shape->n_head_kv != tle::kNHeadKv ||
+        shape->head_dim != tle::kHeadDim)
+        return set_error(TLE_ERR_UNSUPPORTED,
+                         "attention kernels are built for n_head=32, n_head_kv=4, head_dim=64 "
+                         "(got %d, %d, %d)",
+                         shape->n_head, shape->n_head_kv, shape->head_dim);
+    if (shape->n_layers <= 0) return set_error(TLE_ERR_INVALID, "n_layers must be > 0");
+    if (!(shape->rope_freq_base > 0.f)) return set_error(TLE_ERR_INVALID, "rope_freq_base must be > 0");
+    return TLE_OK;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    return n;
+}
+
+// Number of CTAs for `rows` attended rows: about one per SM, but never fewer
+// than kMinRowsPerCta rows per CTA.
+int choose_ctas(int64_t rows, int max_ctas) {
+    if (max_ctas <= 0) max_ctas = sm_count();
+    max_ctas = std::min(max_ctas, tle::kMaxCtas);
+    const int64_t by_rows = (rows + tle::kMinRowsPerCta - 1) / tle::kMinRowsPerCta;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_ctas, by_rows)));
+}
+
+size_t partial_bytes(int n_slots) {
+    return static_cast<size_t>(n_slots) * tle::kPartialFloats * sizeof(float);
+}
+
+int single_decode(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                  float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
+                  void* workspace, size_t workspace_bytes, void* stream, int rotate) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!out || !q || !k || !v || !key_cache || !value_cache)
+        return set_error(TLE_ERR_INVALID, "null buffer pointer");
+    if (!aligned16(out) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(key_cache) ||
+        !aligned16(value_cache))
+        return set_error(TLE_ERR_INVALID, "buffers must be 16-byte aligned");
+    if (n_ctx <= 0 || pos < 0 || pos >= n_ctx)
+        return set_error(TLE_ERR_INVALID, "need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", pos, n_ctx);
+    if (layer < 0 || layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
+    tle::DecodeArgs a{};
+    a.seqs = nullptr;
+    a.cta_start = nullptr;
+    a.seq_ctas = nullptr;
+    a.single.key_cache = key_cache;
+    a.single.value_cache = value_cache;
+    a.single.n_ctx = n_ctx;
+    a.single.pos = pos;
+    a.n_seqs = 1;
+    a.n_ctas = choose_ctas(static_cast<int64_t>(pos) + 1, 0);
+    if (a.n_ctas > 1) {
+        if (!workspace) return set_error(TLE_ERR_WORKSPACE, "workspace is NULL");
+        if (workspace_bytes < partial_bytes(a.n_ctas + 1))
+            return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes,
+                             partial_bytes(a.n_ctas + 1));
+        if (!aligned16(workspace)) return set_error(TLE_ERR_INVALID, "workspace must be 16-byte aligned");
+    }
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.partials = static_cast<float*>(workspace);
+    a.layer = layer;
+    a.rotate = rotate;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    cudaError_t e = tle::error_word(&a.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "decode launch");
+    return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tle_last_error(void) { return g_last_error.c_str(); }
+
+const char* tle_version(void) { return "tle_attn 0.1 (sm_100a)"; }
+
+int tle_rope(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv, float freq_base,
+             void* stream) {
+    if (!q || (n_head_kv > 0 && !k)) return set_error(TLE_ERR_INVALID, "null q/k");
+    if (head_dim <= 0 || (head_dim & 1) || head_dim > 256)
+        return set_error(TLE_ERR_UNSUPPORTED, "head_dim must be even and <= 256 (got %d)", head_dim);
+    if (n_head <= 0 || n_head_kv < 0) return set_error(TLE_ERR_INVALID, "bad head counts");
+    if (pos < 0) return set_error(TLE_ERR_INVALID, "pos must be >= 0");
+    tle::RopeArgs a{};
+    a.q = q;
+    a.k = k;
+    a.pos = pos;
+    a.half = head_dim / 2;
+    a.n_head = n_head;
+    a.n_head_kv = n_head_kv;
+    fill_inv_freq(a.inv_freq, a.half, freq_base);
+    cudaError_t e = tle::launch_rope(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "rope launch");
+    return ok();
+}
+
+size_t tle_attention_workspace_bytes(const tle_shape_t* shape, int n_ctx) {
+    (void)shape;
+    (void)n_ctx;
+    return partial_bytes(tle::kMaxCtas + 1);
+}
+
+int tle_attention(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                  float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
+                         workspace_bytes, stream, 0);
+}
+
+int tle_rope_attention(float* out, const float* q, const float* k, const float* v,
+                       float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                       const tle_shape_t* shape, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
+                         workspace_bytes, stream, 1);
+}
+
+size_t tle_decode_desc_bytes(int n_seqs, int max_ctas) {
+    if (n_seqs < 0) n_seqs = 0;
+    if (max_ctas <= 0 || max_ctas > tle::kMaxCtas) max_ctas = tle::kMaxCtas;
+    return tle::desc_seqctas_offset(n_seqs, max_ctas) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+}
+
+int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs, int max_ctas,
+                    void* desc_host, size_t desc_bytes, int* n_ctas_out) {
+    if (int rc = check_shape(shape)) return rc;
+    if (n_seqs <= 0 || !seqs || !desc_host || !n_ctas_out)
+        return set_error(TLE_ERR_INVALID, "need n_seqs > 0 and non-null seqs/desc/n_ctas");
+    int64_t total = 0;
+    for (int s = 0; s < n_seqs; ++s) {
+        const tle_seq_t& q = seqs[s];
+        if (!q.key_cache || !q.value_cache || !aligned16(q.key_cache) || !aligned16(q.value_cache))
+            return set_error(TLE_ERR_INVALID, "sequence %d: caches must be non-null and 16-byte aligned", s);
+        if (q.n_ctx <= 0 || q.pos < 0 || q.pos >= q.n_ctx)
+            return set_error(TLE_ERR_INVALID, "sequence %d: need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", s,
+                             q.pos, q.n_ctx);
+        total += static_cast<int64_t>(q.pos) + 1;
+    }
+    const int G = choose_ctas(total, max_ctas);
+    const size_t need = tle::desc_seqctas_offset(n_seqs, G) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+    if (desc_bytes < need)
+        return set_error(TLE_ERR_INVALID, "descriptor buffer %zu bytes < %zu needed", desc_bytes, need);
+    unsigned char* base = static_cast<unsigned char*>(desc_host);
+    tle::DescHeader hdr{};
+    hdr.magic = tle::kDescMagic;
+    hdr.n_seqs = n_seqs;
+    hdr.n_ctas = G;
+    hdr.total_rows = total;
+    std::memcpy(base, &hdr, sizeof hdr);
+    std::memcpy(base + tle::desc_seqs_offset(), seqs, sizeof(tle_seq_t) * static_cast<size_t>(n_seqs));
+    auto* cs = reinterpret_cast<tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
+    auto* sc = reinterpret_cast<tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, G));
+    // CTA c owns concatenated rows [c*total/G, (c+1)*total/G).
+    std::vector<int64_t> prefix(static_cast<size_t>(n_seqs) + 1, 0);
+    for (int s = 0; s < n_seqs; ++s) prefix[s + 1] = prefix[s] + seqs[s].pos + 1;
+    int s = 0;
+    for (int c = 0; c <= G; ++c) {
+        const int64_t x = (c == G) ? total : static_cast<int64_t>(c) * total / G;
+        while (s < n_seqs && prefix[s + 1] <= x) ++s;
+        cs[c].seq = s;
+        cs[c].off = (s < n_seqs) ? static_cast<int32_t>(x - prefix[s]) : 0;
+    }
+    // CTAs covering each sequence.
+    int c = 0;
+    for (int t = 0; t < n_seqs; ++t) {
+        const int64_t first = prefix[t], last = prefix[t + 1] - 1;
+        while (c + 1 < G && static_cast<int64_t>(c + 1) * total / G <= first) ++c;
+        int hi = c;
+        while (hi + 1 < G && static_cast<int64_t>(hi + 1) * total / G <= last) ++hi;
+        sc[t].lo = c;
+        sc[t].hi = hi;
+    }
+    *n_ctas_out = G;
+    return ok();
+}
+
+size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ctas) {
+    (void)shape;
+    if (n_ctas <= 0) n_ctas = tle::kMaxCtas;
+    return partial_bytes(n_ctas + std::max(n_seqs, 0));
+}
+
+int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
+                     const float* q, const float* k, const float* v, float* out, int layer, int rotate,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!desc_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (n_seqs <= 0 || n_ctas <= 0 || n_ctas > tle::kMaxCtas)
+        return set_error(TLE_ERR_INVALID, "bad n_seqs/n_ctas (%d, %d)", n_seqs, n_ctas);
+    if (!aligned16(desc_dev) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return set_error(TLE_ERR_INVALID, "buffers must be 16-byte aligned");
+    if (layer < 0 || layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
+    const size_t need = partial_bytes(n_ctas + n_seqs);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+        return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed (or unaligned)",
+                         workspace_bytes, need);
+    const unsigned char* base = static_cast<const unsigned char*>(desc_dev);
+    tle::DecodeArgs a{};
+    a.seqs = reinterpret_cast<const tle_seq_t*>(base + tle::desc_seqs_offset());
+    a.cta_start = reinterpret_cast<const tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
+    a.seq_ctas = reinterpret_cast<const tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, n_ctas));
+    a.n_seqs = n_seqs;
+    a.n_ctas = n_ctas;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.partials = static_cast<float*>(workspace);
+    a.layer = layer;
+    a.rotate = rotate ? 1 : 0;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    cudaError_t e = tle::error_word(&a.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "decode launch");
+    return ok();
+}
+
+size_t tle_prefill_workspace_bytes(const tle_shape_t* shape, int n_tokens, int pos0) {
+    (void)shape;
+    return tle::prefill_workspace_bytes(n_tokens, pos0);
+}
+
+int tle_prefill(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                float* value_cache, int layer, int pos0, int n_tokens, int n_ctx,
+                const tle_shape_t* shape, void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!out || !q || !k || !v || !key_cache || !value_cache)
+        return set_error(TLE_ERR_INVALID, "null buffer pointer");
+    if (!aligned16(out) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(key_cache) ||
+        !aligned16(value_cache))
+        return set_error(TLE_ERR_INVALID, "buffers must be 16-byte aligned");
+    if (n_tokens <= 0 || pos0 < 0 || static_cast<int64_t>(pos0) + n_tokens > n_ctx)
+        return set_error(TLE_ERR_INVALID, "need n_tokens > 0 and pos0 + n_tokens <= n_ctx");
+    if (layer < 0 || layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
+    const size_t need = tle::prefill_workspace_bytes(n_tokens, pos0);
+    if (!workspace || workspace_bytes < need)
+        return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, need);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 1023u) != 0)
+        return set_error(TLE_ERR_INVALID, "prefill workspace must be 1024-byte aligned");
+    tle::PrefillArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.key_cache = key_cache;
+    a.value_cache = value_cache;
+    a.layer = layer;
+    a.pos0 = pos0;
+    a.n_tokens = n_tokens;
+    a.n_ctx = n_ctx;
+    a.workspace = workspace;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    cudaError_t e = tle::error_word(&a.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_prefill(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "prefill launch");
+    return ok();
+}
+
+int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* rank_of_seq) {
+    if (n_seqs < 0 || n_ranks <= 0 || (n_seqs > 0 && (!lengths || !rank_of_seq)))
+        return set_error(TLE_ERR_INVALID, "bad partition arguments");
+    std::vector<int> order(static_cast<size_t>(n_seqs));
+    std::iota(order.begin(), order.end(), 0);
+    // Longest first; equal lengths keep sequence order.
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return lengths[a] > lengths[b]; });
+    std::vector<int64_t> load(static_cast<size_t>(n_ranks), 0);
+    for (int s : order) {
+        int best = 0;
+        for (int r = 1; r < n_ranks; ++r)
+            if (load[r] < load[best]) best = r;
+        rank_of_seq[s] = best;
+        load[best] += lengths[s];
+    }
+    return ok();
+}
+
+int tle_device_error(int clear, uint32_t* code) {
+    if (!code) return set_error(TLE_ERR_INVALID, "code is NULL");
+    cudaError_t e = tle::read_device_error(clear, code);
+    if (e != cudaSuccess) return cuda_error(e, "device error read");
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,105 @@
+// common.cuh -- sm_100a PTX helpers shared by the attention kernels:
+// mbarriers with bounded waits, 1-D bulk (TMA) copies, named barriers and the
+// device error word.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define TLE_DEV __device__ __forceinline__
+
+namespace tle {
+
+// Device error codes recorded in g_tle_error (first writer wins).
+enum : uint32_t {
+    kErrNone = 0,
+    kErrWaitFull = 0x101,   // consumer gave up waiting for a stage to fill
+    kErrWaitEmpty = 0x102,  // producer gave up waiting for a stage to drain
+    kErrWaitMma = 0x103,    // waiter gave up on a tensor-core commit
+    kErrDrain = 0x104,      // exit-time wait for in-flight copies gave up
+};
+
+// A bounded wait gives up after this long (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+
+// Records `code` in the device error word (first writer wins).
+TLE_DEV void record_error(uint32_t* word, uint32_t code) {
+    if (word) atomicCAS(word, 0u, code);
+}
+
+TLE_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+TLE_DEV uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+TLE_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+TLE_DEV void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+TLE_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+TLE_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+TLE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete; false after
+// kWaitTimeoutNs (the caller records an error and unwinds).
+TLE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+    }
+}
+
+// L2 policy for data read exactly once (the KV stream).
+TLE_DEV uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 1-D bulk copy global -> shared (TMA engine), completion counted on `bar`
+// in bytes.  dst, src 16-byte aligned; bytes a multiple of 16.
+TLE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
+TLE_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace tle

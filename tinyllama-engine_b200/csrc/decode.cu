@@ -1,0 +1,495 @@
+// decode.cu -- fused RoPE + KV append + split-K flash-decoding for TinyLlama
+// GQA (32 query heads, 4 KV heads, head_dim 64, fp32 cache).
+//
+// Reference semantics: rope() src/ops.cpp:1223-1281 followed by attention()
+// src/ops.cpp:1317-1515, per sequence:
+//   append k,v at row pos (ops.cpp:1370-1371); for each query head qh with KV
+//   head qh/8 (ops.cpp:1383): s_p = (q.K_p)/sqrt(64) for p <= pos
+//   (ops.cpp:1425-1433), softmax (ops.cpp:1445), out = sum_p w_p V_p
+//   (ops.cpp:1494-1508).
+//
+// Design (B200): the rows of all sequences in a batch are concatenated and
+// split evenly over the CTAs (one per SM).  A CTA walks its row range as
+// segments of one sequence each; a producer warp streams 32-row K and V
+// tiles (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with
+// 1-D bulk copies; 8 consumer warps each own 4 rows of every tile and all 32
+// query heads (lane = head), so every K/V element read from HBM serves its 8
+// query heads.  Scores, an online softmax and the PV accumulation run in fp32
+// FFMA (TF32 tensor cores would miss the 1e-4 parity bound).  Each lane reads
+// its KV head's 16-byte chunks in an order rotated by the KV-head index, so
+// the four distinct addresses of a warp-wide load fall in four different
+// bank groups (conflict-free broadcast).  Warps merge in shared memory at the
+// end of a segment; a segment that is a whole sequence writes the output,
+// otherwise its (m, l, o) partial goes to the workspace and merge_kernel
+// combines the partials of that sequence.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tle {
+
+namespace {
+
+__device__ uint32_t g_tle_error = 0;
+
+
+constexpr int HD = kHeadDim;
+constexpr int NH = kNHead;
+constexpr int ROWF = kRowFloats;   // 256 floats per cache row
+constexpr int ROWB = ROWF * 4;     // 1024 bytes
+constexpr int TILE = 32;           // rows per pipeline stage
+constexpr int NSTAGE = 3;
+constexpr int NCW = 8;             // consumer warps
+constexpr int NCT = NCW * 32;      // consumer threads
+constexpr int NTHR = NCT + 32;     // + one producer warp
+constexpr int RPW = TILE / NCW;    // rows per consumer warp per tile (4)
+constexpr int QS = HD + 4;         // padded q/o row stride in shared memory
+constexpr float kScale = 0.125f;   // 1/sqrt(64), exact in fp32
+
+struct __align__(128) DecodeSmem {
+    float k[NSTAGE][TILE * ROWF];
+    float v[NSTAGE][TILE * ROWF];
+    float qo[NH * QS];       // scaled rotated q (segment start) / merged o (segment end)
+    float newk[ROWF];        // rotated k of the token being decoded
+    float newv[ROWF];
+    float ml[NCW][NH][2];    // per-warp (m, l)
+    float fin[NH][2];        // merged (m, l)
+    uint64_t full[NSTAGE];
+    uint64_t empty[NSTAGE];
+    uint64_t csync;          // consumer-warp barrier
+    uint64_t prod_done;      // producer finished issuing
+    int issued;              // tiles issued by the producer
+    volatile int abort_flag;
+};
+
+struct Segment {
+    int s, a, b;  // sequence, rows [a, b)
+};
+
+// CTA c's row range as (start seq, start off) .. (end seq, end off), exclusive end.
+__device__ __forceinline__ void cta_range(const DecodeArgs& A, int c, int& s0, int& o0, int& s1,
+                                          int& o1) {
+    if (A.seqs) {
+        const CtaStart b = A.cta_start[c], e = A.cta_start[c + 1];
+        s0 = b.seq; o0 = b.off; s1 = e.seq; o1 = e.off;
+    } else {
+        const int L = A.single.pos + 1;
+        s0 = 0;
+        o0 = static_cast<int>(static_cast<int64_t>(c) * L / A.n_ctas);
+        const int e = static_cast<int>(static_cast<int64_t>(c + 1) * L / A.n_ctas);
+        if (e >= L) { s1 = 1; o1 = 0; } else { s1 = 0; o1 = e; }
+    }
+}
+
+__device__ __forceinline__ tle_seq_t load_seq(const DecodeArgs& A, int s) {
+    return A.seqs ? A.seqs[s] : A.single;
+}
+
+// Consumer-only barrier on an mbarrier (bounded wait; false on timeout).
+__device__ __forceinline__ bool consumer_sync(DecodeSmem& S, uint32_t& phase, int lane) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.csync);
+    const bool ok = mbar_wait(&S.csync, phase);
+    phase ^= 1u;
+    __syncwarp();
+    return ok;
+}
+
+__device__ __forceinline__ void fail(const DecodeArgs& A, DecodeSmem& S, uint32_t code) {
+    record_error(A.err, code);
+    S.abort_flag = 1;
+}
+
+__global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArgs A) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    DecodeSmem& S = *reinterpret_cast<DecodeSmem*>(smem_raw);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int cta = blockIdx.x;
+
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE; ++i) {
+            mbar_init(&S.full[i], 1);
+            mbar_init(&S.empty[i], NCW);
+        }
+        mbar_init(&S.csync, NCW);
+        mbar_init(&S.prod_done, 1);
+        S.issued = 0;
+        S.abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    int s0, o0, s1, o1;
+    cta_range(A, cta, s0, o0, s1, o1);
+
+    if (warp == NCW) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            int it = 0;
+            bool ok = true;
+            for (int s = s0, off = o0; ok && (s < s1 || (s == s1 && off < o1)); ++s, off = 0) {
+                const tle_seq_t sq = load_seq(A, s);
+                const int L = sq.pos + 1;
+                const int b = (s == s1) ? o1 : L;
+                const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
+                const float* kb = sq.key_cache + base;
+                const float* vb = sq.value_cache + base;
+                for (int ta = off; ta < b; ta += TILE) {
+                    const int tb = min(ta + TILE, b);
+                    const int st = it % NSTAGE;
+                    if (S.abort_flag || !mbar_wait(&S.empty[st], ((it / NSTAGE) & 1) ^ 1)) {
+                        if (!S.abort_flag) fail(A, S, kErrWaitEmpty);
+                        ok = false;
+                        break;
+                    }
+                    // Row `pos` (the token being decoded) is never read from the
+                    // cache: the consumers take it from newk/newv.
+                    const int n = min(tb, sq.pos) - ta;
+                    if (n > 0) {
+                        const uint32_t bytes = static_cast<uint32_t>(n) * ROWB;
+                        mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
+                        bulk_g2s(S.k[st], kb + static_cast<size_t>(ta) * ROWF, bytes, &S.full[st], pol);
+                        bulk_g2s(S.v[st], vb + static_cast<size_t>(ta) * ROWF, bytes, &S.full[st], pol);
+                    } else {
+                        mbar_arrive(&S.full[st]);
+                    }
+                    ++it;
+                    S.issued = it;
+                }
+            }
+            mbar_arrive(&S.prod_done);
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    const int g = lane >> 3;       // KV head of this lane's query head
+    const int h = lane;            // query head
+    uint32_t cphase = 0;
+    int it = 0;
+    bool ok = true;
+
+    for (int s = s0, off = o0; ok && (s < s1 || (s == s1 && off < o1)); ++s, off = 0) {
+        const tle_seq_t sq = load_seq(A, s);
+        const int L = sq.pos + 1;
+        const int seg_a = off;
+        const int seg_b = (s == s1) ? o1 : L;
+
+        // q for this sequence: rotate (rope, ops.cpp:1229-1260), pre-scale by
+        // 1/sqrt(64) (exact power of two, so (q/8).k == (q.k)/8 bit for bit).
+        {
+            const float2* qsrc = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(s) * NH * HD);
+            for (int j = tid; j < NH * HD / 2; j += NCT) {
+                const int hh = j >> 5, i = j & 31;
+                const float2 x = qsrc[j];
+                float y0 = x.x, y1 = x.y;
+                if (A.rotate) {
+                    float sn, cs;
+                    sincosf(static_cast<float>(sq.pos) * A.inv_freq[i], &sn, &cs);
+                    y0 = x.x * cs - x.y * sn;
+                    y1 = x.x * sn + x.y * cs;
+                }
+                S.qo[hh * QS + 2 * i] = y0 * kScale;
+                S.qo[hh * QS + 2 * i + 1] = y1 * kScale;
+            }
+        }
+        // The new token's k (rotated) and v: append to the cache at row pos
+        // (ops.cpp:1370-1371) and keep a copy for this CTA's last tile.
+        if (seg_b == L) {
+            const size_t row = (static_cast<size_t>(A.layer) * sq.n_ctx + sq.pos) * ROWF;
+            if (tid < ROWF / 2) {
+                const int i = tid & 31;
+                const float2 x = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(s) * ROWF)[tid];
+                float y0 = x.x, y1 = x.y;
+                if (A.rotate) {
+                    float sn, cs;
+                    sincosf(static_cast<float>(sq.pos) * A.inv_freq[i], &sn, &cs);
+                    y0 = x.x * cs - x.y * sn;
+                    y1 = x.x * sn + x.y * cs;
+                }
+                const float2 y = make_float2(y0, y1);
+                reinterpret_cast<float2*>(S.newk)[tid] = y;
+                reinterpret_cast<float2*>(sq.key_cache + row)[tid] = y;
+            } else {
+                const int t2 = tid - ROWF / 2;
+                const float2 x = reinterpret_cast<const float2*>(A.v + static_cast<size_t>(s) * ROWF)[t2];
+                reinterpret_cast<float2*>(S.newv)[t2] = x;
+                reinterpret_cast<float2*>(sq.value_cache + row)[t2] = x;
+            }
+        }
+        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+
+        // This lane's query head, its 16-byte chunks in KV-head-rotated order.
+        float4 q[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+            q[c] = *reinterpret_cast<const float4*>(&S.qo[h * QS + 4 * ((c + g) & 15)]);
+
+        float m_run = -INFINITY, l_run = 0.f;
+        float4 acc[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+        for (int ta = seg_a; ta < seg_b; ta += TILE) {
+            const int nrows = min(ta + TILE, seg_b) - ta;
+            const int st = it % NSTAGE;
+            if (!mbar_wait(&S.full[st], (it / NSTAGE) & 1)) { fail(A, S, kErrWaitFull); ok = false; break; }
+            const int r0 = warp * RPW;
+            if (r0 < nrows) {
+                const float* kp[RPW];
+                const float* vp[RPW];
+                bool valid[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    valid[r] = (r0 + r) < nrows;
+                    const int rr = valid[r] ? r0 + r : r0;  // invalid rows alias a valid one
+                    const bool is_new = (ta + rr) == sq.pos;
+                    kp[r] = (is_new ? S.newk : &S.k[st][rr * ROWF]) + g * HD;
+                    vp[r] = (is_new ? S.newv : &S.v[st][rr * ROWF]) + g * HD;
+                }
+                // scores s_r = (q/8) . K_r
+                float sc[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) sc[r] = 0.f;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const int o = 4 * ((c + g) & 15);
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        const float4 kv = *reinterpret_cast<const float4*>(kp[r] + o);
+                        sc[r] = fmaf(q[c].x, kv.x, sc[r]);
+                        sc[r] = fmaf(q[c].y, kv.y, sc[r]);
+                        sc[r] = fmaf(q[c].z, kv.z, sc[r]);
+                        sc[r] = fmaf(q[c].w, kv.w, sc[r]);
+                    }
+                }
+                // online softmax over this warp's rows
+                float mb = -INFINITY;
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    if (!valid[r]) sc[r] = -INFINITY;
+                    mb = fmaxf(mb, sc[r]);
+                }
+                if (mb > m_run) {
+                    const float f = expf(m_run - mb);
+                    l_run *= f;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        acc[c].x *= f; acc[c].y *= f; acc[c].z *= f; acc[c].w *= f;
+                    }
+                    m_run = mb;
+                }
+                float p[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    p[r] = expf(sc[r] - m_run);
+                    l_run += p[r];
+                }
+                // out += p_r * V_r
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const int o = 4 * ((c + g) & 15);
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        const float4 vv = *reinterpret_cast<const float4*>(vp[r] + o);
+                        acc[c].x = fmaf(p[r], vv.x, acc[c].x);
+                        acc[c].y = fmaf(p[r], vv.y, acc[c].y);
+                        acc[c].z = fmaf(p[r], vv.z, acc[c].z);
+                        acc[c].w = fmaf(p[r], vv.w, acc[c].w);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[st]);
+            ++it;
+        }
+        if (!ok) break;
+
+        // ---- merge the 8 warps' (m, l, acc) for this segment ----
+        S.ml[warp][h][0] = m_run;
+        S.ml[warp][h][1] = l_run;
+        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+        float mstar = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) mstar = fmaxf(mstar, S.ml[w][h][0]);
+        float lstar = 0.f;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+            const float mw = S.ml[w][h][0];
+            if (mw != -INFINITY) lstar += S.ml[w][h][1] * expf(mw - mstar);
+        }
+        const float f = (m_run == -INFINITY) ? 0.f : expf(m_run - mstar);
+        if (warp == 0) {
+            S.fin[h][0] = mstar;
+            S.fin[h][1] = lstar;
+        }
+        for (int w = 0; w < NCW && ok; ++w) {
+            if (warp == w) {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    float4* dst = reinterpret_cast<float4*>(&S.qo[h * QS + 4 * ((c + g) & 15)]);
+                    float4 val = make_float4(acc[c].x * f, acc[c].y * f, acc[c].z * f, acc[c].w * f);
+                    if (w > 0) {
+                        const float4 old = *dst;
+                        val.x += old.x; val.y += old.y; val.z += old.z; val.w += old.w;
+                    }
+                    *dst = val;
+                }
+            }
+            if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; }
+        }
+        if (!ok) break;
+
+        // ---- write: whole sequence -> output; otherwise a partial ----
+        {
+            const int hh = tid >> 3;
+            const int d0 = (tid & 7) * 8;
+            const float4 o0 = *reinterpret_cast<const float4*>(&S.qo[hh * QS + d0]);
+            const float4 o1v = *reinterpret_cast<const float4*>(&S.qo[hh * QS + d0 + 4]);
+            if (seg_a == 0 && seg_b == L) {
+                const float lf = S.fin[hh][1];
+                float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + hh * HD + d0);
+                dst[0] = make_float4(o0.x / lf, o0.y / lf, o0.z / lf, o0.w / lf);
+                dst[1] = make_float4(o1v.x / lf, o1v.y / lf, o1v.z / lf, o1v.w / lf);
+            } else {
+                float* P = A.partials + static_cast<size_t>(s + cta) * kPartialFloats;
+                float4* dst = reinterpret_cast<float4*>(P + hh * HD + d0);
+                dst[0] = o0;
+                dst[1] = o1v;
+                if (tid < NH) {
+                    P[NH * HD + tid] = S.fin[tid][0];
+                    P[NH * HD + NH + tid] = S.fin[tid][1];
+                }
+            }
+        }
+        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+    }
+
+    // Exit: every bulk copy the producer issued must have landed before the
+    // CTA's shared memory goes away (only matters on the error path).
+    if (tid == 0) {
+        if (!mbar_wait(&S.prod_done, 0)) {
+            record_error(A.err, kErrDrain);
+        } else {
+            for (int t = it; t < S.issued; ++t)
+                if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
+        }
+    }
+}
+
+// Combines the split-K partials of every sequence covered by more than one CTA.
+__global__ void __launch_bounds__(256) merge_kernel(const __grid_constant__ DecodeArgs A) {
+    const int s = blockIdx.x;
+    int lo = 0, hi = A.n_ctas - 1;
+    if (A.seq_ctas) {
+        const SeqCtas sc = A.seq_ctas[s];
+        lo = sc.lo;
+        hi = sc.hi;
+    }
+    if (lo >= hi) return;
+    const int t = threadIdx.x;
+    const int h = t >> 3;
+    const int d0 = (t & 7) * 8;
+    float mstar = -INFINITY;
+    for (int c = lo; c <= hi; ++c)
+        mstar = fmaxf(mstar, A.partials[static_cast<size_t>(s + c) * kPartialFloats + NH * HD + h]);
+    float lsum = 0.f;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int c = lo; c <= hi; ++c) {
+        const float* P = A.partials + static_cast<size_t>(s + c) * kPartialFloats;
+        const float mc = P[NH * HD + h];
+        if (mc == -INFINITY) continue;
+        const float f = expf(mc - mstar);
+        lsum += P[NH * HD + NH + h] * f;
+        const float4 a0 = *reinterpret_cast<const float4*>(P + h * HD + d0);
+        const float4 a1 = *reinterpret_cast<const float4*>(P + h * HD + d0 + 4);
+        o[0] = fmaf(a0.x, f, o[0]); o[1] = fmaf(a0.y, f, o[1]);
+        o[2] = fmaf(a0.z, f, o[2]); o[3] = fmaf(a0.w, f, o[3]);
+        o[4] = fmaf(a1.x, f, o[4]); o[5] = fmaf(a1.y, f, o[5]);
+        o[6] = fmaf(a1.z, f, o[6]); o[7] = fmaf(a1.w, f, o[7]);
+    }
+    float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + h * HD + d0);
+    dst[0] = make_float4(o[0] / lsum, o[1] / lsum, o[2] / lsum, o[3] / lsum);
+    dst[1] = make_float4(o[4] / lsum, o[5] / lsum, o[6] / lsum, o[7] / lsum);
+}
+
+// rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
+__global__ void rope_kernel(const __grid_constant__ RopeArgs A) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int total = (A.n_head + A.n_head_kv) * A.half;
+    if (j >= total) return;
+    const int hh = j / A.half, i = j - hh * A.half;
+    float* x = hh < A.n_head ? A.q + static_cast<size_t>(hh) * 2 * A.half
+                             : A.k + static_cast<size_t>(hh - A.n_head) * 2 * A.half;
+    float sn, cs;
+    sincosf(static_cast<float>(A.pos) * A.inv_freq[i], &sn, &cs);
+    const float x0 = x[2 * i], x1 = x[2 * i + 1];
+    x[2 * i] = x0 * cs - x1 * sn;
+    x[2 * i + 1] = x0 * sn + x1 * cs;
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
+    static int configured_device = -1;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int smem = static_cast<int>(sizeof(DecodeSmem));
+    if (configured_device != dev) {
+        e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured_device = dev;
+    }
+    decode_kernel<<<a.n_ctas, NTHR, smem, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (a.n_ctas > 1) {
+        merge_kernel<<<a.n_seqs, 256, 0, stream>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t stream) {
+    const int total = (a.n_head + a.n_head_kv) * a.half;
+    rope_kernel<<<(total + 255) / 256, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t error_word(uint32_t** word) {
+    static uint32_t* cached[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!cached[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tle_error);
+        if (e != cudaSuccess) return e;
+        cached[dev] = static_cast<uint32_t*>(p);
+    }
+    *word = cached[dev];
+    return cudaSuccess;
+}
+
+cudaError_t read_device_error(int clear, uint32_t* code) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpyFromSymbol(code, g_tle_error, sizeof(uint32_t));
+    if (e != cudaSuccess) return e;
+    if (clear && *code) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbol(g_tle_error, &zero, sizeof(uint32_t));
+    }
+    return e;
+}
+
+}  // namespace tle

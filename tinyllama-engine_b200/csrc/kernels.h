@@ -1,0 +1,108 @@
+// kernels.h -- internal interface between the C ABI (abi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tle_attn.h"
+
+namespace tle {
+
+// TinyLlama attention geometry the decode/prefill kernels are built for.
+constexpr int kHeadDim = 64;
+constexpr int kNHead = 32;
+constexpr int kNHeadKv = 4;
+constexpr int kRowFloats = kNHeadKv * kHeadDim;          // one cache row, all kv heads
+constexpr int kPartialFloats = kNHead * (kHeadDim + 2);  // o[32][64], m[32], l[32]
+constexpr int kMaxCtas = 1024;                            // upper bound on decode CTAs
+constexpr int kMinRowsPerCta = 32;                        // smallest split worth a CTA
+
+// Batch descriptor (built on the host by tle_decode_desc, read by the kernels):
+//   DescHeader | tle_seq_t seqs[n_seqs] | CtaStart cta_start[n_ctas+1] | SeqCtas seq_ctas[n_seqs]
+struct DescHeader {
+    int32_t magic;
+    int32_t n_seqs;
+    int32_t n_ctas;
+    int32_t reserved;
+    int64_t total_rows;
+    int64_t reserved2;
+};
+static_assert(sizeof(DescHeader) == 32, "descriptor header is 32 bytes");
+static_assert(sizeof(tle_seq_t) == 24, "tle_seq_t is 24 bytes");
+constexpr int32_t kDescMagic = 0x544c4544;  // "TLED"
+
+// CTA c processes the concatenated rows [cta_start[c], cta_start[c+1]) of the
+// batch, each start given as (sequence, row offset in that sequence).
+struct CtaStart {
+    int32_t seq;
+    int32_t off;
+};
+// Sequence s is covered by CTAs lo..hi; lo == hi means one CTA wrote the
+// final output directly and no merge is needed.
+struct SeqCtas {
+    int32_t lo;
+    int32_t hi;
+};
+
+inline size_t desc_seqs_offset() { return sizeof(DescHeader); }
+inline size_t desc_cta_offset(int n_seqs) {
+    return sizeof(DescHeader) + sizeof(tle_seq_t) * static_cast<size_t>(n_seqs);
+}
+inline size_t desc_seqctas_offset(int n_seqs, int n_ctas) {
+    return desc_cta_offset(n_seqs) + sizeof(CtaStart) * static_cast<size_t>(n_ctas + 1);
+}
+
+struct DecodeArgs {
+    const tle_seq_t* seqs;       // batch mode: device array; nullptr = single mode
+    const CtaStart* cta_start;   // batch mode: [n_ctas+1]
+    const SeqCtas* seq_ctas;     // batch mode: [n_seqs]
+    tle_seq_t single;            // single mode: the one sequence
+    int n_seqs;
+    int n_ctas;
+    const float* q;              // [n_seqs][32*64]
+    const float* k;              // [n_seqs][4*64]
+    const float* v;              // [n_seqs][4*64]
+    float* out;                  // [n_seqs][32*64]
+    float* partials;             // [n_ctas + n_seqs][kPartialFloats]
+    int layer;
+    int rotate;
+    uint32_t* err;               // device error word
+    float inv_freq[kHeadDim / 2];
+};
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
+
+struct RopeArgs {
+    float* q;
+    float* k;
+    int pos;
+    int half;  // head_dim / 2
+    int n_head;
+    int n_head_kv;
+    float inv_freq[128];
+};
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t stream);
+
+struct PrefillArgs {
+    const float* q;       // [n_tokens][32*64] unrotated
+    const float* k;       // [n_tokens][4*64]  unrotated
+    const float* v;       // [n_tokens][4*64]
+    float* out;           // [n_tokens][32*64]
+    float* key_cache;     // [n_layers][n_ctx][256]
+    float* value_cache;
+    int layer;
+    int pos0;
+    int n_tokens;
+    int n_ctx;
+    void* workspace;
+    uint32_t* err;        // device error word
+    float inv_freq[kHeadDim / 2];
+};
+size_t prefill_workspace_bytes(int n_tokens, int pos0);
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+
+cudaError_t read_device_error(int clear, uint32_t* code);
+// Device address of the error word on the current device.
+cudaError_t error_word(uint32_t** word);
+
+}  // namespace tle

@@ -1,0 +1,133 @@
+// ops_gpu.cpp -- implementation of the ops.h-shaped C++ layer (ops_gpu.h).
+#include "ops_gpu.h"
+
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace tle {
+
+namespace {
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        throw std::runtime_error(std::string("tle: ") + what + ": " + cudaGetErrorString(e));
+}
+}  // namespace
+
+std::size_t attention_workspace_floats(const AttnConfig& cfg) {
+    const tle_shape_t s = shape_of(cfg);
+    return (tle_attention_workspace_bytes(&s, static_cast<int>(cfg.n_ctx)) + sizeof(float) - 1) /
+           sizeof(float);
+}
+
+void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv, float freq_base,
+              void* stream) {
+    check(tle_rope(q, k, pos, head_dim, n_head, n_head_kv, freq_base, stream));
+}
+
+void attention_gpu(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                   float* value_cache, float* att, int layer, int pos, const AttnConfig& cfg,
+                   void* stream) {
+    const tle_shape_t s = shape_of(cfg);
+    check(tle_attention(out, q, k, v, key_cache, value_cache, layer, pos, static_cast<int>(cfg.n_ctx),
+                        &s, att, attention_workspace_floats(cfg) * sizeof(float), stream));
+}
+
+void rope_attention_gpu(float* out, const float* q, const float* k, const float* v,
+                        float* key_cache, float* value_cache, float* att, int layer, int pos,
+                        const AttnConfig& cfg, void* stream) {
+    const tle_shape_t s = shape_of(cfg);
+    check(tle_rope_attention(out, q, k, v, key_cache, value_cache, layer, pos,
+                             static_cast<int>(cfg.n_ctx), &s, att,
+                             attention_workspace_floats(cfg) * sizeof(float), stream));
+}
+
+float* device_alloc_floats(std::size_t n) {
+    void* p = nullptr;
+    cuda_check(cudaMalloc(&p, std::max<std::size_t>(n, 1) * sizeof(float)), "cudaMalloc");
+    return static_cast<float*>(p);
+}
+void device_free(void* p) {
+    if (p) cudaFree(p);
+}
+void copy_to_device(float* dst, const float* src, std::size_t n) {
+    cuda_check(cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+}
+void copy_to_host(float* dst, const float* src, std::size_t n) {
+    cuda_check(cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+}
+void device_zero(float* p, std::size_t n) {
+    cuda_check(cudaMemset(p, 0, n * sizeof(float)), "cudaMemset");
+}
+void device_sync() { cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize"); }
+
+void DeviceRunState::allocate(const AttnConfig& cfg) {
+    free_buffers();
+    const std::size_t hd = cfg.head_dim(), kv_dim = cfg.n_head_kv * hd;
+    const std::size_t cache = static_cast<std::size_t>(cfg.n_layers) * cfg.n_ctx * kv_dim;
+    xb2 = device_alloc_floats(cfg.n_embd);
+    q = device_alloc_floats(cfg.n_embd);
+    k = device_alloc_floats(kv_dim);
+    v = device_alloc_floats(kv_dim);
+    att = device_alloc_floats(attention_workspace_floats(cfg));
+    key_cache = device_alloc_floats(cache);
+    value_cache = device_alloc_floats(cache);
+    for (auto [p, n] : {std::pair{xb2, std::size_t(cfg.n_embd)}, std::pair{q, std::size_t(cfg.n_embd)},
+                        std::pair{k, kv_dim}, std::pair{v, kv_dim}, std::pair{key_cache, cache},
+                        std::pair{value_cache, cache}})
+        device_zero(p, n);
+    pos = 0;
+}
+
+void DeviceRunState::free_buffers() {
+    for (float** p : {&xb2, &q, &k, &v, &att, &key_cache, &value_cache}) {
+        device_free(*p);
+        *p = nullptr;
+    }
+}
+
+DecodeBatch::DecodeBatch(const AttnConfig& cfg, std::vector<tle_seq_t> seqs, int max_ctas)
+    : shape_(shape_of(cfg)), seqs_(std::move(seqs)), max_ctas_(max_ctas) {
+    if (seqs_.empty()) throw std::runtime_error("tle: DecodeBatch needs at least one sequence");
+    upload();
+}
+
+DecodeBatch::~DecodeBatch() {
+    device_free(desc_dev_);
+    device_free(ws_);
+}
+
+void DecodeBatch::set_positions(const std::vector<int32_t>& pos) {
+    if (pos.size() != seqs_.size()) throw std::runtime_error("tle: position count mismatch");
+    for (std::size_t i = 0; i < pos.size(); ++i) seqs_[i].pos = pos[i];
+    upload();
+}
+
+void DecodeBatch::upload() {
+    const int n = static_cast<int>(seqs_.size());
+    const std::size_t bytes = tle_decode_desc_bytes(n, max_ctas_);
+    desc_host_.assign(bytes, 0);
+    check(tle_decode_desc(&shape_, seqs_.data(), n, max_ctas_, desc_host_.data(), bytes, &n_ctas_));
+    if (bytes > desc_cap_) {
+        device_free(desc_dev_);
+        desc_dev_ = nullptr;
+        cuda_check(cudaMalloc(&desc_dev_, bytes), "cudaMalloc desc");
+        desc_cap_ = bytes;
+    }
+    cuda_check(cudaMemcpy(desc_dev_, desc_host_.data(), bytes, cudaMemcpyHostToDevice), "desc upload");
+    const std::size_t ws = tle_decode_workspace_bytes(&shape_, n, n_ctas_);
+    if (ws > ws_bytes_) {
+        device_free(ws_);
+        ws_ = nullptr;
+        cuda_check(cudaMalloc(&ws_, ws), "cudaMalloc workspace");
+        ws_bytes_ = ws;
+    }
+}
+
+void DecodeBatch::run(const float* q, const float* k, const float* v, float* out, int layer,
+                      bool rotate, void* stream) {
+    check(tle_decode_batch(&shape_, desc_dev_, static_cast<int>(seqs_.size()), n_ctas_, q, k, v, out,
+                           layer, rotate ? 1 : 0, ws_, ws_bytes_, stream));
+}
+
+}  // namespace tle

@@ -1,0 +1,141 @@
+// ops_gpu.h -- C++20 host layer above the C ABI, shaped like the reference's
+// ops.h / run_state.h so forward.cpp changes only where its pointers live.
+//
+//   reference (src/ops.h)                      this header
+//   rope(q, k, pos, hd, nh, nkv, base)          tle::rope_gpu(...)        ops.h:175-176
+//   attention(out, q, k, v, Kc, Vc, att,        tle::attention_gpu(...)   ops.h:204-206
+//             layer, pos, cfg)
+//   rope + attention (forward.cpp:192-208)      tle::rope_attention_gpu(...)
+//   RunState (run_state.h:27-182)               tle::DeviceRunState
+//
+// All pointers are device pointers.  Errors throw std::runtime_error, the
+// reference's convention (e.g. ops.cpp:978-979, forward.cpp:143-145).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "tle_attn.h"
+
+namespace tle {
+
+// The llama_config_t fields (reference src/gguf.h:139-168) attention reads.
+struct AttnConfig {
+    std::uint32_t n_layers = 0;
+    std::uint32_t n_embd = 0;
+    std::uint32_t n_head = 0;
+    std::uint32_t n_head_kv = 0;
+    std::uint32_t n_ctx = 2048;
+    float rope_freq_base = 10000.0f;
+    std::uint32_t head_dim() const { return n_head > 0 ? n_embd / n_head : 0; }
+};
+
+// Accepts the reference's llama_config_t (or anything with the same fields).
+template <class Cfg>
+AttnConfig to_attn_config(const Cfg& c) {
+    AttnConfig a;
+    a.n_layers = c.n_layers;
+    a.n_embd = c.n_embd;
+    a.n_head = c.n_head;
+    a.n_head_kv = c.n_head_kv;
+    a.n_ctx = c.n_ctx;
+    a.rope_freq_base = c.rope_freq_base;
+    return a;
+}
+
+inline void check(int rc) {
+    if (rc != TLE_OK) throw std::runtime_error(std::string("tle: ") + tle_last_error());
+}
+
+inline tle_shape_t shape_of(const AttnConfig& c) {
+    tle_shape_t s;
+    s.n_layers = static_cast<int32_t>(c.n_layers);
+    s.n_head = static_cast<int32_t>(c.n_head);
+    s.n_head_kv = static_cast<int32_t>(c.n_head_kv);
+    s.head_dim = static_cast<int32_t>(c.head_dim());
+    s.rope_freq_base = c.rope_freq_base;
+    return s;
+}
+
+// Floats of the `att` buffer attention_gpu needs (its split-K workspace).
+std::size_t attention_workspace_floats(const AttnConfig& cfg);
+
+// ops.h:175-176, in place on device q/k.
+void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv, float freq_base,
+              void* stream = nullptr);
+
+// ops.h:204-206 with device pointers; `att` is the device workspace of
+// attention_workspace_floats(cfg) floats (the reference's score scratch).
+void attention_gpu(float* out, const float* q, const float* k, const float* v, float* key_cache,
+                   float* value_cache, float* att, int layer, int pos, const AttnConfig& cfg,
+                   void* stream = nullptr);
+
+// forward.cpp:192-208 fused: q, k unrotated (left unmodified).
+void rope_attention_gpu(float* out, const float* q, const float* k, const float* v,
+                        float* key_cache, float* value_cache, float* att, int layer, int pos,
+                        const AttnConfig& cfg, void* stream = nullptr);
+
+// Device-memory helpers so C++ callers need no CUDA headers of their own.
+float* device_alloc_floats(std::size_t n);
+void device_free(void* p);
+void copy_to_device(float* dst, const float* src, std::size_t n);
+void copy_to_host(float* dst, const float* src, std::size_t n);
+void device_zero(float* p, std::size_t n);
+void device_sync();
+
+// run_state.h:27-182 for the attention block, in HBM: q/k/v/xb2 activations,
+// the [n_layers][n_ctx][kv_dim] fp32 KV cache (zeroed, run_state.h:152-153)
+// and the attention workspace that replaces `att`.
+struct DeviceRunState {
+    float* xb2 = nullptr;  // attention output [n_embd]
+    float* q = nullptr;    // [n_embd]
+    float* k = nullptr;    // [kv_dim]
+    float* v = nullptr;    // [kv_dim]
+    float* att = nullptr;  // workspace [attention_workspace_floats]
+    float* key_cache = nullptr;
+    float* value_cache = nullptr;
+    int pos = 0;
+
+    DeviceRunState() = default;
+    DeviceRunState(const DeviceRunState&) = delete;
+    DeviceRunState& operator=(const DeviceRunState&) = delete;
+    ~DeviceRunState() { free_buffers(); }
+
+    void allocate(const AttnConfig& cfg);
+    void free_buffers();
+};
+
+// Many independent sequences decoded together (batched decode).
+class DecodeBatch {
+public:
+    DecodeBatch(const AttnConfig& cfg, std::vector<tle_seq_t> seqs, int max_ctas = 0);
+    ~DecodeBatch();
+    DecodeBatch(const DecodeBatch&) = delete;
+    DecodeBatch& operator=(const DecodeBatch&) = delete;
+
+    // Re-plans after positions change (e.g. every decode step: pos += 1).
+    void set_positions(const std::vector<int32_t>& pos);
+    // One layer of decode for all sequences; q/k/v/out are device arrays
+    // [n][n_embd], [n][kv_dim], [n][kv_dim], [n][n_embd].
+    void run(const float* q, const float* k, const float* v, float* out, int layer, bool rotate,
+             void* stream = nullptr);
+    int n_ctas() const { return n_ctas_; }
+    int n_seqs() const { return static_cast<int>(seqs_.size()); }
+
+private:
+    void upload();
+    tle_shape_t shape_;
+    std::vector<tle_seq_t> seqs_;
+    int max_ctas_;
+    int n_ctas_ = 0;
+    std::vector<unsigned char> desc_host_;
+    void* desc_dev_ = nullptr;
+    std::size_t desc_cap_ = 0;
+    void* ws_ = nullptr;
+    std::size_t ws_bytes_ = 0;
+};
+
+}  // namespace tle

@@ -1,0 +1,269 @@
+"""Python plumbing over the C ABI in include/tle_attn.h (libtle_attn.so).
+
+The product is the C ABI and the sm_100a kernels behind it; this module only
+marshals torch CUDA tensors (device memory, streams) into those calls, the
+way the reference's callers pass raw float pointers (src/ops.h:175-206).
+There is no fallback: if libtle_attn.so is missing or a call fails, an
+exception is raised.
+
+Names follow the reference: ``rope`` (ops.h:175), ``attention`` (ops.h:204),
+``rope_attention`` (forward.cpp:192-208 fused), ``DecodeBatch`` (attention()
+for many sequences), ``prefill`` (generate.cpp:56-59 as one causal kernel).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Iterable, List, Optional, Sequence
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtle_attn.so")
+
+TLE_OK = 0
+TLE_ERR_INVALID = 1
+TLE_ERR_UNSUPPORTED = 2
+TLE_ERR_WORKSPACE = 3
+TLE_ERR_CUDA = 4
+TLE_ERR_DEVICE = 5
+
+# Every symbol include/tle_attn.h declares (tests check the .so exports them).
+EXPORTED = (
+    "tle_last_error", "tle_version", "tle_rope", "tle_attention_workspace_bytes",
+    "tle_attention", "tle_rope_attention", "tle_decode_desc_bytes", "tle_decode_desc",
+    "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
+    "tle_prefill", "tle_partition_lpt", "tle_device_error",
+)
+
+
+class TleError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"tle error {code}: {msg}")
+        self.code = code
+
+
+class Shape(ctypes.Structure):
+    """tle_shape_t: the llama_config_t fields attention reads (gguf.h:139-168)."""
+    _fields_ = [("n_layers", ctypes.c_int32), ("n_head", ctypes.c_int32),
+                ("n_head_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("rope_freq_base", ctypes.c_float)]
+
+
+class Seq(ctypes.Structure):
+    """tle_seq_t: one sequence's device KV cache and decode position."""
+    _fields_ = [("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
+                ("n_ctx", ctypes.c_int32), ("pos", ctypes.c_int32)]
+
+
+def tinyllama_shape(n_layers: int = 22) -> Shape:
+    return Shape(n_layers, 32, 4, 64, 10000.0)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libtle_attn.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} missing: run `make` (or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i, f, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+        P = ctypes.POINTER
+        L.tle_last_error.restype = ctypes.c_char_p
+        L.tle_version.restype = ctypes.c_char_p
+        L.tle_rope.argtypes = [vp, vp, i, i, i, i, f, vp]
+        L.tle_attention_workspace_bytes.argtypes = [P(Shape), i]
+        L.tle_attention_workspace_bytes.restype = sz
+        for name in ("tle_attention", "tle_rope_attention"):
+            getattr(L, name).argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), vp, sz, vp]
+        L.tle_decode_desc_bytes.argtypes = [i, i]
+        L.tle_decode_desc_bytes.restype = sz
+        L.tle_decode_desc.argtypes = [P(Shape), P(Seq), i, i, vp, sz, P(i)]
+        L.tle_decode_workspace_bytes.argtypes = [P(Shape), i, i]
+        L.tle_decode_workspace_bytes.restype = sz
+        L.tle_decode_batch.argtypes = [P(Shape), vp, i, i, vp, vp, vp, vp, i, i, vp, sz, vp]
+        L.tle_prefill_workspace_bytes.argtypes = [P(Shape), i, i]
+        L.tle_prefill_workspace_bytes.restype = sz
+        L.tle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, P(Shape), vp, sz, vp]
+        L.tle_partition_lpt.argtypes = [P(ctypes.c_int32), i, i, P(ctypes.c_int32)]
+        L.tle_device_error.argtypes = [i, P(ctypes.c_uint32)]
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != TLE_OK:
+        raise TleError(rc, lib().tle_last_error().decode())
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream(stream) -> int:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+def _want(t, numel: int, name: str):
+    import torch
+    if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name}: need a contiguous float32 CUDA tensor")
+    if t.numel() < numel:
+        raise ValueError(f"{name}: need at least {numel} elements, got {t.numel()}")
+
+
+def version() -> str:
+    return lib().tle_version().decode()
+
+
+# ---------------------------------------------------------------- ops.h:175
+def rope(q, k, pos: int, head_dim: int = 64, n_head: int = 32, n_head_kv: int = 4,
+         freq_base: float = 10000.0, stream=None) -> None:
+    """In-place RoPE on device q [n_head*hd] and k [n_head_kv*hd] (ops.cpp:1223)."""
+    _want(q, n_head * head_dim, "q")
+    _want(k, n_head_kv * head_dim, "k")
+    _check(lib().tle_rope(_ptr(q), _ptr(k), pos, head_dim, n_head, n_head_kv, freq_base,
+                          _stream(stream)))
+
+
+def attention_workspace(shape: Shape, n_ctx: int):
+    import torch
+    n = lib().tle_attention_workspace_bytes(ctypes.byref(shape), n_ctx)
+    return torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
+
+
+def _single(fn, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace, stream):
+    _want(out, 2048, "out"); _want(q, 2048, "q"); _want(k, 256, "k"); _want(v, 256, "v")
+    _want(key_cache, (layer + 1) * n_ctx * 256, "key_cache")
+    _want(value_cache, (layer + 1) * n_ctx * 256, "value_cache")
+    if workspace is None:
+        workspace = attention_workspace(shape, n_ctx)
+    _check(fn(_ptr(out), _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), layer,
+              pos, n_ctx, ctypes.byref(shape), _ptr(workspace), workspace.numel() * 4,
+              _stream(stream)))
+
+
+# ---------------------------------------------------------------- ops.h:204
+def attention(out, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx: int,
+              shape: Optional[Shape] = None, workspace=None, stream=None) -> None:
+    """attention() with device buffers; q, k already rotated (ops.cpp:1317)."""
+    shape = shape or tinyllama_shape()
+    _single(lib().tle_attention, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape,
+            workspace, stream)
+
+
+def rope_attention(out, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx: int,
+                   shape: Optional[Shape] = None, workspace=None, stream=None) -> None:
+    """rope()+attention() (forward.cpp:192-208) in one launch; q, k unrotated."""
+    shape = shape or tinyllama_shape()
+    _single(lib().tle_rope_attention, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx,
+            shape, workspace, stream)
+
+
+# ----------------------------------------------------------- batched decode
+class DecodeBatch:
+    """attention() for many independent sequences in one launch per layer.
+
+    ``caches`` is a list of (key_cache, value_cache, n_ctx) device tensors,
+    each [n_layers][n_ctx][256] fp32.  ``set_positions`` re-plans the split
+    of rows over CTAs (host) and uploads the descriptor (one H2D copy).
+    """
+
+    def __init__(self, caches: Sequence, positions: Sequence[int], shape: Optional[Shape] = None,
+                 max_ctas: int = 0):
+        import torch
+        self.shape = shape or tinyllama_shape()
+        self.caches = list(caches)
+        self.n = len(self.caches)
+        self.max_ctas = max_ctas
+        L = lib()
+        self.desc_bytes = L.tle_decode_desc_bytes(self.n, max_ctas)
+        self._desc_host = torch.empty(self.desc_bytes, dtype=torch.uint8).pin_memory()
+        self._desc_dev = torch.empty(self.desc_bytes, dtype=torch.uint8, device="cuda")
+        self.workspace = None
+        self.n_ctas = 0
+        self.set_positions(positions)
+
+    def build_host(self, positions: Sequence[int]) -> int:
+        """Fills the pinned host descriptor; returns the CTA count."""
+        if len(positions) != self.n:
+            raise ValueError("one position per sequence")
+        seqs = (Seq * self.n)()
+        for i, (kc, vc, n_ctx) in enumerate(self.caches):
+            seqs[i] = Seq(_ptr(kc), _ptr(vc), int(n_ctx), int(positions[i]))
+        n_ctas = ctypes.c_int(0)
+        _check(lib().tle_decode_desc(ctypes.byref(self.shape), seqs, self.n, self.max_ctas,
+                                     self._desc_host.data_ptr(), self.desc_bytes,
+                                     ctypes.byref(n_ctas)))
+        return n_ctas.value
+
+    def set_positions(self, positions: Sequence[int], stream=None) -> None:
+        import torch
+        self.positions = [int(p) for p in positions]
+        self.n_ctas = self.build_host(self.positions)
+        nbytes = lib().tle_decode_workspace_bytes(ctypes.byref(self.shape), self.n, self.n_ctas)
+        if self.workspace is None or self.workspace.numel() * 4 < nbytes:
+            self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device="cuda")
+        self.upload(stream)
+
+    def upload(self, stream=None) -> None:
+        """H2D copy of the descriptor on `stream` (pinned -> device)."""
+        import torch
+        s = stream or torch.cuda.current_stream()
+        with torch.cuda.stream(s):
+            self._desc_dev.copy_(self._desc_host, non_blocking=True)
+
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+        n = self.n
+        _want(q, n * 2048, "q"); _want(k, n * 256, "k"); _want(v, n * 256, "v")
+        _want(out, n * 2048, "out")
+        _check(lib().tle_decode_batch(ctypes.byref(self.shape), self._desc_dev.data_ptr(), n,
+                                      self.n_ctas, _ptr(q), _ptr(k), _ptr(v), _ptr(out), layer,
+                                      1 if rotate else 0, _ptr(self.workspace),
+                                      self.workspace.numel() * 4, _stream(stream)))
+
+
+# ------------------------------------------------------------------ prefill
+def prefill_workspace(n_tokens: int, pos0: int = 0, shape: Optional[Shape] = None):
+    import torch
+    shape = shape or tinyllama_shape()
+    n = lib().tle_prefill_workspace_bytes(ctypes.byref(shape), n_tokens, pos0)
+    # over-allocate by 1 KB so the buffer can start on a 1024-byte boundary
+    raw = torch.empty(n + 1024, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % 1024
+    return raw[off:off + n] if n > 0 else raw[off:off + 1024]
+
+
+def prefill(out, q, k, v, key_cache, value_cache, layer: int, pos0: int, n_ctx: int,
+            shape: Optional[Shape] = None, workspace=None, stream=None) -> None:
+    """S successive rope+attention steps as one causal kernel (generate.cpp:56-59)."""
+    shape = shape or tinyllama_shape()
+    n_tokens = q.numel() // 2048
+    _want(out, n_tokens * 2048, "out"); _want(k, n_tokens * 256, "k"); _want(v, n_tokens * 256, "v")
+    if workspace is None:
+        workspace = prefill_workspace(n_tokens, pos0, shape)
+    _check(lib().tle_prefill(_ptr(out), _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache),
+                             _ptr(value_cache), layer, pos0, n_tokens, n_ctx, ctypes.byref(shape),
+                             _ptr(workspace), workspace.numel() * workspace.element_size(),
+                             _stream(stream)))
+
+
+# ---------------------------------------------------------- multi-GPU plan
+def partition_lpt(lengths: Iterable[int], n_ranks: int) -> List[int]:
+    """Rank of each sequence under greedy longest-processing-time balancing."""
+    lengths = [int(x) for x in lengths]
+    n = len(lengths)
+    arr = (ctypes.c_int32 * max(n, 1))(*lengths)
+    out = (ctypes.c_int32 * max(n, 1))()
+    _check(lib().tle_partition_lpt(arr, n, n_ranks, out))
+    return [int(out[i]) for i in range(n)]
+
+
+def device_error(clear: bool = True) -> int:
+    code = ctypes.c_uint32(0)
+    _check(lib().tle_device_error(1 if clear else 0, ctypes.byref(code)))
+    return code.value
