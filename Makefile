@@ -19,7 +19,7 @@ HOST_SRCS := $(HOST)/ops_gpu.cpp
 CU_OBJS := $(patsubst $(CSRC)/%.cu,_build/%.o,$(CU_SRCS))
 HOST_OBJS := $(patsubst $(HOST)/%.cpp,_build/host_%.o,$(HOST_SRCS))
 
-all: $(LIB) oracle
+all: $(LIB) oracle cpptest
 
 _build:
 	mkdir -p _build
@@ -36,7 +36,9 @@ $(LIB): $(CU_OBJS) $(HOST_OBJS)
 oracle:
 	$(MAKE) -C oracle
 
-cpptest: $(LIB) tests/cpp/test_ops_gpu.cpp
+cpptest: tests/cpp/test_ops_gpu
+
+tests/cpp/test_ops_gpu: $(LIB) tests/cpp/test_ops_gpu.cpp $(HOST)/ops_gpu.h
 	g++ -std=c++20 -O2 -Wall -Iinclude -I$(HOST) tests/cpp/test_ops_gpu.cpp \
 	    -L$(PKG) -ltle_attn -Wl,-rpath,'$$ORIGIN/../../$(PKG)' -o tests/cpp/test_ops_gpu
 

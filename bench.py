@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--seqs", type=int, default=N_SEQS)
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the config-3 prefill and config-4 ragged-decode lines")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target wall time of the CPU-baseline sample")
     return ap.parse_args()
@@ -203,12 +205,11 @@ def main():
                                 device_id=dev)
 
     # ---- shard the sequences (LPT by length; all equal here) ----
-    lengths = [args.ctx] * args.seqs
-    owner = tle.partition_lpt(lengths, world)
-    mine = [s for s in range(args.seqs) if owner[s] == rank]
-    counts = [owner.count(r) for r in range(world)]
-    max_local = max(counts)
+    import shard
+    plan = shard.plan([args.ctx] * args.seqs, world)
+    mine = plan.mine(rank)
     n = len(mine)
+    max_local = plan.max_local
 
     # ---- device-resident state (KV caches of my sequences) ----
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -222,18 +223,8 @@ def main():
     hv = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
     q = hq.to(dev); k = hk.to(dev); v = hv.to(dev)
     out = torch.zeros((max_local, QD), device=dev)
-    gathered = torch.zeros((world * max_local, QD), device=dev)
+    gather = shard.OutputGather(plan, QD, dev)
     hout = torch.zeros((args.seqs, QD)).pin_memory()
-    # global sequence order of the gathered rows
-    order = []
-    for r in range(world):
-        rs = [s for s in range(args.seqs) if owner[s] == r]
-        order += rs + [-1] * (max_local - len(rs))
-    inv = torch.empty(args.seqs, dtype=torch.long)
-    for i, s in enumerate(order):
-        if s >= 0:
-            inv[s] = i
-    inv = inv.to(dev)
     stream = torch.cuda.current_stream(dev)
 
     def decode_only():
@@ -241,10 +232,7 @@ def main():
 
     def step():
         decode_only()
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            return gathered.index_select(0, inv)
-        return out
+        return gather(out)   # NCCL all-gather + reorder (world > 1)
 
     def barrier():
         if world > 1:
@@ -269,9 +257,7 @@ def main():
         kev[i][0].record(stream)
         decode_only()
         kev[i][1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            gathered.index_select(0, inv)
+        gather(out)
     ev[1].record(stream)
     barrier()
     t_ms = ev[0].elapsed_time(ev[1])
@@ -286,11 +272,7 @@ def main():
         q.copy_(hq, non_blocking=True)
         k.copy_(hk, non_blocking=True)
         v.copy_(hv, non_blocking=True)
-        res = step()
-        if world > 1:
-            hout.copy_(res, non_blocking=True)
-        else:
-            hout[:n].copy_(res[:n], non_blocking=True)
+        hout.copy_(step(), non_blocking=True)
     e2[1].record(stream)
     barrier()
     e2e_ms = e2[0].elapsed_time(e2[1])
@@ -336,13 +318,16 @@ def main():
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(hq[:n].numel() * 4 + hk[:n].numel() * 4
                                               + hv[:n].numel() * 4 + batch.desc_bytes),
-                    "d2h_bytes_per_step": int(args.seqs * QD * 4 if world > 1 else n * QD * 4),
+                    "d2h_bytes_per_step": int(args.seqs * QD * 4),
                     "ms_per_step": round(e2e_ms / args.steps, 4),
                     "path": "tle.DecodeBatch.run (C ABI tle_decode_batch) with pinned host q/k/v "
                             "in and host out back every step"},
             "gpu_launches": 2 * args.steps,
             "clocks": clk,
         }
+        if world == 1 and not args.no_secondary:
+            line["secondary"] = {"prefill_config3": measure_prefill(dev, peaks),
+                                 "decode_config4": measure_config4(dev, peaks)}
         if world == 1 and not args.no_cpu_baseline:
             gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
             line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
@@ -351,6 +336,93 @@ def main():
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def _time_steps(fn, steps, warmup, stream):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def measure_prefill(dev, peaks, steps=10, warmup=3):
+    """Config 3: causal prefill S=2048 (32 q / 4 kv heads, hd 64) for each of
+    22 layers; a step is the 22 tle_prefill calls (distinct per-layer inputs,
+    440 MB > L2).  FLOPs are algorithmic: 4*64*32*S(S+1)/2 per layer."""
+    import torch
+    import tle
+    S, n_layers = 2048, 22
+    g = torch.Generator(device=dev).manual_seed(33)
+    q = torch.randn((n_layers, S, QD), generator=g, device=dev)
+    k = torch.randn((n_layers, S, KVD), generator=g, device=dev)
+    v = torch.randn((n_layers, S, KVD), generator=g, device=dev)
+    kc = torch.zeros((n_layers, S, KVD), device=dev)
+    vc = torch.zeros_like(kc)
+    out = torch.zeros((S, QD), device=dev)
+    shape = tle.tinyllama_shape(n_layers)
+    ws = tle.prefill_workspace(S, 0, shape)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(n_layers):
+            tle.prefill(out, q[l], k[l], v[l], kc, vc, l, 0, S, shape, ws, stream)
+
+    ms = _time_steps(step, steps, warmup, stream)
+    flops = n_layers * 4.0 * HD * NH * S * (S + 1) / 2
+    tflops = flops / (ms / 1e3) / 1e12
+    return {"workload": "config3: causal prefill S=2048, 22 layers per step, bf16 tcgen05 MMA, "
+                        "fp32 softmax, fused rope+append (prep kernel)",
+            "metric": "prefill attn TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4), "ms_per_layer": round(ms / n_layers, 4),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(tflops / peaks["bf16_tflops"], 4),
+                         "peak_source": peaks["source"] + ", burst"},
+            "gpu_launches": 2 * n_layers * steps}
+
+
+def measure_config4(dev, peaks, steps=20, warmup=3):
+    """Config 4: 64 sequences, attended lengths U[128, 2048] (seeded), 22-layer
+    fp32 caches; a step is one decode token for every sequence = 22
+    tle_decode_batch calls (3.1 GB of KV, > L2)."""
+    import numpy as np
+    import torch
+    import tle
+    n_layers = 22
+    lengths = np.random.default_rng(4).integers(128, 2049, 64)
+    g = torch.Generator(device=dev).manual_seed(44)
+    caches = []
+    for L in lengths:
+        caches.append((torch.randn((n_layers, int(L), KVD), generator=g, device=dev),
+                       torch.randn((n_layers, int(L), KVD), generator=g, device=dev), int(L)))
+    batch = tle.DecodeBatch(caches, [int(L) - 1 for L in lengths], tle.tinyllama_shape(n_layers))
+    q = torch.randn((64, QD), generator=g, device=dev)
+    k = torch.randn((64, KVD), generator=g, device=dev)
+    v = torch.randn((64, KVD), generator=g, device=dev)
+    out = torch.zeros((64, QD), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(n_layers):
+            batch.run(q, k, v, out, l, True, stream)
+
+    ms = _time_steps(step, steps, warmup, stream)
+    kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    return {"workload": "config4: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step" % int(lengths.sum()),
+            "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+            "n_ctas": batch.n_ctas,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+            "gpu_launches": 2 * n_layers * steps}
 
 
 def load_peaks():

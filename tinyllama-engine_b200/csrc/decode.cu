@@ -40,10 +40,9 @@ constexpr int ROWF = kRowFloats;   // 256 floats per cache row
 constexpr int ROWB = ROWF * 4;     // 1024 bytes
 constexpr int TILE = 32;           // rows per pipeline stage
 constexpr int NSTAGE = 3;
-constexpr int NCW = 8;             // consumer warps
-constexpr int NCT = NCW * 32;      // consumer threads
-constexpr int NTHR = NCT + 32;     // + one producer warp
-constexpr int RPW = TILE / NCW;    // rows per consumer warp per tile (4)
+constexpr int NCW = 8;             // warps (all consume; warp 0 lane 0 also issues the copies)
+constexpr int NCT = NCW * 32;      // threads per CTA
+constexpr int RPW = TILE / NCW;    // rows per warp per tile (4)
 constexpr int QS = HD + 4;         // padded q/o row stride in shared memory
 constexpr float kScale = 0.125f;   // 1/sqrt(64), exact in fp32
 
@@ -57,14 +56,7 @@ struct __align__(128) DecodeSmem {
     float fin[NH][2];        // merged (m, l)
     uint64_t full[NSTAGE];
     uint64_t empty[NSTAGE];
-    uint64_t csync;          // consumer-warp barrier
-    uint64_t prod_done;      // producer finished issuing
-    int issued;              // tiles issued by the producer
-    volatile int abort_flag;
-};
-
-struct Segment {
-    int s, a, b;  // sequence, rows [a, b)
+    uint64_t csync;          // all-warp barrier (bounded waits)
 };
 
 // CTA c's row range as (start seq, start off) .. (end seq, end off), exclusive end.
@@ -86,8 +78,56 @@ __device__ __forceinline__ tle_seq_t load_seq(const DecodeArgs& A, int s) {
     return A.seqs ? A.seqs[s] : A.single;
 }
 
-// Consumer-only barrier on an mbarrier (bounded wait; false on timeout).
-__device__ __forceinline__ bool consumer_sync(DecodeSmem& S, uint32_t& phase, int lane) {
+__device__ __forceinline__ bool in_range(int s, int off, int s1, int o1) {
+    return s < s1 || (s == s1 && off < o1);
+}
+
+// The copy issuer's position in the CTA's sequence of tiles (it runs up to
+// NSTAGE tiles ahead of the consumers).
+struct TileCursor {
+    int s, ta, b;
+    bool done;
+    const float* kb;
+    const float* vb;
+    int pos;
+};
+
+__device__ __forceinline__ void cursor_load(TileCursor& c, const DecodeArgs& A, int s, int off,
+                                            int s1, int o1) {
+    c.s = s;
+    c.ta = off;
+    c.done = !in_range(s, off, s1, o1);
+    if (!c.done) {
+        const tle_seq_t sq = load_seq(A, s);
+        c.b = (s == s1) ? o1 : sq.pos + 1;
+        const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
+        c.kb = sq.key_cache + base;
+        c.vb = sq.value_cache + base;
+        c.pos = sq.pos;
+    }
+}
+
+// Issues the cursor's tile into stage st (1-D bulk copies of whole 1 KB rows)
+// and advances the cursor.  Row `pos` (the token being decoded) is never read
+// from the cache: the consumers take it from newk/newv.
+__device__ __forceinline__ void cursor_issue(TileCursor& c, const DecodeArgs& A, DecodeSmem& S,
+                                             int st, int s1, int o1, uint64_t pol) {
+    const int tb = min(c.ta + TILE, c.b);
+    const int n = min(tb, c.pos) - c.ta;
+    if (n > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(n) * ROWB;
+        mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
+        bulk_g2s(S.k[st], c.kb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
+        bulk_g2s(S.v[st], c.vb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
+    } else {
+        mbar_arrive(&S.full[st]);
+    }
+    c.ta = tb;
+    if (c.ta >= c.b) cursor_load(c, A, c.s + 1, 0, s1, o1);
+}
+
+// All-warp barrier on an mbarrier (bounded wait; false on timeout).
+__device__ __forceinline__ bool cta_sync(DecodeSmem& S, uint32_t& phase, int lane) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.csync);
     const bool ok = mbar_wait(&S.csync, phase);
@@ -96,18 +136,14 @@ __device__ __forceinline__ bool consumer_sync(DecodeSmem& S, uint32_t& phase, in
     return ok;
 }
 
-__device__ __forceinline__ void fail(const DecodeArgs& A, DecodeSmem& S, uint32_t code) {
-    record_error(A.err, code);
-    S.abort_flag = 1;
-}
-
-__global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArgs A) {
+__global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ DecodeArgs A) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     DecodeSmem& S = *reinterpret_cast<DecodeSmem*>(smem_raw);
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int cta = blockIdx.x;
+    const bool issuer = (tid == 0);
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; ++i) {
@@ -115,9 +151,6 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
             mbar_init(&S.empty[i], NCW);
         }
         mbar_init(&S.csync, NCW);
-        mbar_init(&S.prod_done, 1);
-        S.issued = 0;
-        S.abort_flag = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -125,56 +158,26 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
     int s0, o0, s1, o1;
     cta_range(A, cta, s0, o0, s1, o1);
 
-    if (warp == NCW) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            const uint64_t pol = l2_evict_first_policy();
-            int it = 0;
-            bool ok = true;
-            for (int s = s0, off = o0; ok && (s < s1 || (s == s1 && off < o1)); ++s, off = 0) {
-                const tle_seq_t sq = load_seq(A, s);
-                const int L = sq.pos + 1;
-                const int b = (s == s1) ? o1 : L;
-                const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
-                const float* kb = sq.key_cache + base;
-                const float* vb = sq.value_cache + base;
-                for (int ta = off; ta < b; ta += TILE) {
-                    const int tb = min(ta + TILE, b);
-                    const int st = it % NSTAGE;
-                    if (S.abort_flag || !mbar_wait(&S.empty[st], ((it / NSTAGE) & 1) ^ 1)) {
-                        if (!S.abort_flag) fail(A, S, kErrWaitEmpty);
-                        ok = false;
-                        break;
-                    }
-                    // Row `pos` (the token being decoded) is never read from the
-                    // cache: the consumers take it from newk/newv.
-                    const int n = min(tb, sq.pos) - ta;
-                    if (n > 0) {
-                        const uint32_t bytes = static_cast<uint32_t>(n) * ROWB;
-                        mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
-                        bulk_g2s(S.k[st], kb + static_cast<size_t>(ta) * ROWF, bytes, &S.full[st], pol);
-                        bulk_g2s(S.v[st], vb + static_cast<size_t>(ta) * ROWF, bytes, &S.full[st], pol);
-                    } else {
-                        mbar_arrive(&S.full[st]);
-                    }
-                    ++it;
-                    S.issued = it;
-                }
-            }
-            mbar_arrive(&S.prod_done);
+    // Prologue: the issuer fills the first NSTAGE stages.
+    TileCursor cur;
+    uint64_t pol = 0;
+    int issued = 0;
+    if (issuer) {
+        pol = l2_evict_first_policy();
+        cursor_load(cur, A, s0, o0, s1, o1);
+        while (!cur.done && issued < NSTAGE) {
+            cursor_issue(cur, A, S, issued, s1, o1, pol);
+            ++issued;
         }
-        __syncwarp();
-        return;
     }
 
-    // ------------------------------ consumers ------------------------------
     const int g = lane >> 3;       // KV head of this lane's query head
     const int h = lane;            // query head
     uint32_t cphase = 0;
     int it = 0;
     bool ok = true;
 
-    for (int s = s0, off = o0; ok && (s < s1 || (s == s1 && off < o1)); ++s, off = 0) {
+    for (int s = s0, off = o0; ok && in_range(s, off, s1, o1); ++s, off = 0) {
         const tle_seq_t sq = load_seq(A, s);
         const int L = sq.pos + 1;
         const int seg_a = off;
@@ -222,7 +225,7 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
                 reinterpret_cast<float2*>(sq.value_cache + row)[t2] = x;
             }
         }
-        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
 
         // This lane's query head, its 16-byte chunks in KV-head-rotated order.
         float4 q[16];
@@ -236,9 +239,25 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
         for (int c = 0; c < 16; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
 
         for (int ta = seg_a; ta < seg_b; ta += TILE) {
+            // Refill: the stage of tile it-1 takes tile it-1+NSTAGE once all
+            // warps have released it.
+            if (issuer && it >= 1 && !cur.done) {
+                const int ps = (it - 1) % NSTAGE;
+                if (!mbar_wait(&S.empty[ps], ((it - 1) / NSTAGE) & 1)) {
+                    record_error(A.err, kErrWaitEmpty);
+                    cur.done = true;
+                } else {
+                    cursor_issue(cur, A, S, ps, s1, o1, pol);
+                    ++issued;
+                }
+            }
             const int nrows = min(ta + TILE, seg_b) - ta;
             const int st = it % NSTAGE;
-            if (!mbar_wait(&S.full[st], (it / NSTAGE) & 1)) { fail(A, S, kErrWaitFull); ok = false; break; }
+            if (!mbar_wait(&S.full[st], (it / NSTAGE) & 1)) {
+                record_error(A.err, kErrWaitFull);
+                ok = false;
+                break;
+            }
             const int r0 = warp * RPW;
             if (r0 < nrows) {
                 const float* kp[RPW];
@@ -313,7 +332,7 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
         // ---- merge the 8 warps' (m, l, acc) for this segment ----
         S.ml[warp][h][0] = m_run;
         S.ml[warp][h][1] = l_run;
-        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
         float mstar = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NCW; ++w) mstar = fmaxf(mstar, S.ml[w][h][0]);
@@ -341,7 +360,7 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
                     *dst = val;
                 }
             }
-            if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; }
+            if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; }
         }
         if (!ok) break;
 
@@ -367,18 +386,14 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeArg
                 }
             }
         }
-        if (!consumer_sync(S, cphase, lane)) { fail(A, S, kErrWaitFull); ok = false; break; }
+        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
     }
 
-    // Exit: every bulk copy the producer issued must have landed before the
-    // CTA's shared memory goes away (only matters on the error path).
-    if (tid == 0) {
-        if (!mbar_wait(&S.prod_done, 0)) {
-            record_error(A.err, kErrDrain);
-        } else {
-            for (int t = it; t < S.issued; ++t)
-                if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
-        }
+    // Exit (error path only): every copy the issuer started must land before
+    // the CTA's shared memory is released.
+    if (issuer) {
+        for (int t = it; t < issued; ++t)
+            if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
     }
 }
 
@@ -448,7 +463,7 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
-    decode_kernel<<<a.n_ctas, NTHR, smem, stream>>>(a);
+    decode_kernel<<<a.n_ctas, NCT, smem, stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (a.n_ctas > 1) {
