@@ -115,6 +115,31 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
                      const float* q, const float* k, const float* v, float* out, int layer,
                      int rotate, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- decode without allocation ----
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc:
+ * a host framework that owns all device memory through its own pool, or a
+ * per-token loop that must not pay cudaMalloc/cudaFree's implicit device
+ * synchronisation.  Same kernels and results as tle_decode_batch, but the
+ * batch descriptor is built from HOST records (seqs) and both it and the
+ * split-K partials live in a fixed file-scope device array of about 4.2 MB
+ * (TLE_NOALLOC_MAX_SEQS sequences, up to 256 CTAs) that every GPU loading
+ * the library keeps until the process exits.  The caller passes only inputs
+ * and outputs; nothing is allocated (no cudaMalloc/cudaFree, no allocating
+ * library routine).
+ *  - n_seqs > TLE_NOALLOC_MAX_SEQS is rejected with TLE_ERR_INVALID.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - Every call shares the one array: calls that overlap on the GPU (other
+ *    streams, other host threads on the same device) race.  Calls on one
+ *    stream are ordered.  Nothing in the array needs to start at zero: each
+ *    call rewrites the descriptor and every partial it reads.
+ *  - The descriptor is copied from pageable host memory on `stream`, which
+ *    makes the call wait for earlier work on that stream. */
+#define TLE_NOALLOC_MAX_SEQS 256
+int tle_decode_batch_noalloc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
+                             const float* q, const float* k, const float* v, float* out, int layer,
+                             int rotate, void* stream);
+
 /* ---- prefill ---- */
 
 /* Workspace for tle_prefill with n_rows = pos0 + n_tokens attended rows. */

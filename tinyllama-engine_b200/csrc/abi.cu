@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -347,3 +348,156 @@ int tle_device_error(int clear, uint32_t* code) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without allocation (tle_decode_batch_noalloc).
+//
+// For callers that cannot call cudaMalloc -- a host framework that owns all
+// device memory through its own pool, or a per-token loop that must not pay
+// cudaMalloc/cudaFree's implicit device synchronisation.  Its scratch (the
+// batch descriptor and the split-K partials) lives in this fixed-size
+// file-scope device array, which every GPU that loads the library keeps until
+// the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxSeqs = TLE_NOALLOC_MAX_SEQS;
+constexpr int kNoAllocMaxCtas = 256;
+constexpr size_t kNoAllocDescBytes = 32768;
+constexpr size_t kNoAllocPartialBytes =
+    static_cast<size_t>(kNoAllocMaxSeqs + kNoAllocMaxCtas) * tle::kPartialFloats * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocDescBytes + kNoAllocPartialBytes;
+static_assert(sizeof(tle::DescHeader) + sizeof(tle_seq_t) * kNoAllocMaxSeqs +
+                      sizeof(tle::CtaStart) * (kNoAllocMaxCtas + 1) +
+                      sizeof(tle::SeqCtas) * kNoAllocMaxSeqs <=
+                  kNoAllocDescBytes,
+              "descriptor region too small");
+constexpr int kNoAllocMaxDevices = 64;
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Host staging for the descriptor: fixed size, per host thread, no malloc.
+thread_local unsigned char t_noalloc_desc[kNoAllocDescBytes];
+
+}  // namespace
+
+// The scratch itself.  In host code this name is only a stand-in for the
+// symbol: its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_tle_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+
+// Device address of the scratch on the current device; looked up once per
+// device (the first call on a device) and cached.
+int noalloc_scratch(unsigned char** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return set_error(TLE_ERR_UNSUPPORTED, "device %d beyond the no-allocation table", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tle_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(no-allocation scratch)");
+        g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return TLE_OK;
+}
+
+// Same plan as tle_decode_desc, written into a caller-provided buffer with
+// running sums instead of a prefix array (no host allocation).
+void fill_desc_noalloc(const tle_seq_t* seqs, int n_seqs, int G, int64_t total, unsigned char* base) {
+    tle::DescHeader hdr{};
+    hdr.magic = tle::kDescMagic;
+    hdr.n_seqs = n_seqs;
+    hdr.n_ctas = G;
+    hdr.total_rows = total;
+    std::memcpy(base, &hdr, sizeof hdr);
+    std::memcpy(base + tle::desc_seqs_offset(), seqs, sizeof(tle_seq_t) * static_cast<size_t>(n_seqs));
+    auto* cs = reinterpret_cast<tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
+    auto* sc = reinterpret_cast<tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, G));
+    int s = 0;
+    int64_t start_s = 0;  // first concatenated row of sequence s
+    for (int c = 0; c <= G; ++c) {
+        const int64_t x = (c == G) ? total : static_cast<int64_t>(c) * total / G;
+        while (s < n_seqs && start_s + seqs[s].pos + 1 <= x) {
+            start_s += seqs[s].pos + 1;
+            ++s;
+        }
+        cs[c].seq = s;
+        cs[c].off = (s < n_seqs) ? static_cast<int32_t>(x - start_s) : 0;
+    }
+    int c = 0;
+    int64_t first = 0;
+    for (int t = 0; t < n_seqs; ++t) {
+        const int64_t last = first + seqs[t].pos;
+        while (c + 1 < G && static_cast<int64_t>(c + 1) * total / G <= first) ++c;
+        int hi = c;
+        while (hi + 1 < G && static_cast<int64_t>(hi + 1) * total / G <= last) ++hi;
+        sc[t].lo = c;
+        sc[t].hi = hi;
+        first = last + 1;
+    }
+}
+
+}  // namespace
+
+extern "C" int tle_decode_batch_noalloc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
+                                        const float* q, const float* k, const float* v, float* out,
+                                        int layer, int rotate, void* stream) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!seqs || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (n_seqs <= 0) return set_error(TLE_ERR_INVALID, "n_seqs must be > 0");
+    if (n_seqs > kNoAllocMaxSeqs)
+        return set_error(TLE_ERR_INVALID,
+                         "n_seqs=%d exceeds the no-allocation scratch limit of %d sequences "
+                         "(TLE_NOALLOC_MAX_SEQS); use tle_decode_batch with a workspace",
+                         n_seqs, kNoAllocMaxSeqs);
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return set_error(TLE_ERR_INVALID, "buffers must be 16-byte aligned");
+    if (layer < 0 || layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
+    int64_t total = 0;
+    for (int s = 0; s < n_seqs; ++s) {
+        const tle_seq_t& r = seqs[s];
+        if (!r.key_cache || !r.value_cache || !aligned16(r.key_cache) || !aligned16(r.value_cache))
+            return set_error(TLE_ERR_INVALID, "sequence %d: caches must be non-null and 16-byte aligned", s);
+        if (r.n_ctx <= 0 || r.pos < 0 || r.pos >= r.n_ctx)
+            return set_error(TLE_ERR_INVALID, "sequence %d: need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", s,
+                             r.pos, r.n_ctx);
+        total += static_cast<int64_t>(r.pos) + 1;
+    }
+    unsigned char* scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+    const int G = choose_ctas(total, std::min(sm_count(), kNoAllocMaxCtas));
+    fill_desc_noalloc(seqs, n_seqs, G, total, t_noalloc_desc);
+    const size_t desc_bytes =
+        tle::desc_seqctas_offset(n_seqs, G) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Pageable source: the copy is staged before this call returns, so the
+    // host buffer may be refilled by the next call.
+    cudaError_t e = cudaMemcpyAsync(scratch, t_noalloc_desc, desc_bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_error(e, "descriptor upload");
+    tle::DecodeArgs a{};
+    a.seqs = reinterpret_cast<const tle_seq_t*>(scratch + tle::desc_seqs_offset());
+    a.cta_start = reinterpret_cast<const tle::CtaStart*>(scratch + tle::desc_cta_offset(n_seqs));
+    a.seq_ctas = reinterpret_cast<const tle::SeqCtas*>(scratch + tle::desc_seqctas_offset(n_seqs, G));
+    a.n_seqs = n_seqs;
+    a.n_ctas = G;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.partials = reinterpret_cast<float*>(scratch + kNoAllocDescBytes);
+    a.layer = layer;
+    a.rotate = rotate ? 1 : 0;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    e = tle::error_word(&a.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_decode(a, st);
+    if (e != cudaSuccess) return cuda_error(e, "decode launch");
+    return ok();
+}

@@ -31,7 +31,7 @@ EXPORTED = (
     "tle_last_error", "tle_version", "tle_rope", "tle_attention_workspace_bytes",
     "tle_attention", "tle_rope_attention", "tle_decode_desc_bytes", "tle_decode_desc",
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
-    "tle_prefill", "tle_partition_lpt", "tle_device_error",
+    "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
 )
 
 
@@ -88,6 +88,7 @@ def lib() -> ctypes.CDLL:
         L.tle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, P(Shape), vp, sz, vp]
         L.tle_partition_lpt.argtypes = [P(ctypes.c_int32), i, i, P(ctypes.c_int32)]
         L.tle_device_error.argtypes = [i, P(ctypes.c_uint32)]
+        L.tle_decode_batch_noalloc.argtypes = [P(Shape), P(Seq), i, vp, vp, vp, vp, i, i, vp]
         _lib = L
     return _lib
 
@@ -225,6 +226,26 @@ class DecodeBatch:
                                       self.n_ctas, _ptr(q), _ptr(k), _ptr(v), _ptr(out), layer,
                                       1 if rotate else 0, _ptr(self.workspace),
                                       self.workspace.numel() * 4, _stream(stream)))
+
+
+# ------------------------------------------------- decode without allocation
+NOALLOC_MAX_SEQS = 256  # TLE_NOALLOC_MAX_SEQS
+
+
+def decode_batch_noalloc(caches: Sequence, positions: Sequence[int], q, k, v, out, layer: int,
+                         rotate: bool = True, shape: Optional[Shape] = None, stream=None) -> None:
+    """tle_decode_batch_noalloc: the batched decode for callers that cannot
+    allocate device memory (the library's fixed scratch array is used; see
+    include/tle_attn.h).  ``caches`` as for DecodeBatch, records stay on the host."""
+    shape = shape or tinyllama_shape()
+    n = len(caches)
+    _want(q, n * 2048, "q"); _want(k, n * 256, "k"); _want(v, n * 256, "v")
+    _want(out, n * 2048, "out")
+    seqs = (Seq * max(n, 1))()
+    for i, (kc, vc, n_ctx) in enumerate(caches):
+        seqs[i] = Seq(_ptr(kc), _ptr(vc), int(n_ctx), int(positions[i]))
+    _check(lib().tle_decode_batch_noalloc(ctypes.byref(shape), seqs, n, _ptr(q), _ptr(k), _ptr(v),
+                                          _ptr(out), layer, 1 if rotate else 0, _stream(stream)))
 
 
 # ------------------------------------------------------------------ prefill
