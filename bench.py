@@ -352,6 +352,34 @@ def _time_steps(fn, steps, warmup, stream):
     return e0.elapsed_time(e1) / steps
 
 
+def _time_graph(fn, steps, warmup, dev):
+    """Captures one step (fn) in a CUDA graph and times `steps` replays with
+    CUDA events (removes the per-launch host cost of the Python plumbing)."""
+    import torch
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            fn(side)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / steps
+
+
 def measure_prefill(dev, peaks, steps=10, warmup=3):
     """Config 3: causal prefill S=2048 (32 q / 4 kv heads, hd 64) for each of
     22 layers; a step is the 22 tle_prefill calls (distinct per-layer inputs,
@@ -370,17 +398,19 @@ def measure_prefill(dev, peaks, steps=10, warmup=3):
     ws = tle.prefill_workspace(S, 0, shape)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(st=stream):
         for l in range(n_layers):
-            tle.prefill(out, q[l], k[l], v[l], kc, vc, l, 0, S, shape, ws, stream)
+            tle.prefill(out, q[l], k[l], v[l], kc, vc, l, 0, S, shape, ws, st)
 
-    ms = _time_steps(step, steps, warmup, stream)
+    ms_eager = _time_steps(step, steps, warmup, stream)
+    ms = _time_graph(step, steps, warmup, dev)
     flops = n_layers * 4.0 * HD * NH * S * (S + 1) / 2
     tflops = flops / (ms / 1e3) / 1e12
-    return {"workload": "config3: causal prefill S=2048, 22 layers per step, bf16 tcgen05 MMA, "
-                        "fp32 softmax, fused rope+append (prep kernel)",
+    return {"workload": "config3: causal prefill S=2048, 22 layers per step (CUDA graph of the 22 "
+                        "tle_prefill calls), bf16 tcgen05 MMA, fp32 softmax, rope+append prep kernel",
             "metric": "prefill attn TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s",
             "ms_per_step": round(ms, 4), "ms_per_layer": round(ms / n_layers, 4),
+            "ms_per_step_eager": round(ms_eager, 4),
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tflops / peaks["bf16_tflops"], 4),
@@ -409,16 +439,19 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
     out = torch.zeros((64, QD), device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(st=stream):
         for l in range(n_layers):
-            batch.run(q, k, v, out, l, True, stream)
+            batch.run(q, k, v, out, l, True, st)
 
-    ms = _time_steps(step, steps, warmup, stream)
+    ms_eager = _time_steps(step, steps, warmup, stream)
+    ms = _time_graph(step, steps, warmup, dev)
     kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
     gbs = kv_bytes / (ms / 1e3) / 1e9
-    return {"workload": "config4: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step" % int(lengths.sum()),
+    return {"workload": "config4: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step "
+                        "(CUDA graph of the 22 tle_decode_batch calls)" % int(lengths.sum()),
             "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
             "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+            "ms_per_step_eager": round(ms_eager, 4),
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},

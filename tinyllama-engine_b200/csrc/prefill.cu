@@ -44,8 +44,7 @@ constexpr int NKV = kNHeadKv;  // 4
 constexpr int GQA = NH / NKV;  // 8
 constexpr int BM = 128;        // query rows per CTA
 constexpr int BN = 128;        // kv rows per tile
-constexpr int ATTN_THREADS = 128;
-constexpr uint32_t TMEM_COLS = 256;  // S: cols [0,128), O_j: cols [128,192)
+constexpr int ATTN_THREADS = 384;
 constexpr float kQScale = 0.125f;    // 1/sqrt(64)
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -81,74 +80,113 @@ struct PrepArgs {
     float inv_freq[HD / 2];
 };
 
-// Grid: blockIdx.y == 0 -> Q jobs, == 1 -> K/V jobs (64-row blocks).
-// Q job: one thread per (token, head, pair) over S_pad rows.
-// K/V job: a block handles 64 rows x one KV head; V is transposed through
-// shared memory so the Vt writes are 128-byte rows.
-__global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
-    __shared__ float vtile[64][HD + 1];
+constexpr int kPrepThreads = 256;
+static_assert(kPrepThreads == NKV * HD, "the V^T writer maps one thread to one (kv head, d) row");
+constexpr int kPrepTokensPerBlock = kPrepThreads / 32;  // one token per warp
+constexpr int kVtRows = 32;                              // rows per transpose block
+constexpr int kVtPitch = NKV * HD + 8;                   // bf16 pitch of the transpose tile
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+// blockIdx.y == 0: one token per warp, lane = rotation pair p.  One sincosf
+//   per (token, pair) serves the 32 query heads and 4 key heads: rotated
+//   q * 1/8 -> Qb, rotated k -> cache (append) and Kb, v -> cache (append).
+//   Token slots in [n_tokens, S_pad) zero their Qb rows.
+// blockIdx.y == 1: 64 rows x all 4 KV heads: V rows (cache prefix, new
+//   tokens, zero pad) are transposed through shared memory into Vt; Kb rows
+//   of the cache prefix (bf16 of the cached rotated k) and of the pad (zero).
+__global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
+    __shared__ __align__(16) __nv_bfloat16 vtile[kVtRows * kVtPitch];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
     if (blockIdx.y == 0) {
-        const int64_t total = static_cast<int64_t>(A.S_pad) * NH * (HD / 2);
-        for (int64_t j = blockIdx.x * 256ll + threadIdx.x; j < total; j += 256ll * gridDim.x) {
-            const int i = static_cast<int>(j / (NH * (HD / 2)));   // token
-            const int rem = static_cast<int>(j % (NH * (HD / 2)));
-            const int h = rem / (HD / 2), p = rem % (HD / 2);
-            float y0 = 0.f, y1 = 0.f;
-            if (i < A.n_tokens) {
-                const float2 x = reinterpret_cast<const float2*>(A.q)[static_cast<size_t>(i) * NH * HD / 2 + rem];
-                float sn, cs;
-                sincosf(static_cast<float>(A.pos0 + i) * A.inv_freq[p], &sn, &cs);
-                y0 = (x.x * cs - x.y * sn) * kQScale;
-                y1 = (x.x * sn + x.y * cs) * kQScale;
-            }
-            reinterpret_cast<__nv_bfloat162*>(A.qb)[(static_cast<size_t>(h) * A.S_pad + i) * (HD / 2) + p] =
-                __floats2bfloat162_rn(y0, y1);
+        const int i = blockIdx.x * kPrepTokensPerBlock + warp;  // token
+        if (i >= A.S_pad) return;
+        uint32_t* qb32 = reinterpret_cast<uint32_t*>(A.qb);
+        if (i >= A.n_tokens) {
+#pragma unroll 4
+            for (int h = 0; h < NH; ++h) qb32[(static_cast<size_t>(h) * A.S_pad + i) * (HD / 2) + lane] = 0u;
+            return;
+        }
+        const int pos = A.pos0 + i;
+        float sn, cs;
+        sincosf(static_cast<float>(pos) * A.inv_freq[lane], &sn, &cs);
+        const float2* qs = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(i) * NH * HD);
+        float2 xq[NH];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) xq[h] = qs[h * (HD / 2) + lane];   // 32 loads in flight
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            const float2 x = xq[h];
+            qb32[(static_cast<size_t>(h) * A.S_pad + i) * (HD / 2) + lane] =
+                pack_bf16((x.x * cs - x.y * sn) * kQScale, (x.x * sn + x.y * cs) * kQScale);
+        }
+        const float2* ks = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(i) * NKV * HD);
+        const float2* vs = reinterpret_cast<const float2*>(A.v + static_cast<size_t>(i) * NKV * HD);
+        float2* kcr = reinterpret_cast<float2*>(A.kc + static_cast<size_t>(pos) * NKV * HD);
+        float2* vcr = reinterpret_cast<float2*>(A.vc + static_cast<size_t>(pos) * NKV * HD);
+        uint32_t* kb32 = reinterpret_cast<uint32_t*>(A.kb);
+#pragma unroll
+        for (int g = 0; g < NKV; ++g) {
+            const float2 x = ks[g * (HD / 2) + lane];
+            const float2 y = make_float2(x.x * cs - x.y * sn, x.x * sn + x.y * cs);
+            kcr[g * (HD / 2) + lane] = y;                                     // append (ops.cpp:1370)
+            kb32[(static_cast<size_t>(g) * A.R_pad + pos) * (HD / 2) + lane] = pack_bf16(y.x, y.y);
+            vcr[g * (HD / 2) + lane] = vs[g * (HD / 2) + lane];               // append (ops.cpp:1371)
         }
         return;
     }
-    // K / V: blockIdx.x over (row block of 64, kv head)
-    const int nblk = A.R_pad / 64;
-    for (int b = blockIdx.x; b < nblk * NKV; b += gridDim.x) {
-        const int kvh = b % NKV;
-        const int r0 = (b / NKV) * 64;
-        // each thread: 16 (row, pair) items of the 64 x 32 pairs
-        for (int t = threadIdx.x; t < 64 * (HD / 2); t += 256) {
-            const int rr = t / (HD / 2), p = t % (HD / 2);
-            const int r = r0 + rr;
-            float k0 = 0.f, k1 = 0.f, v0 = 0.f, v1 = 0.f;
-            if (r < A.R) {
-                const size_t off = static_cast<size_t>(r) * (NKV * HD) + kvh * HD + 2 * p;
-                if (r < A.pos0) {
-                    const float2 kk = *reinterpret_cast<const float2*>(A.kc + off);
-                    const float2 vv = *reinterpret_cast<const float2*>(A.vc + off);
-                    k0 = kk.x; k1 = kk.y; v0 = vv.x; v1 = vv.y;
-                } else {
-                    const int i = r - A.pos0;
-                    const size_t src = static_cast<size_t>(i) * (NKV * HD) + kvh * HD + 2 * p;
-                    const float2 kk = *reinterpret_cast<const float2*>(A.k + src);
-                    const float2 vv = *reinterpret_cast<const float2*>(A.v + src);
-                    float sn, cs;
-                    sincosf(static_cast<float>(r) * A.inv_freq[p], &sn, &cs);
-                    k0 = kk.x * cs - kk.y * sn;
-                    k1 = kk.x * sn + kk.y * cs;
-                    v0 = vv.x; v1 = vv.y;
-                    *reinterpret_cast<float2*>(A.kc + off) = make_float2(k0, k1);  // append
-                    *reinterpret_cast<float2*>(A.vc + off) = make_float2(v0, v1);
-                }
-            }
-            reinterpret_cast<__nv_bfloat162*>(A.kb)[(static_cast<size_t>(kvh) * A.R_pad + r) * (HD / 2) + p] =
-                __floats2bfloat162_rn(k0, k1);
-            vtile[rr][2 * p] = v0;
-            vtile[rr][2 * p + 1] = v1;
+    // ---- V^T and the Kb rows not written by the token role ----
+    const int r0 = blockIdx.x * kVtRows;
+    if (r0 >= A.R_pad) return;
+    constexpr int kVec = NKV * HD / 4;                       // float4 per row (64)
+    constexpr int kPerThread = kVtRows * kVec / kPrepThreads; // 8
+    float4 vv[kPerThread];
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {                   // all loads in flight
+        const int t = threadIdx.x + u * kPrepThreads;
+        const int rr = t / kVec, c4 = t % kVec;
+        const int r = r0 + rr;
+        vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < A.pos0)
+            vv[u] = reinterpret_cast<const float4*>(A.vc + static_cast<size_t>(r) * NKV * HD)[c4];
+        else if (r < A.R)
+            vv[u] = reinterpret_cast<const float4*>(A.v + static_cast<size_t>(r - A.pos0) * NKV * HD)[c4];
+    }
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {
+        const int t = threadIdx.x + u * kPrepThreads;
+        const int rr = t / kVec, c4 = t % kVec;
+        const int r = r0 + rr;
+        *reinterpret_cast<uint2*>(&vtile[rr * kVtPitch + 4 * c4]) =
+            make_uint2(pack_bf16(vv[u].x, vv[u].y), pack_bf16(vv[u].z, vv[u].w));
+        // Kb rows outside [pos0, R): bf16 of the cached prefix, zero pad
+        if (r < A.pos0 || r >= A.R) {
+            float4 kk = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < A.pos0) kk = reinterpret_cast<const float4*>(A.kc + static_cast<size_t>(r) * NKV * HD)[c4];
+            const int g = c4 / (HD / 4), d4 = c4 % (HD / 4);
+            *reinterpret_cast<uint2*>(A.kb + (static_cast<size_t>(g) * A.R_pad + r) * HD + 4 * d4) =
+                make_uint2(pack_bf16(kk.x, kk.y), pack_bf16(kk.z, kk.w));
         }
-        __syncthreads();
-        // Vt[kvh][d][r0 .. r0+63]: thread -> (d, pair of rows)
-        for (int t = threadIdx.x; t < HD * 32; t += 256) {
-            const int d = t / 32, rp = t % 32;
-            reinterpret_cast<__nv_bfloat162*>(A.vt)[((static_cast<size_t>(kvh) * HD + d) * A.R_pad + r0) / 2 + rp] =
-                __floats2bfloat162_rn(vtile[2 * rp][d], vtile[2 * rp + 1][d]);
+    }
+    __syncthreads();
+    // thread -> one (kv head, d) row of Vt: kVtRows consecutive kv positions
+    {
+        const int gd = threadIdx.x;  // 0 .. NKV*HD-1
+        uint32_t w[kVtRows / 2];
+#pragma unroll
+        for (int e = 0; e < kVtRows / 2; ++e) {
+            const __nv_bfloat16 lo = vtile[(2 * e) * kVtPitch + gd];
+            const __nv_bfloat16 hi = vtile[(2 * e + 1) * kVtPitch + gd];
+            w[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
+                   (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
         }
-        __syncthreads();
+        uint4* dst = reinterpret_cast<uint4*>(A.vt + static_cast<size_t>(gd) * A.R_pad + r0);
+#pragma unroll
+        for (int e = 0; e < kVtRows / 8; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
     }
 }
 
@@ -161,17 +199,37 @@ struct AttnArgs {
     uint32_t* err;
 };
 
-// 97 KB: two CTAs fit on one SM (TMEM: 2 x 256 columns).
+// Warp roles of prefill_attn_kernel (384 threads, one CTA per SM):
+//   warpgroup 0: warp 0 issues TMA loads, warp 1 issues tcgen05.mma,
+//                warps 2-3 idle (56 registers each after setmaxnreg.dec);
+//   warpgroups 1, 2: softmax of query head h0 / h1 (224 registers each),
+//                one TMEM lane (= query row) per thread.
+// Register split: 384 x 168 at launch = 128 x 56 + 256 x 224.
+constexpr int KSTAGES = 4;
+constexpr int kRegsControl = 56;
+constexpr int kRegsSoftmax = 224;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= ATTN_THREADS * 168,
+              "setmaxnreg split exceeds the launch register budget");
+
+// TMEM columns (512, the whole SM): S_i = Q_i K^T (fp32, 128 columns each),
+// P_i = softmax numerators (bf16 pairs, 64 columns), O_i = P V (fp32, 64).
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColP0 = 256, kColP1 = 320, kColO0 = 384, kColO1 = 448;
+constexpr uint32_t TMEM_COLS2 = 512;
+// Lazy rescale: the running reference max only moves when the row max grows
+// by more than 8 (log2 units), so O in TMEM is rescaled rarely; P <= 2^8.
+constexpr float kRescaleThreshold = 8.0f;
+
 struct AttnSmem {
-    __nv_bfloat16 q[BM * HD];          // 16 KB, SW128 K-major
-    __nv_bfloat16 k[2][BN * HD];       // 2 stages x 16 KB
-    __nv_bfloat16 vt[2][HD * 64];      // [kv half] 64 rows (d) x 64 kv: 2 x 8 KB
-    __nv_bfloat16 p[2][BM * 64];       // [kv half] 128 rows x 64 kv: 2 x 16 KB
+    __nv_bfloat16 q[2][BM * HD];           // 2 heads x 16 KB, SW128 K-major
+    __nv_bfloat16 k[KSTAGES][BN * HD];     // 16 KB per stage
+    __nv_bfloat16 vt[KSTAGES][2][HD * 64]; // 16 KB per stage (two 64-kv halves)
     uint64_t bar_q;
-    uint64_t bar_k[2];
-    uint64_t bar_v;
-    uint64_t bar_s;
-    uint64_t bar_o;
+    uint64_t kv_full[KSTAGES];
+    uint64_t kv_empty[KSTAGES];
+    uint64_t s_full[2];
+    uint64_t s_free[2];
+    uint64_t p_full[2];
+    uint64_t p_free[2];
     uint32_t tmem_base;
 };
 
@@ -180,191 +238,321 @@ constexpr uint32_t kTileBytesV = 2 * HD * 64 * 2;    // 16 KB
 constexpr uint32_t kIdescS = idesc_bf16_f32(BM, BN);
 constexpr uint32_t kIdescO = idesc_bf16_f32(BM, HD);
 
-__device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                             uint32_t code) {
-    if (!mbar_wait(bar, parity)) record_error(err, code);
+// 2^x on the SFU (MUFU.EX2, flush-to-zero; 2^-inf = 0).
+__device__ __forceinline__ float ex2_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-__global__ void __launch_bounds__(ATTN_THREADS) prefill_attn_kernel(const __grid_constant__ AttnArgs A) {
+// sm_100 packed fp32x2 arithmetic (two lanes of work per instruction).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for a pair, on the FMA/ALU pipes, for a share of the elements so that the SFU is not
+// the only exponential unit: round-to-nearest split x = n + f (f in
+// [-1/2, 1/2]) with the 1.5*2^23 shifter, 2^f by a cubic fitted to 2^f on
+// [-1/2, 1/2] (least squares on relative error, Chebyshev nodes, Lawson
+// reweighting; max relative error 7.5e-5, far below the bf16 rounding of P),
+// and n added to the exponent field.  x is clamped at -126 so masked (-inf)
+// scores give ~1e-38 instead of a denormal.
+__device__ __forceinline__ void ex2_poly2(uint64_t x2, float& r0, float& r1) {
+    float x0, x1;
+    f2_split(x2, x0, x1);
+    x2 = f2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+    const uint64_t sh = f2(12582912.0f, 12582912.0f);
+    const uint64_t nsh = f2(-12582912.0f, -12582912.0f);
+    const uint64_t t = fadd2(x2, sh);
+    const uint64_t n = fadd2(t, nsh);
+    const uint64_t f = ffma2(n, f2(-1.0f, -1.0f), x2);
+    uint64_t p = ffma2(f2(0.0551716648f, 0.0551716648f), f, f2(0.2426111251f, 0.2426111251f));
+    p = ffma2(p, f, f2(0.6932609677f, 0.6932609677f));
+    p = ffma2(p, f, f2(0.9999280572f, 0.9999280572f));
+    float t0, t1, p0, p1;
+    f2_split(t, t0, t1);
+    f2_split(p, p0, p1);
+    const int kSh = __float_as_int(12582912.0f);
+    r0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - kSh) << 23));
+    r1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - kSh) << 23));
+}
+
+// Bounded wait; after the first expiry in a thread every later wait of that
+// thread returns at once, so a broken pipeline unwinds in ~one timeout.
+__device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                             uint32_t code, bool& failed) {
+    if (failed) return;
+    if (!mbar_wait(bar, parity)) {
+        record_error(err, code);
+        failed = true;
+    }
+}
+
+__global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __grid_constant__ AttnArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // SW128 atoms need 1024-byte aligned tiles (the launch adds 1 KB of slack)
     AttnSmem& S = *reinterpret_cast<AttnSmem*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    // heaviest query tiles first
-    const int qt = A.n_qt - 1 - static_cast<int>(blockIdx.x) / NH;
-    const int h = static_cast<int>(blockIdx.x) % NH;
-    const int kvh = h / GQA;
-    const int q0 = qt * BM;                                   // first query row (token index)
+    const int lane = tid & 31;
+    const int wg = warp >> 2;
+    // heaviest query tiles first; two query heads of one KV head per CTA
+    const int qt = A.n_qt - 1 - static_cast<int>(blockIdx.x) / (NH / 2);
+    const int h0 = 2 * (static_cast<int>(blockIdx.x) % (NH / 2));
+    const int kvh = h0 / GQA;
+    const int q0 = qt * BM;
     const int last_tok = min(q0 + BM, A.n_tokens) - 1;
-    const int n_kv = (A.pos0 + last_tok) / BN + 1;            // kv tiles needed
-    const int first_pos = A.pos0 + q0;                        // position of row 0
+    const int n_kv = (A.pos0 + last_tok) / BN + 1;
 
     if (tid == 0) {
         mbar_init(&S.bar_q, 1);
-        mbar_init(&S.bar_k[0], 1);
-        mbar_init(&S.bar_k[1], 1);
-        mbar_init(&S.bar_v, 1);
-        mbar_init(&S.bar_s, 1);
-        mbar_init(&S.bar_o, 1);
+        for (int i = 0; i < KSTAGES; ++i) {
+            mbar_init(&S.kv_full[i], 1);
+            mbar_init(&S.kv_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S.s_full[i], 1);
+            mbar_init(&S.s_free[i], 4);   // one arrival per softmax warp
+            mbar_init(&S.p_full[i], 4);
+            mbar_init(&S.p_free[i], 1);
+        }
         fence_barrier_init();
         prefetch_tmap(&A.tm_q);
         prefetch_tmap(&A.tm_k);
         prefetch_tmap(&A.tm_vt);
     }
     if (warp == 0) {
-        tmem_alloc(&S.tmem_base, TMEM_COLS);
+        tmem_alloc(&S.tmem_base, TMEM_COLS2);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
-    const uint32_t tmem_s = tmem;
-    const uint32_t tmem_o = tmem + 128;
+    bool failed = false;
 
-    // K tiles are double-buffered; the V^T tile is single-buffered and
-    // reloaded as soon as the PV MMA that read it has completed.
-    auto issue_k = [&](int j) {
-        const int st = j & 1;
-        mbar_arrive_expect_tx(&S.bar_k[st], kTileBytesK);
-        tma_load_2d(S.k[st], &A.tm_k, 0, kvh * A.R_pad + j * BN, &S.bar_k[st]);
-    };
-    auto issue_v = [&](int j) {
-        mbar_arrive_expect_tx(&S.bar_v, kTileBytesV);
-        tma_load_2d(S.vt[0], &A.tm_vt, j * BN, kvh * HD, &S.bar_v);
-        tma_load_2d(S.vt[1], &A.tm_vt, j * BN + 64, kvh * HD, &S.bar_v);
-    };
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&S.bar_q, BM * HD * 2);
-        tma_load_2d(S.q, &A.tm_q, 0, h * A.S_pad + q0, &S.bar_q);
-        issue_k(0);
-        issue_v(0);
-        if (n_kv > 1) issue_k(1);
-    }
-
-    const int row = tid;                      // query row of this thread (TMEM lane)
-    const int my_pos = first_pos + row;       // its position (rows past n_tokens are discarded)
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
-
-    const uint32_t q_addr = smem_u32(S.q);
-    for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        // ---- S = Q K_j^T ----
-        if (tid == 0) {
-            if (j == 0) wait_or_flag(&S.bar_q, 0, A.err, kErrWaitFull);
-            wait_or_flag(&S.bar_k[st], (j >> 1) & 1, A.err, kErrWaitFull);
-            tc_fence_after();
-            const uint32_t k_addr = smem_u32(S.k[st]);
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk)
-                umma_bf16(tmem_s, sw128_desc(q_addr + 32 * kk), sw128_desc(k_addr + 32 * kk), kIdescS,
-                          kk > 0);
-            umma_commit(&S.bar_s);
-        }
-        wait_or_flag(&S.bar_s, j & 1, A.err, kErrWaitMma);
-        tc_fence_after();
-
-        // ---- online softmax on this thread's row ----
-        float s[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-            float tmp[32];
-            tmem_ld32(tmem_s + lane_off + 32 * c, tmp);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[32 * c + i] = tmp[i];
-        }
-        tmem_wait_ld();
-        const int kv0 = j * BN;
-        float mt = -INFINITY;
-        if (kv0 + BN - 1 > my_pos) {
-#pragma unroll
-            for (int i = 0; i < BN; ++i)
-                if (kv0 + i > my_pos) s[i] = -INFINITY;
-        }
-#pragma unroll
-        for (int i = 0; i < BN; ++i) mt = fmaxf(mt, s[i]);
-        const float m_new = fmaxf(m_run, mt);
-        const float alpha = (m_run == -INFINITY) ? 0.f : exp2f((m_run - m_new) * kLog2e);
-        const float mb = m_new * kLog2e;
-        float lsum = 0.f;
-        // P (bf16) into the swizzled K-major tile: row `row`, kv column c.
-        unsigned char* prow0 = reinterpret_cast<unsigned char*>(S.p[0]) + row * 128;
-        unsigned char* prow1 = reinterpret_cast<unsigned char*>(S.p[1]) + row * 128;
-#pragma unroll
-        for (int ch = 0; ch < BN / 8; ++ch) {   // 16 chunks of 8 kv columns (16 bytes)
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p0 = exp2f(fmaf(s[8 * ch + 2 * e], kLog2e, -mb));
-                const float p1 = exp2f(fmaf(s[8 * ch + 2 * e + 1], kLog2e, -mb));
-                const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
-                const float2 bf = __bfloat1622float2(b);
-                lsum += bf.x + bf.y;
-                w[e] = *reinterpret_cast<const uint32_t*>(&b);
+    if (wg == 0) {
+        regs_dealloc<kRegsControl>();
+        if (warp == 0) {
+            // ------------------------------ TMA producer ------------------------------
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&S.bar_q, 2 * BM * HD * 2);
+                tma_load_2d(S.q[0], &A.tm_q, 0, h0 * A.S_pad + q0, &S.bar_q);
+                tma_load_2d(S.q[1], &A.tm_q, 0, (h0 + 1) * A.S_pad + q0, &S.bar_q);
             }
-            const int blk = ch >> 3, cc = ch & 7;
-            unsigned char* dst = (blk ? prow1 : prow0) + ((cc ^ (row & 7)) << 4);
-            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        l_run = l_run * alpha + lsum;
-        m_run = m_new;
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- O_j = P V_j ----
-        if (tid == 0) {
-            wait_or_flag(&S.bar_v, j & 1, A.err, kErrWaitFull);
-            tc_fence_after();
-            const uint32_t p_addr = smem_u32(S.p[0]);
-            const uint32_t v_addr = smem_u32(S.vt[0]);
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-                const uint32_t blk = kk >> 2, off = (kk & 3) * 32;
-                umma_bf16(tmem_o, sw128_desc(p_addr + blk * (BM * 64 * 2) + off),
-                          sw128_desc(v_addr + blk * (HD * 64 * 2) + off), kIdescO, kk > 0);
+            for (int j = 0; j < n_kv; ++j) {
+                const int st = j % KSTAGES;
+                wait_or_flag(&S.kv_empty[st], ((j / KSTAGES) & 1) ^ 1, A.err, kErrWaitEmpty, failed);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&S.kv_full[st], kTileBytesK + kTileBytesV);
+                    tma_load_2d(S.k[st], &A.tm_k, 0, kvh * A.R_pad + j * BN, &S.kv_full[st]);
+                    tma_load_2d(S.vt[st][0], &A.tm_vt, j * BN, kvh * HD, &S.kv_full[st]);
+                    tma_load_2d(S.vt[st][1], &A.tm_vt, j * BN + 64, kvh * HD, &S.kv_full[st]);
+                }
+                __syncwarp();
             }
-            umma_commit(&S.bar_o);
+        } else if (warp == 1) {
+            // ------------------------------ MMA issuer --------------------------------
+            // Descriptors are built once, warp-uniform; the K-slice advance is
+            // +32 bytes (+2 in the >>4 address field) inside a 128-byte row, and
+            // the second 64-kv half of V^T / P starts 8 KB further on.
+            const uint64_t dq[2] = {sw128_desc(smem_u32(S.q[0])), sw128_desc(smem_u32(S.q[1]))};
+            const uint64_t dk0 = sw128_desc(smem_u32(S.k[0]));
+            const uint64_t dv0 = sw128_desc(smem_u32(S.vt[0][0]));
+            constexpr uint64_t kStageK = (BN * HD * 2) >> 4;        // stage stride, descriptor units
+            constexpr uint64_t kStageV = (2 * HD * 64 * 2) >> 4;
+            const uint32_t tS[2] = {tmem + kColS0, tmem + kColS1};
+            const uint32_t tP[2] = {tmem + kColP0, tmem + kColP1};
+            const uint32_t tO[2] = {tmem + kColO0, tmem + kColO1};
+            constexpr uint64_t kHalfV = (HD * 64 * 2) >> 4;   // 8 KB in descriptor units
+            // Issue order per KV tile j: S_0(j), S_1(j), then O_0 += P_0(j-1) V,
+            // O_1 += P_1(j-1) V -- the PV products lag one tile so the tensor
+            // core computes scores while both softmax warpgroups work.
+            wait_or_flag(&S.bar_q, 0, A.err, kErrWaitFull, failed);
+            for (int j = 0; j <= n_kv; ++j) {
+                if (j < n_kv) {
+                    const int st = j % KSTAGES;
+                    wait_or_flag(&S.kv_full[st], (j / KSTAGES) & 1, A.err, kErrWaitFull, failed);
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        if (j > 0) wait_or_flag(&S.s_free[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
+                        tc_fence_after();
+                        if (elect_one()) {
+#pragma unroll
+                            for (int kk = 0; kk < HD / 16; ++kk)
+                                umma_bf16(tS[i], dq[i] + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdescS, kk > 0);
+                            umma_commit(&S.s_full[i]);
+                        }
+                        __syncwarp();
+                    }
+                }
+                if (j > 0) {
+                    const int st = (j - 1) % KSTAGES;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        wait_or_flag(&S.p_full[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
+                        tc_fence_after();
+                        if (elect_one()) {
+#pragma unroll
+                            for (int kk = 0; kk < BN / 16; ++kk)
+                                umma_bf16_tmem_a(tO[i], tP[i] + 8 * kk,
+                                                 dv0 + st * kStageV + (kk >> 2) * kHalfV + 2 * (kk & 3), kIdescO,
+                                                 (j > 1 || kk > 0) ? 1u : 0u);
+                            umma_commit(&S.p_free[i]);
+                            if (i == 1) umma_commit(&S.kv_empty[st]);
+                        }
+                        __syncwarp();
+                    }
+                }
+            }
         }
-        wait_or_flag(&S.bar_o, j & 1, A.err, kErrWaitMma);
+    } else {
+        // ------------------------------ softmax ------------------------------------
+        regs_alloc<kRegsSoftmax>();
+        const int i = wg - 1;                       // which query head of the pair
+        const int row = tid - 128 * wg;             // query row = TMEM lane
+        const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lanes + (i ? kColS1 : kColS0);
+        const uint32_t tP = tmem + lanes + (i ? kColP1 : kColP0);
+        const uint32_t tO = tmem + lanes + (i ? kColO1 : kColO0);
+        const int my_pos = A.pos0 + q0 + row;
+        float m_ref = -INFINITY;   // reference max, log2 units
+        float l_run = 0.f;
+        for (int j = 0; j < n_kv; ++j) {
+            wait_or_flag(&S.s_full[i], j & 1, A.err, kErrWaitMma, failed);
+            tc_fence_after();
+            float s[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                float tmp[32];
+                tmem_ld32(tS + 32 * c, tmp);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s[32 * c + e] = tmp[e];
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.s_free[i]);   // the MMA may overwrite S_i
+
+            const int kv0 = j * BN;
+            if (kv0 + BN - 1 > my_pos) {
+#pragma unroll
+                for (int e = 0; e < BN; ++e)
+                    if (kv0 + e > my_pos) s[e] = -INFINITY;
+            }
+            // row max as 16 independent 8-element chains, then a 3-input tree
+            float mc[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                float m = fmax3(s[8 * c], s[8 * c + 1], s[8 * c + 2]);
+                m = fmax3(m, s[8 * c + 3], s[8 * c + 4]);
+                m = fmax3(m, s[8 * c + 5], s[8 * c + 6]);
+                mc[c] = fmaxf(m, s[8 * c + 7]);
+            }
+#pragma unroll
+            for (int c = 0; c < 5; ++c) mc[c] = fmax3(mc[3 * c], mc[3 * c + 1], mc[3 * c + 2]);
+            float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[15]), -INFINITY);
+            mt *= kLog2e;
+            float alpha = 1.f;
+            const bool move = mt > m_ref + kRescaleThreshold;
+            if (move) {
+                alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - mt);
+                m_ref = mt;
+            }
+            // P = 2^(s*log2e - m_ref) in fp32 (one pair in four on the FMA
+            // pipe, the rest on the SFU), packed to bf16 pairs; fp32 row sum.
+            const uint64_t l2e2 = f2(kLog2e, kLog2e);
+            const uint64_t negm2 = f2(-m_ref, -m_ref);
+            uint32_t pk[BN / 2];
+            uint64_t lsum2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+            for (int e = 0; e < BN / 2; ++e) {
+                const uint64_t x2 = ffma2(f2(s[2 * e], s[2 * e + 1]), l2e2, negm2);
+                float p0, p1;
+                if ((e & 3) == 3) {
+                    ex2_poly2(x2, p0, p1);
+                } else {
+                    float x0, x1;
+                    f2_split(x2, x0, x1);
+                    p0 = ex2_sfu(x0);
+                    p1 = ex2_sfu(x1);
+                }
+                lsum2[e & 3] = fadd2(lsum2[e & 3], f2(p0, p1));
+                pk[e] = pack_bf16(p0, p1);
+            }
+            float lsum0, lsum1;
+            f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
+            const float lsum = lsum0 + lsum1;
+            l_run = l_run * alpha + lsum;
+            // P_i and O_i may be touched once the previous PV MMA is done
+            if (j > 0) {
+                wait_or_flag(&S.p_free[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, move)) {
+#pragma unroll
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(tO + 32 * c, o);
+                        tmem_wait_ld();
+                        uint32_t ob[32];
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(o[e] * alpha);
+                        tmem_st32(tO + 32 * c, ob);
+                    }
+                }
+            }
+            tmem_st32(tP, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+            tmem_st32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.p_full[i]);
+        }
+        // ---- epilogue: out[token][h][:] = O / l ----
+        wait_or_flag(&S.p_free[i], (n_kv - 1) & 1, A.err, kErrWaitMma, failed);
         tc_fence_after();
-        // K stage st and the V^T buffer are free once the PV MMA finished
-        if (tid == 0) {
-            if (j + 1 < n_kv) issue_v(j + 1);
-            if (j + 2 < n_kv) issue_k(j + 2);
-        }
+        const int tok = q0 + row;
+        const float inv = 1.0f / l_run;
+        float* dst = A.out + static_cast<size_t>(tok) * NH * HD + (h0 + i) * HD;
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
-            float tmp[32];
-            tmem_ld32(tmem_o + lane_off + 32 * c, tmp);
+            float o[32];
+            tmem_ld32(tO + 32 * c, o);
             tmem_wait_ld();
+            if (tok < A.n_tokens) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[32 * c + i] = fmaf(o[32 * c + i], alpha, tmp[i]);
+                for (int e = 0; e < 32; e += 4)
+                    *reinterpret_cast<float4*>(dst + 32 * c + e) =
+                        make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+            }
         }
-        tc_fence_before();
-        __syncthreads();   // S / O_j TMEM and the P buffer may be reused
-    }
-
-    // ---- epilogue: out[token][h][:] = O / l ----
-    const int tok = q0 + row;
-    if (tok < A.n_tokens) {
-        const float inv = 1.0f / l_run;
-        float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(tok) * NH * HD + h * HD);
-#pragma unroll
-        for (int d = 0; d < HD / 4; ++d)
-            dst[d] = make_float4(o[4 * d] * inv, o[4 * d + 1] * inv, o[4 * d + 2] * inv, o[4 * d + 3] * inv);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, TMEM_COLS2);
     }
 }
 
@@ -431,11 +619,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     p.R_pad = L.R_pad;
     for (int i = 0; i < HD / 2; ++i) p.inv_freq[i] = a.inv_freq[i];
     {
-        const int64_t qjobs = static_cast<int64_t>(L.S_pad) * NH * (HD / 2);
-        const int gx = static_cast<int>(std::min<int64_t>((qjobs + 255) / 256, 148 * 8));
-        const int kvblocks = (L.R_pad / 64) * NKV;
-        dim3 grid(std::max(gx, std::min(kvblocks, 148 * 8)), 2);
-        prefill_prep_kernel<<<grid, 256, 0, stream>>>(p);
+        const int gx = std::max((L.S_pad + kPrepTokensPerBlock - 1) / kPrepTokensPerBlock, L.R_pad / kVtRows);
+        prefill_prep_kernel<<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -463,7 +648,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
-    prefill_attn_kernel<<<t.n_qt * NH, ATTN_THREADS, smem, stream>>>(t);
+    prefill_attn_kernel<<<t.n_qt * (NH / 2), ATTN_THREADS, smem, stream>>>(t);
     return cudaGetLastError();
 }
 
