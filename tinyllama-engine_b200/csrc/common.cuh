@@ -67,10 +67,39 @@ TLE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-suspending probe of a phase (never parks the warp).
+TLE_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Spin wait for short, latency-critical handoffs: test_wait probes, bounded
+// by %globaltimer like mbar_wait.
+TLE_DEV bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (mbar_test_wait(bar, parity)) return true;
+        if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+    }
+}
+
 // Waits for the phase with the given parity to complete; false after
-// kWaitTimeoutNs (the caller records an error and unwinds).
+// kWaitTimeoutNs (the caller records an error and unwinds).  The first probe
+// is test_wait: on an already-completed phase it costs ~10 cycles where
+// try_wait costs ~110 (measured on B200); try_wait, which may park the warp,
+// is only used once the phase is known to be pending.
 TLE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
 #pragma unroll 1

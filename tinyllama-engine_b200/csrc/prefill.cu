@@ -75,7 +75,7 @@ struct PrepArgs {
     float* vc;
     __nv_bfloat16* qb;
     __nv_bfloat16* kb;
-    __nv_bfloat16* vt;
+    uint16_t* vt;         // bf16 bits
     int pos0, n_tokens, S_pad, R, R_pad;
     float inv_freq[HD / 2];
 };
@@ -99,7 +99,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 //   tokens, zero pad) are transposed through shared memory into Vt; Kb rows
 //   of the cache prefix (bf16 of the cached rotated k) and of the pad (zero).
 __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
-    __shared__ __align__(16) __nv_bfloat16 vtile[kVtRows * kVtPitch];
+    __shared__ __align__(16) uint16_t vtile[kVtRows * kVtPitch];   // bf16 bits
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (blockIdx.y == 0) {
@@ -179,10 +179,8 @@ __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid
         uint32_t w[kVtRows / 2];
 #pragma unroll
         for (int e = 0; e < kVtRows / 2; ++e) {
-            const __nv_bfloat16 lo = vtile[(2 * e) * kVtPitch + gd];
-            const __nv_bfloat16 hi = vtile[(2 * e + 1) * kVtPitch + gd];
-            w[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
-                   (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
+            w[e] = static_cast<uint32_t>(vtile[(2 * e) * kVtPitch + gd]) |
+                   (static_cast<uint32_t>(vtile[(2 * e + 1) * kVtPitch + gd]) << 16);
         }
         uint4* dst = reinterpret_cast<uint4*>(A.vt + static_cast<size_t>(gd) * A.R_pad + r0);
 #pragma unroll
@@ -199,16 +197,18 @@ struct AttnArgs {
     uint32_t* err;
 };
 
-// Warp roles of prefill_attn_kernel (384 threads, one CTA per SM):
-//   warpgroup 0: warp 0 issues TMA loads, warp 1 issues tcgen05.mma,
-//                warps 2-3 idle (56 registers each after setmaxnreg.dec);
-//   warpgroups 1, 2: softmax of query head h0 / h1 (224 registers each),
-//                one TMEM lane (= query row) per thread.
+// Warp roles of prefill_attn_kernel (384 threads = 3 warpgroups, one CTA/SM):
+//   warpgroup 0: warp 0 issues TMA loads, warps 1 and 2 issue tcgen05.mma
+//                for query head h0 and h0+1, warp 3 idle (56 registers each
+//                after setmaxnreg.dec);
+//   warpgroups 1, 2: softmax of query head h0 / h0+1 (224 registers each),
+//                one TMEM lane (= query row) per thread, all 128 columns.
 // Register split: 384 x 168 at launch = 128 x 56 + 256 x 224.
 constexpr int KSTAGES = 4;
 constexpr int kRegsControl = 56;
 constexpr int kRegsSoftmax = 224;
-static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= ATTN_THREADS * 168,
+constexpr int kLaunchRegs = 168;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= ATTN_THREADS * kLaunchRegs,
               "setmaxnreg split exceeds the launch register budget");
 
 // TMEM columns (512, the whole SM): S_i = Q_i K^T (fp32, 128 columns each),
@@ -329,11 +329,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
         mbar_init(&S.bar_q, 1);
         for (int i = 0; i < KSTAGES; ++i) {
             mbar_init(&S.kv_full[i], 1);
-            mbar_init(&S.kv_empty[i], 1);
+            mbar_init(&S.kv_empty[i], 2);   // last PV of each head
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&S.s_full[i], 1);
-            mbar_init(&S.s_free[i], 4);   // one arrival per softmax warp
+            mbar_init(&S.s_free[i], 4);   // one arrival per softmax warp of the head
             mbar_init(&S.p_full[i], 4);
             mbar_init(&S.p_free[i], 1);
         }
@@ -372,59 +372,56 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
                 }
                 __syncwarp();
             }
-        } else if (warp == 1) {
-            // ------------------------------ MMA issuer --------------------------------
-            // Descriptors are built once, warp-uniform; the K-slice advance is
-            // +32 bytes (+2 in the >>4 address field) inside a 128-byte row, and
-            // the second 64-kv half of V^T / P starts 8 KB further on.
-            const uint64_t dq[2] = {sw128_desc(smem_u32(S.q[0])), sw128_desc(smem_u32(S.q[1]))};
+        } else if (warp == 1 || warp == 2) {
+            // ------------------------------ MMA issuers --------------------------------
+            // One issuing warp per query head, so the two heads' pipelines do
+            // not wait on each other: head i issues S_i(n+1) as soon as its
+            // softmax has read S_i(n), and O_i += P_i(n) V_n as soon as P_i(n)
+            // is in TMEM.  A K/V stage is released when both heads' last
+            // readers of it have committed (kv_empty counts 2 arrivals).
+            const int i = warp - 1;
+            const uint64_t dq = sw128_desc(smem_u32(S.q[i]));
             const uint64_t dk0 = sw128_desc(smem_u32(S.k[0]));
             const uint64_t dv0 = sw128_desc(smem_u32(S.vt[0][0]));
             constexpr uint64_t kStageK = (BN * HD * 2) >> 4;        // stage stride, descriptor units
             constexpr uint64_t kStageV = (2 * HD * 64 * 2) >> 4;
-            const uint32_t tS[2] = {tmem + kColS0, tmem + kColS1};
-            const uint32_t tP[2] = {tmem + kColP0, tmem + kColP1};
-            const uint32_t tO[2] = {tmem + kColO0, tmem + kColO1};
-            constexpr uint64_t kHalfV = (HD * 64 * 2) >> 4;   // 8 KB in descriptor units
-            // Issue order per KV tile j: S_0(j), S_1(j), then O_0 += P_0(j-1) V,
-            // O_1 += P_1(j-1) V -- the PV products lag one tile so the tensor
-            // core computes scores while both softmax warpgroups work.
+            constexpr uint64_t kHalfV = (HD * 64 * 2) >> 4;         // 8 KB in descriptor units
+            const uint32_t tS = tmem + (i ? kColS1 : kColS0);
+            const uint32_t tP = tmem + (i ? kColP1 : kColP0);
+            const uint32_t tO = tmem + (i ? kColO1 : kColO0);
+            auto issue_s = [&](int n) {   // S_i = Q_i K_n^T
+                const int st = n % KSTAGES;
+                wait_or_flag(&S.kv_full[st], (n / KSTAGES) & 1, A.err, kErrWaitFull, failed);
+                if (n > 0) wait_or_flag(&S.s_free[i], (n - 1) & 1, A.err, kErrWaitMma, failed);
+                tc_fence_after();
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        umma_bf16(tS, dq + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdescS, kk > 0);
+                    umma_commit(&S.s_full[i]);
+                }
+                __syncwarp();
+            };
+            auto issue_pv = [&](int n) {  // O_i (+)= P_i(n) V_n
+                const int st = n % KSTAGES;
+                wait_or_flag(&S.p_full[i], n & 1, A.err, kErrWaitMma, failed);
+                tc_fence_after();
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk)
+                        umma_bf16_tmem_a(tO, tP + 8 * kk,
+                                         dv0 + st * kStageV + (kk >> 2) * kHalfV + 2 * (kk & 3), kIdescO,
+                                         (n > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&S.p_free[i]);
+                    umma_commit(&S.kv_empty[st]);
+                }
+                __syncwarp();
+            };
             wait_or_flag(&S.bar_q, 0, A.err, kErrWaitFull, failed);
-            for (int j = 0; j <= n_kv; ++j) {
-                if (j < n_kv) {
-                    const int st = j % KSTAGES;
-                    wait_or_flag(&S.kv_full[st], (j / KSTAGES) & 1, A.err, kErrWaitFull, failed);
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        if (j > 0) wait_or_flag(&S.s_free[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
-                        tc_fence_after();
-                        if (elect_one()) {
-#pragma unroll
-                            for (int kk = 0; kk < HD / 16; ++kk)
-                                umma_bf16(tS[i], dq[i] + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdescS, kk > 0);
-                            umma_commit(&S.s_full[i]);
-                        }
-                        __syncwarp();
-                    }
-                }
-                if (j > 0) {
-                    const int st = (j - 1) % KSTAGES;
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        wait_or_flag(&S.p_full[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
-                        tc_fence_after();
-                        if (elect_one()) {
-#pragma unroll
-                            for (int kk = 0; kk < BN / 16; ++kk)
-                                umma_bf16_tmem_a(tO[i], tP[i] + 8 * kk,
-                                                 dv0 + st * kStageV + (kk >> 2) * kHalfV + 2 * (kk & 3), kIdescO,
-                                                 (j > 1 || kk > 0) ? 1u : 0u);
-                            umma_commit(&S.p_free[i]);
-                            if (i == 1) umma_commit(&S.kv_empty[st]);
-                        }
-                        __syncwarp();
-                    }
-                }
+            issue_s(0);
+            for (int n = 0; n < n_kv; ++n) {
+                if (n + 1 < n_kv) issue_s(n + 1);   // scores of the next tile first
+                issue_pv(n);
             }
         }
     } else {
@@ -472,8 +469,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
             }
 #pragma unroll
             for (int c = 0; c < 5; ++c) mc[c] = fmax3(mc[3 * c], mc[3 * c + 1], mc[3 * c + 2]);
-            float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[15]), -INFINITY);
-            mt *= kLog2e;
+            const float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[15]), -INFINITY) * kLog2e;
             float alpha = 1.f;
             const bool move = mt > m_ref + kRescaleThreshold;
             if (move) {
@@ -503,8 +499,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
             }
             float lsum0, lsum1;
             f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
-            const float lsum = lsum0 + lsum1;
-            l_run = l_run * alpha + lsum;
+            l_run = l_run * alpha + (lsum0 + lsum1);
             // P_i and O_i may be touched once the previous PV MMA is done
             if (j > 0) {
                 wait_or_flag(&S.p_free[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
@@ -579,7 +574,8 @@ cudaError_t get_encoder(EncodeTiledFn* fn) {
 
 // 2-D bf16 map over a row-major [rows][cols] array, box {64, box_rows},
 // 128-byte swizzle (the UMMA K-major SW128 layout).
-cudaError_t make_map(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+cudaError_t make_map(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                     CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     EncodeTiledFn enc = nullptr;
     cudaError_t e = get_encoder(&enc);
     if (e != cudaSuccess) return e;
@@ -587,7 +583,7 @@ cudaError_t make_map(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, u
     const cuuint64_t strides[1] = {cols * 2};
     const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+    CUresult r = enc(m, dtype, 2, base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
@@ -611,7 +607,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     p.vc = a.value_cache + static_cast<size_t>(a.layer) * a.n_ctx * kRowFloats;
     p.qb = reinterpret_cast<__nv_bfloat16*>(ws + L.qb_off);
     p.kb = reinterpret_cast<__nv_bfloat16*>(ws + L.kb_off);
-    p.vt = reinterpret_cast<__nv_bfloat16*>(ws + L.vt_off);
+    p.vt = reinterpret_cast<uint16_t*>(ws + L.vt_off);
     p.pos0 = a.pos0;
     p.n_tokens = a.n_tokens;
     p.S_pad = L.S_pad;
@@ -629,7 +625,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     e = make_map(&t.tm_k, p.kb, HD, static_cast<uint64_t>(NKV) * L.R_pad, BN);
     if (e != cudaSuccess) return e;
-    e = make_map(&t.tm_vt, p.vt, static_cast<uint64_t>(L.R_pad), static_cast<uint64_t>(NKV) * HD, 64);
+    e = make_map(&t.tm_vt, p.vt, static_cast<uint64_t>(L.R_pad), static_cast<uint64_t>(NKV) * HD, 64,
+                 CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
     if (e != cudaSuccess) return e;
     t.out = a.out;
     t.pos0 = a.pos0;
