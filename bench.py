@@ -312,7 +312,7 @@ def main():
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"],
                          "traffic": profile_traffic(local_bytes),
-                         "kernel": "tle_decode_batch (decode_kernel + merge_kernel), rank 0",
+                         "kernel": "tle_decode_batch (decode_kernel, split-K merge fused), rank 0",
                          "algorithmic_bytes_per_launch": local_bytes,
                          "kernel_ms": round(kernel_ms, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -322,7 +322,7 @@ def main():
                     "ms_per_step": round(e2e_ms / args.steps, 4),
                     "path": "tle.DecodeBatch.run (C ABI tle_decode_batch) with pinned host q/k/v "
                             "in and host out back every step"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,   # one decode_kernel per tle_decode_batch call
             "clocks": clk,
         }
         if world == 1 and not args.no_secondary:
@@ -455,7 +455,7 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
-            "gpu_launches": 2 * n_layers * steps}
+            "gpu_launches": n_layers * steps}
 
 
 def load_peaks():

@@ -65,11 +65,16 @@ def build_desc(positions, n_ctx, max_ctas):
     return rc, buf, n_ctas.value
 
 
-@pytest.mark.parametrize("seed", [0, 1, 2])
+SEG_COST = 64  # rows of streaming time charged per sequence segment by the planner
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3])
 def test_decode_plan_covers_every_row_once(seed):
     rng = np.random.default_rng(seed)
     n = int(rng.integers(1, 70))
     n_ctx = rng.integers(1, 3000, n).astype(int)
+    if seed == 3:
+        n_ctx[:] = rng.integers(1, 6, n)  # many tiny sequences
     pos = [int(rng.integers(0, c)) for c in n_ctx]
     max_ctas = int(rng.integers(1, 300))
     rc, buf, G = build_desc(pos, list(n_ctx), max_ctas)
@@ -79,20 +84,31 @@ def test_decode_plan_covers_every_row_once(seed):
     assert ns == n and nc == G and total == int(L.sum())
     assert 1 <= G <= max_ctas and G <= max(1, -(-total // 32))
     prefix = np.concatenate([[0], np.cumsum(L)])
-    # CTA c starts at global row c*total//G, expressed as (seq, offset)
+    row = lambda c: prefix[cs[c, 0]] + cs[c, 1] if cs[c, 0] < n else total
+    # CTA ranges are contiguous and monotone, and cover every row exactly once
+    assert row(0) == 0 and row(G) == total
     covered = np.zeros(total, np.int32)
     owner = np.full(total, -1)
+    cost = np.zeros(G)
     for c in range(G):
-        a = prefix[cs[c, 0]] + cs[c, 1] if cs[c, 0] < n else total
-        b = prefix[cs[c + 1, 0]] + cs[c + 1, 1] if cs[c + 1, 0] < n else total
-        assert a == c * total // G and b == (c + 1) * total // G
-        assert b > a  # no empty CTA
+        a, b = row(c), row(c + 1)
+        assert b >= a
+        assert cs[c, 0] == n or cs[c, 1] < L[cs[c, 0]]
         covered[a:b] += 1
         owner[a:b] = c
+        if b > a:
+            segs = len(set(np.searchsorted(prefix, np.arange(a, b), side="right") - 1))
+            cost[c] = (b - a) + SEG_COST * segs
     assert np.all(covered == 1)
+    # per-sequence CTA range = first and last owner of its rows, all in between own rows of it
     for s in range(n):
         lo, hi = sc[s]
-        assert lo == owner[prefix[s]] and hi == owner[prefix[s + 1] - 1]
+        own = owner[prefix[s]:prefix[s + 1]]
+        assert lo == own.min() and hi == own.max()
+        assert set(range(lo, hi + 1)) == set(own.tolist())
+    # cost balance: no CTA above the even share by more than two segment overheads
+    share = (total + SEG_COST * n) / G
+    assert cost.max() <= share + 2 * SEG_COST + 1
 
 
 def test_decode_plan_rejects_bad_sequences():

@@ -249,3 +249,35 @@ def test_invalid_arguments_fail_loudly(cuda):
     with pytest.raises(tle.TleError) as e:
         tle.attention(out, q, k, v, kc, vc, 1, 3, 8, shape)   # layer >= shape.n_layers
     assert e.value.code == tle.TLE_ERR_INVALID
+
+
+def test_batch_replay_without_upload(cuda):
+    """The split-K merge runs in the last CTA of each sequence, counted in the
+    descriptor's arrival words; the merging CTA resets them, so running the
+    same uploaded descriptor again (as a CUDA graph replay does) gives the same
+    output and leaves every count at zero."""
+    import torch
+    import tle
+    rng = np.random.default_rng(21)
+    lengths = [3000, 17, 900, 2500, 64, 1]
+    n = len(lengths)
+    caches, pos = [], []
+    for L in lengths:
+        kc = dev(rng.standard_normal((1, L + 2, KVD), dtype=np.float32))
+        vc = dev(rng.standard_normal((1, L + 2, KVD), dtype=np.float32))
+        caches.append((kc, vc, L + 2)); pos.append(L - 1)
+    batch = tle.DecodeBatch(caches, pos, tle.tinyllama_shape(1), 40)
+    assert batch.n_ctas > n
+    q = dev(rng.standard_normal((n, QD), dtype=np.float32))
+    k = dev(rng.standard_normal((n, KVD), dtype=np.float32))
+    v = dev(rng.standard_normal((n, KVD), dtype=np.float32))
+    outs = []
+    for _ in range(3):
+        o = torch.full((n, QD), float("nan"), device="cuda")
+        batch.run(q, k, v, o, 0, rotate=True)
+        outs.append(host(o))
+    assert np.all(np.isfinite(outs[0]))
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    off = 32 + 24 * n + 8 * (batch.n_ctas + 1) + 8 * n
+    arrivals = batch._desc_dev[off:off + 4 * n].cpu().numpy()
+    assert not arrivals.any(), arrivals

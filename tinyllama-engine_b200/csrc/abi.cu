@@ -78,6 +78,50 @@ int choose_ctas(int64_t rows, int max_ctas) {
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_ctas, by_rows)));
 }
 
+// Splits a batch over G CTAs in "cost" units: every sequence costs its rows
+// plus kSegCostRows (the per-segment setup of the decode kernel: q rotation,
+// warp merge, output write, about three microseconds of streaming time), so a
+// CTA that holds several short segments gets fewer rows.  CTA boundaries are
+// cost positions mapped to (sequence, row); a boundary inside a sequence's
+// overhead lands on its first row.  seq_ctas[t] = first and last CTA owning a
+// row of t.  No allocation (shared by the no-allocation entry point).
+constexpr int64_t kSegCostRows = 64;
+
+void plan_ctas(const tle_seq_t* seqs, int n, int G, tle::CtaStart* cs, tle::SeqCtas* sc) {
+    int64_t T = 0;
+    for (int t = 0; t < n; ++t) T += seqs[t].pos + 1 + kSegCostRows;
+    int s = 0;
+    int64_t X = 0;  // cost position where sequence s starts
+    for (int c = 0; c <= G; ++c) {
+        const int64_t x = (c == G) ? T : static_cast<int64_t>(c) * T / G;
+        while (s < n && X + seqs[s].pos + 1 + kSegCostRows <= x) {
+            X += seqs[s].pos + 1 + kSegCostRows;
+            ++s;
+        }
+        if (s >= n) {
+            cs[c].seq = n;
+            cs[c].off = 0;
+            continue;
+        }
+        const int64_t r = x - X - kSegCostRows;
+        cs[c].seq = s;
+        cs[c].off = r > 0 ? static_cast<int32_t>(r) : 0;
+    }
+    for (int t = 0; t < n; ++t) {
+        sc[t].lo = G;
+        sc[t].hi = -1;
+    }
+    for (int c = 0; c < G; ++c) {
+        const tle::CtaStart b = cs[c], e = cs[c + 1];
+        if (b.seq == e.seq && b.off == e.off) continue;  // empty CTA
+        const int last = (e.off > 0) ? e.seq : e.seq - 1;
+        for (int t = b.seq; t <= last && t < n; ++t) {
+            if (c < sc[t].lo) sc[t].lo = c;
+            if (c > sc[t].hi) sc[t].hi = c;
+        }
+    }
+}
+
 size_t partial_bytes(int n_slots) {
     return static_cast<size_t>(n_slots) * tle::kPartialFloats * sizeof(float);
 }
@@ -99,6 +143,7 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
     a.seqs = nullptr;
     a.cta_start = nullptr;
     a.seq_ctas = nullptr;
+    a.arrivals = nullptr;
     a.single.key_cache = key_cache;
     a.single.value_cache = value_cache;
     a.single.n_ctx = n_ctx;
@@ -179,7 +224,7 @@ int tle_rope_attention(float* out, const float* q, const float* k, const float* 
 size_t tle_decode_desc_bytes(int n_seqs, int max_ctas) {
     if (n_seqs < 0) n_seqs = 0;
     if (max_ctas <= 0 || max_ctas > tle::kMaxCtas) max_ctas = tle::kMaxCtas;
-    return tle::desc_seqctas_offset(n_seqs, max_ctas) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+    return tle::desc_total_bytes(n_seqs, max_ctas);
 }
 
 int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs, int max_ctas,
@@ -198,7 +243,7 @@ int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
         total += static_cast<int64_t>(q.pos) + 1;
     }
     const int G = choose_ctas(total, max_ctas);
-    const size_t need = tle::desc_seqctas_offset(n_seqs, G) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+    const size_t need = tle::desc_total_bytes(n_seqs, G);
     if (desc_bytes < need)
         return set_error(TLE_ERR_INVALID, "descriptor buffer %zu bytes < %zu needed", desc_bytes, need);
     unsigned char* base = static_cast<unsigned char*>(desc_host);
@@ -211,26 +256,8 @@ int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
     std::memcpy(base + tle::desc_seqs_offset(), seqs, sizeof(tle_seq_t) * static_cast<size_t>(n_seqs));
     auto* cs = reinterpret_cast<tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
     auto* sc = reinterpret_cast<tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, G));
-    // CTA c owns concatenated rows [c*total/G, (c+1)*total/G).
-    std::vector<int64_t> prefix(static_cast<size_t>(n_seqs) + 1, 0);
-    for (int s = 0; s < n_seqs; ++s) prefix[s + 1] = prefix[s] + seqs[s].pos + 1;
-    int s = 0;
-    for (int c = 0; c <= G; ++c) {
-        const int64_t x = (c == G) ? total : static_cast<int64_t>(c) * total / G;
-        while (s < n_seqs && prefix[s + 1] <= x) ++s;
-        cs[c].seq = s;
-        cs[c].off = (s < n_seqs) ? static_cast<int32_t>(x - prefix[s]) : 0;
-    }
-    // CTAs covering each sequence.
-    int c = 0;
-    for (int t = 0; t < n_seqs; ++t) {
-        const int64_t first = prefix[t], last = prefix[t + 1] - 1;
-        while (c + 1 < G && static_cast<int64_t>(c + 1) * total / G <= first) ++c;
-        int hi = c;
-        while (hi + 1 < G && static_cast<int64_t>(hi + 1) * total / G <= last) ++hi;
-        sc[t].lo = c;
-        sc[t].hi = hi;
-    }
+    plan_ctas(seqs, n_seqs, G, cs, sc);
+    std::memset(base + tle::desc_arrivals_offset(n_seqs, G), 0, sizeof(int32_t) * static_cast<size_t>(n_seqs));
     *n_ctas_out = G;
     return ok();
 }
@@ -261,6 +288,7 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
     a.seqs = reinterpret_cast<const tle_seq_t*>(base + tle::desc_seqs_offset());
     a.cta_start = reinterpret_cast<const tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
     a.seq_ctas = reinterpret_cast<const tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, n_ctas));
+    a.arrivals = reinterpret_cast<int32_t*>(const_cast<unsigned char*>(base) + tle::desc_arrivals_offset(n_seqs, n_ctas));
     a.n_seqs = n_seqs;
     a.n_ctas = n_ctas;
     a.q = q;
@@ -369,7 +397,7 @@ constexpr size_t kNoAllocPartialBytes =
 constexpr size_t kNoAllocBytes = kNoAllocDescBytes + kNoAllocPartialBytes;
 static_assert(sizeof(tle::DescHeader) + sizeof(tle_seq_t) * kNoAllocMaxSeqs +
                       sizeof(tle::CtaStart) * (kNoAllocMaxCtas + 1) +
-                      sizeof(tle::SeqCtas) * kNoAllocMaxSeqs <=
+                      (sizeof(tle::SeqCtas) + sizeof(int32_t)) * kNoAllocMaxSeqs <=
                   kNoAllocDescBytes,
               "descriptor region too small");
 constexpr int kNoAllocMaxDevices = 64;
@@ -407,8 +435,8 @@ int noalloc_scratch(unsigned char** out) {
     return TLE_OK;
 }
 
-// Same plan as tle_decode_desc, written into a caller-provided buffer with
-// running sums instead of a prefix array (no host allocation).
+// The descriptor of tle_decode_desc, written into a caller-provided buffer
+// (plan_ctas allocates nothing).
 void fill_desc_noalloc(const tle_seq_t* seqs, int n_seqs, int G, int64_t total, unsigned char* base) {
     tle::DescHeader hdr{};
     hdr.magic = tle::kDescMagic;
@@ -419,28 +447,8 @@ void fill_desc_noalloc(const tle_seq_t* seqs, int n_seqs, int G, int64_t total, 
     std::memcpy(base + tle::desc_seqs_offset(), seqs, sizeof(tle_seq_t) * static_cast<size_t>(n_seqs));
     auto* cs = reinterpret_cast<tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
     auto* sc = reinterpret_cast<tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, G));
-    int s = 0;
-    int64_t start_s = 0;  // first concatenated row of sequence s
-    for (int c = 0; c <= G; ++c) {
-        const int64_t x = (c == G) ? total : static_cast<int64_t>(c) * total / G;
-        while (s < n_seqs && start_s + seqs[s].pos + 1 <= x) {
-            start_s += seqs[s].pos + 1;
-            ++s;
-        }
-        cs[c].seq = s;
-        cs[c].off = (s < n_seqs) ? static_cast<int32_t>(x - start_s) : 0;
-    }
-    int c = 0;
-    int64_t first = 0;
-    for (int t = 0; t < n_seqs; ++t) {
-        const int64_t last = first + seqs[t].pos;
-        while (c + 1 < G && static_cast<int64_t>(c + 1) * total / G <= first) ++c;
-        int hi = c;
-        while (hi + 1 < G && static_cast<int64_t>(hi + 1) * total / G <= last) ++hi;
-        sc[t].lo = c;
-        sc[t].hi = hi;
-        first = last + 1;
-    }
+    plan_ctas(seqs, n_seqs, G, cs, sc);
+    std::memset(base + tle::desc_arrivals_offset(n_seqs, G), 0, sizeof(int32_t) * static_cast<size_t>(n_seqs));
 }
 
 }  // namespace
@@ -474,8 +482,7 @@ extern "C" int tle_decode_batch_noalloc(const tle_shape_t* shape, const tle_seq_
     if (int rc = noalloc_scratch(&scratch)) return rc;
     const int G = choose_ctas(total, std::min(sm_count(), kNoAllocMaxCtas));
     fill_desc_noalloc(seqs, n_seqs, G, total, t_noalloc_desc);
-    const size_t desc_bytes =
-        tle::desc_seqctas_offset(n_seqs, G) + sizeof(tle::SeqCtas) * static_cast<size_t>(n_seqs);
+    const size_t desc_bytes = tle::desc_total_bytes(n_seqs, G);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // Pageable source: the copy is staged before this call returns, so the
     // host buffer may be refilled by the next call.
@@ -485,6 +492,7 @@ extern "C" int tle_decode_batch_noalloc(const tle_shape_t* shape, const tle_seq_
     a.seqs = reinterpret_cast<const tle_seq_t*>(scratch + tle::desc_seqs_offset());
     a.cta_start = reinterpret_cast<const tle::CtaStart*>(scratch + tle::desc_cta_offset(n_seqs));
     a.seq_ctas = reinterpret_cast<const tle::SeqCtas*>(scratch + tle::desc_seqctas_offset(n_seqs, G));
+    a.arrivals = reinterpret_cast<int32_t*>(scratch + tle::desc_arrivals_offset(n_seqs, G));
     a.n_seqs = n_seqs;
     a.n_ctas = G;
     a.q = q;

@@ -126,6 +126,15 @@ TLE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
         : "memory");
 }
 
+// 1-D bulk copy global -> shared with the default L2 policy.
+TLE_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
 TLE_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -10,18 +10,21 @@
 //
 // Design (B200): the rows of all sequences in a batch are concatenated and
 // split evenly over the CTAs (one per SM).  A CTA walks its row range as
-// segments of one sequence each; a producer warp streams 32-row K and V
-// tiles (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with
-// 1-D bulk copies; 8 consumer warps each own 4 rows of every tile and all 32
-// query heads (lane = head), so every K/V element read from HBM serves its 8
-// query heads.  Scores, an online softmax and the PV accumulation run in fp32
-// FFMA (TF32 tensor cores would miss the 1e-4 parity bound).  Each lane reads
-// its KV head's 16-byte chunks in an order rotated by the KV-head index, so
-// the four distinct addresses of a warp-wide load fall in four different
-// bank groups (conflict-free broadcast).  Warps merge in shared memory at the
-// end of a segment; a segment that is a whole sequence writes the output,
-// otherwise its (m, l, o) partial goes to the workspace and merge_kernel
-// combines the partials of that sequence.
+// segments of one sequence each.  Warp 0 lane 0 streams 24-row K and V tiles
+// (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with 1-D
+// bulk copies (refilling a stage once all warps released it), and prefetches
+// each segment's q and new k/v rows one segment ahead into a double buffer.
+// The 8 warps each own 3 rows of every tile and all 32 query heads (lane =
+// head), so every K/V element read from HBM serves its 8 query heads.
+// Scores, an online softmax and the PV accumulation run in fp32 FFMA (TF32
+// tensor cores would miss the 1e-4 parity bound).  Each lane reads its KV
+// head's 16-byte chunks in an order rotated by the KV-head index, so the four
+// distinct addresses of a warp-wide load fall in four different bank groups
+// (conflict-free broadcast).  At the end of a segment the warps merge in a
+// 3-level tree in shared memory; warp 0 writes the output of a segment that
+// is a whole sequence, otherwise its (m, l, o) partial goes to the workspace
+// and the last CTA to finish a partial of that sequence combines them (batch
+// mode; merge_kernel does it for the single-sequence entry points).
 #include <math.h>
 
 #include "common.cuh"
@@ -38,25 +41,28 @@ constexpr int HD = kHeadDim;
 constexpr int NH = kNHead;
 constexpr int ROWF = kRowFloats;   // 256 floats per cache row
 constexpr int ROWB = ROWF * 4;     // 1024 bytes
-constexpr int TILE = 32;           // rows per pipeline stage
+constexpr int TILE = 24;           // rows per pipeline stage
 constexpr int NSTAGE = 3;
 constexpr int NCW = 8;             // warps (all consume; warp 0 lane 0 also issues the copies)
 constexpr int NCT = NCW * 32;      // threads per CTA
-constexpr int RPW = TILE / NCW;    // rows per warp per tile (4)
+constexpr int RPW = TILE / NCW;    // rows per warp per tile (3)
 constexpr int QS = HD + 4;         // padded q/o row stride in shared memory
+constexpr int MS = HD + 4;         // merge-buffer row: acc[64], m, l, pad
 constexpr float kScale = 0.125f;   // 1/sqrt(64), exact in fp32
 
 struct __align__(128) DecodeSmem {
     float k[NSTAGE][TILE * ROWF];
     float v[NSTAGE][TILE * ROWF];
-    float qo[NH * QS];       // scaled rotated q (segment start) / merged o (segment end)
-    float newk[ROWF];        // rotated k of the token being decoded
+    float qraw[2][NH * HD];     // q of a segment's sequence (bulk copy, double-buffered by segment)
+    float kvraw[2][2 * ROWF];   // that sequence's new k row and v row (segments holding row pos)
+    float qo[NH * QS];          // rotated, scaled q of the current segment
+    float newk[ROWF];           // rotated k of the token being decoded
     float newv[ROWF];
-    float ml[NCW][NH][2];    // per-warp (m, l)
-    float fin[NH][2];        // merged (m, l)
+    float mbuf[4][NH * MS];     // tree merge of the warps' (acc, m, l)
     uint64_t full[NSTAGE];
     uint64_t empty[NSTAGE];
-    uint64_t csync;          // all-warp barrier (bounded waits)
+    uint64_t qfull[2];
+    uint64_t csync;             // all-warp barrier (bounded waits)
 };
 
 // CTA c's row range as (start seq, start off) .. (end seq, end off), exclusive end.
@@ -126,6 +132,132 @@ __device__ __forceinline__ void cursor_issue(TileCursor& c, const DecodeArgs& A,
     if (c.ta >= c.b) cursor_load(c, A, c.s + 1, 0, s1, o1);
 }
 
+// Bulk copies of segment n's per-sequence inputs into buffer n & 1: q of its
+// sequence and, when the segment holds row pos, the new k and v rows.
+// Segment n of a CTA is sequence s0 + n.
+// Returns false (nothing issued) when the CTA has no segment n.
+__device__ __forceinline__ bool issue_q(const DecodeArgs& A, DecodeSmem& S, int n, int s0, int o0,
+                                        int s1, int o1) {
+    const int s = s0 + n;
+    if (!in_range(s, n == 0 ? o0 : 0, s1, o1)) return false;
+    const tle_seq_t sq = load_seq(A, s);
+    const int L = sq.pos + 1;
+    const bool has_new = ((s == s1) ? o1 : L) == L;
+    const int b = n & 1;
+    mbar_arrive_expect_tx(&S.qfull[b], NH * HD * 4 + (has_new ? 2 * ROWB : 0));
+    bulk_g2s_plain(S.qraw[b], A.q + static_cast<size_t>(s) * NH * HD, NH * HD * 4, &S.qfull[b]);
+    if (has_new) {
+        bulk_g2s_plain(S.kvraw[b], A.k + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
+        bulk_g2s_plain(S.kvraw[b] + ROWF, A.v + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
+    }
+    return true;
+}
+
+// Folds another warp's (m2, l2, acc2) of the same query head into (m, l, acc).
+__device__ __forceinline__ void merge_in(float& m, float& l, float4 (&acc)[16], const float* src) {
+    const float m2 = src[HD], l2 = src[HD + 1];
+    const float mn = fmaxf(m, m2);
+    const float f1 = (m == -INFINITY) ? 0.f : expf(m - mn);
+    const float f2 = (m2 == -INFINITY) ? 0.f : expf(m2 - mn);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const float4 a2 = *reinterpret_cast<const float4*>(src + 4 * c);
+        acc[c].x = fmaf(acc[c].x, f1, a2.x * f2);
+        acc[c].y = fmaf(acc[c].y, f1, a2.y * f2);
+        acc[c].z = fmaf(acc[c].z, f1, a2.z * f2);
+        acc[c].w = fmaf(acc[c].w, f1, a2.w * f2);
+    }
+    l = fmaf(l, f1, l2 * f2);
+    m = mn;
+}
+
+__device__ __forceinline__ void merge_out(float m, float l, const float4 (&acc)[16], float* dst) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(dst + 4 * c) = acc[c];
+    dst[HD] = m;
+    dst[HD + 1] = l;
+}
+
+// Batch mode, warp 0 (lane = query head h), after this CTA wrote its partial
+// of sequence s covered by CTAs sc.lo..sc.hi: counts the arrival and returns
+// true in the CTA whose arrival completes the count (the fence + atomic "last
+// block" pattern; no CTA ever waits).  That CTA resets the count for the next
+// call.  The release fence orders the whole warp's partial stores (made
+// visible to lane 0 by __syncwarp) before the count.
+__device__ __forceinline__ bool arrive_last(const DecodeArgs& A, int s, int lane, SeqCtas sc) {
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        last = (atomicAdd(&A.arrivals[s], 1) == sc.hi - sc.lo);
+        if (last) {
+            A.arrivals[s] = 0;
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        }
+    }
+    return __shfl_sync(0xffffffffu, last, 0) != 0;
+}
+
+// Warp-wide coalesced view of a [32 heads][64] block: float4 number 32 i + lane
+// holds head 2 i + (lane >> 4), chunk lane & 15.
+__device__ __forceinline__ int coalesced_head(int i, int lane) { return 2 * i + (lane >> 4); }
+
+// Loads the partial of CTA c: m, l of head `lane`, o in the coalesced view.
+__device__ __forceinline__ void load_partial(const DecodeArgs& A, int s, int c, int lane,
+                                             float& m, float& l, float4 (&o)[16]) {
+    const float* P = A.partials + static_cast<size_t>(s + c) * kPartialFloats;
+    m = __ldcg(P + NH * HD + lane);
+    l = __ldcg(P + NH * HD + NH + lane);
+    const float4* src = reinterpret_cast<const float4*>(P) + lane;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __ldcg(src + 32 * i);
+}
+
+// The last CTA of sequence s combines the partials of CTAs sc.lo..sc.hi (its
+// own included, re-read from L2) into out[s].  The fold order is fixed, CTA
+// lo first and then two partials per round, so the output does not depend on
+// which CTA finished last; the loads of a round are issued together.  Every
+// partial covers at least one row, so every m is finite.
+__device__ __forceinline__ void merge_partials(const DecodeArgs& A, int s, int lane, SeqCtas sc) {
+    float m, l;
+    float4 acc[16];
+    load_partial(A, s, sc.lo, lane, m, l, acc);
+    for (int c = sc.lo + 1; c <= sc.hi; c += 2) {
+        const bool two = c + 1 <= sc.hi;
+        float m1, l1, m2 = -INFINITY, l2 = 0.f;
+        float4 o1[16], o2[16];
+        load_partial(A, s, c, lane, m1, l1, o1);
+        if (two) {
+            load_partial(A, s, c + 1, lane, m2, l2, o2);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o2[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float mn = fmaxf(m, fmaxf(m1, m2));
+        const float f0 = expf(m - mn), f1 = expf(m1 - mn), f2 = two ? expf(m2 - mn) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int hh = coalesced_head(i, lane);
+            const float a0 = __shfl_sync(0xffffffffu, f0, hh);
+            const float a1 = __shfl_sync(0xffffffffu, f1, hh);
+            const float a2 = __shfl_sync(0xffffffffu, f2, hh);
+            acc[i].x = fmaf(acc[i].x, a0, fmaf(o1[i].x, a1, o2[i].x * a2));
+            acc[i].y = fmaf(acc[i].y, a0, fmaf(o1[i].y, a1, o2[i].y * a2));
+            acc[i].z = fmaf(acc[i].z, a0, fmaf(o1[i].z, a1, o2[i].z * a2));
+            acc[i].w = fmaf(acc[i].w, a0, fmaf(o1[i].w, a1, o2[i].w * a2));
+        }
+        l = fmaf(l, f0, fmaf(l1, f1, l2 * f2));
+        m = mn;
+    }
+    const float inv = 1.0f / l;
+    float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD) + lane;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float f = __shfl_sync(0xffffffffu, inv, coalesced_head(i, lane));
+        dst[32 * i] = make_float4(acc[i].x * f, acc[i].y * f, acc[i].z * f, acc[i].w * f);
+    }
+}
+
 // All-warp barrier on an mbarrier (bounded wait; false on timeout).
 __device__ __forceinline__ bool cta_sync(DecodeSmem& S, uint32_t& phase, int lane) {
     __syncwarp();
@@ -150,6 +282,8 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             mbar_init(&S.full[i], 1);
             mbar_init(&S.empty[i], NCW);
         }
+        mbar_init(&S.qfull[0], 1);
+        mbar_init(&S.qfull[1], 1);
         mbar_init(&S.csync, NCW);
         fence_barrier_init();
     }
@@ -158,12 +292,14 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     int s0, o0, s1, o1;
     cta_range(A, cta, s0, o0, s1, o1);
 
-    // Prologue: the issuer fills the first NSTAGE stages.
+    // Prologue: the issuer starts segment 0's q copy, then fills the stages.
     TileCursor cur;
     uint64_t pol = 0;
     int issued = 0;
+    int q_issued = 0;   // segments 0 .. q_issued-1 have their q copy issued
     if (issuer) {
         pol = l2_evict_first_policy();
+        if (issue_q(A, S, 0, s0, o0, s1, o1)) q_issued = 1;
         cursor_load(cur, A, s0, o0, s1, o1);
         while (!cur.done && issued < NSTAGE) {
             cursor_issue(cur, A, S, issued, s1, o1, pol);
@@ -175,30 +311,35 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     const int h = lane;            // query head
     uint32_t cphase = 0;
     int it = 0;
+    int n = 0;                     // segment index within this CTA
     bool ok = true;
 
-    for (int s = s0, off = o0; ok && in_range(s, off, s1, o1); ++s, off = 0) {
+    for (int s = s0, off = o0; ok && in_range(s, off, s1, o1); ++s, off = 0, ++n) {
         const tle_seq_t sq = load_seq(A, s);
         const int L = sq.pos + 1;
         const int seg_a = off;
         const int seg_b = (s == s1) ? o1 : L;
+        const int qb = n & 1;
+        if (!mbar_wait(&S.qfull[qb], (n >> 1) & 1)) { record_error(A.err, kErrWaitFull); ok = false; break; }
 
-        // q for this sequence: rotate (rope, ops.cpp:1229-1260), pre-scale by
-        // 1/sqrt(64) (exact power of two, so (q/8).k == (q.k)/8 bit for bit).
+        // q: rotate (rope, ops.cpp:1229-1260), pre-scale by 1/sqrt(64) (exact
+        // power of two, so (q/8).k == (q.k)/8 bit for bit).  Every pair this
+        // thread rotates (j = tid + 256 i, here and for the new k row) has
+        // rotation index j & 31 == lane, so one sincosf serves them all.
+        float sn = 0.f, cs = 1.f;
+        if (A.rotate) sincosf(static_cast<float>(sq.pos) * A.inv_freq[lane], &sn, &cs);
         {
-            const float2* qsrc = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(s) * NH * HD);
+            const float2* qsrc = reinterpret_cast<const float2*>(S.qraw[qb]);
             for (int j = tid; j < NH * HD / 2; j += NCT) {
-                const int hh = j >> 5, i = j & 31;
+                const int hh = j >> 5;
                 const float2 x = qsrc[j];
                 float y0 = x.x, y1 = x.y;
                 if (A.rotate) {
-                    float sn, cs;
-                    sincosf(static_cast<float>(sq.pos) * A.inv_freq[i], &sn, &cs);
                     y0 = x.x * cs - x.y * sn;
                     y1 = x.x * sn + x.y * cs;
                 }
-                S.qo[hh * QS + 2 * i] = y0 * kScale;
-                S.qo[hh * QS + 2 * i + 1] = y1 * kScale;
+                S.qo[hh * QS + 2 * lane] = y0 * kScale;
+                S.qo[hh * QS + 2 * lane + 1] = y1 * kScale;
             }
         }
         // The new token's k (rotated) and v: append to the cache at row pos
@@ -206,12 +347,9 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         if (seg_b == L) {
             const size_t row = (static_cast<size_t>(A.layer) * sq.n_ctx + sq.pos) * ROWF;
             if (tid < ROWF / 2) {
-                const int i = tid & 31;
-                const float2 x = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(s) * ROWF)[tid];
+                const float2 x = reinterpret_cast<const float2*>(S.kvraw[qb])[tid];
                 float y0 = x.x, y1 = x.y;
                 if (A.rotate) {
-                    float sn, cs;
-                    sincosf(static_cast<float>(sq.pos) * A.inv_freq[i], &sn, &cs);
                     y0 = x.x * cs - x.y * sn;
                     y1 = x.x * sn + x.y * cs;
                 }
@@ -220,12 +358,15 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                 reinterpret_cast<float2*>(sq.key_cache + row)[tid] = y;
             } else {
                 const int t2 = tid - ROWF / 2;
-                const float2 x = reinterpret_cast<const float2*>(A.v + static_cast<size_t>(s) * ROWF)[t2];
+                const float2 x = reinterpret_cast<const float2*>(S.kvraw[qb] + ROWF)[t2];
                 reinterpret_cast<float2*>(S.newv)[t2] = x;
                 reinterpret_cast<float2*>(sq.value_cache + row)[t2] = x;
             }
         }
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
+        // Buffer (n+1)&1 was last read in segment n-1's prologue: prefetch the
+        // next segment's q (and new rows) while this segment streams.
+        if (issuer && q_issued == n + 1 && issue_q(A, S, n + 1, s0, o0, s1, o1)) q_issued = n + 2;
 
         // This lane's query head, its 16-byte chunks in KV-head-rotated order.
         float4 q[16];
@@ -329,64 +470,48 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         }
         if (!ok) break;
 
-        // ---- merge the 8 warps' (m, l, acc) for this segment ----
-        S.ml[warp][h][0] = m_run;
-        S.ml[warp][h][1] = l_run;
+        // ---- tree merge of the 8 warps' (m, l, acc): 8 -> 4 -> 2 -> 1 ----
+        // (every lane of a pair of warps holds the same query head with the
+        // same chunk rotation, so rows are merged in place)
+        if (warp >= 4) merge_out(m_run, l_run, acc, &S.mbuf[warp - 4][h * MS]);
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
-        float mstar = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NCW; ++w) mstar = fmaxf(mstar, S.ml[w][h][0]);
-        float lstar = 0.f;
-#pragma unroll
-        for (int w = 0; w < NCW; ++w) {
-            const float mw = S.ml[w][h][0];
-            if (mw != -INFINITY) lstar += S.ml[w][h][1] * expf(mw - mstar);
-        }
-        const float f = (m_run == -INFINITY) ? 0.f : expf(m_run - mstar);
+        if (warp < 4) merge_in(m_run, l_run, acc, &S.mbuf[warp][h * MS]);
+        if (warp == 2 || warp == 3) merge_out(m_run, l_run, acc, &S.mbuf[warp][h * MS]);
+        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
+        if (warp < 2) merge_in(m_run, l_run, acc, &S.mbuf[warp + 2][h * MS]);
+        if (warp == 1) merge_out(m_run, l_run, acc, &S.mbuf[1][h * MS]);
+        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
         if (warp == 0) {
-            S.fin[h][0] = mstar;
-            S.fin[h][1] = lstar;
-        }
-        for (int w = 0; w < NCW && ok; ++w) {
-            if (warp == w) {
+            // CTAs sharing this sequence (the load overlaps the stores below).
+            SeqCtas sc{0, 0};
+            if (A.arrivals && !(seg_a == 0 && seg_b == L)) sc = A.seq_ctas[s];
+            merge_in(m_run, l_run, acc, &S.mbuf[1][h * MS]);
+            // ---- write: whole sequence -> output; otherwise a partial ----
+            // Staged through shared memory (mbuf[0], free until the next
+            // segment's tree merge) so the global stores are coalesced.
+            float* T = &S.mbuf[0][0];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    float4* dst = reinterpret_cast<float4*>(&S.qo[h * QS + 4 * ((c + g) & 15)]);
-                    float4 val = make_float4(acc[c].x * f, acc[c].y * f, acc[c].z * f, acc[c].w * f);
-                    if (w > 0) {
-                        const float4 old = *dst;
-                        val.x += old.x; val.y += old.y; val.z += old.z; val.w += old.w;
-                    }
-                    *dst = val;
-                }
+            for (int c = 0; c < 16; ++c)
+                *reinterpret_cast<float4*>(T + h * MS + 4 * ((c + g) & 15)) = acc[c];
+            __syncwarp();
+            const bool whole = (seg_a == 0 && seg_b == L);
+            const float scale = whole ? 1.0f / l_run : 1.0f;
+            float* dst = whole ? A.out + static_cast<size_t>(s) * NH * HD
+                               : A.partials + static_cast<size_t>(s + cta) * kPartialFloats;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int hh = coalesced_head(i, lane);
+                const float f = __shfl_sync(0xffffffffu, scale, hh);
+                const float4 v = *reinterpret_cast<const float4*>(T + hh * MS + 4 * (lane & 15));
+                reinterpret_cast<float4*>(dst)[32 * i + lane] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
             }
-            if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; }
-        }
-        if (!ok) break;
-
-        // ---- write: whole sequence -> output; otherwise a partial ----
-        {
-            const int hh = tid >> 3;
-            const int d0 = (tid & 7) * 8;
-            const float4 o0 = *reinterpret_cast<const float4*>(&S.qo[hh * QS + d0]);
-            const float4 o1v = *reinterpret_cast<const float4*>(&S.qo[hh * QS + d0 + 4]);
-            if (seg_a == 0 && seg_b == L) {
-                const float lf = S.fin[hh][1];
-                float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + hh * HD + d0);
-                dst[0] = make_float4(o0.x / lf, o0.y / lf, o0.z / lf, o0.w / lf);
-                dst[1] = make_float4(o1v.x / lf, o1v.y / lf, o1v.z / lf, o1v.w / lf);
-            } else {
-                float* P = A.partials + static_cast<size_t>(s + cta) * kPartialFloats;
-                float4* dst = reinterpret_cast<float4*>(P + hh * HD + d0);
-                dst[0] = o0;
-                dst[1] = o1v;
-                if (tid < NH) {
-                    P[NH * HD + tid] = S.fin[tid][0];
-                    P[NH * HD + NH + tid] = S.fin[tid][1];
-                }
+            if (!whole) {
+                dst[NH * HD + h] = m_run;
+                dst[NH * HD + NH + h] = l_run;
+                if (A.arrivals && arrive_last(A, s, lane, sc)) merge_partials(A, s, lane, sc);
             }
+            __syncwarp();
         }
-        if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
     }
 
     // Exit (error path only): every copy the issuer started must land before
@@ -394,10 +519,12 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     if (issuer) {
         for (int t = it; t < issued; ++t)
             if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
+        for (int m = n; m < q_issued; ++m)
+            if (!mbar_wait(&S.qfull[m & 1], (m >> 1) & 1)) { record_error(A.err, kErrDrain); break; }
     }
 }
 
-// Combines the split-K partials of every sequence covered by more than one CTA.
+// Single-sequence mode: combines the split-K partials of the CTAs.
 __global__ void __launch_bounds__(256) merge_kernel(const __grid_constant__ DecodeArgs A) {
     const int s = blockIdx.x;
     int lo = 0, hi = A.n_ctas - 1;
@@ -466,7 +593,7 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     decode_kernel<<<a.n_ctas, NCT, smem, stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (a.n_ctas > 1) {
+    if (a.n_ctas > 1 && a.seqs == nullptr) {   // batch mode merges inside decode_kernel
         merge_kernel<<<a.n_seqs, 256, 0, stream>>>(a);
         e = cudaGetLastError();
     }

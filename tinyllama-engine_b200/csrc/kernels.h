@@ -19,6 +19,10 @@ constexpr int kMinRowsPerCta = 32;                        // smallest split wort
 
 // Batch descriptor (built on the host by tle_decode_desc, read by the kernels):
 //   DescHeader | tle_seq_t seqs[n_seqs] | CtaStart cta_start[n_ctas+1] | SeqCtas seq_ctas[n_seqs]
+//   | int32 arrivals[n_seqs]
+// arrivals[] are zero in every upload; the decode kernel counts the CTAs that
+// finished a partial of each sequence there and the last one merges them and
+// resets the count to zero.
 struct DescHeader {
     int32_t magic;
     int32_t n_seqs;
@@ -51,11 +55,18 @@ inline size_t desc_cta_offset(int n_seqs) {
 inline size_t desc_seqctas_offset(int n_seqs, int n_ctas) {
     return desc_cta_offset(n_seqs) + sizeof(CtaStart) * static_cast<size_t>(n_ctas + 1);
 }
+inline size_t desc_arrivals_offset(int n_seqs, int n_ctas) {
+    return desc_seqctas_offset(n_seqs, n_ctas) + sizeof(SeqCtas) * static_cast<size_t>(n_seqs);
+}
+inline size_t desc_total_bytes(int n_seqs, int n_ctas) {
+    return desc_arrivals_offset(n_seqs, n_ctas) + sizeof(int32_t) * static_cast<size_t>(n_seqs);
+}
 
 struct DecodeArgs {
     const tle_seq_t* seqs;       // batch mode: device array; nullptr = single mode
     const CtaStart* cta_start;   // batch mode: [n_ctas+1]
     const SeqCtas* seq_ctas;     // batch mode: [n_seqs]
+    int32_t* arrivals;           // batch mode: [n_seqs] partial-arrival counts (merge in the last CTA)
     tle_seq_t single;            // single mode: the one sequence
     int n_seqs;
     int n_ctas;
