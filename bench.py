@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 prefill and config-4 ragged-decode lines")
+    ap.add_argument("--only", choices=["prefill3", "decode4"], default=None,
+                    help="run one secondary workload alone (--steps/--warmup apply) and print "
+                         "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target wall time of the CPU-baseline sample")
     return ap.parse_args()
@@ -199,6 +202,12 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.only:
+        fn = measure_prefill if args.only == "prefill3" else measure_config4
+        res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
+        print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
+                              warmup=max(3, args.warmup))), flush=True)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),

@@ -10,18 +10,19 @@
 //
 // Design (B200): the rows of all sequences in a batch are concatenated and
 // split evenly over the CTAs (one per SM).  A CTA walks its row range as
-// segments of one sequence each.  Warp 0 lane 0 streams 24-row K and V tiles
+// segments of one sequence each.  Warp 0 lane 0 streams 32-row K and V tiles
 // (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with 1-D
 // bulk copies (refilling a stage once all warps released it), and prefetches
-// each segment's q and new k/v rows one segment ahead into a double buffer.
-// The 8 warps each own 3 rows of every tile and all 32 query heads (lane =
+// each segment's q and new k/v rows one segment ahead.
+// The 8 warps each own 4 rows of every tile and all 32 query heads (lane =
 // head), so every K/V element read from HBM serves its 8 query heads.
 // Scores, an online softmax and the PV accumulation run in fp32 FFMA (TF32
 // tensor cores would miss the 1e-4 parity bound).  Each lane reads its KV
 // head's 16-byte chunks in an order rotated by the KV-head index, so the four
 // distinct addresses of a warp-wide load fall in four different bank groups
 // (conflict-free broadcast).  At the end of a segment the warps merge in a
-// 3-level tree in shared memory; warp 0 writes the output of a segment that
+// 3-level tree (8 -> 4 through tensor memory, which the kernel otherwise
+// does not use, 4 -> 2 -> 1 through shared memory); warp 0 writes the output of a segment that
 // is a whole sequence, otherwise its (m, l, o) partial goes to the workspace
 // and the last CTA to finish a partial of that sequence combines them (batch
 // mode; merge_kernel does it for the single-sequence entry points).
@@ -29,6 +30,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace tle {
 
@@ -41,24 +43,31 @@ constexpr int HD = kHeadDim;
 constexpr int NH = kNHead;
 constexpr int ROWF = kRowFloats;   // 256 floats per cache row
 constexpr int ROWB = ROWF * 4;     // 1024 bytes
-constexpr int TILE = 24;           // rows per pipeline stage
+constexpr int TILE = 32;           // rows per pipeline stage
 constexpr int NSTAGE = 3;
 constexpr int NCW = 8;             // warps (all consume; warp 0 lane 0 also issues the copies)
 constexpr int NCT = NCW * 32;      // threads per CTA
-constexpr int RPW = TILE / NCW;    // rows per warp per tile (3)
-constexpr int QS = HD + 4;         // padded q/o row stride in shared memory
-constexpr int MS = HD + 4;         // merge-buffer row: acc[64], m, l, pad
+constexpr int RPW = TILE / NCW;    // rows per warp per tile (4)
+constexpr int QS = HD + 4;         // padded row of the q / tree buffers: 64 floats, m, l, pad
+constexpr uint32_t kTmemCols = 128;  // tree-merge exchange: acc[64], m, l per lane
 constexpr float kScale = 0.125f;   // 1/sqrt(64), exact in fp32
 
 struct __align__(128) DecodeSmem {
     float k[NSTAGE][TILE * ROWF];
     float v[NSTAGE][TILE * ROWF];
-    float qraw[2][NH * HD];     // q of a segment's sequence (bulk copy, double-buffered by segment)
-    float kvraw[2][2 * ROWF];   // that sequence's new k row and v row (segments holding row pos)
-    float qo[NH * QS];          // rotated, scaled q of the current segment
+    // q of a segment's sequence (one 8 KB bulk copy), double-buffered by
+    // segment; after the prologue it is the tree merge's buffer A (chunk c of
+    // row h stored at chunk (c + h) & 15: conflict-free), m and l in mlA.
+    float qraw[2][NH * HD];
+    float kvraw[2 * ROWF];      // that sequence's new k row and v row (segments holding row pos)
     float newk[ROWF];           // rotated k of the token being decoded
     float newv[ROWF];
-    float mbuf[4][NH * MS];     // tree merge of the warps' (acc, m, l)
+    // Rotated, scaled q of the current segment in padded rows (stride 68:
+    // the rotated-order reads are conflict-free); once the q registers are
+    // loaded it is the tree merge's buffer B (m, l in the row padding).
+    float qo[NH * QS];
+    float mlA[2 * NH];
+    uint32_t tmem_base;
     uint64_t full[NSTAGE];
     uint64_t empty[NSTAGE];
     uint64_t qfull[2];
@@ -132,50 +141,114 @@ __device__ __forceinline__ void cursor_issue(TileCursor& c, const DecodeArgs& A,
     if (c.ta >= c.b) cursor_load(c, A, c.s + 1, 0, s1, o1);
 }
 
-// Bulk copies of segment n's per-sequence inputs into buffer n & 1: q of its
-// sequence and, when the segment holds row pos, the new k and v rows.
-// Segment n of a CTA is sequence s0 + n.
-// Returns false (nothing issued) when the CTA has no segment n.
+// Bulk copies of segment n's per-sequence inputs into buffer n & 1, issued by
+// warp 0: q of its sequence and, when the segment holds row pos, the new k and
+// v rows.  Segment n of a CTA is sequence s0 + n.  Returns false (nothing
+// issued) when the CTA has no segment n; warp-uniform.
 __device__ __forceinline__ bool issue_q(const DecodeArgs& A, DecodeSmem& S, int n, int s0, int o0,
-                                        int s1, int o1) {
+                                        int s1, int o1, int lane) {
     const int s = s0 + n;
     if (!in_range(s, n == 0 ? o0 : 0, s1, o1)) return false;
     const tle_seq_t sq = load_seq(A, s);
     const int L = sq.pos + 1;
     const bool has_new = ((s == s1) ? o1 : L) == L;
     const int b = n & 1;
-    mbar_arrive_expect_tx(&S.qfull[b], NH * HD * 4 + (has_new ? 2 * ROWB : 0));
-    bulk_g2s_plain(S.qraw[b], A.q + static_cast<size_t>(s) * NH * HD, NH * HD * 4, &S.qfull[b]);
-    if (has_new) {
-        bulk_g2s_plain(S.kvraw[b], A.k + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
-        bulk_g2s_plain(S.kvraw[b] + ROWF, A.v + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
+    if (lane == 0) {
+        mbar_arrive_expect_tx(&S.qfull[b], NH * HD * 4 + (has_new ? 2 * ROWB : 0));
+        bulk_g2s_plain(S.qraw[b], A.q + static_cast<size_t>(s) * NH * HD, NH * HD * 4, &S.qfull[b]);
+        if (has_new) {
+            bulk_g2s_plain(S.kvraw, A.k + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
+            bulk_g2s_plain(S.kvraw + ROWF, A.v + static_cast<size_t>(s) * ROWF, ROWB, &S.qfull[b]);
+        }
     }
+    __syncwarp();
     return true;
 }
 
-// Folds another warp's (m2, l2, acc2) of the same query head into (m, l, acc).
-__device__ __forceinline__ void merge_in(float& m, float& l, float4 (&acc)[16], const float* src) {
-    const float m2 = src[HD], l2 = src[HD + 1];
+// Folds (m2, l2, a2) of the same query head into (m, l, acc[c0 .. c0+7]) /
+// computes the factors; split so TMEM can be read 32 columns at a time.
+struct FoldFactors {
+    float f1, f2;
+};
+__device__ __forceinline__ FoldFactors fold_factors(float& m, float& l, float m2, float l2) {
     const float mn = fmaxf(m, m2);
-    const float f1 = (m == -INFINITY) ? 0.f : expf(m - mn);
-    const float f2 = (m2 == -INFINITY) ? 0.f : expf(m2 - mn);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        const float4 a2 = *reinterpret_cast<const float4*>(src + 4 * c);
-        acc[c].x = fmaf(acc[c].x, f1, a2.x * f2);
-        acc[c].y = fmaf(acc[c].y, f1, a2.y * f2);
-        acc[c].z = fmaf(acc[c].z, f1, a2.z * f2);
-        acc[c].w = fmaf(acc[c].w, f1, a2.w * f2);
-    }
-    l = fmaf(l, f1, l2 * f2);
+    FoldFactors f;
+    f.f1 = (m == -INFINITY) ? 0.f : expf(m - mn);
+    f.f2 = (m2 == -INFINITY) ? 0.f : expf(m2 - mn);
+    l = fmaf(l, f.f1, l2 * f.f2);
     m = mn;
+    return f;
+}
+__device__ __forceinline__ void fold4(float4& a, float4 b, FoldFactors f) {
+    a.x = fmaf(a.x, f.f1, b.x * f.f2);
+    a.y = fmaf(a.y, f.f1, b.y * f.f2);
+    a.z = fmaf(a.z, f.f1, b.z * f.f2);
+    a.w = fmaf(a.w, f.f1, b.w * f.f2);
 }
 
-__device__ __forceinline__ void merge_out(float m, float l, const float4 (&acc)[16], float* dst) {
+// Shared-memory tree steps: another warp's (acc, m, l) of the same query
+// head, acc in the lanes' shared chunk order.  Buffer B: row h of a [32][QS]
+// buffer (m, l in the padding).
+__device__ __forceinline__ void merge_in(float& m, float& l, float4 (&acc)[16], const float* row) {
+    const FoldFactors f = fold_factors(m, l, row[HD], row[HD + 1]);
 #pragma unroll
-    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(dst + 4 * c) = acc[c];
-    dst[HD] = m;
-    dst[HD + 1] = l;
+    for (int c = 0; c < 16; ++c) fold4(acc[c], *reinterpret_cast<const float4*>(row + 4 * c), f);
+}
+__device__ __forceinline__ void merge_out(float m, float l, const float4 (&acc)[16], float* row) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(row + 4 * c) = acc[c];
+    row[HD] = m;
+    row[HD + 1] = l;
+}
+// Buffer A: dense [32][64] with chunk c of row h at chunk (c + h) & 15, m and l in ml.
+__device__ __forceinline__ void merge_in_a(float& m, float& l, float4 (&acc)[16], const float* O,
+                                           const float* ml, int h) {
+    const FoldFactors f = fold_factors(m, l, ml[h], ml[NH + h]);
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+        fold4(acc[c], *reinterpret_cast<const float4*>(O + h * HD + 4 * ((c + h) & 15)), f);
+}
+__device__ __forceinline__ void merge_out_a(float m, float l, const float4 (&acc)[16], float* O, float* ml,
+                                            int h) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) *reinterpret_cast<float4*>(O + h * HD + 4 * ((c + h) & 15)) = acc[c];
+    ml[h] = m;
+    ml[NH + h] = l;
+}
+
+// Tensor-memory tree step: warp w + 4 stores its (acc, m, l) in its TMEM lane
+// quadrant (w & 3), warp w reads it (a warp reaches only its own quadrant).
+__device__ __forceinline__ void tmem_put(uint32_t tq, float m, float l, const float4 (&acc)[16]) {
+    uint32_t r[32];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 a = acc[8 * half + c];
+            r[4 * c] = __float_as_uint(a.x);
+            r[4 * c + 1] = __float_as_uint(a.y);
+            r[4 * c + 2] = __float_as_uint(a.z);
+            r[4 * c + 3] = __float_as_uint(a.w);
+        }
+        tmem_st32(tq + 32 * half, r);
+    }
+    tmem_st2(tq + 64, m, l);
+    tmem_wait_st();
+}
+__device__ __forceinline__ void tmem_merge_in(uint32_t tq, float& m, float& l, float4 (&acc)[16]) {
+    float m2, l2;
+    tmem_ld2(tq + 64, m2, l2);
+    tmem_wait_ld();
+    const FoldFactors f = fold_factors(m, l, m2, l2);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        float v[32];
+        tmem_ld32(tq + 32 * half, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            fold4(acc[8 * half + c], make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]), f);
+    }
 }
 
 // Batch mode, warp 0 (lane = query head h), after this CTA wrote its partial
@@ -262,7 +335,7 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& A, int s, int l
 __device__ __forceinline__ bool cta_sync(DecodeSmem& S, uint32_t& phase, int lane) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.csync);
-    const bool ok = mbar_wait(&S.csync, phase);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&S.csync, phase));  // warp-uniform
     phase ^= 1u;
     __syncwarp();
     return ok;
@@ -277,35 +350,47 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     const int cta = blockIdx.x;
     const bool issuer = (tid == 0);
 
-    if (tid == 0) {
-        for (int i = 0; i < NSTAGE; ++i) {
-            mbar_init(&S.full[i], 1);
-            mbar_init(&S.empty[i], NCW);
-        }
-        mbar_init(&S.qfull[0], 1);
-        mbar_init(&S.qfull[1], 1);
-        mbar_init(&S.csync, NCW);
-        fence_barrier_init();
-    }
-    __syncthreads();
-
     int s0, o0, s1, o1;
     cta_range(A, cta, s0, o0, s1, o1);
 
-    // Prologue: the issuer starts segment 0's q copy, then fills the stages.
+    // Prologue: thread 0 (the tile issuer) initialises the barriers, warp 0
+    // starts segment 0's q copy and thread 0 the first NSTAGE tiles, while
+    // warp 1 allocates the tensor memory; the other warps touch none of it
+    // before the __syncthreads below.
     TileCursor cur;
     uint64_t pol = 0;
     int issued = 0;
-    int q_issued = 0;   // segments 0 .. q_issued-1 have their q copy issued
-    if (issuer) {
-        pol = l2_evict_first_policy();
-        if (issue_q(A, S, 0, s0, o0, s1, o1)) q_issued = 1;
-        cursor_load(cur, A, s0, o0, s1, o1);
-        while (!cur.done && issued < NSTAGE) {
-            cursor_issue(cur, A, S, issued, s1, o1, pol);
-            ++issued;
+    int q_issued = 0;   // (warp 0) segments 0 .. q_issued-1 have their q copy issued
+    if (warp == 0) {
+        if (issuer) {
+            for (int i = 0; i < NSTAGE; ++i) {
+                mbar_init(&S.full[i], 1);
+                mbar_init(&S.empty[i], NCW);
+            }
+            mbar_init(&S.qfull[0], 1);
+            mbar_init(&S.qfull[1], 1);
+            mbar_init(&S.csync, NCW);
+            fence_barrier_init();
+        }
+        __syncwarp();
+        if (issue_q(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
+        if (issuer) {
+            pol = l2_evict_first_policy();
+            cursor_load(cur, A, s0, o0, s1, o1);
+            while (!cur.done && issued < NSTAGE) {
+                cursor_issue(cur, A, S, issued, s1, o1, pol);
+                ++issued;
+            }
         }
     }
+    if (warp == 1) {
+        tmem_alloc(&S.tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tq = S.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 
     const int g = lane >> 3;       // KV head of this lane's query head
     const int h = lane;            // query head
@@ -320,7 +405,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         const int seg_a = off;
         const int seg_b = (s == s1) ? o1 : L;
         const int qb = n & 1;
-        if (!mbar_wait(&S.qfull[qb], (n >> 1) & 1)) { record_error(A.err, kErrWaitFull); ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&S.qfull[qb], (n >> 1) & 1))) { record_error(A.err, kErrWaitFull); ok = false; break; }
 
         // q: rotate (rope, ops.cpp:1229-1260), pre-scale by 1/sqrt(64) (exact
         // power of two, so (q/8).k == (q.k)/8 bit for bit).  Every pair this
@@ -329,17 +414,18 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         float sn = 0.f, cs = 1.f;
         if (A.rotate) sincosf(static_cast<float>(sq.pos) * A.inv_freq[lane], &sn, &cs);
         {
-            const float2* qsrc = reinterpret_cast<const float2*>(S.qraw[qb]);
-            for (int j = tid; j < NH * HD / 2; j += NCT) {
-                const int hh = j >> 5;
-                const float2 x = qsrc[j];
+            // Pair `lane` of heads warp + 8 i.
+            const float2* Q = reinterpret_cast<const float2*>(S.qraw[qb]);
+#pragma unroll
+            for (int i = 0; i < NH / NCW; ++i) {
+                const int hh = warp + NCW * i;
+                const float2 x = Q[hh * (HD / 2) + lane];
                 float y0 = x.x, y1 = x.y;
                 if (A.rotate) {
                     y0 = x.x * cs - x.y * sn;
                     y1 = x.x * sn + x.y * cs;
                 }
-                S.qo[hh * QS + 2 * lane] = y0 * kScale;
-                S.qo[hh * QS + 2 * lane + 1] = y1 * kScale;
+                *reinterpret_cast<float2*>(&S.qo[hh * QS + 2 * lane]) = make_float2(y0 * kScale, y1 * kScale);
             }
         }
         // The new token's k (rotated) and v: append to the cache at row pos
@@ -347,7 +433,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         if (seg_b == L) {
             const size_t row = (static_cast<size_t>(A.layer) * sq.n_ctx + sq.pos) * ROWF;
             if (tid < ROWF / 2) {
-                const float2 x = reinterpret_cast<const float2*>(S.kvraw[qb])[tid];
+                const float2 x = reinterpret_cast<const float2*>(S.kvraw)[tid];
                 float y0 = x.x, y1 = x.y;
                 if (A.rotate) {
                     y0 = x.x * cs - x.y * sn;
@@ -358,15 +444,19 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                 reinterpret_cast<float2*>(sq.key_cache + row)[tid] = y;
             } else {
                 const int t2 = tid - ROWF / 2;
-                const float2 x = reinterpret_cast<const float2*>(S.kvraw[qb] + ROWF)[t2];
+                const float2 x = reinterpret_cast<const float2*>(S.kvraw + ROWF)[t2];
                 reinterpret_cast<float2*>(S.newv)[t2] = x;
                 reinterpret_cast<float2*>(sq.value_cache + row)[t2] = x;
             }
         }
+        // Shared memory written by this thread through the generic proxy
+        // (qraw, kvraw, the tree buffers) is rewritten by later bulk copies.
+        fence_proxy_async_smem();
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
-        // Buffer (n+1)&1 was last read in segment n-1's prologue: prefetch the
-        // next segment's q (and new rows) while this segment streams.
-        if (issuer && q_issued == n + 1 && issue_q(A, S, n + 1, s0, o0, s1, o1)) q_issued = n + 2;
+        // qraw[(n+1)&1] was last used in segment n-1 and kvraw was consumed
+        // above: prefetch the next segment's q (and new rows) while this
+        // segment streams.
+        if (warp == 0 && q_issued == n + 1 && issue_q(A, S, n + 1, s0, o0, s1, o1, lane)) q_issued = n + 2;
 
         // This lane's query head, its 16-byte chunks in KV-head-rotated order.
         float4 q[16];
@@ -394,7 +484,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             }
             const int nrows = min(ta + TILE, seg_b) - ta;
             const int st = it % NSTAGE;
-            if (!mbar_wait(&S.full[st], (it / NSTAGE) & 1)) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&S.full[st], (it / NSTAGE) & 1))) {
                 record_error(A.err, kErrWaitFull);
                 ok = false;
                 break;
@@ -472,27 +562,46 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
 
         // ---- tree merge of the 8 warps' (m, l, acc): 8 -> 4 -> 2 -> 1 ----
         // (every lane of a pair of warps holds the same query head with the
-        // same chunk rotation, so rows are merged in place)
-        if (warp >= 4) merge_out(m_run, l_run, acc, &S.mbuf[warp - 4][h * MS]);
+        // same chunk rotation, so rows are merged in place).  8 -> 4 through
+        // TMEM.  Then buffers A (qraw[qb], free since the prologue barrier,
+        // next rewritten by segment n + 2's q copy) and B (qo, free once
+        // every warp has loaded its q registers, which the first barrier
+        // guarantees; B's last reader passes the third barrier before any
+        // warp rotates the next segment's q into it).
+        if (warp >= 4) {
+            tc_fence_after();
+            tmem_put(tq, m_run, l_run, acc);
+            tc_fence_before();
+        }
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
-        if (warp < 4) merge_in(m_run, l_run, acc, &S.mbuf[warp][h * MS]);
-        if (warp == 2 || warp == 3) merge_out(m_run, l_run, acc, &S.mbuf[warp][h * MS]);
+        float* OA = S.qraw[qb];
+        if (warp < 4) {
+            tc_fence_after();
+            tmem_merge_in(tq, m_run, l_run, acc);
+            tc_fence_before();
+        }
+        if (warp == 2) merge_out(m_run, l_run, acc, S.qo + h * QS);
+        if (warp == 3) merge_out_a(m_run, l_run, acc, OA, S.mlA, h);
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
-        if (warp < 2) merge_in(m_run, l_run, acc, &S.mbuf[warp + 2][h * MS]);
-        if (warp == 1) merge_out(m_run, l_run, acc, &S.mbuf[1][h * MS]);
+        if (warp == 0) merge_in(m_run, l_run, acc, S.qo + h * QS);
+        if (warp == 1) {
+            merge_in_a(m_run, l_run, acc, OA, S.mlA, h);
+            __syncwarp();
+            merge_out_a(m_run, l_run, acc, OA, S.mlA, h);
+        }
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
         if (warp == 0) {
             // CTAs sharing this sequence (the load overlaps the stores below).
             SeqCtas sc{0, 0};
             if (A.arrivals && !(seg_a == 0 && seg_b == L)) sc = A.seq_ctas[s];
-            merge_in(m_run, l_run, acc, &S.mbuf[1][h * MS]);
+            merge_in_a(m_run, l_run, acc, OA, S.mlA, h);
             // ---- write: whole sequence -> output; otherwise a partial ----
-            // Staged through shared memory (mbuf[0], free until the next
-            // segment's tree merge) so the global stores are coalesced.
-            float* T = &S.mbuf[0][0];
+            // Staged through buffer A (only warp 0 touches it from here to
+            // the next segment's prologue) so the global stores are coalesced.
+            __syncwarp();
 #pragma unroll
             for (int c = 0; c < 16; ++c)
-                *reinterpret_cast<float4*>(T + h * MS + 4 * ((c + g) & 15)) = acc[c];
+                *reinterpret_cast<float4*>(OA + h * HD + 4 * ((((c + g) & 15) + h) & 15)) = acc[c];
             __syncwarp();
             const bool whole = (seg_a == 0 && seg_b == L);
             const float scale = whole ? 1.0f / l_run : 1.0f;
@@ -502,7 +611,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             for (int i = 0; i < 16; ++i) {
                 const int hh = coalesced_head(i, lane);
                 const float f = __shfl_sync(0xffffffffu, scale, hh);
-                const float4 v = *reinterpret_cast<const float4*>(T + hh * MS + 4 * (lane & 15));
+                const float4 v = *reinterpret_cast<const float4*>(OA + hh * HD + 4 * (((lane & 15) + hh) & 15));
                 reinterpret_cast<float4*>(dst)[32 * i + lane] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
             }
             if (!whole) {
@@ -521,6 +630,14 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
         for (int m = n; m < q_issued; ++m)
             if (!mbar_wait(&S.qfull[m & 1], (m >> 1) & 1)) { record_error(A.err, kErrDrain); break; }
+    }
+    // Every warp gets here (all waits are bounded); the allocating warp frees
+    // the tensor memory once no warp can touch it.
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(S.tmem_base, kTmemCols);
     }
 }
 

@@ -138,6 +138,21 @@ TLE_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 TLE_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- 2 columns per lane (32 lanes x 2 x 32-bit)
+TLE_DEV void tmem_st2(uint32_t taddr, float a, float b) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(taddr),
+                 "r"(__float_as_uint(a)), "r"(__float_as_uint(b))
+                 : "memory");
+}
+TLE_DEV void tmem_ld2(uint32_t taddr, float& a, float& b) {
+    uint32_t r0, r1;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(taddr));
+    a = __uint_as_float(r0);
+    b = __uint_as_float(r1);
+}
+
 // ---- per-warpgroup register budget (all 4 warps of the warpgroup execute it)
 template <uint32_t N>
 TLE_DEV void regs_dealloc() {
