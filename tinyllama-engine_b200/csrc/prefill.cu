@@ -93,13 +93,18 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 // blockIdx.y == 0: one token per warp, lane = rotation pair p.  One sincosf
 //   per (token, pair) serves the 32 query heads and 4 key heads: rotated
-//   q * 1/8 -> Qb, rotated k -> cache (append) and Kb, v -> cache (append).
-//   Token slots in [n_tokens, S_pad) zero their Qb rows.
-// blockIdx.y == 1: 64 rows x all 4 KV heads: V rows (cache prefix, new
-//   tokens, zero pad) are transposed through shared memory into Vt; Kb rows
-//   of the cache prefix (bf16 of the cached rotated k) and of the pad (zero).
-__global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
+//   q * 1/8 -> Qb, rotated k -> cache (append) and Kb.  Token slots in
+//   [n_tokens, S_pad) zero their Qb rows.
+// blockIdx.y == 1: 32 rows x all 4 KV heads: V rows (cache prefix, new
+//   tokens, zero pad) are transposed through shared memory into Vt, and the
+//   new tokens' v rows are appended to the cache; Kb rows of the cache prefix
+//   (bf16 of the cached rotated k) and of the pad (zero).
+__global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
     __shared__ __align__(16) uint16_t vtile[kVtRows * kVtPitch];   // bf16 bits
+    // The attention launch may start now (programmatic dependent launch): it
+    // sets up its barriers and TMEM while this grid runs, and its TMA
+    // producer waits for this grid to complete before loading the operands.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (blockIdx.y == 0) {
@@ -114,28 +119,30 @@ __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid
         const int pos = A.pos0 + i;
         float sn, cs;
         sincosf(static_cast<float>(pos) * A.inv_freq[lane], &sn, &cs);
+        // Every load of the token first (36 in flight per lane), then the
+        // stores: loads placed after stores could not be hoisted above them.
+        // (The v row is appended by the V^T role, which reads it anyway.)
         const float2* qs = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(i) * NH * HD);
-        float2 xq[NH];
+        const float2* ks = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(i) * NKV * HD);
+        float2 xq[NH], xk[NKV];
 #pragma unroll
-        for (int h = 0; h < NH; ++h) xq[h] = qs[h * (HD / 2) + lane];   // 32 loads in flight
+        for (int h = 0; h < NH; ++h) xq[h] = qs[h * (HD / 2) + lane];
+#pragma unroll
+        for (int g = 0; g < NKV; ++g) xk[g] = ks[g * (HD / 2) + lane];
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
             const float2 x = xq[h];
             qb32[(static_cast<size_t>(h) * A.S_pad + i) * (HD / 2) + lane] =
                 pack_bf16((x.x * cs - x.y * sn) * kQScale, (x.x * sn + x.y * cs) * kQScale);
         }
-        const float2* ks = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(i) * NKV * HD);
-        const float2* vs = reinterpret_cast<const float2*>(A.v + static_cast<size_t>(i) * NKV * HD);
         float2* kcr = reinterpret_cast<float2*>(A.kc + static_cast<size_t>(pos) * NKV * HD);
-        float2* vcr = reinterpret_cast<float2*>(A.vc + static_cast<size_t>(pos) * NKV * HD);
         uint32_t* kb32 = reinterpret_cast<uint32_t*>(A.kb);
 #pragma unroll
         for (int g = 0; g < NKV; ++g) {
-            const float2 x = ks[g * (HD / 2) + lane];
+            const float2 x = xk[g];
             const float2 y = make_float2(x.x * cs - x.y * sn, x.x * sn + x.y * cs);
             kcr[g * (HD / 2) + lane] = y;                                     // append (ops.cpp:1370)
             kb32[(static_cast<size_t>(g) * A.R_pad + pos) * (HD / 2) + lane] = pack_bf16(y.x, y.y);
-            vcr[g * (HD / 2) + lane] = vs[g * (HD / 2) + lane];               // append (ops.cpp:1371)
         }
         return;
     }
@@ -161,6 +168,8 @@ __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid
         const int t = threadIdx.x + u * kPrepThreads;
         const int rr = t / kVec, c4 = t % kVec;
         const int r = r0 + rr;
+        if (r >= A.pos0 && r < A.R)   // append v of the new tokens (ops.cpp:1371)
+            reinterpret_cast<float4*>(A.vc + static_cast<size_t>(r) * NKV * HD)[c4] = vv[u];
         *reinterpret_cast<uint2*>(&vtile[rr * kVtPitch + 4 * c4]) =
             make_uint2(pack_bf16(vv[u].x, vv[u].y), pack_bf16(vv[u].z, vv[u].w));
         // Kb rows outside [pos0, R): bf16 of the cached prefix, zero pad
@@ -356,6 +365,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
         regs_dealloc<kRegsControl>();
         if (warp == 0) {
             // ------------------------------ TMA producer ------------------------------
+            // Qb, Kb and Vt are written by prefill_prep_kernel, the preceding
+            // launch on the stream (no-op without programmatic dependent launch).
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             if (lane == 0) {
                 mbar_arrive_expect_tx(&S.bar_q, 2 * BM * HD * 2);
                 tma_load_2d(S.q[0], &A.tm_q, 0, h0 * A.S_pad + q0, &S.bar_q);
@@ -645,8 +657,19 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
-    prefill_attn_kernel<<<t.n_qt * (NH / 2), ATTN_THREADS, smem, stream>>>(t);
-    return cudaGetLastError();
+    // Programmatic dependent launch: the attention grid may start while the
+    // prep grid runs; only its TMA producer waits (griddepcontrol.wait).
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(t.n_qt * (NH / 2));
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, t);
 }
 
 }  // namespace tle
