@@ -14,16 +14,18 @@
 //        Kb [4 kv][R_pad][64]       rotated k (rows < pos0 from the cache)
 //        Vt [4 kv][64][R_pad]       v transposed so PV's B operand is K-major
 //     (R = pos0 + S rows; pads are zero).
-//  2. prefill_attn_kernel: one CTA per (128-query tile, query head).  TMA
-//     (SWIZZLE_128B, no multicast) loads the Q tile once and double-buffers
-//     128-row K / V^T tiles of the head's KV head; one thread issues
-//     S = Q K^T (M=128, N=128, K=64) into TMEM; 128 threads (one per query
-//     row) read S back, apply the causal mask and an fp32 online softmax,
-//     write P (bf16) into shared memory in the swizzled K-major layout; the
-//     same thread issues O_j = P V_j (M=128, N=64, K=128) into TMEM; the rows
-//     accumulate O in registers with the softmax rescale.  Q, K, V and P
-//     enter the MMA as bf16 with fp32 accumulation (the north-star prefill
-//     contract, tolerance 2e-2).
+//  2. prefill_attn_kernel: persistent, one CTA per SM walking work items
+//     (128-query tile, pair of query heads of one KV head), heaviest first in
+//     snake order.  TMA (SWIZZLE_128B, no multicast) loads each item's two Q
+//     tiles (double-buffered across items) and a 4-stage ring of 128-row K /
+//     V^T tiles; one warp per head issues S = Q K^T (M=128, N=128, K=64) into
+//     TMEM and O += P V (M=128, N=64, K=128, P read from TMEM); 128 threads
+//     per head (one per query row) read S back, apply the causal mask and an
+//     fp32 online softmax with a lazy rescale, and write P (bf16) to TMEM.
+//     The next item's first scores are computed during this item's epilogue,
+//     which stages O through the dead Q buffer for coalesced stores.  Q, K,
+//     V and P enter the MMA as bf16 with fp32 accumulation (the north-star
+//     prefill contract, tolerance 2e-2).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <math.h>
@@ -229,10 +231,12 @@ constexpr uint32_t TMEM_COLS2 = 512;
 constexpr float kRescaleThreshold = 8.0f;
 
 struct AttnSmem {
-    __nv_bfloat16 q[2][BM * HD];           // 2 heads x 16 KB, SW128 K-major
+    __nv_bfloat16 q[2][2][BM * HD];        // [item parity][head] 16 KB each, SW128 K-major
     __nv_bfloat16 k[KSTAGES][BN * HD];     // 16 KB per stage
     __nv_bfloat16 vt[KSTAGES][2][HD * 64]; // 16 KB per stage (two 64-kv halves)
-    uint64_t bar_q;
+    uint64_t bar_q[2];                     // Q tiles of an item landed
+    uint64_t q_free[2];                    // Q buffer reusable: both heads' last S MMA of the
+                                           // item done and its epilogue staging read back
     uint64_t kv_full[KSTAGES];
     uint64_t kv_empty[KSTAGES];
     uint64_t s_full[2];
@@ -317,6 +321,27 @@ __device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, uin
     }
 }
 
+// Work items: (128-query tile, pair of query heads of one KV head), numbered
+// heaviest query tile first.  The persistent CTAs take them in snake order
+// (round r: CTA c takes r G + c for even r, r G + G - 1 - c for odd r), which
+// evens out the causal tile counts.
+struct Item {
+    int h0, kvh, q0, n_kv;
+};
+__device__ __forceinline__ int item_index(int k, int c, int G) {
+    return k * G + ((k & 1) ? G - 1 - c : c);
+}
+__device__ __forceinline__ Item item_at(const AttnArgs& A, int idx) {
+    Item it;
+    const int qt = A.n_qt - 1 - idx / (NH / 2);
+    it.h0 = 2 * (idx % (NH / 2));
+    it.kvh = it.h0 / GQA;
+    it.q0 = qt * BM;
+    const int last_tok = min(it.q0 + BM, A.n_tokens) - 1;
+    it.n_kv = (A.pos0 + last_tok) / BN + 1;
+    return it;
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __grid_constant__ AttnArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // SW128 atoms need 1024-byte aligned tiles (the launch adds 1 KB of slack)
@@ -326,16 +351,17 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int wg = warp >> 2;
-    // heaviest query tiles first; two query heads of one KV head per CTA
-    const int qt = A.n_qt - 1 - static_cast<int>(blockIdx.x) / (NH / 2);
-    const int h0 = 2 * (static_cast<int>(blockIdx.x) % (NH / 2));
-    const int kvh = h0 / GQA;
-    const int q0 = qt * BM;
-    const int last_tok = min(q0 + BM, A.n_tokens) - 1;
-    const int n_kv = (A.pos0 + last_tok) / BN + 1;
+    const int n_items = A.n_qt * (NH / 2);
+    const int G = static_cast<int>(gridDim.x);
+    const int cta = static_cast<int>(blockIdx.x);
+    int my_items = 0;   // items of this CTA: k = 0 .. my_items-1
+    while (item_index(my_items, cta, G) < n_items) ++my_items;
 
     if (tid == 0) {
-        mbar_init(&S.bar_q, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.bar_q[b], 1);
+            mbar_init(&S.q_free[b], 2 + 8);   // a commit per head's MMA warp + the 8 softmax warps
+        }
         for (int i = 0; i < KSTAGES; ++i) {
             mbar_init(&S.kv_full[i], 1);
             mbar_init(&S.kv_empty[i], 2);   // last PV of each head
@@ -368,31 +394,40 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
             // Qb, Kb and Vt are written by prefill_prep_kernel, the preceding
             // launch on the stream (no-op without programmatic dependent launch).
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&S.bar_q, 2 * BM * HD * 2);
-                tma_load_2d(S.q[0], &A.tm_q, 0, h0 * A.S_pad + q0, &S.bar_q);
-                tma_load_2d(S.q[1], &A.tm_q, 0, (h0 + 1) * A.S_pad + q0, &S.bar_q);
-            }
-            for (int j = 0; j < n_kv; ++j) {
-                const int st = j % KSTAGES;
-                wait_or_flag(&S.kv_empty[st], ((j / KSTAGES) & 1) ^ 1, A.err, kErrWaitEmpty, failed);
+            int ring = 0;   // K/V tiles issued so far (across items)
+            for (int k = 0; k < my_items; ++k) {
+                const Item it = item_at(A, item_index(k, cta, G));
+                const int b = k & 1;
+                // Q buffer b was last read by item k-2's S MMAs
+                if (k >= 2) wait_or_flag(&S.q_free[b], ((k >> 1) - 1) & 1, A.err, kErrWaitEmpty, failed);
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&S.kv_full[st], kTileBytesK + kTileBytesV);
-                    tma_load_2d(S.k[st], &A.tm_k, 0, kvh * A.R_pad + j * BN, &S.kv_full[st]);
-                    tma_load_2d(S.vt[st][0], &A.tm_vt, j * BN, kvh * HD, &S.kv_full[st]);
-                    tma_load_2d(S.vt[st][1], &A.tm_vt, j * BN + 64, kvh * HD, &S.kv_full[st]);
+                    mbar_arrive_expect_tx(&S.bar_q[b], 2 * BM * HD * 2);
+                    tma_load_2d(S.q[b][0], &A.tm_q, 0, it.h0 * A.S_pad + it.q0, &S.bar_q[b]);
+                    tma_load_2d(S.q[b][1], &A.tm_q, 0, (it.h0 + 1) * A.S_pad + it.q0, &S.bar_q[b]);
                 }
-                __syncwarp();
+                for (int j = 0; j < it.n_kv; ++j, ++ring) {
+                    const int st = ring % KSTAGES;
+                    wait_or_flag(&S.kv_empty[st], ((ring / KSTAGES) & 1) ^ 1, A.err, kErrWaitEmpty, failed);
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&S.kv_full[st], kTileBytesK + kTileBytesV);
+                        tma_load_2d(S.k[st], &A.tm_k, 0, it.kvh * A.R_pad + j * BN, &S.kv_full[st]);
+                        tma_load_2d(S.vt[st][0], &A.tm_vt, j * BN, it.kvh * HD, &S.kv_full[st]);
+                        tma_load_2d(S.vt[st][1], &A.tm_vt, j * BN + 64, it.kvh * HD, &S.kv_full[st]);
+                    }
+                    __syncwarp();
+                }
             }
         } else if (warp == 1 || warp == 2) {
             // ------------------------------ MMA issuers --------------------------------
             // One issuing warp per query head, so the two heads' pipelines do
-            // not wait on each other: head i issues S_i(n+1) as soon as its
-            // softmax has read S_i(n), and O_i += P_i(n) V_n as soon as P_i(n)
-            // is in TMEM.  A K/V stage is released when both heads' last
-            // readers of it have committed (kv_empty counts 2 arrivals).
+            // not wait on each other: head i issues S_i of its next tile as
+            // soon as its softmax has read the current one (across item
+            // boundaries too, so the next item's first scores are computed
+            // during this item's epilogue), and O_i += P_i V as soon as P_i is
+            // in TMEM.  A K/V stage is released when both heads' last readers
+            // of it have committed (kv_empty counts 2 arrivals); a Q buffer
+            // when both heads' last S MMA of the item has (q_free, 2).
             const int i = warp - 1;
-            const uint64_t dq = sw128_desc(smem_u32(S.q[i]));
             const uint64_t dk0 = sw128_desc(smem_u32(S.k[0]));
             const uint64_t dv0 = sw128_desc(smem_u32(S.vt[0][0]));
             constexpr uint64_t kStageK = (BN * HD * 2) >> 4;        // stage stride, descriptor units
@@ -401,22 +436,28 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
             const uint32_t tS = tmem + (i ? kColS1 : kColS0);
             const uint32_t tP = tmem + (i ? kColP1 : kColP0);
             const uint32_t tO = tmem + (i ? kColO1 : kColO0);
-            auto issue_s = [&](int n) {   // S_i = Q_i K_n^T
-                const int st = n % KSTAGES;
-                wait_or_flag(&S.kv_full[st], (n / KSTAGES) & 1, A.err, kErrWaitFull, failed);
-                if (n > 0) wait_or_flag(&S.s_free[i], (n - 1) & 1, A.err, kErrWaitMma, failed);
+            // S_i of global tile g (item k, tile n; the stage of a tile is its
+            // global index: the producer walks the same sequence)
+            auto issue_s = [&](int g, int k, int n, int n_kv) {
+                const int st = g % KSTAGES;
+                const int b = k & 1;
+                if (n == 0) wait_or_flag(&S.bar_q[b], (k >> 1) & 1, A.err, kErrWaitFull, failed);
+                wait_or_flag(&S.kv_full[st], (g / KSTAGES) & 1, A.err, kErrWaitFull, failed);
+                if (g > 0) wait_or_flag(&S.s_free[i], (g - 1) & 1, A.err, kErrWaitMma, failed);
                 tc_fence_after();
                 if (elect_one()) {
+                    const uint64_t dq = sw128_desc(smem_u32(S.q[b][i]));
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk)
                         umma_bf16(tS, dq + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdescS, kk > 0);
                     umma_commit(&S.s_full[i]);
+                    if (n == n_kv - 1) umma_commit(&S.q_free[b]);   // last read of Q buffer b
                 }
                 __syncwarp();
             };
-            auto issue_pv = [&](int n) {  // O_i (+)= P_i(n) V_n
-                const int st = n % KSTAGES;
-                wait_or_flag(&S.p_full[i], n & 1, A.err, kErrWaitMma, failed);
+            auto issue_pv = [&](int g, int n) {  // O_i (+)= P_i V of global tile g (tile n of its item)
+                const int st = g % KSTAGES;
+                wait_or_flag(&S.p_full[i], g & 1, A.err, kErrWaitMma, failed);
                 tc_fence_after();
                 if (elect_one()) {
 #pragma unroll
@@ -429,11 +470,28 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
                 }
                 __syncwarp();
             };
-            wait_or_flag(&S.bar_q, 0, A.err, kErrWaitFull, failed);
-            issue_s(0);
-            for (int n = 0; n < n_kv; ++n) {
-                if (n + 1 < n_kv) issue_s(n + 1);   // scores of the next tile first
-                issue_pv(n);
+            if (my_items > 0) {
+                int k = 0, n = 0, g = 0;
+                Item it = item_at(A, item_index(0, cta, G));
+                issue_s(0, 0, 0, it.n_kv);
+                for (;;) {
+                    // the tile after (k, n): scores first, then this tile's PV
+                    int k2 = k, n2 = n + 1;
+                    Item it2 = it;
+                    if (n2 == it.n_kv) {
+                        k2 = k + 1;
+                        n2 = 0;
+                        if (k2 < my_items) it2 = item_at(A, item_index(k2, cta, G));
+                    }
+                    const bool more = k2 < my_items;
+                    if (more) issue_s(g + 1, k2, n2, it2.n_kv);
+                    issue_pv(g, n);
+                    if (!more) break;
+                    k = k2;
+                    n = n2;
+                    it = it2;
+                    ++g;
+                }
             }
         }
     } else {
@@ -445,114 +503,140 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
         const uint32_t tS = tmem + lanes + (i ? kColS1 : kColS0);
         const uint32_t tP = tmem + lanes + (i ? kColP1 : kColP0);
         const uint32_t tO = tmem + lanes + (i ? kColO1 : kColO0);
-        const int my_pos = A.pos0 + q0 + row;
-        float m_ref = -INFINITY;   // reference max, log2 units
-        float l_run = 0.f;
-        for (int j = 0; j < n_kv; ++j) {
-            wait_or_flag(&S.s_full[i], j & 1, A.err, kErrWaitMma, failed);
-            tc_fence_after();
-            float s[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                float tmp[32];
-                tmem_ld32(tS + 32 * c, tmp);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) s[32 * c + e] = tmp[e];
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.s_free[i]);   // the MMA may overwrite S_i
-
-            const int kv0 = j * BN;
-            if (kv0 + BN - 1 > my_pos) {
-#pragma unroll
-                for (int e = 0; e < BN; ++e)
-                    if (kv0 + e > my_pos) s[e] = -INFINITY;
-            }
-            // row max as 16 independent 8-element chains, then a 3-input tree
-            float mc[16];
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                float m = fmax3(s[8 * c], s[8 * c + 1], s[8 * c + 2]);
-                m = fmax3(m, s[8 * c + 3], s[8 * c + 4]);
-                m = fmax3(m, s[8 * c + 5], s[8 * c + 6]);
-                mc[c] = fmaxf(m, s[8 * c + 7]);
-            }
-#pragma unroll
-            for (int c = 0; c < 5; ++c) mc[c] = fmax3(mc[3 * c], mc[3 * c + 1], mc[3 * c + 2]);
-            const float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[15]), -INFINITY) * kLog2e;
-            float alpha = 1.f;
-            const bool move = mt > m_ref + kRescaleThreshold;
-            if (move) {
-                alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - mt);
-                m_ref = mt;
-            }
-            // P = 2^(s*log2e - m_ref) in fp32 (one pair in four on the FMA
-            // pipe, the rest on the SFU), packed to bf16 pairs; fp32 row sum.
-            const uint64_t l2e2 = f2(kLog2e, kLog2e);
-            const uint64_t negm2 = f2(-m_ref, -m_ref);
-            uint32_t pk[BN / 2];
-            uint64_t lsum2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
-#pragma unroll
-            for (int e = 0; e < BN / 2; ++e) {
-                const uint64_t x2 = ffma2(f2(s[2 * e], s[2 * e + 1]), l2e2, negm2);
-                float p0, p1;
-                if ((e & 3) == 3) {
-                    ex2_poly2(x2, p0, p1);
-                } else {
-                    float x0, x1;
-                    f2_split(x2, x0, x1);
-                    p0 = ex2_sfu(x0);
-                    p1 = ex2_sfu(x1);
-                }
-                lsum2[e & 3] = fadd2(lsum2[e & 3], f2(p0, p1));
-                pk[e] = pack_bf16(p0, p1);
-            }
-            float lsum0, lsum1;
-            f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
-            l_run = l_run * alpha + (lsum0 + lsum1);
-            // P_i and O_i may be touched once the previous PV MMA is done
-            if (j > 0) {
-                wait_or_flag(&S.p_free[i], (j - 1) & 1, A.err, kErrWaitMma, failed);
+        int g = 0;   // global tile index of this head (barrier phases run across items)
+        for (int k = 0; k < my_items; ++k) {
+            const Item it = item_at(A, item_index(k, cta, G));
+            const int q0 = it.q0;
+            const int n_kv = it.n_kv;
+            const int my_pos = A.pos0 + q0 + row;
+            float m_ref = -INFINITY;   // reference max, log2 units
+            float l_run = 0.f;
+            for (int j = 0; j < n_kv; ++j, ++g) {
+                wait_or_flag(&S.s_full[i], g & 1, A.err, kErrWaitMma, failed);
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, move)) {
+                float s[BN];
 #pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(tO + 32 * c, o);
-                        tmem_wait_ld();
-                        uint32_t ob[32];
+                for (int c = 0; c < BN / 32; ++c) {
+                    float tmp[32];
+                    tmem_ld32(tS + 32 * c, tmp);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(o[e] * alpha);
-                        tmem_st32(tO + 32 * c, ob);
+                    for (int e = 0; e < 32; ++e) s[32 * c + e] = tmp[e];
+                }
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.s_free[i]);   // the MMA may overwrite S_i
+
+                const int kv0 = j * BN;
+                if (kv0 + BN - 1 > my_pos) {
+#pragma unroll
+                    for (int e = 0; e < BN; ++e)
+                        if (kv0 + e > my_pos) s[e] = -INFINITY;
+                }
+                // row max as 16 independent 8-element chains, then a 3-input tree
+                float mc[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    float m = fmax3(s[8 * c], s[8 * c + 1], s[8 * c + 2]);
+                    m = fmax3(m, s[8 * c + 3], s[8 * c + 4]);
+                    m = fmax3(m, s[8 * c + 5], s[8 * c + 6]);
+                    mc[c] = fmaxf(m, s[8 * c + 7]);
+                }
+#pragma unroll
+                for (int c = 0; c < 5; ++c) mc[c] = fmax3(mc[3 * c], mc[3 * c + 1], mc[3 * c + 2]);
+                const float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[15]), -INFINITY) * kLog2e;
+                float alpha = 1.f;
+                const bool move = mt > m_ref + kRescaleThreshold;
+                if (move) {
+                    alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - mt);
+                    m_ref = mt;
+                }
+                // P = 2^(s*log2e - m_ref) in fp32 (one pair in four on the FMA
+                // pipe, the rest on the SFU), packed to bf16 pairs; fp32 row sum.
+                const uint64_t l2e2 = f2(kLog2e, kLog2e);
+                const uint64_t negm2 = f2(-m_ref, -m_ref);
+                uint32_t pk[BN / 2];
+                uint64_t lsum2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+                for (int e = 0; e < BN / 2; ++e) {
+                    const uint64_t x2 = ffma2(f2(s[2 * e], s[2 * e + 1]), l2e2, negm2);
+                    float p0, p1;
+                    if ((e & 3) == 3) {
+                        ex2_poly2(x2, p0, p1);
+                    } else {
+                        float x0, x1;
+                        f2_split(x2, x0, x1);
+                        p0 = ex2_sfu(x0);
+                        p1 = ex2_sfu(x1);
+                    }
+                    lsum2[e & 3] = fadd2(lsum2[e & 3], f2(p0, p1));
+                    pk[e] = pack_bf16(p0, p1);
+                }
+                float lsum0, lsum1;
+                f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
+                l_run = l_run * alpha + (lsum0 + lsum1);
+                // P_i and O_i may be touched once the previous PV MMA is done
+                if (j > 0) {
+                    wait_or_flag(&S.p_free[i], (g - 1) & 1, A.err, kErrWaitMma, failed);
+                    tc_fence_after();
+                    if (__any_sync(0xffffffffu, move)) {
+#pragma unroll
+                        for (int c = 0; c < HD / 32; ++c) {
+                            float o[32];
+                            tmem_ld32(tO + 32 * c, o);
+                            tmem_wait_ld();
+                            uint32_t ob[32];
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(o[e] * alpha);
+                            tmem_st32(tO + 32 * c, ob);
+                        }
                     }
                 }
+                tmem_st32(tP, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+                tmem_st32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.p_full[i]);
             }
-            tmem_st32(tP, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-            tmem_st32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
-            tmem_wait_st();
-            tc_fence_before();
+            // ---- epilogue: out[token][h][:] = O / l (the wait also frees P and
+            // O for the next item's first tile).  O goes through this head's
+            // Q buffer (its last reader, the item's last S MMA, finished
+            // before S was read) so the global stores are coalesced: each
+            // warp stages its own 32 rows, 32 columns at a time, 16-byte
+            // chunk j of row r at chunk j ^ (r & 7) (conflict-free both ways),
+            // then writes 4 rows x 128 B per store instruction. ----
+            wait_or_flag(&S.p_free[i], (g - 1) & 1, A.err, kErrWaitMma, failed);
+            tc_fence_after();
+            const float inv = 1.0f / l_run;
+            float* stg = reinterpret_cast<float*>(S.q[k & 1][i]);   // [128 rows][32 floats]
+            const int qd = warp & 3;
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+                float o[32];
+                tmem_ld32(tO + 32 * c, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int jc = 0; jc < 8; ++jc)
+                    *reinterpret_cast<float4*>(stg + row * 32 + 4 * (jc ^ (row & 7))) =
+                        make_float4(o[4 * jc] * inv, o[4 * jc + 1] * inv, o[4 * jc + 2] * inv, o[4 * jc + 3] * inv);
+                __syncwarp();
+#pragma unroll
+                for (int kq = 0; kq < 8; ++kq) {
+                    const int rr = 32 * qd + 4 * kq + (lane >> 3);
+                    const int jc = lane & 7;
+                    const float4 v = *reinterpret_cast<const float4*>(stg + rr * 32 + 4 * (jc ^ (rr & 7)));
+                    const int tok = q0 + rr;
+                    if (tok < A.n_tokens)
+                        *reinterpret_cast<float4*>(A.out + static_cast<size_t>(tok) * NH * HD + (it.h0 + i) * HD +
+                                                   32 * c + 4 * jc) = v;
+                }
+                __syncwarp();
+            }
+            // the Q buffer is rewritten by a TMA load (async proxy) once q_free completes
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.p_full[i]);
-        }
-        // ---- epilogue: out[token][h][:] = O / l ----
-        wait_or_flag(&S.p_free[i], (n_kv - 1) & 1, A.err, kErrWaitMma, failed);
-        tc_fence_after();
-        const int tok = q0 + row;
-        const float inv = 1.0f / l_run;
-        float* dst = A.out + static_cast<size_t>(tok) * NH * HD + (h0 + i) * HD;
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-            float o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld();
-            if (tok < A.n_tokens) {
-#pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(dst + 32 * c + e) =
-                        make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
-            }
+            if (lane == 0) mbar_arrive(&S.q_free[k & 1]);
         }
     }
     tc_fence_before();
@@ -659,8 +743,11 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     }
     // Programmatic dependent launch: the attention grid may start while the
     // prep grid runs; only its TMA producer waits (griddepcontrol.wait).
+    int n_sm = 0;
+    e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(t.n_qt * (NH / 2));
+    cfg.gridDim = dim3(std::min(t.n_qt * (NH / 2), n_sm));   // persistent: one CTA per SM
     cfg.blockDim = dim3(ATTN_THREADS);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
