@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 prefill and config-4 ragged-decode lines")
-    ap.add_argument("--only", choices=["prefill3", "decode4"], default=None,
+    ap.add_argument("--only", choices=["prefill3", "decode4", "decode1"], default=None,
                     help="run one secondary workload alone (--steps/--warmup apply) and print "
                          "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -203,7 +203,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if args.only:
-        fn = measure_prefill if args.only == "prefill3" else measure_config4
+        fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1}[args.only]
         res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
         print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
                               warmup=max(3, args.warmup))), flush=True)
@@ -336,7 +336,8 @@ def main():
         }
         if world == 1 and not args.no_secondary:
             line["secondary"] = {"prefill_config3": measure_prefill(dev, peaks),
-                                 "decode_config4": measure_config4(dev, peaks)}
+                                 "decode_config4": measure_config4(dev, peaks),
+                                 "decode_config1": measure_config1(dev, peaks)}
         if world == 1 and not args.no_cpu_baseline:
             gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
             line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
@@ -465,6 +466,95 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
             "gpu_launches": n_layers * steps}
+
+
+def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
+    """Config 1: one sequence, 22 layers, cache capacity 512, rows 0..510
+    cached, the new token at pos 511 (L = 512); a step is the 22
+    tle_rope_attention calls of one decode token (forward.cpp:192-208 per
+    layer), 23.07 MB of K+V.  That fits L2, so the warm number is latency-
+    bound; the cold variant rotates `copies` cache copies (184 MB > L2)."""
+    import torch
+    import tle
+    n_layers, n_ctx, pos = 22, 512, 511
+    shape = tle.tinyllama_shape(n_layers)
+    g = torch.Generator(device=dev).manual_seed(11)
+    caches = [(torch.randn((n_layers, n_ctx, KVD), generator=g, device=dev),
+               torch.randn((n_layers, n_ctx, KVD), generator=g, device=dev)) for _ in range(copies)]
+    q = torch.randn(QD, generator=g, device=dev)
+    k = torch.randn(KVD, generator=g, device=dev)
+    v = torch.randn(KVD, generator=g, device=dev)
+    out = torch.zeros(QD, device=dev)
+    ws = tle.attention_workspace(shape, n_ctx)
+
+    def step_on(c):
+        def step(st):
+            kc, vc = caches[c]
+            for l in range(n_layers):
+                tle.rope_attention(out, q, k, v, kc, vc, l, pos, n_ctx, shape, ws, st)
+        return step
+
+    ms_warm = _time_graph(step_on(0), steps, warmup, dev)
+    # cold: one captured graph per cache copy, replayed in rotation
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = []
+    with torch.cuda.stream(side):
+        for c in range(copies):
+            step_on(c)(side)
+    torch.cuda.synchronize(dev)
+    for c in range(copies):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(gr, stream=side):
+                step_on(c)(side)
+        graphs.append(gr)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(copies):
+        graphs[i].replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        graphs[i % copies].replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_cold = e0.elapsed_time(e1) / steps
+    kv_bytes = n_layers * (pos + 1) * ROW_BYTES
+    # the reference's own per-token cost: its rope+attention (oracle/_ref,
+    # src/ops.cpp compiled unmodified) for the 22 layers on one host thread
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    kind = "reference" if oracle.have_reference() else "port"
+    lib = oracle.reference() if kind == "reference" else oracle.port()
+    kc_h, vc_h = caches[0][0].cpu().numpy(), caches[0][1].cpu().numpy()
+    q_h, k_h, v_h = q.cpu().numpy()[None], k.cpu().numpy()[None], v.cpu().numpy()[None]
+    out_h = np.zeros((1, QD), np.float32)
+    ref_times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        for l in range(n_layers):
+            lib.decode_batch([kc_h], [vc_h], [n_ctx], [pos], q_h.copy(), k_h.copy(), v_h, out_h, l,
+                             n_threads=1)
+        ref_times.append(time.perf_counter() - t0)
+    ref_us = statistics.median(ref_times) * 1e6
+    return {"workload": "config1: 1 sequence, 22 layers, L=512 (pos 511, capacity 512); a step is "
+                        "the 22 tle_rope_attention calls of one token (CUDA graph)",
+            "metric": "decode token latency (22 layers)", "unit": "us", "higher_is_better": False,
+            "value": round(ms_warm * 1e3, 2), "value_cold_l2": round(ms_cold * 1e3, 2),
+            "kv_gbs_warm": round(kv_bytes / (ms_warm / 1e3) / 1e9, 1),
+            "kv_gbs_cold": round(kv_bytes / (ms_cold / 1e3) / 1e9, 1),
+            "cold_l2": "%d cache copies rotated (%.0f MB > 126 MB L2)" % (copies, copies * 2 * n_layers * n_ctx * KVD * 4 / 1e6),
+            "roofline": {"bound": "latency (23 MB of K+V fits L2)",
+                         "achieved_cold_gbs": round(kv_bytes / (ms_cold / 1e3) / 1e9, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac_cold": round(kv_bytes / (ms_cold / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "cpu_reference": {"kind": kind, "cores": 1, "us_per_token": round(ref_us, 1),
+                              "sample": "22 layers of rope+attention at L=512, one host thread, "
+                                        "median of 3 tokens"},
+            "gpu_launches": 2 * n_layers * steps}
 
 
 def load_peaks():

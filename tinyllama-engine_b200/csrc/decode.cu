@@ -344,6 +344,9 @@ __device__ __forceinline__ bool cta_sync(DecodeSmem& S, uint32_t& phase, int lan
 __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ DecodeArgs A) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     DecodeSmem& S = *reinterpret_cast<DecodeSmem*>(smem_raw);
+    // Single-sequence mode: merge_kernel is launched as a programmatic
+    // dependent and may be scheduled now (it waits for this grid's results).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
@@ -641,42 +644,62 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     }
 }
 
-// Single-sequence mode: combines the split-K partials of the CTAs.
+// Single-sequence mode: combines the split-K partials of the CTAs.  Thread
+// t owns query head t / 8, dims 8 (t % 8) .. +8.  The partials are folded in
+// chunks of 8 with every load of a chunk issued before any is used (one L2
+// round trip per chunk), with an online rescale between chunks.  Launched as
+// a programmatic dependent of decode_kernel: it may start while the decode
+// grid runs and waits (griddepcontrol.wait) for its partials.
+constexpr int kMergeChunk = 8;
 __global__ void __launch_bounds__(256) merge_kernel(const __grid_constant__ DecodeArgs A) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int s = blockIdx.x;
-    int lo = 0, hi = A.n_ctas - 1;
-    if (A.seq_ctas) {
-        const SeqCtas sc = A.seq_ctas[s];
-        lo = sc.lo;
-        hi = sc.hi;
-    }
+    const int lo = 0, hi = A.n_ctas - 1;
     if (lo >= hi) return;
     const int t = threadIdx.x;
     const int h = t >> 3;
     const int d0 = (t & 7) * 8;
-    float mstar = -INFINITY;
-    for (int c = lo; c <= hi; ++c)
-        mstar = fmaxf(mstar, A.partials[static_cast<size_t>(s + c) * kPartialFloats + NH * HD + h]);
-    float lsum = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = 0.f;
-    for (int c = lo; c <= hi; ++c) {
-        const float* P = A.partials + static_cast<size_t>(s + c) * kPartialFloats;
-        const float mc = P[NH * HD + h];
-        if (mc == -INFINITY) continue;
-        const float f = expf(mc - mstar);
-        lsum += P[NH * HD + NH + h] * f;
-        const float4 a0 = *reinterpret_cast<const float4*>(P + h * HD + d0);
-        const float4 a1 = *reinterpret_cast<const float4*>(P + h * HD + d0 + 4);
-        o[0] = fmaf(a0.x, f, o[0]); o[1] = fmaf(a0.y, f, o[1]);
-        o[2] = fmaf(a0.z, f, o[2]); o[3] = fmaf(a0.w, f, o[3]);
-        o[4] = fmaf(a1.x, f, o[4]); o[5] = fmaf(a1.y, f, o[5]);
-        o[6] = fmaf(a1.z, f, o[6]); o[7] = fmaf(a1.w, f, o[7]);
+    for (int c0 = lo; c0 <= hi; c0 += kMergeChunk) {
+        float mc[kMergeChunk], lc[kMergeChunk];
+        float4 a0[kMergeChunk], a1[kMergeChunk];
+#pragma unroll
+        for (int u = 0; u < kMergeChunk; ++u) {
+            mc[u] = -INFINITY;
+            lc[u] = 0.f;
+            a0[u] = a1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c0 + u <= hi) {
+                const float* P = A.partials + static_cast<size_t>(s + c0 + u) * kPartialFloats;
+                mc[u] = __ldcg(P + NH * HD + h);
+                lc[u] = __ldcg(P + NH * HD + NH + h);
+                a0[u] = __ldcg(reinterpret_cast<const float4*>(P + h * HD + d0));
+                a1[u] = __ldcg(reinterpret_cast<const float4*>(P + h * HD + d0 + 4));
+            }
+        }
+        float mn = m_run;
+#pragma unroll
+        for (int u = 0; u < kMergeChunk; ++u) mn = fmaxf(mn, mc[u]);
+        const float fr = (m_run == -INFINITY) ? 0.f : expf(m_run - mn);
+        l_run *= fr;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] *= fr;
+#pragma unroll
+        for (int u = 0; u < kMergeChunk; ++u) {
+            const float f = (mc[u] == -INFINITY) ? 0.f : expf(mc[u] - mn);
+            l_run = fmaf(lc[u], f, l_run);
+            o[0] = fmaf(a0[u].x, f, o[0]); o[1] = fmaf(a0[u].y, f, o[1]);
+            o[2] = fmaf(a0[u].z, f, o[2]); o[3] = fmaf(a0[u].w, f, o[3]);
+            o[4] = fmaf(a1[u].x, f, o[4]); o[5] = fmaf(a1[u].y, f, o[5]);
+            o[6] = fmaf(a1[u].z, f, o[6]); o[7] = fmaf(a1[u].w, f, o[7]);
+        }
+        m_run = mn;
     }
     float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + h * HD + d0);
-    dst[0] = make_float4(o[0] / lsum, o[1] / lsum, o[2] / lsum, o[3] / lsum);
-    dst[1] = make_float4(o[4] / lsum, o[5] / lsum, o[6] / lsum, o[7] / lsum);
+    dst[0] = make_float4(o[0] / l_run, o[1] / l_run, o[2] / l_run, o[3] / l_run);
+    dst[1] = make_float4(o[4] / l_run, o[5] / l_run, o[6] / l_run, o[7] / l_run);
 }
 
 // rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
@@ -711,8 +734,16 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (a.n_ctas > 1 && a.seqs == nullptr) {   // batch mode merges inside decode_kernel
-        merge_kernel<<<a.n_seqs, 256, 0, stream>>>(a);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(a.n_seqs);
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, merge_kernel, a);
     }
     return e;
 }
