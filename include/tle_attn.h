@@ -170,6 +170,14 @@ int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* 
  * when a bounded wait expires; 0 = no error.  Synchronises the device. */
 int tle_device_error(int clear, uint32_t* code);
 
+/* Exercises the failure path of the kernels' bounded waits without a fault:
+ * launches one block that waits, through the same bounded mbarrier wait the
+ * kernels use, on a barrier nothing ever arrives at, with a limit of
+ * limit_us microseconds (1 .. 1000000).  When the limit expires the block
+ * records code 0x1ff in the device error word and returns, leaving the
+ * context usable; read it with tle_device_error.  No reference counterpart. */
+int tle_selftest_wait_timeout(uint32_t limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -281,3 +281,18 @@ def test_batch_replay_without_upload(cuda):
     off = 32 + 24 * n + 8 * (batch.n_ctas + 1) + 8 * n
     arrivals = batch._desc_dev[off:off + 4 * n].cpu().numpy()
     assert not arrivals.any(), arrivals
+
+
+def test_bounded_wait_expiry_is_reported_and_context_survives(cuda):
+    """The kernels' bounded mbarrier wait, planted on a barrier nothing
+    arrives at (tle_selftest_wait_timeout, 20 ms limit), records 0x1ff in
+    the device error word and returns; the context then runs a decode that
+    matches the oracle."""
+    import tle
+    assert tle.device_error() == 0
+    tle.selftest_wait_timeout(20000)
+    assert tle.device_error() == 0x1FF
+    assert tle.device_error() == 0            # cleared by the read above
+    err, _ = run_batch_case([300, 40], n_layers=1, layer=0, max_ctas=4, seed=99)
+    assert err <= ATOL, err
+    assert tle.device_error() == 0

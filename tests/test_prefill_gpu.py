@@ -136,3 +136,52 @@ def test_prefill_rejects_bad_arguments(cuda):
         tle.prefill(dev(np.zeros((10, QD))), dev(np.zeros((10, QD))), dev(np.zeros((10, KVD))),
                     dev(np.zeros((10, KVD))), kc, vc, 0, 8, 16, tle.tinyllama_shape(1))
     assert e.value.code == tle.TLE_ERR_INVALID
+
+
+def test_prefill_long_with_prefix_many_items_per_cta(cuda):
+    """S = 3000 new tokens after a 1000-row cached prefix: 24 query tiles x 16
+    head pairs = 384 work items, so every persistent CTA walks two or three
+    items (the Q double buffer is reused) with ragged causal tile counts.
+    Checked against a torch fp32 causal GQA attention of the same rows."""
+    import torch
+    import tle
+    S, pos0, n_ctx = 3000, 1000, 4096
+    g = torch.Generator(device="cuda").manual_seed(17)
+    kc = torch.zeros((1, n_ctx, KVD), device="cuda")
+    vc = torch.zeros_like(kc)
+    kc[0, :pos0] = torch.randn((pos0, KVD), generator=g, device="cuda")
+    vc[0, :pos0] = torch.randn((pos0, KVD), generator=g, device="cuda")
+    prefix_k, prefix_v = kc[0, :pos0].clone(), vc[0, :pos0].clone()
+    q = torch.randn((S, QD), generator=g, device="cuda")
+    k = torch.randn((S, KVD), generator=g, device="cuda")
+    v = torch.randn((S, KVD), generator=g, device="cuda")
+    out = torch.full((S, QD), float("nan"), device="cuda")
+    tle.prefill(out, q, k, v, kc, vc, 0, pos0, n_ctx, tle.tinyllama_shape(1))
+    torch.cuda.synchronize()
+    assert tle.device_error() == 0
+    half = HD // 2
+    inv = torch.tensor([1.0 / np.power(np.float32(10000.0), np.float32(2 * i) / np.float32(HD))
+                        for i in range(half)], dtype=torch.float32, device="cuda")
+    ang = torch.arange(pos0, pos0 + S, device="cuda", dtype=torch.float32)[:, None] * inv[None, :]
+    cs, sn = torch.cos(ang), torch.sin(ang)
+
+    def rot(x, nh):
+        x = x.view(S, nh, half, 2)
+        x0, x1 = x[..., 0], x[..., 1]
+        return torch.stack([x0 * cs[:, None] - x1 * sn[:, None],
+                            x0 * sn[:, None] + x1 * cs[:, None]], -1).view(S, nh, HD)
+
+    R = pos0 + S
+    keys = torch.cat([prefix_k.view(pos0, NKV, HD), rot(k, NKV)], 0)       # [R][4][64]
+    vals = torch.cat([prefix_v, v], 0).view(R, NKV, HD)
+    qr = rot(q, NH)
+    scores = torch.einsum("qhd,khd->hqk", qr, keys.repeat_interleave(NH // NKV, 1)) / 8.0
+    allowed = torch.arange(R, device="cuda")[None, :] <= (pos0 + torch.arange(S, device="cuda"))[:, None]
+    scores.masked_fill_(~allowed, float("-inf"))
+    ref = torch.einsum("hqk,khd->qhd", torch.softmax(scores, -1),
+                       vals.repeat_interleave(NH // NKV, 1)).reshape(S, QD)
+    err = float((out - ref).abs().max())
+    assert err <= ATOL, err
+    # prefix rows untouched, new v rows appended as given
+    assert torch.equal(kc[0, :pos0], prefix_k) and torch.equal(vc[0, :pos0], prefix_v)
+    assert torch.equal(vc[0, pos0:R], v)

@@ -375,6 +375,18 @@ int tle_device_error(int clear, uint32_t* code) {
     return ok();
 }
 
+int tle_selftest_wait_timeout(uint32_t limit_us, void* stream) {
+    if (limit_us < 1 || limit_us > 1000000)
+        return set_error(TLE_ERR_INVALID, "limit_us %u outside [1, 1000000]", limit_us);
+    uint32_t* err = nullptr;
+    cudaError_t e = tle::error_word(&err);
+    if (e != cudaSuccess) return cuda_error(e, "error word");
+    e = tle::launch_selftest_wait(err, static_cast<uint64_t>(limit_us) * 1000u,
+                                  static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "selftest launch");
+    return ok();
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

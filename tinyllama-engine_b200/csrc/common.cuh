@@ -17,6 +17,7 @@ enum : uint32_t {
     kErrWaitEmpty = 0x102,  // producer gave up waiting for a stage to drain
     kErrWaitMma = 0x103,    // waiter gave up on a tensor-core commit
     kErrDrain = 0x104,      // exit-time wait for in-flight copies gave up
+    kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 
 // A bounded wait gives up after this long (nanoseconds of %globaltimer).
@@ -98,16 +99,17 @@ TLE_DEV bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
 // is test_wait: on an already-completed phase it costs ~10 cycles where
 // try_wait costs ~110 (measured on B200); try_wait, which may park the warp,
 // is only used once the phase is known to be pending.
-TLE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+TLE_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+        if (globaltimer() - t0 > limit_ns) return false;
     }
 }
+TLE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) { return mbar_wait_for(bar, parity, kWaitTimeoutNs); }
 
 // L2 policy for data read exactly once (the KV stream).
 TLE_DEV uint64_t l2_evict_first_policy() {

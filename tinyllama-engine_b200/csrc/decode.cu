@@ -719,6 +719,20 @@ __global__ void rope_kernel(const __grid_constant__ RopeArgs A) {
 
 }  // namespace
 
+// Failure-path self-test: the planted barrier (count 1) never receives an
+// arrival, so every thread's bounded wait expires after limit_ns; thread 0
+// records the code.  Nothing asynchronous is in flight when the block exits.
+__global__ void __launch_bounds__(32) selftest_wait_kernel(uint32_t* err, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    const bool ok = mbar_wait_for(&bar, 0, limit_ns);
+    if (!__all_sync(0xffffffffu, ok) && threadIdx.x == 0) record_error(err, kErrSelfTest);
+}
+
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     static int configured_device = -1;
     int dev = 0;
@@ -780,6 +794,11 @@ cudaError_t read_device_error(int clear, uint32_t* code) {
         e = cudaMemcpyToSymbol(g_tle_error, &zero, sizeof(uint32_t));
     }
     return e;
+}
+
+cudaError_t launch_selftest_wait(uint32_t* err, uint64_t limit_ns, cudaStream_t stream) {
+    selftest_wait_kernel<<<1, 32, 0, stream>>>(err, limit_ns);
+    return cudaGetLastError();
 }
 
 }  // namespace tle

@@ -113,6 +113,9 @@ size_t prefill_workspace_bytes(int n_tokens, int pos0);
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 
 cudaError_t read_device_error(int clear, uint32_t* code);
+// One block waiting (bounded by limit_ns) on a barrier nothing arrives at;
+// records kErrSelfTest in err when the limit expires.
+cudaError_t launch_selftest_wait(uint32_t* err, uint64_t limit_ns, cudaStream_t stream);
 // Device address of the error word on the current device.
 cudaError_t error_word(uint32_t** word);
 

@@ -737,6 +737,13 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (configured_device != dev) {
+        // setmaxnreg.inc waits until the block's launch registers cover the
+        // split; refuse to launch (instead of hanging) if the compiled kernel
+        // was given fewer registers than the split assumes.
+        cudaFuncAttributes fa{};
+        e = cudaFuncGetAttributes(&fa, prefill_attn_kernel);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs < kLaunchRegs) return cudaErrorInvalidConfiguration;
         e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured_device = dev;

@@ -32,6 +32,7 @@ EXPORTED = (
     "tle_attention", "tle_rope_attention", "tle_decode_desc_bytes", "tle_decode_desc",
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
+    "tle_selftest_wait_timeout",
 )
 
 
@@ -88,6 +89,7 @@ def lib() -> ctypes.CDLL:
         L.tle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, P(Shape), vp, sz, vp]
         L.tle_partition_lpt.argtypes = [P(ctypes.c_int32), i, i, P(ctypes.c_int32)]
         L.tle_device_error.argtypes = [i, P(ctypes.c_uint32)]
+        L.tle_selftest_wait_timeout.argtypes = [ctypes.c_uint32, ctypes.c_void_p]
         L.tle_decode_batch_noalloc.argtypes = [P(Shape), P(Seq), i, vp, vp, vp, vp, i, i, vp]
         _lib = L
     return _lib
@@ -288,3 +290,9 @@ def device_error(clear: bool = True) -> int:
     code = ctypes.c_uint32(0)
     _check(lib().tle_device_error(1 if clear else 0, ctypes.byref(code)))
     return code.value
+
+
+def selftest_wait_timeout(limit_us: int = 20000, stream=None) -> None:
+    """Launches a block whose bounded wait is planted to expire after
+    limit_us (tle_selftest_wait_timeout); read the result with device_error."""
+    _check(lib().tle_selftest_wait_timeout(int(limit_us), _stream(stream)))
