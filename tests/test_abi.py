@@ -65,7 +65,7 @@ def build_desc(positions, n_ctx, max_ctas):
     return rc, buf, n_ctas.value
 
 
-SEG_COST = 64  # rows of streaming time charged per sequence segment by the planner
+SEG_COST = 128  # rows of streaming time charged per sequence segment by the planner
 
 
 @pytest.mark.parametrize("seed", [0, 1, 2, 3])

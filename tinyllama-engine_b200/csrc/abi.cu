@@ -80,12 +80,13 @@ int choose_ctas(int64_t rows, int max_ctas) {
 
 // Splits a batch over G CTAs in "cost" units: every sequence costs its rows
 // plus kSegCostRows (the per-segment setup of the decode kernel: q rotation,
-// warp merge, output write, about three microseconds of streaming time), so a
+// warp merge, output write: about three microseconds of streaming time; 128
+// measured best on a 64-sequence ragged batch against 32 .. 256), so a
 // CTA that holds several short segments gets fewer rows.  CTA boundaries are
 // cost positions mapped to (sequence, row); a boundary inside a sequence's
 // overhead lands on its first row.  seq_ctas[t] = first and last CTA owning a
 // row of t.  No allocation (shared by the no-allocation entry point).
-constexpr int64_t kSegCostRows = 64;
+constexpr int64_t kSegCostRows = 128;
 
 void plan_ctas(const tle_seq_t* seqs, int n, int G, tle::CtaStart* cs, tle::SeqCtas* sc) {
     int64_t T = 0;

@@ -85,7 +85,7 @@ struct PrepArgs {
 constexpr int kPrepThreads = 256;
 static_assert(kPrepThreads == NKV * HD, "the V^T writer maps one thread to one (kv head, d) row");
 constexpr int kPrepTokensPerBlock = kPrepThreads / 32;  // one token per warp
-constexpr int kVtRows = 32;                              // rows per transpose block
+constexpr int kVtRows = 8;                               // rows per transpose block
 constexpr int kVtPitch = NKV * HD + 8;                   // bf16 pitch of the transpose tile
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
