@@ -557,20 +557,28 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
                 const uint64_t negm2 = f2(-m_ref, -m_ref);
                 uint32_t pk[BN / 2];
                 uint64_t lsum2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+                // pass 1: all exponent arguments (in place of the scores)
+#pragma unroll
+                for (int e = 0; e < BN / 2; ++e)
+                    f2_split(ffma2(f2(s[2 * e], s[2 * e + 1]), l2e2, negm2), s[2 * e], s[2 * e + 1]);
+                // pass 2: exponentials, SFU and FMA-pipe pairs interleaved
 #pragma unroll
                 for (int e = 0; e < BN / 2; ++e) {
-                    const uint64_t x2 = ffma2(f2(s[2 * e], s[2 * e + 1]), l2e2, negm2);
                     float p0, p1;
                     if ((e & 3) == 3) {
-                        ex2_poly2(x2, p0, p1);
+                        ex2_poly2(f2(s[2 * e], s[2 * e + 1]), p0, p1);
                     } else {
-                        float x0, x1;
-                        f2_split(x2, x0, x1);
-                        p0 = ex2_sfu(x0);
-                        p1 = ex2_sfu(x1);
+                        p0 = ex2_sfu(s[2 * e]);
+                        p1 = ex2_sfu(s[2 * e + 1]);
                     }
-                    lsum2[e & 3] = fadd2(lsum2[e & 3], f2(p0, p1));
-                    pk[e] = pack_bf16(p0, p1);
+                    s[2 * e] = p0;
+                    s[2 * e + 1] = p1;
+                }
+                // pass 3: row sum and bf16 packing
+#pragma unroll
+                for (int e = 0; e < BN / 2; ++e) {
+                    lsum2[e & 3] = fadd2(lsum2[e & 3], f2(s[2 * e], s[2 * e + 1]));
+                    pk[e] = pack_bf16(s[2 * e], s[2 * e + 1]);
                 }
                 float lsum0, lsum1;
                 f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
