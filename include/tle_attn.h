@@ -80,6 +80,25 @@ int tle_attention(float* out, const float* q, const float* k, const float* v, fl
                   float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Context split of one long sequence over several GPUs (no reference
+ * counterpart; the reference is single-process).  tle_attention plus the
+ * log-sum-exp of every head's scaled scores, lse[n_head] (device, 16-byte
+ * aligned): a GPU holding rows [r0, r1) of the sequence calls it on its
+ * shard (local rows, q and k rotated for the global position), and
+ * tle_merge_lse combines the shards' (out, lse) into the attention over all
+ * rows.  A shard that does not hold the new token passes its own last
+ * cached row as k, v with pos = its last local row (the append rewrites the
+ * row with itself). */
+int tle_attention_lse(float* out, float* lse, const float* q, const float* k, const float* v,
+                      float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                      const tle_shape_t* shape, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* out[32*64] = sum_r exp(lses[r][h] - LSE_h) parts[r][h][:], LSE_h =
+ * log sum_r exp(lses[r][h]); parts [n_parts][32*64], lses [n_parts][32],
+ * all device pointers.  TinyLlama geometry (32 heads x 64). */
+int tle_merge_lse(float* out, const float* parts, const float* lses, int n_parts, void* stream);
+
 /* forward.cpp:192-208 in one launch: rope(q, k, pos) then attention().
  * q and k are the UNROTATED projections and are left unmodified; the rotated
  * k is what lands in the cache, as in the reference. */

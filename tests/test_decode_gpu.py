@@ -296,3 +296,55 @@ def test_bounded_wait_expiry_is_reported_and_context_survives(cuda):
     err, _ = run_batch_case([300, 40], n_layers=1, layer=0, max_ctas=4, seed=99)
     assert err <= ATOL, err
     assert tle.device_error() == 0
+
+
+@pytest.mark.parametrize("n_rows,world", [(10000, 3), (700, 2), (4096, 8)])
+def test_context_split_matches_oracle(cuda, n_rows, world):
+    """One sequence whose rows are split over `world` shards (shard.context_plan),
+    each decoded with tle_attention_lse on its own cache, the (out, lse) pairs
+    merged with tle_merge_lse: equals the oracle's rope + attention over all
+    rows, and the shard holding the new row appends it as the oracle does."""
+    import torch
+    import tle
+    import shard
+    rng = np.random.default_rng(n_rows + world)
+    n_layers, layer = 2, 1
+    pos = n_rows - 1
+    kc = rng.standard_normal((n_layers, n_rows + 3, KVD), dtype=np.float32)
+    vc = rng.standard_normal((n_layers, n_rows + 3, KVD), dtype=np.float32)
+    q = rng.standard_normal(QD, dtype=np.float32)
+    k = rng.standard_normal(KVD, dtype=np.float32)
+    v = rng.standard_normal(KVD, dtype=np.float32)
+    plan = shard.context_plan(n_rows, world)
+    shape = tle.tinyllama_shape(n_layers)
+    qd, kd = dev(q), dev(k)
+    tle.rope(qd, kd, pos)                             # global position, in place
+    parts = torch.empty((world, QD), device="cuda")
+    lses = torch.empty((world, 32), device="cuda")
+    shards = []
+    for r, (r0, r1) in enumerate(plan.bounds):
+        cap = r1 - r0 + 1
+        skc = dev(np.ascontiguousarray(kc[:, r0:r0 + cap]))
+        svc = dev(np.ascontiguousarray(vc[:, r0:r0 + cap]))
+        shards.append((skc, svc))
+        if r == world - 1:
+            tle.attention_lse(parts[r], lses[r], qd, kd, dev(v), skc, svc, layer, pos - r0, cap, shape)
+        else:
+            row = r1 - r0 - 1
+            tle.attention_lse(parts[r], lses[r], qd, skc[layer, row], svc[layer, row], skc, svc,
+                              layer, row, cap, shape)
+    out = torch.empty(QD, device="cuda")
+    tle.merge_lse(out, parts, lses)
+    want = np.zeros(QD, np.float32)
+    P = oracle.port()
+    q2, k2 = q.copy(), k.copy()
+    P.rope(q2, k2, pos)
+    P.attention(want, q2, k2, v, kc, vc, layer, pos, n_rows + 3)
+    assert maxabs(host(out), want) <= ATOL
+    r0 = plan.bounds[-1][0]
+    assert maxabs(host(shards[-1][0])[layer, pos - r0], kc[layer, pos]) <= ROT_ATOL
+    assert np.array_equal(host(shards[-1][1])[layer, pos - r0], v)
+    for r in range(world - 1):                         # earlier shards unchanged
+        a, b = plan.bounds[r]
+        assert np.array_equal(host(shards[r][0])[layer, :b - a], kc[layer, a:b])
+    assert tle.device_error() == 0

@@ -117,3 +117,15 @@ def test_plan_gather_rows_are_a_permutation():
         for r in range(world):
             for i, s in enumerate(p.local[r]):
                 assert p.gather_row[s] == r * p.max_local + i
+
+
+def test_context_plan_covers_rows_and_last_rank_holds_newest():
+    import shard
+    for n, w in [(10, 3), (8, 8), (32768, 8), (1000003, 7)]:
+        p = shard.context_plan(n, w)
+        assert p.bounds[0][0] == 0 and p.bounds[-1][1] == n
+        assert all(p.bounds[r][1] == p.bounds[r + 1][0] for r in range(w - 1))
+        sizes = [b - a for a, b in p.bounds]
+        assert max(sizes) - min(sizes) <= 1 and min(sizes) >= 1
+    with pytest.raises(ValueError):
+        shard.context_plan(3, 4)

@@ -129,7 +129,8 @@ size_t partial_bytes(int n_slots) {
 
 int single_decode(float* out, const float* q, const float* k, const float* v, float* key_cache,
                   float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
-                  void* workspace, size_t workspace_bytes, void* stream, int rotate) {
+                  void* workspace, size_t workspace_bytes, void* stream, int rotate,
+                  float* lse = nullptr) {
     if (int rc = check_shape(shape)) return rc;
     if (!out || !q || !k || !v || !key_cache || !value_cache)
         return set_error(TLE_ERR_INVALID, "null buffer pointer");
@@ -163,6 +164,7 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
     a.v = v;
     a.out = out;
     a.partials = static_cast<float*>(workspace);
+    a.lse = lse;
     a.layer = layer;
     a.rotate = rotate;
     fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
@@ -212,6 +214,24 @@ int tle_attention(float* out, const float* q, const float* k, const float* v, fl
                   void* workspace, size_t workspace_bytes, void* stream) {
     return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
                          workspace_bytes, stream, 0);
+}
+
+int tle_attention_lse(float* out, float* lse, const float* q, const float* k, const float* v,
+                      float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                      const tle_shape_t* shape, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    if (!lse || !aligned16(lse)) return set_error(TLE_ERR_INVALID, "lse must be a 16-byte aligned buffer");
+    return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
+                         workspace_bytes, stream, 0, lse);
+}
+
+int tle_merge_lse(float* out, const float* parts, const float* lses, int n_parts, void* stream) {
+    if (!out || !parts || !lses) return set_error(TLE_ERR_INVALID, "null buffer pointer");
+    if (!aligned16(out) || !aligned16(parts)) return set_error(TLE_ERR_INVALID, "buffers must be 16-byte aligned");
+    if (n_parts < 1) return set_error(TLE_ERR_INVALID, "n_parts %d < 1", n_parts);
+    cudaError_t e = tle::launch_merge_lse(out, parts, lses, n_parts, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "merge launch");
+    return ok();
 }
 
 int tle_rope_attention(float* out, const float* q, const float* k, const float* v,

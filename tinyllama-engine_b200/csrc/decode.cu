@@ -617,6 +617,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                 const float4 v = *reinterpret_cast<const float4*>(OA + hh * HD + 4 * (((lane & 15) + hh) & 15));
                 reinterpret_cast<float4*>(dst)[32 * i + lane] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
             }
+            if (whole && A.lse) A.lse[h] = m_run + logf(l_run);   // single mode only
             if (!whole) {
                 dst[NH * HD + h] = m_run;
                 dst[NH * HD + NH + h] = l_run;
@@ -700,6 +701,36 @@ __global__ void __launch_bounds__(256) merge_kernel(const __grid_constant__ Deco
     float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + h * HD + d0);
     dst[0] = make_float4(o[0] / l_run, o[1] / l_run, o[2] / l_run, o[3] / l_run);
     dst[1] = make_float4(o[4] / l_run, o[5] / l_run, o[6] / l_run, o[7] / l_run);
+    if (A.lse && (t & 7) == 0) A.lse[h] = m_run + logf(l_run);
+}
+
+// Context-split combine: thread t owns head t / 8, dims 8 (t % 8) .. +8;
+// all parts' loads of a head are independent (one round trip per 8 parts).
+__global__ void __launch_bounds__(256) merge_lse_kernel(float* out, const float* parts, const float* lses,
+                                                        int n_parts) {
+    const int t = threadIdx.x;
+    const int h = t >> 3;
+    const int d0 = (t & 7) * 8;
+    float mx = -INFINITY;
+    for (int r = 0; r < n_parts; ++r) mx = fmaxf(mx, lses[static_cast<size_t>(r) * NH + h]);
+    float wsum = 0.f;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int r = 0; r < n_parts; ++r) {
+        const float lr = lses[static_cast<size_t>(r) * NH + h];
+        const float w = (lr == -INFINITY) ? 0.f : expf(lr - mx);
+        wsum += w;
+        const float4* src = reinterpret_cast<const float4*>(parts + static_cast<size_t>(r) * NH * HD + h * HD + d0);
+        const float4 a0 = src[0], a1 = src[1];
+        o[0] = fmaf(a0.x, w, o[0]); o[1] = fmaf(a0.y, w, o[1]);
+        o[2] = fmaf(a0.z, w, o[2]); o[3] = fmaf(a0.w, w, o[3]);
+        o[4] = fmaf(a1.x, w, o[4]); o[5] = fmaf(a1.y, w, o[5]);
+        o[6] = fmaf(a1.z, w, o[6]); o[7] = fmaf(a1.w, w, o[7]);
+    }
+    float4* dst = reinterpret_cast<float4*>(out + h * HD + d0);
+    dst[0] = make_float4(o[0] / wsum, o[1] / wsum, o[2] / wsum, o[3] / wsum);
+    dst[1] = make_float4(o[4] / wsum, o[5] / wsum, o[6] / wsum, o[7] / wsum);
 }
 
 // rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
@@ -798,6 +829,12 @@ cudaError_t read_device_error(int clear, uint32_t* code) {
 
 cudaError_t launch_selftest_wait(uint32_t* err, uint64_t limit_ns, cudaStream_t stream) {
     selftest_wait_kernel<<<1, 32, 0, stream>>>(err, limit_ns);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_lse(float* out, const float* parts, const float* lses, int n_parts,
+                             cudaStream_t stream) {
+    merge_lse_kernel<<<1, 256, 0, stream>>>(out, parts, lses, n_parts);
     return cudaGetLastError();
 }
 

@@ -75,6 +75,7 @@ struct DecodeArgs {
     const float* v;              // [n_seqs][4*64]
     float* out;                  // [n_seqs][32*64]
     float* partials;             // [n_ctas + n_seqs][kPartialFloats]
+    float* lse;                  // single mode, optional: [32] log-sum-exp of each head's scores
     int layer;
     int rotate;
     uint32_t* err;               // device error word
@@ -82,6 +83,11 @@ struct DecodeArgs {
 };
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
+// out[32*64] = sum_r w_r parts[r] with w_r = exp(lses[r][h] - LSE_h),
+// LSE_h = log sum_r exp(lses[r][h]): the attention over the union of the
+// parts' key sets, each part normalised over its own keys.
+cudaError_t launch_merge_lse(float* out, const float* parts, const float* lses, int n_parts,
+                             cudaStream_t stream);
 
 struct RopeArgs {
     float* q;

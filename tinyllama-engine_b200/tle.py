@@ -32,7 +32,7 @@ EXPORTED = (
     "tle_attention", "tle_rope_attention", "tle_decode_desc_bytes", "tle_decode_desc",
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
-    "tle_selftest_wait_timeout",
+    "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
 )
 
 
@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
         L.tle_partition_lpt.argtypes = [P(ctypes.c_int32), i, i, P(ctypes.c_int32)]
         L.tle_device_error.argtypes = [i, P(ctypes.c_uint32)]
         L.tle_selftest_wait_timeout.argtypes = [ctypes.c_uint32, ctypes.c_void_p]
+        L.tle_attention_lse.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), vp, sz, vp]
+        L.tle_merge_lse.argtypes = [vp, vp, vp, i, vp]
         L.tle_decode_batch_noalloc.argtypes = [P(Shape), P(Seq), i, vp, vp, vp, vp, i, i, vp]
         _lib = L
     return _lib
@@ -165,6 +167,29 @@ def rope_attention(out, q, k, v, key_cache, value_cache, layer: int, pos: int, n
     shape = shape or tinyllama_shape()
     _single(lib().tle_rope_attention, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx,
             shape, workspace, stream)
+
+
+def attention_lse(out, lse, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx: int,
+                  shape: Optional[Shape] = None, workspace=None, stream=None) -> None:
+    """attention() plus each head's score log-sum-exp lse[32] (context split
+    of one sequence over GPUs; see tle_attention_lse).  q, k already rotated."""
+    shape = shape or tinyllama_shape()
+    _want(lse, 32, "lse")
+    _want(out, 2048, "out"); _want(q, 2048, "q"); _want(k, 256, "k"); _want(v, 256, "v")
+    _want(key_cache, (layer + 1) * n_ctx * 256, "key_cache")
+    _want(value_cache, (layer + 1) * n_ctx * 256, "value_cache")
+    if workspace is None:
+        workspace = attention_workspace(shape, n_ctx)
+    _check(lib().tle_attention_lse(_ptr(out), _ptr(lse), _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache),
+                                   _ptr(value_cache), layer, pos, n_ctx, ctypes.byref(shape),
+                                   _ptr(workspace), workspace.numel() * 4, _stream(stream)))
+
+
+def merge_lse(out, parts, lses, stream=None) -> None:
+    """out[2048] from parts[n][2048] and lses[n][32] (tle_merge_lse)."""
+    n = int(parts.shape[0])
+    _want(out, 2048, "out"); _want(parts, n * 2048, "parts"); _want(lses, n * 32, "lses")
+    _check(lib().tle_merge_lse(_ptr(out), _ptr(parts), _ptr(lses), n, _stream(stream)))
 
 
 # ----------------------------------------------------------- batched decode
