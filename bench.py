@@ -54,7 +54,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 prefill and config-4 ragged-decode lines")
-    ap.add_argument("--only", choices=["prefill3", "decode4", "decode1"], default=None,
+    ap.add_argument("--ctx-rows", type=int, default=4 * 1024 * 1024,
+                    help="rows of the single sequence for --only ctxsplit")
+    ap.add_argument("--only", choices=["prefill3", "decode4", "decode1", "ctxsplit"], default=None,
                     help="run one secondary workload alone (--steps/--warmup apply) and print "
                          "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -202,6 +204,9 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.only == "ctxsplit":
+        measure_ctxsplit(args, dev, rank, world, local)
+        return
     if args.only:
         fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1}[args.only]
         res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
@@ -591,6 +596,75 @@ def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
                               "sample": "22 layers of rope+attention at L=512, one host thread, "
                                         "median of 3 tokens"},
             "gpu_launches": 2 * n_layers * steps}
+
+
+def measure_ctxsplit(args, dev, rank, world, local):
+    """One sequence of --ctx-rows rows split by rows over the ranks
+    (shard.ContextSplitDecode): a step is rope of the new q/k at the global
+    position, each rank's tle_attention_lse over its shard, the NCCL
+    all-gather of the (out, lse) pairs and tle_merge_lse.  Prints one JSON
+    line (rank 0); time is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import tle
+    import shard
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    L = args.ctx_rows
+    pos = L - 1
+    plan = shard.context_plan(L, world)
+    n_loc = plan.local_rows(rank)
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    kc = torch.randn((1, n_loc + 1, KVD), generator=g, device=dev)
+    vc = torch.randn((1, n_loc + 1, KVD), generator=g, device=dev)
+    g0 = torch.Generator(device=dev).manual_seed(7)
+    q = torch.randn(QD, generator=g0, device=dev)
+    k = torch.randn(KVD, generator=g0, device=dev)
+    v = torch.randn(KVD, generator=g0, device=dev)
+    qw, kw = q.clone(), k.clone()
+    shape = tle.tinyllama_shape(1)
+    cs = shard.ContextSplitDecode(plan, rank, kc, vc, n_loc + 1, shape, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        qw.copy_(q)
+        kw.copy_(k)
+        tle.rope(qw, kw, pos)
+        return cs.step(qw, kw, v, 0, pos)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    if rank == 0:
+        peaks = load_peaks()
+        gbs = L * ROW_BYTES / (ms / 1e3) / 1e9
+        print(json.dumps({"metric": "ctx-split decode KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+                          "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+                          "dtype": "f32", "data": "synthetic N(0,1) fp32, seeded",
+                          "config": {"workload": "1 sequence x %d rows split by rows over %d GPU(s), "
+                                                 "1 layer per step (rope + tle_attention_lse per shard + "
+                                                 "NCCL all-gather of (out, lse) + tle_merge_lse)" % (L, world)},
+                          "per_gpu_frac_hbm": round(gbs / world / peaks["hbm_gbs"], 4),
+                          "gpu_launches": 4 * args.steps}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def load_peaks():
