@@ -765,16 +765,12 @@ __global__ void __launch_bounds__(32) selftest_wait_kernel(uint32_t* err, uint64
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
-    static int configured_device = -1;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
+    static PerDeviceOnce once;
     const int smem = static_cast<int>(sizeof(DecodeSmem));
-    if (configured_device != dev) {
-        e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured_device = dev;
-    }
+    cudaError_t e = once.run([&](int) {
+        return cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (e != cudaSuccess) return e;
     decode_kernel<<<a.n_ctas, NCT, smem, stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -800,18 +796,20 @@ cudaError_t launch_rope(const RopeArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t error_word(uint32_t** word) {
-    static uint32_t* cached[64] = {};
+    static std::atomic<uint32_t*> cached[kMaxDevices] = {};   // thread-safe lazy lookup
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!cached[dev]) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    uint32_t* w = cached[dev].load(std::memory_order_acquire);
+    if (!w) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_tle_error);
         if (e != cudaSuccess) return e;
-        cached[dev] = static_cast<uint32_t*>(p);
+        w = static_cast<uint32_t*>(p);
+        cached[dev].store(w, std::memory_order_release);
     }
-    *word = cached[dev];
+    *word = w;
     return cudaSuccess;
 }
 

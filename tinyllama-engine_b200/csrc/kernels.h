@@ -4,6 +4,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "tle_attn.h"
 
 namespace tle {
@@ -119,6 +122,27 @@ size_t prefill_workspace_bytes(int n_tokens, int pos0);
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 
 cudaError_t read_device_error(int clear, uint32_t* code);
+
+// Runs `configure` (kernel attributes) once per device, thread-safe; later
+// calls cost one atomic load.
+constexpr int kMaxDevices = 64;
+struct PerDeviceOnce {
+    std::atomic<bool> done[kMaxDevices] = {};
+    std::mutex mu;
+    template <class F>
+    cudaError_t run(F&& configure) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+        std::lock_guard<std::mutex> lock(mu);
+        if (done[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+        e = configure(dev);
+        if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
+        return e;
+    }
+};
 // One block waiting (bounded by limit_ns) on a barrier nothing arrives at;
 // records kErrSelfTest in err when the limit expires.
 cudaError_t launch_selftest_wait(uint32_t* err, uint64_t limit_ns, cudaStream_t stream);

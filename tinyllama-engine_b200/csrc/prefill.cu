@@ -741,27 +741,27 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     t.n_qt = L.S_pad / BM;
     t.err = a.err;
     const int smem = static_cast<int>(sizeof(AttnSmem)) + 1024;
-    static int configured_device = -1;
-    int dev = 0;
-    e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (configured_device != dev) {
+    static PerDeviceOnce once;
+    static int sm_count_of[kMaxDevices];
+    e = once.run([&](int dev) {
+        cudaError_t r0 = cudaDeviceGetAttribute(&sm_count_of[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (r0 != cudaSuccess) return r0;
         // setmaxnreg.inc waits until the block's launch registers cover the
         // split; refuse to launch (instead of hanging) if the compiled kernel
         // was given fewer registers than the split assumes.
         cudaFuncAttributes fa{};
-        e = cudaFuncGetAttributes(&fa, prefill_attn_kernel);
-        if (e != cudaSuccess) return e;
+        cudaError_t r = cudaFuncGetAttributes(&fa, prefill_attn_kernel);
+        if (r != cudaSuccess) return r;
         if (fa.numRegs < kLaunchRegs) return cudaErrorInvalidConfiguration;
-        e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured_device = dev;
-    }
+        return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (e != cudaSuccess) return e;
     // Programmatic dependent launch: the attention grid may start while the
     // prep grid runs; only its TMA producer waits (griddepcontrol.wait).
-    int n_sm = 0;
-    e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    int dev = 0;
+    e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    const int n_sm = sm_count_of[dev];
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(std::min(t.n_qt * (NH / 2), n_sm));   // persistent: one CTA per SM
     cfg.blockDim = dim3(ATTN_THREADS);
