@@ -348,3 +348,16 @@ def test_context_split_matches_oracle(cuda, n_rows, world):
         a, b = plan.bounds[r]
         assert np.array_equal(host(shards[r][0])[layer, :b - a], kc[layer, a:b])
     assert tle.device_error() == 0
+
+
+def test_many_short_sequences_per_cta(cuda):
+    """2000 sequences of 1..120 rows: far more sequences than CTAs, so every
+    CTA walks dozens of whole-sequence segments (q prefetch across segments,
+    the tile ring running ahead over segment boundaries); a sample of 300
+    sequences is checked against the oracle."""
+    rng = np.random.default_rng(77)
+    lengths = rng.integers(1, 121, 2000)
+    check = sorted(rng.choice(2000, 300, replace=False).tolist())
+    err, n_ctas = run_batch_case(lengths, n_layers=1, layer=0, max_ctas=0, seed=77, check=check)
+    assert n_ctas >= 100
+    assert err <= ATOL, err
