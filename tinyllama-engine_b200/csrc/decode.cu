@@ -9,8 +9,8 @@
 //   (ops.cpp:1494-1508).
 //
 // Design (B200): the rows of all sequences in a batch are concatenated and
-// split evenly over the CTAs (one per SM).  A CTA walks its row range as
-// segments of one sequence each.  Warp 0 lane 0 streams 32-row K and V tiles
+// split over the CTAs (one per SM), balanced in rows plus a fixed cost per
+// segment.  A CTA walks its row range as segments of one sequence each.  Warp 0 lane 0 streams 32-row K and V tiles
 // (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with 1-D
 // bulk copies (refilling a stage once all warps released it), and prefetches
 // each segment's q and new k/v rows one segment ahead.
@@ -22,10 +22,11 @@
 // distinct addresses of a warp-wide load fall in four different bank groups
 // (conflict-free broadcast).  At the end of a segment the warps merge in a
 // 3-level tree (8 -> 4 through tensor memory, which the kernel otherwise
-// does not use, 4 -> 2 -> 1 through shared memory); warp 0 writes the output of a segment that
-// is a whole sequence, otherwise its (m, l, o) partial goes to the workspace
-// and the last CTA to finish a partial of that sequence combines them (batch
-// mode; merge_kernel does it for the single-sequence entry points).
+// does not use, 4 -> 2 -> 1 through shared memory); warp 0 writes the output
+// of a segment that is a whole sequence, otherwise its (m, l, o) partial goes
+// to the workspace and the last CTA to finish a partial of that sequence
+// combines them (batch mode; merge_kernel does it for the single-sequence
+// entry points).
 #include <math.h>
 
 #include "common.cuh"
