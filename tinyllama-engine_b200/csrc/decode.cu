@@ -10,7 +10,8 @@
 //
 // Design (B200): the rows of all sequences in a batch are concatenated and
 // split over the CTAs (one per SM), balanced in rows plus a fixed cost per
-// segment.  A CTA walks its row range as segments of one sequence each.  Warp 0 lane 0 streams 32-row K and V tiles
+// segment.  A CTA walks its row range as segments of one sequence each.
+// Warp 0 lane 0 streams 32-row K and V tiles
 // (1 KB per row: all 4 KV heads) into a 3-stage shared-memory ring with 1-D
 // bulk copies (refilling a stage once all warps released it), and prefetches
 // each segment's q and new k/v rows one segment ahead.
@@ -409,7 +410,11 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         const int seg_a = off;
         const int seg_b = (s == s1) ? o1 : L;
         const int qb = n & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&S.qfull[qb], (n >> 1) & 1))) { record_error(A.err, kErrWaitFull); ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&S.qfull[qb], (n >> 1) & 1))) {
+            record_error(A.err, kErrWaitFull);
+            ok = false;
+            break;
+        }
 
         // q: rotate (rope, ops.cpp:1229-1260), pre-scale by 1/sqrt(64) (exact
         // power of two, so (q/8).k == (q.k)/8 bit for bit).  Every pair this
