@@ -523,7 +523,87 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                 break;
             }
             const int r0 = warp * RPW;
-            if (r0 < nrows) {
+            // One tile: scores, online softmax and PV for this warp's RPW rows
+            // at kp[r] / vp[r] (already offset to the lane's KV head).
+            auto tile_rows = [&](const float* const (&kp)[RPW], const float* const (&vp)[RPW],
+                                 const bool (&valid)[RPW]) __attribute__((always_inline)) {
+                    // scores s_r = (q/8) . K_r, as (even, odd) dimension partial
+                    // sums in f32x2 lanes, added at the end
+                    float sc[RPW];
+                    uint64_t sc2[RPW];
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) sc2[r] = 0ull;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int o = 4 * ((c + g) & 15);
+                        const uint64_t qa = pk2(q[c].x, q[c].y), qb2 = pk2(q[c].z, q[c].w);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            const float4 kv = *reinterpret_cast<const float4*>(kp[r] + o);
+                            sc2[r] = fma2(qa, pk2(kv.x, kv.y), sc2[r]);
+                            sc2[r] = fma2(qb2, pk2(kv.z, kv.w), sc2[r]);
+                        }
+                    }
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        float a0, a1;
+                        up2(sc2[r], a0, a1);
+                        sc[r] = a0 + a1;
+                    }
+                    // online softmax over this warp's rows
+                    float mb = -INFINITY;
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        if (!valid[r]) sc[r] = -INFINITY;
+                        mb = fmaxf(mb, sc[r]);
+                    }
+                    if (mb > m_run) {
+                        const float f = exp_sfu(m_run - mb);
+                        l_run *= f;
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            acc[c].x *= f; acc[c].y *= f; acc[c].z *= f; acc[c].w *= f;
+                        }
+                        m_run = mb;
+                    }
+                    float p[RPW];
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        p[r] = exp_sfu(sc[r] - m_run);
+                        l_run += p[r];
+                    }
+                    // out += p_r * V_r
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const int o = 4 * ((c + g) & 15);
+                        uint64_t axy = pk2(acc[c].x, acc[c].y), azw = pk2(acc[c].z, acc[c].w);
+#pragma unroll
+                        for (int r = 0; r < RPW; ++r) {
+                            const float4 vv = *reinterpret_cast<const float4*>(vp[r] + o);
+                            const uint64_t pp = pk2(p[r], p[r]);
+                            axy = fma2(pp, pk2(vv.x, vv.y), axy);
+                            azw = fma2(pp, pk2(vv.z, vv.w), azw);
+                        }
+                        up2(axy, acc[c].x, acc[c].y);
+                        up2(azw, acc[c].z, acc[c].w);
+                    }
+            };
+            if (nrows == TILE && !(ta <= sq.pos && sq.pos < ta + TILE)) {
+                // full tile without the new row: rows at a constant stride
+                // from one base, so the loads use immediate offsets
+                const float* kb = &S.k[st][r0 * ROWF] + g * HD;
+                const float* vb = &S.v[st][r0 * ROWF] + g * HD;
+                const float* kp[RPW];
+                const float* vp[RPW];
+                bool valid[RPW];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    kp[r] = kb + r * ROWF;
+                    vp[r] = vb + r * ROWF;
+                    valid[r] = true;
+                }
+                tile_rows(kp, vp, valid);
+            } else if (r0 < nrows) {
                 const float* kp[RPW];
                 const float* vp[RPW];
                 bool valid[RPW];
@@ -535,66 +615,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                     kp[r] = (is_new ? S.newk : &S.k[st][rr * ROWF]) + g * HD;
                     vp[r] = (is_new ? S.newv : &S.v[st][rr * ROWF]) + g * HD;
                 }
-                // scores s_r = (q/8) . K_r, as (even, odd) dimension partial
-                // sums in f32x2 lanes, added at the end
-                float sc[RPW];
-                uint64_t sc2[RPW];
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) sc2[r] = 0ull;
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const int o = 4 * ((c + g) & 15);
-                    const uint64_t qa = pk2(q[c].x, q[c].y), qb2 = pk2(q[c].z, q[c].w);
-#pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        const float4 kv = *reinterpret_cast<const float4*>(kp[r] + o);
-                        sc2[r] = fma2(qa, pk2(kv.x, kv.y), sc2[r]);
-                        sc2[r] = fma2(qb2, pk2(kv.z, kv.w), sc2[r]);
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) {
-                    float a0, a1;
-                    up2(sc2[r], a0, a1);
-                    sc[r] = a0 + a1;
-                }
-                // online softmax over this warp's rows
-                float mb = -INFINITY;
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) {
-                    if (!valid[r]) sc[r] = -INFINITY;
-                    mb = fmaxf(mb, sc[r]);
-                }
-                if (mb > m_run) {
-                    const float f = exp_sfu(m_run - mb);
-                    l_run *= f;
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        acc[c].x *= f; acc[c].y *= f; acc[c].z *= f; acc[c].w *= f;
-                    }
-                    m_run = mb;
-                }
-                float p[RPW];
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) {
-                    p[r] = exp_sfu(sc[r] - m_run);
-                    l_run += p[r];
-                }
-                // out += p_r * V_r
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const int o = 4 * ((c + g) & 15);
-                    uint64_t axy = pk2(acc[c].x, acc[c].y), azw = pk2(acc[c].z, acc[c].w);
-#pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        const float4 vv = *reinterpret_cast<const float4*>(vp[r] + o);
-                        const uint64_t pp = pk2(p[r], p[r]);
-                        axy = fma2(pp, pk2(vv.x, vv.y), axy);
-                        azw = fma2(pp, pk2(vv.z, vv.w), azw);
-                    }
-                    up2(axy, acc[c].x, acc[c].y);
-                    up2(azw, acc[c].z, acc[c].w);
-                }
+                tile_rows(kp, vp, valid);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[st]);
