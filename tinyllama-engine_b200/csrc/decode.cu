@@ -492,15 +492,20 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         if (warp == 0 && q_issued == n + 1 && issue_q(A, S, n + 1, s0, o0, s1, o1, lane)) q_issued = n + 2;
 
         // This lane's query head, its 16-byte chunks in KV-head-rotated order.
-        float4 q[16];
+        // q and the accumulator as f32x2 pairs: chunk c is pairs 2c (x, y)
+        // and 2c + 1 (z, w)
+        uint64_t q2[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-            q[c] = *reinterpret_cast<const float4*>(&S.qo[h * QS + 4 * ((c + g) & 15)]);
+        for (int c = 0; c < 16; ++c) {
+            const float4 qc = *reinterpret_cast<const float4*>(&S.qo[h * QS + 4 * ((c + g) & 15)]);
+            q2[2 * c] = pk2(qc.x, qc.y);
+            q2[2 * c + 1] = pk2(qc.z, qc.w);
+        }
 
         float m_run = -INFINITY, l_run = 0.f;
-        float4 acc[16];
+        uint64_t a2[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < 32; ++i) a2[i] = 0ull;
 
         for (int ta = seg_a; ta < seg_b; ta += TILE) {
             // Refill: the stage of tile it-1 takes tile it-1+NSTAGE once all
@@ -536,7 +541,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const int o = 4 * ((c + g) & 15);
-                        const uint64_t qa = pk2(q[c].x, q[c].y), qb2 = pk2(q[c].z, q[c].w);
+                        const uint64_t qa = q2[2 * c], qb2 = q2[2 * c + 1];
 #pragma unroll
                         for (int r = 0; r < RPW; ++r) {
                             const float4 kv = *reinterpret_cast<const float4*>(kp[r] + o);
@@ -561,9 +566,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                         const float f = exp_sfu(m_run - mb);
                         l_run *= f;
 #pragma unroll
-                        for (int c = 0; c < 16; ++c) {
-                            acc[c].x *= f; acc[c].y *= f; acc[c].z *= f; acc[c].w *= f;
-                        }
+                        for (int i = 0; i < 32; ++i) a2[i] = fma2(a2[i], pk2(f, f), 0ull);
                         m_run = mb;
                     }
                     float p[RPW];
@@ -576,7 +579,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const int o = 4 * ((c + g) & 15);
-                        uint64_t axy = pk2(acc[c].x, acc[c].y), azw = pk2(acc[c].z, acc[c].w);
+                        uint64_t axy = a2[2 * c], azw = a2[2 * c + 1];
 #pragma unroll
                         for (int r = 0; r < RPW; ++r) {
                             const float4 vv = *reinterpret_cast<const float4*>(vp[r] + o);
@@ -584,8 +587,8 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                             axy = fma2(pp, pk2(vv.x, vv.y), axy);
                             azw = fma2(pp, pk2(vv.z, vv.w), azw);
                         }
-                        up2(axy, acc[c].x, acc[c].y);
-                        up2(azw, acc[c].z, acc[c].w);
+                        a2[2 * c] = axy;
+                        a2[2 * c + 1] = azw;
                     }
             };
             if (nrows == TILE && !(ta <= sq.pos && sq.pos < ta + TILE)) {
@@ -622,6 +625,12 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             ++it;
         }
         if (!ok) break;
+        float4 acc[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            up2(a2[2 * c], acc[c].x, acc[c].y);
+            up2(a2[2 * c + 1], acc[c].z, acc[c].w);
+        }
 
         // ---- tree merge of the 8 warps' (m, l, acc): 8 -> 4 -> 2 -> 1 ----
         // (every lane of a pair of warps holds the same query head with the
