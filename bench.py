@@ -56,7 +56,8 @@ def parse():
                     help="skip the config-3 prefill and config-4 ragged-decode lines")
     ap.add_argument("--ctx-rows", type=int, default=4 * 1024 * 1024,
                     help="rows of the single sequence for --only ctxsplit")
-    ap.add_argument("--only", choices=["prefill3", "decode4", "decode1", "ctxsplit"], default=None,
+    ap.add_argument("--only", choices=["prefill3", "decode4", "decode1", "ctxsplit", "decode5paged",
+                                       "decode4paged"], default=None,
                     help="run one secondary workload alone (--steps/--warmup apply) and print "
                          "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -208,7 +209,8 @@ def main():
         measure_ctxsplit(args, dev, rank, world, local)
         return
     if args.only:
-        fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1}[args.only]
+        fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1,
+              "decode5paged": measure_paged5, "decode4paged": measure_paged4}[args.only]
         res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
         print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
                               warmup=max(3, args.warmup))), flush=True)
@@ -378,7 +380,9 @@ def main():
         if world == 1 and not args.no_secondary:
             line["secondary"] = {"prefill_config3": measure_prefill(dev, peaks),
                                  "decode_config4": measure_config4(dev, peaks),
-                                 "decode_config1": measure_config1(dev, peaks)}
+                                 "decode_config1": measure_config1(dev, peaks),
+                                 "decode_config4_paged": measure_paged4(dev, peaks),
+                                 "decode_config5_paged": measure_paged5(dev, peaks)}
         if world == 1 and not args.no_cpu_baseline:
             gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
             line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
@@ -503,6 +507,80 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
             "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
             "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
             "ms_per_step_eager": round(ms_eager, 4),
+            "n_ctas": batch.n_ctas,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+            "gpu_launches": n_layers * steps}
+
+
+def _paged_setup(dev, lengths, n_layers, page_rows, seed, shuffle=True):
+    """Page pools holding every sequence's rows (N(0,1)), pages handed out in
+    a shuffled order (or in pool order), and the PagedDecodeBatch over them."""
+    import numpy as np
+    import torch
+    import tle
+    need = [-(-int(L) // page_rows) for L in lengths]
+    cache = tle.PagedKVCache(sum(need), page_rows, tle.tinyllama_shape(n_layers), device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    cache.key_pool.normal_(generator=g)
+    cache.value_pool.normal_(generator=g)
+    if shuffle:
+        cache._free = [int(i) for i in np.random.default_rng(seed).permutation(sum(need))]
+    tables = [cache.table(cache.alloc(m)) for m in need]
+    batch = tle.PagedDecodeBatch(cache, tables, [int(L) - 1 for L in lengths])
+    n = len(lengths)
+    q = torch.randn((n, QD), generator=g, device=dev)
+    k = torch.randn((n, KVD), generator=g, device=dev)
+    v = torch.randn((n, KVD), generator=g, device=dev)
+    out = torch.zeros((n, QD), device=dev)
+    return cache, batch, q, k, v, out
+
+
+def measure_paged5(dev, peaks, steps=10, warmup=3, page_rows=256, shuffle=True):
+    """Config 5 on a paged cache: 256 sequences x 32768 rows in 256-row pages
+    of one shared pool (shuffled), one tle_decode_batch_paged call per step
+    (17.2 GB of K+V, > L2)."""
+    import torch
+    lengths = [CTX] * N_SEQS
+    cache, batch, q, k, v, out = _paged_setup(dev, lengths, 1, page_rows, 55, shuffle)
+    stream = torch.cuda.current_stream(dev)
+    ms = _time_steps(lambda: batch.run(q, k, v, out, 0, True, stream), steps, warmup, stream)
+    kv_bytes = N_SEQS * CTX * ROW_BYTES
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    del cache
+    return {"workload": "config5 paged: 256 seqs x 32768 rows, %d-row pages in one shuffled pool, "
+                        "1 layer per step (tle_decode_batch_paged)" % page_rows,
+            "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "n_ctas": batch.n_ctas,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+            "gpu_launches": steps}
+
+
+def measure_paged4(dev, peaks, steps=20, warmup=3, page_rows=256, shuffle=True):
+    """Config 4 on a paged cache: 64 sequences, lengths U[128, 2048] (the same
+    seeded lengths as the contiguous line), 22 layers, 256-row pages; a step
+    is 22 tle_decode_batch_paged calls in one CUDA graph."""
+    import numpy as np
+    import torch
+    n_layers = 22
+    lengths = np.random.default_rng(4).integers(128, 2049, 64)
+    cache, batch, q, k, v, out = _paged_setup(dev, lengths, n_layers, page_rows, 44, shuffle)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(st=stream):
+        for l in range(n_layers):
+            batch.run(q, k, v, out, l, True, st)
+
+    ms = _time_graph(step, steps, warmup, dev)
+    kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    del cache
+    return {"workload": "config4 paged: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step, "
+                        "%d-row pages (CUDA graph of the 22 tle_decode_batch_paged calls)"
+                        % (int(lengths.sum()), page_rows),
+            "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},

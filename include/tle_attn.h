@@ -134,6 +134,50 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
                      const float* q, const float* k, const float* v, float* out, int layer,
                      int rotate, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- batched decode over a paged KV cache ----
+ * No counterpart in the reference: run_state.h:20-25 sizes one contiguous
+ * [n_layers][n_ctx][256] cache per sequence and names PagedAttention as the
+ * next step.  Here the rows of all sequences live in one pair of page pools
+ * shared by the batch; each sequence maps its rows to pool pages through a
+ * page table.  Same kernel, same split of rows over CTAs and bit-identical
+ * results to tle_decode_batch on the same rows (a tile of rows reaches
+ * shared memory in the same order whichever layout it came from). */
+
+/* The pools: row r of page p of layer l is at
+ *   pool + ((l * n_pages + p) * page_rows + r) * n_head_kv * head_dim. */
+typedef struct {
+    float* key_pool;    /* device [n_layers][n_pages][page_rows][n_head_kv*head_dim] fp32 */
+    float* value_pool;  /* device, same layout                                            */
+    int32_t n_pages;    /* pages per layer in each pool                                   */
+    int32_t page_rows;  /* rows per page: a power of two, 16 .. 65536                     */
+} tle_page_pool_t;
+
+/* One decoding sequence of a paged batch: its rows 0..pos are rows
+ * r % page_rows of pool pages pages[r / page_rows]. */
+typedef struct {
+    const int32_t* pages; /* DEVICE int32 [n_pages]: page ids in [0, pool n_pages)   */
+    int32_t n_pages;      /* entries in pages; need n_pages * page_rows > pos       */
+    int32_t pos;          /* position of the token being decoded (appended at row pos) */
+} tle_paged_seq_t;
+
+/* tle_decode_desc for a paged batch (same tle_decode_desc_bytes size, same
+ * split of rows over CTAs).  The page tables stay on the device and are
+ * read by the kernel: they must hold valid ids when the decode runs.  An id
+ * outside [0, pool n_pages) is not dereferenced; the kernel skips that
+ * access and tle_device_error then reports 0x105. */
+int tle_decode_desc_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
+                          const tle_paged_seq_t* seqs, int n_seqs, int max_ctas, void* desc_host,
+                          size_t desc_bytes, int* n_ctas);
+
+/* tle_decode_batch over the pools: appends k_s, v_s at row pos_s of each
+ * sequence (through its page table) and attends to rows 0..pos_s.  desc_dev
+ * is the device copy of the tle_decode_desc_paged() output, workspace as
+ * for tle_decode_batch (tle_decode_workspace_bytes). */
+int tle_decode_batch_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
+                           const void* desc_dev, int n_seqs, int n_ctas, const float* q,
+                           const float* k, const float* v, float* out, int layer, int rotate,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- decode without allocation ----
  * No counterpart in the reference.  For callers that cannot call cudaMalloc:
  * a host framework that owns all device memory through its own pool, or a
@@ -185,8 +229,12 @@ int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* 
 
 /* ---- diagnostics ---- */
 
-/* Reads (and clears if clear != 0) the device error word that kernels set
- * when a bounded wait expires; 0 = no error.  Synchronises the device. */
+/* Reads (and clears if clear != 0) the device error word that kernels set;
+ * 0 = no error.  Codes: 0x101-0x104 a bounded wait expired (0x101 a stage
+ * never filled, 0x102 never drained, 0x103 a tensor-core commit never
+ * arrived, 0x104 the exit-time drain), 0x105 a paged decode met a page id
+ * outside the pool, 0x1ff the self-test below.  The first code recorded
+ * stays until cleared.  Synchronises the device. */
 int tle_device_error(int clear, uint32_t* code);
 
 /* Exercises the failure path of the kernels' bounded waits without a fault:

@@ -140,3 +140,67 @@ def test_partition_lpt_balances_and_is_deterministic():
         assert loads.max() <= loads.sum() / ranks + lengths.max()
     # equal lengths: round robin in sequence order
     assert tle.partition_lpt([7] * 8, 4) == [0, 1, 2, 3, 0, 1, 2, 3]
+
+
+# ------------------------------------------------------- paged descriptor
+def build_desc_paged(positions, n_pages, page_rows, max_ctas, pool_pages=1 << 20,
+                     table_ptr=lambda i: 0x4000 * (i + 1)):
+    n = len(positions)
+    shape = tle.tinyllama_shape()
+    pool = tle.PagePool(0x10000000, 0x20000000, pool_pages, page_rows)
+    seqs = (tle.PagedSeq * n)()
+    for i, p in enumerate(positions):
+        seqs[i] = tle.PagedSeq(table_ptr(i), n_pages[i], p)
+    nbytes = tle.lib().tle_decode_desc_bytes(n, max_ctas)
+    buf = (ctypes.c_uint8 * nbytes)()
+    n_ctas = ctypes.c_int(0)
+    rc = tle.lib().tle_decode_desc_paged(ctypes.byref(shape), ctypes.byref(pool), seqs, n,
+                                         max_ctas, buf, nbytes, ctypes.byref(n_ctas))
+    return rc, buf, n_ctas.value
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_paged_plan_equals_contiguous_plan(seed):
+    """The paged descriptor splits rows over CTAs exactly like the contiguous
+    one for the same positions (so the two give bit-identical outputs); its
+    sequence slots carry {page table, 0, n_pages, pos}."""
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(1, 60))
+    page_rows = 64
+    pos = [int(x) for x in rng.integers(0, 5000, n)]
+    n_pages = [p // page_rows + 1 + int(rng.integers(0, 3)) for p in pos]
+    max_ctas = int(rng.integers(1, 300))
+    rc, buf, G = build_desc_paged(pos, n_pages, page_rows, max_ctas)
+    assert rc == 0, tle.lib().tle_last_error()
+    rc2, buf2, G2 = build_desc(pos, [p + 1 for p in pos], max_ctas)
+    assert rc2 == 0 and G2 == G
+    m1, ns, nc, total, cs, sc = parse_desc(buf, n, G)
+    m2, _, _, total2, cs2, sc2 = parse_desc(buf2, n, G)
+    assert m1 == 0x544C4550 and m2 == 0x544C4544
+    assert total == total2 and np.array_equal(cs, cs2) and np.array_equal(sc, sc2)
+    slots = np.frombuffer(bytes(buf)[32:32 + 24 * n], np.uint8).reshape(n, 24)
+    for i in range(n):
+        ptrs = np.frombuffer(slots[i, :16].tobytes(), np.uint64)
+        ints = np.frombuffer(slots[i, 16:].tobytes(), np.int32)
+        assert ptrs[0] == 0x4000 * (i + 1) and ptrs[1] == 0
+        assert ints[0] == n_pages[i] and ints[1] == pos[i]
+
+
+@pytest.mark.parametrize("page_rows,n_pages,pos,table,what", [
+    (48, [4], [10], None, "power of two"),
+    (8, [4], [10], None, "power of two"),
+    (32, [1], [32], None, "n_pages"),        # row 32 needs a second page
+    (32, [2], [-1], None, "pos"),
+    (32, [2], [5], lambda i: 0, "page table"),
+    (32, [2], [5], lambda i: 0x4002, "aligned"),
+])
+def test_paged_desc_rejects_bad_arguments(page_rows, n_pages, pos, table, what):
+    kw = {} if table is None else {"table_ptr": table}
+    rc, _, _ = build_desc_paged(pos, n_pages, page_rows, 8, **kw)
+    assert rc == tle.TLE_ERR_INVALID
+    assert what in tle.lib().tle_last_error().decode()
+
+
+def test_paged_desc_rejects_empty_pool():
+    rc, _, _ = build_desc_paged([3], [1], 32, 8, pool_pages=0)
+    assert rc == tle.TLE_ERR_INVALID

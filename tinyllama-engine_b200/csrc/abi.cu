@@ -248,28 +248,21 @@ size_t tle_decode_desc_bytes(int n_seqs, int max_ctas) {
     return tle::desc_total_bytes(n_seqs, max_ctas);
 }
 
-int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs, int max_ctas,
-                    void* desc_host, size_t desc_bytes, int* n_ctas_out) {
-    if (int rc = check_shape(shape)) return rc;
-    if (n_seqs <= 0 || !seqs || !desc_host || !n_ctas_out)
-        return set_error(TLE_ERR_INVALID, "need n_seqs > 0 and non-null seqs/desc/n_ctas");
+namespace {
+
+// Writes the descriptor for `n_seqs` validated records (their pos fields
+// drive the plan; the records are copied as they are).
+int write_desc(const tle_seq_t* seqs, int n_seqs, int max_ctas, int32_t magic, void* desc_host,
+               size_t desc_bytes, int* n_ctas_out) {
     int64_t total = 0;
-    for (int s = 0; s < n_seqs; ++s) {
-        const tle_seq_t& q = seqs[s];
-        if (!q.key_cache || !q.value_cache || !aligned16(q.key_cache) || !aligned16(q.value_cache))
-            return set_error(TLE_ERR_INVALID, "sequence %d: caches must be non-null and 16-byte aligned", s);
-        if (q.n_ctx <= 0 || q.pos < 0 || q.pos >= q.n_ctx)
-            return set_error(TLE_ERR_INVALID, "sequence %d: need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", s,
-                             q.pos, q.n_ctx);
-        total += static_cast<int64_t>(q.pos) + 1;
-    }
+    for (int s = 0; s < n_seqs; ++s) total += static_cast<int64_t>(seqs[s].pos) + 1;
     const int G = choose_ctas(total, max_ctas);
     const size_t need = tle::desc_total_bytes(n_seqs, G);
     if (desc_bytes < need)
         return set_error(TLE_ERR_INVALID, "descriptor buffer %zu bytes < %zu needed", desc_bytes, need);
     unsigned char* base = static_cast<unsigned char*>(desc_host);
     tle::DescHeader hdr{};
-    hdr.magic = tle::kDescMagic;
+    hdr.magic = magic;
     hdr.n_seqs = n_seqs;
     hdr.n_ctas = G;
     hdr.total_rows = total;
@@ -283,15 +276,28 @@ int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
     return ok();
 }
 
-size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ctas) {
-    (void)shape;
-    if (n_ctas <= 0) n_ctas = tle::kMaxCtas;
-    return partial_bytes(n_ctas + std::max(n_seqs, 0));
+int check_pool(const tle_shape_t* shape, const tle_page_pool_t* pool, int* shift) {
+    if (!pool || !pool->key_pool || !pool->value_pool)
+        return set_error(TLE_ERR_INVALID, "page pool and both pools must be non-null");
+    if (!aligned16(pool->key_pool) || !aligned16(pool->value_pool))
+        return set_error(TLE_ERR_INVALID, "page pools must be 16-byte aligned");
+    const int pr = pool->page_rows;
+    if (pr < 16 || pr > 65536 || (pr & (pr - 1)) != 0)
+        return set_error(TLE_ERR_INVALID, "page_rows %d is not a power of two in [16, 65536]", pr);
+    if (pool->n_pages <= 0) return set_error(TLE_ERR_INVALID, "pool n_pages %d <= 0", pool->n_pages);
+    // row offsets are formed in 64 bits; keep the pool below 2^62 floats
+    const double rows = static_cast<double>(shape->n_layers) * pool->n_pages * pr;
+    if (rows * tle::kRowFloats > 4.0e18) return set_error(TLE_ERR_INVALID, "page pool too large");
+    int sh = 0;
+    while ((1 << sh) < pr) ++sh;
+    *shift = sh;
+    return 0;
 }
 
-int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
-                     const float* q, const float* k, const float* v, float* out, int layer, int rotate,
-                     void* workspace, size_t workspace_bytes, void* stream) {
+// Fills the kernel arguments shared by the contiguous and paged batch calls.
+int batch_args(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas, const float* q,
+               const float* k, const float* v, float* out, int layer, int rotate, void* workspace,
+               size_t workspace_bytes, tle::DecodeArgs& a) {
     if (int rc = check_shape(shape)) return rc;
     if (!desc_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer argument");
     if (n_seqs <= 0 || n_ctas <= 0 || n_ctas > tle::kMaxCtas)
@@ -305,7 +311,7 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
         return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed (or unaligned)",
                          workspace_bytes, need);
     const unsigned char* base = static_cast<const unsigned char*>(desc_dev);
-    tle::DecodeArgs a{};
+    a = tle::DecodeArgs{};
     a.seqs = reinterpret_cast<const tle_seq_t*>(base + tle::desc_seqs_offset());
     a.cta_start = reinterpret_cast<const tle::CtaStart*>(base + tle::desc_cta_offset(n_seqs));
     a.seq_ctas = reinterpret_cast<const tle::SeqCtas*>(base + tle::desc_seqctas_offset(n_seqs, n_ctas));
@@ -322,8 +328,92 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
     fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
     cudaError_t e = tle::error_word(&a.err);
     if (e != cudaSuccess) return cuda_error(e, "device error word");
-    e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
+    return 0;
+}
+
+}  // namespace
+
+int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs, int max_ctas,
+                    void* desc_host, size_t desc_bytes, int* n_ctas_out) {
+    if (int rc = check_shape(shape)) return rc;
+    if (n_seqs <= 0 || !seqs || !desc_host || !n_ctas_out)
+        return set_error(TLE_ERR_INVALID, "need n_seqs > 0 and non-null seqs/desc/n_ctas");
+    for (int s = 0; s < n_seqs; ++s) {
+        const tle_seq_t& q = seqs[s];
+        if (!q.key_cache || !q.value_cache || !aligned16(q.key_cache) || !aligned16(q.value_cache))
+            return set_error(TLE_ERR_INVALID, "sequence %d: caches must be non-null and 16-byte aligned", s);
+        if (q.n_ctx <= 0 || q.pos < 0 || q.pos >= q.n_ctx)
+            return set_error(TLE_ERR_INVALID, "sequence %d: need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", s,
+                             q.pos, q.n_ctx);
+    }
+    return write_desc(seqs, n_seqs, max_ctas, tle::kDescMagic, desc_host, desc_bytes, n_ctas_out);
+}
+
+int tle_decode_desc_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
+                          const tle_paged_seq_t* seqs, int n_seqs, int max_ctas, void* desc_host,
+                          size_t desc_bytes, int* n_ctas_out) {
+    if (int rc = check_shape(shape)) return rc;
+    int shift = 0;
+    if (int rc = check_pool(shape, pool, &shift)) return rc;
+    if (n_seqs <= 0 || !seqs || !desc_host || !n_ctas_out)
+        return set_error(TLE_ERR_INVALID, "need n_seqs > 0 and non-null seqs/desc/n_ctas");
+    // The descriptor's 24-byte sequence slots carry {page table, -, n_pages, pos}.
+    // (a byte vector: nvcc's front end rejects std::vector of the C ABI's
+    // unnamed struct types)
+    std::vector<unsigned char> rec_bytes(sizeof(tle_seq_t) * static_cast<size_t>(n_seqs));
+    tle_seq_t* recs = reinterpret_cast<tle_seq_t*>(rec_bytes.data());
+    for (int s = 0; s < n_seqs; ++s) {
+        const tle_paged_seq_t& q = seqs[s];
+        if (!q.pages || (reinterpret_cast<uintptr_t>(q.pages) & 3u) != 0)
+            return set_error(TLE_ERR_INVALID, "sequence %d: page table must be non-null and 4-byte aligned", s);
+        if (q.n_pages <= 0 || q.pos < 0 ||
+            static_cast<int64_t>(q.n_pages) * pool->page_rows <= q.pos)
+            return set_error(TLE_ERR_INVALID,
+                             "sequence %d: need 0 <= pos < n_pages * page_rows (pos=%d, n_pages=%d)", s,
+                             q.pos, q.n_pages);
+        recs[s].key_cache = const_cast<float*>(reinterpret_cast<const float*>(q.pages));
+        recs[s].value_cache = nullptr;
+        recs[s].n_ctx = q.n_pages;
+        recs[s].pos = q.pos;
+    }
+    return write_desc(recs, n_seqs, max_ctas, tle::kDescMagicPaged, desc_host, desc_bytes,
+                      n_ctas_out);
+}
+
+size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ctas) {
+    (void)shape;
+    if (n_ctas <= 0) n_ctas = tle::kMaxCtas;
+    return partial_bytes(n_ctas + std::max(n_seqs, 0));
+}
+
+int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
+                     const float* q, const float* k, const float* v, float* out, int layer, int rotate,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    tle::DecodeArgs a;
+    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, rotate, workspace,
+                            workspace_bytes, a))
+        return rc;
+    cudaError_t e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, "decode launch");
+    return ok();
+}
+
+int tle_decode_batch_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
+                           const void* desc_dev, int n_seqs, int n_ctas, const float* q,
+                           const float* k, const float* v, float* out, int layer, int rotate,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    tle::DecodeArgs a;
+    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, rotate, workspace,
+                            workspace_bytes, a))
+        return rc;
+    int shift = 0;
+    if (int rc = check_pool(shape, pool, &shift)) return rc;
+    a.key_pool = pool->key_pool;
+    a.value_pool = pool->value_pool;
+    a.pool_pages = pool->n_pages;
+    a.page_shift = shift;
+    cudaError_t e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "paged decode launch");
     return ok();
 }
 

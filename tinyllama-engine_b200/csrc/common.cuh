@@ -17,6 +17,7 @@ enum : uint32_t {
     kErrWaitEmpty = 0x102,  // producer gave up waiting for a stage to drain
     kErrWaitMma = 0x103,    // waiter gave up on a tensor-core commit
     kErrDrain = 0x104,      // exit-time wait for in-flight copies gave up
+    kErrBadPage = 0x105,    // paged decode: a page id outside the pool (access skipped)
     kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 
@@ -49,6 +50,13 @@ TLE_DEV void fence_barrier_init() {
 TLE_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
+                 : "memory");
+}
+
+// Counts `bytes` of the barrier's expected transaction as done without a
+// copy (for a piece the issuer decided not to copy).
+TLE_DEV void mbar_tx_complete(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
 
@@ -135,6 +143,19 @@ TLE_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// 4-byte asynchronous global -> shared copy (cp.async), and an arrival on
+// `bar` once this thread's earlier cp.async copies have landed.  The arrive
+// form without .noinc raises the barrier's pending count when it executes,
+// so issue it before the arrival that could otherwise complete the phase.
+TLE_DEV void cp_async_4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Waits until every cp.async this thread issued has landed.
+TLE_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+TLE_DEV void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15.

@@ -71,6 +71,8 @@ struct __align__(128) DecodeSmem {
     // loaded it is the tree merge's buffer B (m, l in the row padding).
     float qo[NH * QS];
     float mlA[2 * NH];
+    int32_t apage[2];           // paged mode: page id of row pos of the segment's sequence
+    int32_t npage[2];           // paged mode: the issuer's prefetched next page ids (ring)
     uint32_t tmem_base;
     uint64_t full[NSTAGE];
     uint64_t empty[NSTAGE];
@@ -102,53 +104,151 @@ __device__ __forceinline__ bool in_range(int s, int off, int s1, int o1) {
 }
 
 // The copy issuer's position in the CTA's sequence of tiles (it runs up to
-// NSTAGE tiles ahead of the consumers).
+// NSTAGE tiles ahead of the consumers).  Paged mode keeps the id of the page
+// being read (cpi, cid) and prefetches the id of the page after it (npi)
+// when the cursor enters a page: a 4-byte cp.async into npage[slot], so the
+// table read is in flight for a page's worth of tiles and no register waits
+// on it (the issuer is also a consumer thread: a load it waits on stalls its
+// warp and, through the stage barriers, the CTA).
 struct TileCursor {
     int s, ta, b;
     bool done;
     const float* kb;
     const float* vb;
     int pos;
+    const int32_t* pages;
+    int cpi, cid, npi, slot;
 };
 
-__device__ __forceinline__ void cursor_load(TileCursor& c, const DecodeArgs& A, int s, int off,
-                                            int s1, int o1) {
+// Paged mode: a sequence record's key_cache slot holds its page table (the
+// host builds the descriptor that way, see tle_decode_desc_paged).
+__device__ __forceinline__ const int32_t* seq_pages(const tle_seq_t& sq) {
+    return reinterpret_cast<const int32_t*>(sq.key_cache);
+}
+
+// Offset (floats) of row r of page `id` of the current layer in a pool
+// [n_layers][pool_pages][1 << page_shift][256].
+__device__ __forceinline__ size_t pool_row(const DecodeArgs& A, int id, int r) {
+    return ((static_cast<size_t>(A.layer) * A.pool_pages + id) << A.page_shift |
+            static_cast<size_t>(r & ((1 << A.page_shift) - 1))) * ROWF;
+}
+
+// Checked page id: -1 (and the error word set) for an id outside the pool.
+__device__ __forceinline__ int check_page(const DecodeArgs& A, int id) {
+    if (static_cast<unsigned>(id) >= static_cast<unsigned>(A.pool_pages)) {
+        record_error(A.err, kErrBadPage);
+        return -1;
+    }
+    return id;
+}
+
+// Page id of page pi of the cursor's sequence; advances the one-page-ahead
+// prefetch.  Rows below min(b, pos) are the only ones read, so the prefetch
+// never reads past the entries the host checked (n_pages * page_rows > pos).
+__device__ __forceinline__ int cursor_page(TileCursor& c, const DecodeArgs& A, DecodeSmem& S, int pi) {
+    if (pi == c.cpi) return c.cid;
+    int id;
+    if (pi == c.npi) {
+        cp_async_wait_all();
+        id = S.npage[c.slot];
+        c.slot ^= 1;          // the next prefetch goes to the other slot
+    } else {
+        id = __ldg(c.pages + pi);
+    }
+    c.cid = check_page(A, id);
+    c.cpi = pi;
+    c.npi = -1;
+    if (((pi + 1) << A.page_shift) < min(c.b, c.pos)) {
+        c.npi = pi + 1;
+        cp_async_4(&S.npage[c.slot], c.pages + pi + 1);
+    }
+    return c.cid;
+}
+
+// Paged mode: starts the page-table read of the cursor's first page.
+__device__ __forceinline__ void cursor_prefetch(TileCursor& c, const DecodeArgs& A, DecodeSmem& S) {
+    if (!c.done && c.ta < min(c.b, c.pos)) {
+        c.npi = c.ta >> A.page_shift;
+        cp_async_4(&S.npage[c.slot], c.pages + c.npi);
+    }
+}
+
+// Moves the cursor to row `off` of sequence s (done once past the CTA's
+// range).  Paged mode also starts the read of the first page's id unless
+// `table` is false (the kernel's first call, made before the wait on the
+// previous grid: page tables may be that grid's output).
+template <bool PAGED>
+__device__ __forceinline__ void cursor_load(TileCursor& c, const DecodeArgs& A, DecodeSmem& S, int s,
+                                            int off, int s1, int o1, bool table = true) {
     c.s = s;
     c.ta = off;
     c.done = !in_range(s, off, s1, o1);
     if (!c.done) {
         const tle_seq_t sq = load_seq(A, s);
         c.b = (s == s1) ? o1 : sq.pos + 1;
-        const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
-        c.kb = sq.key_cache + base;
-        c.vb = sq.value_cache + base;
         c.pos = sq.pos;
+        if (PAGED) {
+            c.pages = seq_pages(sq);
+            c.cpi = -1;
+            c.npi = -1;
+            if (table) cursor_prefetch(c, A, S);
+        } else {
+            const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
+            c.kb = sq.key_cache + base;
+            c.vb = sq.value_cache + base;
+        }
     }
 }
 
 // Issues the cursor's tile into stage st (1-D bulk copies of whole 1 KB rows)
 // and advances the cursor.  Row `pos` (the token being decoded) is never read
-// from the cache: the consumers take it from newk/newv.
+// from the cache: the consumers take it from newk/newv.  Paged mode copies
+// the tile as one piece per page it touches (a row of the stage is the same
+// row whichever layout it came from).
+template <bool PAGED>
 __device__ __forceinline__ void cursor_issue(TileCursor& c, const DecodeArgs& A, DecodeSmem& S,
                                              int st, int s1, int o1, uint64_t pol) {
     const int tb = min(c.ta + TILE, c.b);
-    const int n = min(tb, c.pos) - c.ta;
+    const int te = min(tb, c.pos);
+    const int n = te - c.ta;
     if (n > 0) {
         const uint32_t bytes = static_cast<uint32_t>(n) * ROWB;
         mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
-        bulk_g2s(S.k[st], c.kb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
-        bulk_g2s(S.v[st], c.vb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
+        if (PAGED) {
+            for (int r = c.ta; r < te;) {
+                const int pi = r >> A.page_shift;
+                const int e = min(te, (pi + 1) << A.page_shift);
+                const uint32_t pb = static_cast<uint32_t>(e - r) * ROWB;
+                const int id = cursor_page(c, A, S, pi);
+                if (id >= 0) {
+                    const size_t o = pool_row(A, id, r);
+                    bulk_g2s(S.k[st] + (r - c.ta) * ROWF, A.key_pool + o, pb, &S.full[st], pol);
+                    bulk_g2s(S.v[st] + (r - c.ta) * ROWF, A.value_pool + o, pb, &S.full[st], pol);
+                } else {
+                    // bad page id (reported): the stage completes without
+                    // this piece, its rows keep stale contents
+                    mbar_tx_complete(&S.full[st], 2 * pb);
+                }
+                r = e;
+            }
+        } else {
+            bulk_g2s(S.k[st], c.kb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
+            bulk_g2s(S.v[st], c.vb + static_cast<size_t>(c.ta) * ROWF, bytes, &S.full[st], pol);
+        }
     } else {
         mbar_arrive(&S.full[st]);
     }
     c.ta = tb;
-    if (c.ta >= c.b) cursor_load(c, A, c.s + 1, 0, s1, o1);
+    if (c.ta >= c.b) cursor_load<PAGED>(c, A, S, c.s + 1, 0, s1, o1);
 }
 
 // Bulk copies of segment n's per-sequence inputs into buffer n & 1, issued by
 // warp 0: q of its sequence and, when the segment holds row pos, the new k and
-// v rows.  Segment n of a CTA is sequence s0 + n.  Returns false (nothing
-// issued) when the CTA has no segment n; warp-uniform.
+// v rows (paged mode: also the page id of row pos, by a 4-byte cp.async that
+// the same barrier waits for, so no thread stalls on the page-table read).
+// Segment n of a CTA is sequence s0 + n.  Returns false (nothing issued) when
+// the CTA has no segment n; warp-uniform.
+template <bool PAGED>
 __device__ __forceinline__ bool issue_q(const DecodeArgs& A, DecodeSmem& S, int n, int s0, int o0,
                                         int s1, int o1, int lane) {
     const int s = s0 + n;
@@ -158,6 +258,10 @@ __device__ __forceinline__ bool issue_q(const DecodeArgs& A, DecodeSmem& S, int 
     const bool has_new = ((s == s1) ? o1 : L) == L;
     const int b = n & 1;
     if (lane == 0) {
+        if (PAGED && has_new) {
+            cp_async_4(&S.apage[b], seq_pages(sq) + (sq.pos >> A.page_shift));
+            cp_async_mbar_arrive(&S.qfull[b]);
+        }
         mbar_arrive_expect_tx(&S.qfull[b], NH * HD * 4 + (has_new ? 2 * ROWB : 0));
         bulk_g2s_plain(S.qraw[b], A.q + static_cast<size_t>(s) * NH * HD, NH * HD * 4, &S.qfull[b]);
         if (has_new) {
@@ -367,11 +471,13 @@ __device__ __forceinline__ bool cta_sync(DecodeSmem& S, uint32_t& phase, int lan
     return ok;
 }
 
+template <bool PAGED>
 __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ DecodeArgs A) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     DecodeSmem& S = *reinterpret_cast<DecodeSmem*>(smem_raw);
-    // Single-sequence mode: merge_kernel is launched as a programmatic
-    // dependent and may be scheduled now (it waits for this grid's results).
+    // The next kernel on the stream (merge_kernel in single-sequence mode,
+    // the next decode launch in batch mode) is a programmatic dependent: it
+    // may be scheduled now and runs its prologue while this grid finishes.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -382,39 +488,46 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     int s0, o0, s1, o1;
     cta_range(A, cta, s0, o0, s1, o1);
 
-    // Prologue: thread 0 (the tile issuer) initialises the barriers, warp 0
-    // starts segment 0's q copy and thread 0 the first NSTAGE tiles, while
-    // warp 1 allocates the tensor memory; the other warps touch none of it
-    // before the __syncthreads below.
+    // Prologue: thread 0 (the tile issuer) initialises the barriers and
+    // reads its first sequence record while warp 1 allocates the tensor
+    // memory.  Up to here only the descriptor is read, which the host wrote
+    // before the launch; everything else (q/k/v, the caches, page tables,
+    // outputs, partials, arrival counts) may belong to the previous kernel
+    // on the stream, so it is touched only after griddepcontrol.wait.  Then
+    // warp 0 starts segment 0's q copy and thread 0 the first NSTAGE tiles;
+    // the other warps touch none of it before the __syncthreads below.
     TileCursor cur;
     uint64_t pol = 0;
     int issued = 0;
     int q_issued = 0;   // (warp 0) segments 0 .. q_issued-1 have their q copy issued
-    if (warp == 0) {
-        if (issuer) {
-            for (int i = 0; i < NSTAGE; ++i) {
-                mbar_init(&S.full[i], 1);
-                mbar_init(&S.empty[i], NCW);
-            }
-            mbar_init(&S.qfull[0], 1);
-            mbar_init(&S.qfull[1], 1);
-            mbar_init(&S.csync, NCW);
-            fence_barrier_init();
+    if (issuer) {
+        for (int i = 0; i < NSTAGE; ++i) {
+            mbar_init(&S.full[i], 1);
+            mbar_init(&S.empty[i], NCW);
         }
-        __syncwarp();
-        if (issue_q(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
-        if (issuer) {
-            pol = l2_evict_first_policy();
-            cursor_load(cur, A, s0, o0, s1, o1);
-            while (!cur.done && issued < NSTAGE) {
-                cursor_issue(cur, A, S, issued, s1, o1, pol);
-                ++issued;
-            }
-        }
+        mbar_init(&S.qfull[0], 1);
+        mbar_init(&S.qfull[1], 1);
+        mbar_init(&S.csync, NCW);
+        fence_barrier_init();
+        cur.slot = 0;
+        cursor_load<PAGED>(cur, A, S, s0, o0, s1, o1, /*table=*/false);
     }
     if (warp == 1) {
         tmem_alloc(&S.tmem_base, kTmemCols);
         tmem_relinquish();
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (warp == 0) {
+        __syncwarp();
+        if (PAGED && issuer) cursor_prefetch(cur, A, S);
+        if (issue_q<PAGED>(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
+        if (issuer) {
+            pol = l2_evict_first_policy();
+            while (!cur.done && issued < NSTAGE) {
+                cursor_issue<PAGED>(cur, A, S, issued, s1, o1, pol);
+                ++issued;
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -464,7 +577,22 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         // The new token's k (rotated) and v: append to the cache at row pos
         // (ops.cpp:1370-1371) and keep a copy for this CTA's last tile.
         if (seg_b == L) {
-            const size_t row = (static_cast<size_t>(A.layer) * sq.n_ctx + sq.pos) * ROWF;
+            // row pos of the contiguous cache, or of the pool page holding it
+            // (a bad page id is reported and the row not written)
+            float* kdst = nullptr;
+            float* vdst = nullptr;
+            if (PAGED) {
+                const int id = check_page(A, S.apage[qb]);
+                if (id >= 0) {
+                    const size_t row = pool_row(A, id, sq.pos);
+                    kdst = A.key_pool + row;
+                    vdst = A.value_pool + row;
+                }
+            } else {
+                const size_t row = (static_cast<size_t>(A.layer) * sq.n_ctx + sq.pos) * ROWF;
+                kdst = sq.key_cache + row;
+                vdst = sq.value_cache + row;
+            }
             if (tid < ROWF / 2) {
                 const float2 x = reinterpret_cast<const float2*>(S.kvraw)[tid];
                 float y0 = x.x, y1 = x.y;
@@ -474,12 +602,12 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                 }
                 const float2 y = make_float2(y0, y1);
                 reinterpret_cast<float2*>(S.newk)[tid] = y;
-                reinterpret_cast<float2*>(sq.key_cache + row)[tid] = y;
+                if (!PAGED || kdst) reinterpret_cast<float2*>(kdst)[tid] = y;
             } else {
                 const int t2 = tid - ROWF / 2;
                 const float2 x = reinterpret_cast<const float2*>(S.kvraw + ROWF)[t2];
                 reinterpret_cast<float2*>(S.newv)[t2] = x;
-                reinterpret_cast<float2*>(sq.value_cache + row)[t2] = x;
+                if (!PAGED || vdst) reinterpret_cast<float2*>(vdst)[t2] = x;
             }
         }
         // Shared memory written by this thread through the generic proxy
@@ -489,7 +617,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         // qraw[(n+1)&1] was last used in segment n-1 and kvraw was consumed
         // above: prefetch the next segment's q (and new rows) while this
         // segment streams.
-        if (warp == 0 && q_issued == n + 1 && issue_q(A, S, n + 1, s0, o0, s1, o1, lane)) q_issued = n + 2;
+        if (warp == 0 && q_issued == n + 1 && issue_q<PAGED>(A, S, n + 1, s0, o0, s1, o1, lane)) q_issued = n + 2;
 
         // This lane's query head, its 16-byte chunks in KV-head-rotated order.
         // q and the accumulator as f32x2 pairs: chunk c is pairs 2c (x, y)
@@ -516,7 +644,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
                     record_error(A.err, kErrWaitEmpty);
                     cur.done = true;
                 } else {
-                    cursor_issue(cur, A, S, ps, s1, o1, pol);
+                    cursor_issue<PAGED>(cur, A, S, ps, s1, o1, pol);
                     ++issued;
                 }
             }
@@ -696,9 +824,11 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         }
     }
 
-    // Exit (error path only): every copy the issuer started must land before
-    // the CTA's shared memory is released.
+    // Exit: every copy the issuer started must land before the CTA's shared
+    // memory is released (tiles and q copies remain only on the error path;
+    // a page-id prefetch can remain in paged mode).
     if (issuer) {
+        if (PAGED) cp_async_wait_all();
         for (int t = it; t < issued; ++t)
             if (!mbar_wait(&S.full[t % NSTAGE], (t / NSTAGE) & 1)) { record_error(A.err, kErrDrain); break; }
         for (int m = n; m < q_issued; ++m)
@@ -837,11 +967,31 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     static PerDeviceOnce once;
     const int smem = static_cast<int>(sizeof(DecodeSmem));
     cudaError_t e = once.run([&](int) {
-        return cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t r = cudaFuncSetAttribute(decode_kernel<false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (r != cudaSuccess) return r;
+        return cudaFuncSetAttribute(decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    smem);
     });
     if (e != cudaSuccess) return e;
-    decode_kernel<<<a.n_ctas, NCT, smem, stream>>>(a);
-    e = cudaGetLastError();
+    // Launched as a programmatic dependent of the previous kernel on the
+    // stream: its CTAs may start (barrier init, tensor-memory allocation,
+    // descriptor reads) as the previous grid drains; griddepcontrol.wait in
+    // the kernel orders everything else after that grid.
+    cudaLaunchConfig_t dcfg{};
+    dcfg.gridDim = dim3(a.n_ctas);
+    dcfg.blockDim = dim3(NCT);
+    dcfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    dcfg.stream = stream;
+    cudaLaunchAttribute dattr[1];
+    dattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    dattr[0].val.programmaticStreamSerializationAllowed = 1;
+    dcfg.attrs = dattr;
+    dcfg.numAttrs = 1;
+    if (a.key_pool)
+        e = cudaLaunchKernelEx(&dcfg, decode_kernel<true>, a);
+    else
+        e = cudaLaunchKernelEx(&dcfg, decode_kernel<false>, a);
     if (e != cudaSuccess) return e;
     if (a.n_ctas > 1 && a.seqs == nullptr) {   // batch mode merges inside decode_kernel
         cudaLaunchConfig_t cfg{};

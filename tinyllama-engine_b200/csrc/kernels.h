@@ -37,6 +37,7 @@ struct DescHeader {
 static_assert(sizeof(DescHeader) == 32, "descriptor header is 32 bytes");
 static_assert(sizeof(tle_seq_t) == 24, "tle_seq_t is 24 bytes");
 constexpr int32_t kDescMagic = 0x544c4544;  // "TLED"
+constexpr int32_t kDescMagicPaged = 0x544c4550;  // "TLEP": slots hold {page table, -, n_pages, pos}
 
 // CTA c processes the concatenated rows [cta_start[c], cta_start[c+1]) of the
 // batch, each start given as (sequence, row offset in that sequence).
@@ -82,6 +83,14 @@ struct DecodeArgs {
     int layer;
     int rotate;
     uint32_t* err;               // device error word
+    // Paged batch mode (key_pool != nullptr): each sequence record's
+    // key_cache slot holds its page table (int32 page ids), and row r of a
+    // sequence is row r % page_rows of page pages[r / page_rows] in the pools
+    // [n_layers][pool_pages][page_rows][256], page_rows = 1 << page_shift.
+    float* key_pool;
+    float* value_pool;
+    int pool_pages;
+    int page_shift;
     float inv_freq[kHeadDim / 2];
 };
 

@@ -33,6 +33,7 @@ EXPORTED = (
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
     "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
+    "tle_decode_desc_paged", "tle_decode_batch_paged",
 )
 
 
@@ -53,6 +54,17 @@ class Seq(ctypes.Structure):
     """tle_seq_t: one sequence's device KV cache and decode position."""
     _fields_ = [("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
                 ("n_ctx", ctypes.c_int32), ("pos", ctypes.c_int32)]
+
+
+class PagePool(ctypes.Structure):
+    """tle_page_pool_t: the key/value page pools of a paged batch."""
+    _fields_ = [("key_pool", ctypes.c_void_p), ("value_pool", ctypes.c_void_p),
+                ("n_pages", ctypes.c_int32), ("page_rows", ctypes.c_int32)]
+
+
+class PagedSeq(ctypes.Structure):
+    """tle_paged_seq_t: one sequence's device page table and decode position."""
+    _fields_ = [("pages", ctypes.c_void_p), ("n_pages", ctypes.c_int32), ("pos", ctypes.c_int32)]
 
 
 def tinyllama_shape(n_layers: int = 22) -> Shape:
@@ -93,6 +105,9 @@ def lib() -> ctypes.CDLL:
         L.tle_attention_lse.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), vp, sz, vp]
         L.tle_merge_lse.argtypes = [vp, vp, vp, i, vp]
         L.tle_decode_batch_noalloc.argtypes = [P(Shape), P(Seq), i, vp, vp, vp, vp, i, i, vp]
+        L.tle_decode_desc_paged.argtypes = [P(Shape), P(PagePool), P(PagedSeq), i, i, vp, sz, P(i)]
+        L.tle_decode_batch_paged.argtypes = [P(Shape), P(PagePool), vp, i, i, vp, vp, vp, vp, i, i,
+                                             vp, sz, vp]
         _lib = L
     return _lib
 
@@ -253,6 +268,108 @@ class DecodeBatch:
                                       self.n_ctas, _ptr(q), _ptr(k), _ptr(v), _ptr(out), layer,
                                       1 if rotate else 0, _ptr(self.workspace),
                                       self.workspace.numel() * 4, _stream(stream)))
+
+
+# ------------------------------------------------------- paged KV cache
+class PagedKVCache:
+    """Key/value page pools shared by a batch of sequences.
+
+    The pools are [n_layers][n_pages][page_rows][256] fp32; a sequence's row
+    r lives in row r % page_rows of page ``table[r // page_rows]``.  Page ids
+    are handed out from a free list (``alloc`` / ``free``); the page tables
+    are int32 CUDA tensors the caller keeps per sequence.  The reference keeps
+    one contiguous [n_layers][n_ctx][256] cache per sequence (run_state.h:20-25).
+    """
+
+    def __init__(self, n_pages: int, page_rows: int = 256, shape: Optional[Shape] = None,
+                 device="cuda"):
+        import torch
+        self.shape = shape or tinyllama_shape()
+        self.n_pages = int(n_pages)
+        self.page_rows = int(page_rows)
+        dims = (self.shape.n_layers, self.n_pages, self.page_rows, 256)
+        self.key_pool = torch.zeros(dims, dtype=torch.float32, device=device)
+        self.value_pool = torch.zeros(dims, dtype=torch.float32, device=device)
+        self._free = list(range(self.n_pages - 1, -1, -1))
+
+    def pool(self) -> PagePool:
+        return PagePool(_ptr(self.key_pool), _ptr(self.value_pool), self.n_pages, self.page_rows)
+
+    def pages_for(self, n_rows: int) -> int:
+        return -(-int(n_rows) // self.page_rows)
+
+    def alloc(self, n: int) -> List[int]:
+        if n > len(self._free):
+            raise MemoryError(f"page pool exhausted: {n} pages wanted, {len(self._free)} free")
+        return [self._free.pop() for _ in range(n)]
+
+    def free(self, ids: Iterable[int]) -> None:
+        self._free.extend(int(i) for i in ids)
+
+    def table(self, ids: Sequence[int]):
+        """The device page table for page ids ``ids``."""
+        import torch
+        return torch.tensor(list(ids), dtype=torch.int32, device=self.key_pool.device)
+
+
+class PagedDecodeBatch:
+    """DecodeBatch over a PagedKVCache: ``tables`` holds one int32 CUDA page
+    table per sequence.  Same kernel, split and results as DecodeBatch on the
+    same rows."""
+
+    def __init__(self, cache: PagedKVCache, tables: Sequence, positions: Sequence[int],
+                 max_ctas: int = 0):
+        import torch
+        self.cache = cache
+        self.shape = cache.shape
+        self.tables = list(tables)
+        self.n = len(self.tables)
+        self.max_ctas = max_ctas
+        L = lib()
+        self.desc_bytes = L.tle_decode_desc_bytes(self.n, max_ctas)
+        self._desc_host = torch.empty(self.desc_bytes, dtype=torch.uint8).pin_memory()
+        self._desc_dev = torch.empty(self.desc_bytes, dtype=torch.uint8, device="cuda")
+        self.workspace = None
+        self.n_ctas = 0
+        self.set_positions(positions)
+
+    def build_host(self, positions: Sequence[int]) -> int:
+        import torch
+        if len(positions) != self.n:
+            raise ValueError("one position per sequence")
+        seqs = (PagedSeq * self.n)()
+        for i, t in enumerate(self.tables):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("page tables must be contiguous int32 CUDA tensors")
+            seqs[i] = PagedSeq(_ptr(t), int(t.numel()), int(positions[i]))
+        pool = self.cache.pool()
+        n_ctas = ctypes.c_int(0)
+        _check(lib().tle_decode_desc_paged(ctypes.byref(self.shape), ctypes.byref(pool), seqs,
+                                           self.n, self.max_ctas, self._desc_host.data_ptr(),
+                                           self.desc_bytes, ctypes.byref(n_ctas)))
+        return n_ctas.value
+
+    def set_positions(self, positions: Sequence[int], stream=None) -> None:
+        import torch
+        self.positions = [int(p) for p in positions]
+        self.n_ctas = self.build_host(self.positions)
+        nbytes = lib().tle_decode_workspace_bytes(ctypes.byref(self.shape), self.n, self.n_ctas)
+        if self.workspace is None or self.workspace.numel() * 4 < nbytes:
+            self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device="cuda")
+        s = stream or torch.cuda.current_stream()
+        with torch.cuda.stream(s):
+            self._desc_dev.copy_(self._desc_host, non_blocking=True)
+
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+        n = self.n
+        _want(q, n * 2048, "q"); _want(k, n * 256, "k"); _want(v, n * 256, "v")
+        _want(out, n * 2048, "out")
+        pool = self.cache.pool()
+        _check(lib().tle_decode_batch_paged(ctypes.byref(self.shape), ctypes.byref(pool),
+                                            self._desc_dev.data_ptr(), n, self.n_ctas, _ptr(q),
+                                            _ptr(k), _ptr(v), _ptr(out), layer,
+                                            1 if rotate else 0, _ptr(self.workspace),
+                                            self.workspace.numel() * 4, _stream(stream)))
 
 
 # ------------------------------------------------- decode without allocation
