@@ -476,7 +476,11 @@ def measure_prefill(dev, peaks, steps=10, warmup=3):
 def measure_config4(dev, peaks, steps=20, warmup=3):
     """Config 4: 64 sequences, attended lengths U[128, 2048] (seeded), 22-layer
     fp32 caches; a step is one decode token for every sequence = 22
-    tle_decode_batch calls (3.1 GB of KV, > L2)."""
+    tle_decode_batch calls (3.5 GB of KV, > L2).  Timed twice: with
+    TLE_DECODE_KV_READY (the headline of this line: each call's previous
+    kernel is the decode of another layer, which writes none of the rows the
+    call reads, as the QKV projection before attention does in a forward
+    pass), and in strict order (every read after the previous kernel)."""
     import numpy as np
     import torch
     import tle
@@ -494,19 +498,26 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
     out = torch.zeros((64, QD), device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(st=stream):
-        for l in range(n_layers):
-            batch.run(q, k, v, out, l, True, st)
+    def stepper(kv_ready):
+        def step(st=stream):
+            for l in range(n_layers):
+                batch.run(q, k, v, out, l, True, st, kv_ready=kv_ready)
+        return step
 
-    ms_eager = _time_steps(step, steps, warmup, stream)
-    ms = _time_graph(step, steps, warmup, dev)
+    ms_eager = _time_steps(stepper(False), steps, warmup, stream)
+    ms_strict = _time_graph(stepper(False), steps, warmup, dev)
+    ms = _time_graph(stepper(True), steps, warmup, dev)
     kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
     gbs = kv_bytes / (ms / 1e3) / 1e9
+    gbs_strict = kv_bytes / (ms_strict / 1e3) / 1e9
     return {"workload": "config4: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step "
-                        "(CUDA graph of the 22 tle_decode_batch calls)" % int(lengths.sum()),
+                        "(CUDA graph of the 22 tle_decode_batch calls, TLE_DECODE_KV_READY)"
+                        % int(lengths.sum()),
             "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
             "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
-            "ms_per_step_eager": round(ms_eager, 4),
+            "strict_order": {"ms_per_step": round(ms_strict, 4), "value": round(gbs_strict, 1),
+                             "frac": round(gbs_strict / peaks["hbm_gbs"], 4)},
+            "ms_per_step_eager_strict": round(ms_eager, 4),
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
@@ -560,7 +571,8 @@ def measure_paged5(dev, peaks, steps=10, warmup=3, page_rows=256, shuffle=True):
 def measure_paged4(dev, peaks, steps=20, warmup=3, page_rows=256, shuffle=True):
     """Config 4 on a paged cache: 64 sequences, lengths U[128, 2048] (the same
     seeded lengths as the contiguous line), 22 layers, 256-row pages; a step
-    is 22 tle_decode_batch_paged calls in one CUDA graph."""
+    is 22 tle_decode_batch_paged calls in one CUDA graph, timed with
+    TLE_DECODE_KV_READY and in strict order like the contiguous line."""
     import numpy as np
     import torch
     n_layers = 22
@@ -568,19 +580,24 @@ def measure_paged4(dev, peaks, steps=20, warmup=3, page_rows=256, shuffle=True):
     cache, batch, q, k, v, out = _paged_setup(dev, lengths, n_layers, page_rows, 44, shuffle)
     stream = torch.cuda.current_stream(dev)
 
-    def step(st=stream):
-        for l in range(n_layers):
-            batch.run(q, k, v, out, l, True, st)
+    def stepper(kv_ready):
+        def step(st=stream):
+            for l in range(n_layers):
+                batch.run(q, k, v, out, l, True, st, kv_ready=kv_ready)
+        return step
 
-    ms = _time_graph(step, steps, warmup, dev)
+    ms_strict = _time_graph(stepper(False), steps, warmup, dev)
+    ms = _time_graph(stepper(True), steps, warmup, dev)
     kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
     gbs = kv_bytes / (ms / 1e3) / 1e9
     del cache
     return {"workload": "config4 paged: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step, "
-                        "%d-row pages (CUDA graph of the 22 tle_decode_batch_paged calls)"
-                        % (int(lengths.sum()), page_rows),
+                        "%d-row pages (CUDA graph of the 22 tle_decode_batch_paged calls, "
+                        "TLE_DECODE_KV_READY)" % (int(lengths.sum()), page_rows),
             "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
             "tok_s": round(64 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+            "strict_order": {"ms_per_step": round(ms_strict, 4),
+                             "value": round(kv_bytes / (ms_strict / 1e3) / 1e9, 1)},
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},

@@ -125,14 +125,27 @@ int tle_decode_desc(const tle_shape_t* shape, const tle_seq_t* seqs, int n_seqs,
 /* Workspace for tle_decode_batch. */
 size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ctas);
 
+/* Flags of tle_decode_batch / tle_decode_batch_paged (a 0/1 `rotate` value
+ * from older callers keeps its meaning). */
+#define TLE_DECODE_ROTATE 1   /* rope(q_s, k_s, pos_s) before attending            */
+/* The caller guarantees that the kernel launched just before this call on
+ * the stream wrote none of the cached rows this call reads (rows < pos_s)
+ * and no page table: the decode kernel then starts streaming them while
+ * that kernel finishes (programmatic dependent launch), and waits for it
+ * only before reading q/k/v and writing anything.  Holds in a forward pass,
+ * where the previous kernel is the QKV projection; does not hold for a
+ * prefill of the same layer issued just before on the same stream. */
+#define TLE_DECODE_KV_READY 2
+
 /* One decode step of layer `layer` for every sequence in the descriptor:
  * per sequence s, with q [n_seqs][n_head*hd], k/v [n_seqs][n_head_kv*hd]:
- * if rotate, rope(q_s, k_s, pos_s) (not written back); append k_s, v_s at
- * row pos_s; out_s = attention over rows 0..pos_s.  desc_dev is the device
- * copy of the tle_decode_desc() output. */
+ * if flags & TLE_DECODE_ROTATE, rope(q_s, k_s, pos_s) (not written back);
+ * append k_s, v_s at row pos_s; out_s = attention over rows 0..pos_s.
+ * desc_dev is the device copy of the tle_decode_desc() output.  Unknown
+ * flag bits are rejected with TLE_ERR_INVALID. */
 int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
                      const float* q, const float* k, const float* v, float* out, int layer,
-                     int rotate, void* workspace, size_t workspace_bytes, void* stream);
+                     int flags, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- batched decode over a paged KV cache ----
  * No counterpart in the reference: run_state.h:20-25 sizes one contiguous
@@ -175,7 +188,7 @@ int tle_decode_desc_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
  * for tle_decode_batch (tle_decode_workspace_bytes). */
 int tle_decode_batch_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
                            const void* desc_dev, int n_seqs, int n_ctas, const float* q,
-                           const float* k, const float* v, float* out, int layer, int rotate,
+                           const float* k, const float* v, float* out, int layer, int flags,
                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- decode without allocation ----

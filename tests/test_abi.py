@@ -204,3 +204,12 @@ def test_paged_desc_rejects_bad_arguments(page_rows, n_pages, pos, table, what):
 def test_paged_desc_rejects_empty_pool():
     rc, _, _ = build_desc_paged([3], [1], 32, 8, pool_pages=0)
     assert rc == tle.TLE_ERR_INVALID
+
+
+def test_decode_batch_rejects_unknown_flags():
+    # checked before any device work: fake (aligned, never dereferenced) pointers
+    shape = tle.tinyllama_shape()
+    p = 0x100000
+    rc = tle.lib().tle_decode_batch(ctypes.byref(shape), p, 1, 1, p, p, p, p, 0, 4, p, 1 << 20, None)
+    assert rc == tle.TLE_ERR_INVALID
+    assert "flags" in tle.lib().tle_last_error().decode()

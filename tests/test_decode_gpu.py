@@ -361,3 +361,36 @@ def test_many_short_sequences_per_cta(cuda):
     err, n_ctas = run_batch_case(lengths, n_layers=1, layer=0, max_ctas=0, seed=77, check=check)
     assert n_ctas >= 100
     assert err <= ATOL, err
+
+
+def test_kv_ready_flag_gives_identical_results(cuda):
+    """TLE_DECODE_KV_READY only moves the first tile copies before the wait
+    on the previous kernel: two back-to-back layers decoded with it (the
+    previous kernel writes a different layer) give bit-identical outputs and
+    appended rows to the strict ordering."""
+    import torch
+    import tle
+    rng = np.random.default_rng(31)
+    lengths = [3000, 17, 900, 2500, 64, 1, 1500]
+    n = len(lengths)
+    caches = []
+    for L in lengths:
+        kc = dev(rng.standard_normal((2, L + 3, KVD), dtype=np.float32))
+        vc = dev(rng.standard_normal((2, L + 3, KVD), dtype=np.float32))
+        caches.append((kc, vc, L + 3))
+    pos = [L - 1 for L in lengths]
+    batch = tle.DecodeBatch(caches, pos, tle.tinyllama_shape(2), 60)
+    q = [dev(rng.standard_normal((n, QD), dtype=np.float32)) for _ in range(2)]
+    k = [dev(rng.standard_normal((n, KVD), dtype=np.float32)) for _ in range(2)]
+    v = [dev(rng.standard_normal((n, KVD), dtype=np.float32)) for _ in range(2)]
+    res = {}
+    for kvr in (False, True, False):
+        outs = [torch.full((n, QD), float("nan"), device="cuda") for _ in range(2)]
+        for layer in range(2):
+            batch.run(q[layer], k[layer], v[layer], outs[layer], layer, True, kv_ready=kvr)
+        res.setdefault(kvr, []).append([host(o) for o in outs])
+    assert tle.device_error() == 0
+    base = res[False][0]
+    assert np.all(np.isfinite(base[0])) and np.all(np.isfinite(base[1]))
+    for got in res[True] + res[False][1:]:
+        assert np.array_equal(got[0], base[0]) and np.array_equal(got[1], base[1])

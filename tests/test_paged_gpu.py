@@ -233,3 +233,22 @@ def test_bad_page_id_is_reported_not_dereferenced(cuda):
     _, _, _, a, b, _ = run_both(case2, 0, 0)
     assert tle.device_error() == 0
     assert np.array_equal(a, b)
+
+
+def test_paged_kv_ready_flag_gives_identical_results(cuda):
+    """Paged decode with TLE_DECODE_KV_READY (first tiles and page-table
+    reads before the wait on the previous kernel) equals the strict order."""
+    import torch
+    import tle
+    case = PagedCase([700, 3000, 90, 1, 257], 2, 64, seed=17)
+    _, _, _, (dq, dk, dv) = case.inputs()
+    paged = tle.PagedDecodeBatch(case.pc, case.tables, case.pos, 40)
+    got = {}
+    for kvr in (False, True):
+        outs = [torch.empty((case.n, QD), device="cuda") for _ in range(2)]
+        for layer in range(2):
+            paged.run(dq, dk, dv, outs[layer], layer, kv_ready=kvr)
+        got[kvr] = [host(o) for o in outs]
+    assert tle.device_error() == 0
+    assert np.all(np.isfinite(got[False][0]))
+    assert np.array_equal(got[False][0], got[True][0]) and np.array_equal(got[False][1], got[True][1])

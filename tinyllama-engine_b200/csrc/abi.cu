@@ -296,7 +296,7 @@ int check_pool(const tle_shape_t* shape, const tle_page_pool_t* pool, int* shift
 
 // Fills the kernel arguments shared by the contiguous and paged batch calls.
 int batch_args(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas, const float* q,
-               const float* k, const float* v, float* out, int layer, int rotate, void* workspace,
+               const float* k, const float* v, float* out, int layer, int flags, void* workspace,
                size_t workspace_bytes, tle::DecodeArgs& a) {
     if (int rc = check_shape(shape)) return rc;
     if (!desc_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer argument");
@@ -323,8 +323,11 @@ int batch_args(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n
     a.v = v;
     a.out = out;
     a.partials = static_cast<float*>(workspace);
+    if (flags & ~(TLE_DECODE_ROTATE | TLE_DECODE_KV_READY))
+        return set_error(TLE_ERR_INVALID, "unknown decode flags 0x%x", flags);
     a.layer = layer;
-    a.rotate = rotate ? 1 : 0;
+    a.rotate = (flags & TLE_DECODE_ROTATE) ? 1 : 0;
+    a.kv_ready = (flags & TLE_DECODE_KV_READY) ? 1 : 0;
     fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
     cudaError_t e = tle::error_word(&a.err);
     if (e != cudaSuccess) return cuda_error(e, "device error word");
@@ -387,10 +390,10 @@ size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ct
 }
 
 int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int n_ctas,
-                     const float* q, const float* k, const float* v, float* out, int layer, int rotate,
+                     const float* q, const float* k, const float* v, float* out, int layer, int flags,
                      void* workspace, size_t workspace_bytes, void* stream) {
     tle::DecodeArgs a;
-    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, rotate, workspace,
+    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, flags, workspace,
                             workspace_bytes, a))
         return rc;
     cudaError_t e = tle::launch_decode(a, static_cast<cudaStream_t>(stream));
@@ -400,10 +403,10 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
 
 int tle_decode_batch_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
                            const void* desc_dev, int n_seqs, int n_ctas, const float* q,
-                           const float* k, const float* v, float* out, int layer, int rotate,
+                           const float* k, const float* v, float* out, int layer, int flags,
                            void* workspace, size_t workspace_bytes, void* stream) {
     tle::DecodeArgs a;
-    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, rotate, workspace,
+    if (int rc = batch_args(shape, desc_dev, n_seqs, n_ctas, q, k, v, out, layer, flags, workspace,
                             workspace_bytes, a))
         return rc;
     int shift = 0;

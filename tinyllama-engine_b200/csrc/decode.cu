@@ -493,9 +493,12 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
     // memory.  Up to here only the descriptor is read, which the host wrote
     // before the launch; everything else (q/k/v, the caches, page tables,
     // outputs, partials, arrival counts) may belong to the previous kernel
-    // on the stream, so it is touched only after griddepcontrol.wait.  Then
-    // warp 0 starts segment 0's q copy and thread 0 the first NSTAGE tiles;
-    // the other warps touch none of it before the __syncthreads below.
+    // on the stream, so it is touched only after griddepcontrol.wait --
+    // except with kv_ready, where the caller guarantees that the previous
+    // kernel wrote no cached row this launch reads and no page table: the
+    // first NSTAGE tiles are then streamed while that kernel drains.  Then
+    // warp 0 starts segment 0's q copy (and thread 0 the first tiles); the
+    // other warps touch none of it before the __syncthreads below.
     TileCursor cur;
     uint64_t pol = 0;
     int issued = 0;
@@ -510,23 +513,32 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         mbar_init(&S.csync, NCW);
         fence_barrier_init();
         cur.slot = 0;
-        cursor_load<PAGED>(cur, A, S, s0, o0, s1, o1, /*table=*/false);
+        cursor_load<PAGED>(cur, A, S, s0, o0, s1, o1, /*table=*/A.kv_ready != 0);
+        pol = l2_evict_first_policy();
     }
     if (warp == 1) {
         tmem_alloc(&S.tmem_base, kTmemCols);
         tmem_relinquish();
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (warp == 0) {
-        __syncwarp();
+    if (!A.kv_ready) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (warp == 0) {
+            __syncwarp();
+            if (issue_q<PAGED>(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
+        }
         if (PAGED && issuer) cursor_prefetch(cur, A, S);
-        if (issue_q<PAGED>(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
-        if (issuer) {
-            pol = l2_evict_first_policy();
-            while (!cur.done && issued < NSTAGE) {
-                cursor_issue<PAGED>(cur, A, S, issued, s1, o1, pol);
-                ++issued;
-            }
+    }
+    if (issuer) {
+        while (!cur.done && issued < NSTAGE) {
+            cursor_issue<PAGED>(cur, A, S, issued, s1, o1, pol);
+            ++issued;
+        }
+    }
+    if (A.kv_ready) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (warp == 0) {
+            __syncwarp();
+            if (issue_q<PAGED>(A, S, 0, s0, o0, s1, o1, lane)) q_issued = 1;
         }
     }
     tc_fence_before();

@@ -82,6 +82,7 @@ struct DecodeArgs {
     float* lse;                  // single mode, optional: [32] log-sum-exp of each head's scores
     int layer;
     int rotate;
+    int kv_ready;                // batch mode: stream the first tiles before waiting on the previous grid
     uint32_t* err;               // device error word
     // Paged batch mode (key_pool != nullptr): each sequence record's
     // key_cache slot holds its page table (int32 page ids), and row r of a

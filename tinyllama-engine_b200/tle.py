@@ -26,6 +26,13 @@ TLE_ERR_WORKSPACE = 3
 TLE_ERR_CUDA = 4
 TLE_ERR_DEVICE = 5
 
+TLE_DECODE_ROTATE = 1
+TLE_DECODE_KV_READY = 2
+
+
+def _decode_flags(rotate: bool, kv_ready: bool) -> int:
+    return (TLE_DECODE_ROTATE if rotate else 0) | (TLE_DECODE_KV_READY if kv_ready else 0)
+
 # Every symbol include/tle_attn.h declares (tests check the .so exports them).
 EXPORTED = (
     "tle_last_error", "tle_version", "tle_rope", "tle_attention_workspace_bytes",
@@ -260,13 +267,16 @@ class DecodeBatch:
         with torch.cuda.stream(s):
             self._desc_dev.copy_(self._desc_host, non_blocking=True)
 
-    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None,
+            kv_ready: bool = False) -> None:
+        """kv_ready: TLE_DECODE_KV_READY (the previous kernel on the stream
+        wrote none of the cached rows read here)."""
         n = self.n
         _want(q, n * 2048, "q"); _want(k, n * 256, "k"); _want(v, n * 256, "v")
         _want(out, n * 2048, "out")
         _check(lib().tle_decode_batch(ctypes.byref(self.shape), self._desc_dev.data_ptr(), n,
                                       self.n_ctas, _ptr(q), _ptr(k), _ptr(v), _ptr(out), layer,
-                                      1 if rotate else 0, _ptr(self.workspace),
+                                      _decode_flags(rotate, kv_ready), _ptr(self.workspace),
                                       self.workspace.numel() * 4, _stream(stream)))
 
 
@@ -360,7 +370,8 @@ class PagedDecodeBatch:
         with torch.cuda.stream(s):
             self._desc_dev.copy_(self._desc_host, non_blocking=True)
 
-    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None,
+            kv_ready: bool = False) -> None:
         n = self.n
         _want(q, n * 2048, "q"); _want(k, n * 256, "k"); _want(v, n * 256, "v")
         _want(out, n * 2048, "out")
@@ -368,7 +379,7 @@ class PagedDecodeBatch:
         _check(lib().tle_decode_batch_paged(ctypes.byref(self.shape), ctypes.byref(pool),
                                             self._desc_dev.data_ptr(), n, self.n_ctas, _ptr(q),
                                             _ptr(k), _ptr(v), _ptr(out), layer,
-                                            1 if rotate else 0, _ptr(self.workspace),
+                                            _decode_flags(rotate, kv_ready), _ptr(self.workspace),
                                             self.workspace.numel() * 4, _stream(stream)))
 
 
