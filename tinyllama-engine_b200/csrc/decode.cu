@@ -73,6 +73,7 @@ struct __align__(128) DecodeSmem {
     float mlA[2 * NH];
     int32_t apage[2];           // paged mode: page id of row pos of the segment's sequence
     int32_t npage[2];           // paged mode: the issuer's prefetched next page ids (ring)
+    const int32_t* cur_pages;   // paged mode: page table of the issuer's current sequence
     uint32_t tmem_base;
     uint64_t full[NSTAGE];
     uint64_t empty[NSTAGE];
@@ -104,20 +105,24 @@ __device__ __forceinline__ bool in_range(int s, int off, int s1, int o1) {
 }
 
 // The copy issuer's position in the CTA's sequence of tiles (it runs up to
-// NSTAGE tiles ahead of the consumers).  Paged mode keeps the id of the page
-// being read (cpi, cid) and prefetches the id of the page after it (npi)
-// when the cursor enters a page: a 4-byte cp.async into npage[slot], so the
-// table read is in flight for a page's worth of tiles and no register waits
-// on it (the issuer is also a consumer thread: a load it waits on stalls its
-// warp and, through the stage barriers, the CTA).
+// NSTAGE tiles ahead of the consumers).  kb/vb: K and V bases such that row
+// r of the sequence is at kb + 256 r (paged mode: valid while r is in page
+// cpi).  Paged mode keeps the index of the page being read (cpi) and
+// prefetches the id of the page after it when the
+// cursor enters a page: a 4-byte cp.async into npage[slot], so the table
+// read is in flight for a page's worth of tiles and no register waits on it
+// (the issuer is also a consumer thread: a load it waits on stalls its warp
+// and, through the stage barriers, the CTA).  pst bit 0: a prefetch of page
+// cpi + 1 is pending; bit 1: its slot.  The page-table pointer itself sits
+// in shared memory (read at page switches only): every register the cursor
+// holds is live through the consumer loop of a kernel at the register limit.
 struct TileCursor {
     int s, ta, b;
     bool done;
     const float* kb;
     const float* vb;
     int pos;
-    const int32_t* pages;
-    int cpi, cid, npi, slot;
+    int cpi, pst;
 };
 
 // Paged mode: a sequence record's key_cache slot holds its page table (the
@@ -146,30 +151,44 @@ __device__ __forceinline__ int check_page(const DecodeArgs& A, int id) {
 // prefetch.  Rows below min(b, pos) are the only ones read, so the prefetch
 // never reads past the entries the host checked (n_pages * page_rows > pos).
 __device__ __forceinline__ int cursor_page(TileCursor& c, const DecodeArgs& A, DecodeSmem& S, int pi) {
-    if (pi == c.cpi) return c.cid;
+    if (pi == c.cpi) return 0;
+    const int32_t* pages = S.cur_pages;
     int id;
-    if (pi == c.npi) {
+    if ((c.pst & 1) && pi == c.cpi + 1) {
         cp_async_wait_all();
-        id = S.npage[c.slot];
-        c.slot ^= 1;          // the next prefetch goes to the other slot
+        id = S.npage[c.pst >> 1];
+        c.pst ^= 2;           // the next prefetch goes to the other slot
     } else {
-        id = __ldg(c.pages + pi);
+        if (c.pst & 1) cp_async_wait_all();   // an unused prefetch must land before its slot is reused
+        id = __ldg(pages + pi);
     }
-    c.cid = check_page(A, id);
-    c.cpi = pi;
-    c.npi = -1;
+    c.pst &= ~1;
+    id = check_page(A, id);
+    // A bad page is never made current, so no tile takes the fast path on it.
+    c.cpi = id >= 0 ? pi : INT_MIN;
+    if (id >= 0) {
+        // bases such that kb + r * 256 is row r of the sequence while r is
+        // in page pi (the offset of page pi's row 0 minus pi's first row)
+        const size_t o = pool_row(A, id, 0) - (static_cast<size_t>(pi) << A.page_shift) * ROWF;
+        c.kb = A.key_pool + o;
+        c.vb = A.value_pool + o;
+    }
     if (((pi + 1) << A.page_shift) < min(c.b, c.pos)) {
-        c.npi = pi + 1;
-        cp_async_4(&S.npage[c.slot], c.pages + pi + 1);
+        cp_async_4(&S.npage[c.pst >> 1], pages + pi + 1);
+        c.pst |= 1;
     }
-    return c.cid;
+    return id;
 }
 
 // Paged mode: starts the page-table read of the cursor's first page.
+// (The first page is announced as "the page after cpi"; tiles only move
+// forward from ta, so page cpi itself is never asked for.)
 __device__ __forceinline__ void cursor_prefetch(TileCursor& c, const DecodeArgs& A, DecodeSmem& S) {
     if (!c.done && c.ta < min(c.b, c.pos)) {
-        c.npi = c.ta >> A.page_shift;
-        cp_async_4(&S.npage[c.slot], c.pages + c.npi);
+        const int first = c.ta >> A.page_shift;
+        c.cpi = first - 1;
+        cp_async_4(&S.npage[c.pst >> 1], S.cur_pages + first);
+        c.pst |= 1;
     }
 }
 
@@ -188,9 +207,9 @@ __device__ __forceinline__ void cursor_load(TileCursor& c, const DecodeArgs& A, 
         c.b = (s == s1) ? o1 : sq.pos + 1;
         c.pos = sq.pos;
         if (PAGED) {
-            c.pages = seq_pages(sq);
-            c.cpi = -1;
-            c.npi = -1;
+            S.cur_pages = seq_pages(sq);
+            c.cpi = INT_MIN;   // no page yet (pages are >= 0, so cpi + 1 matches none)
+            c.pst &= ~1;
             if (table) cursor_prefetch(c, A, S);
         } else {
             const size_t base = (static_cast<size_t>(A.layer) * sq.n_ctx) * ROWF;
@@ -214,16 +233,21 @@ __device__ __forceinline__ void cursor_issue(TileCursor& c, const DecodeArgs& A,
     if (n > 0) {
         const uint32_t bytes = static_cast<uint32_t>(n) * ROWB;
         mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
-        if (PAGED) {
+        // Paged mode: a tile inside the current (valid) page is issued like a
+        // contiguous one, from the page-relative bases kb/vb; a tile that
+        // enters a new page goes piece by piece (one per page it touches).
+        const bool whole_page = !PAGED || ((c.ta >> A.page_shift) == c.cpi &&
+                                           ((te - 1) >> A.page_shift) == c.cpi);
+        if (!whole_page) {
             for (int r = c.ta; r < te;) {
                 const int pi = r >> A.page_shift;
                 const int e = min(te, (pi + 1) << A.page_shift);
                 const uint32_t pb = static_cast<uint32_t>(e - r) * ROWB;
-                const int id = cursor_page(c, A, S, pi);
-                if (id >= 0) {
-                    const size_t o = pool_row(A, id, r);
-                    bulk_g2s(S.k[st] + (r - c.ta) * ROWF, A.key_pool + o, pb, &S.full[st], pol);
-                    bulk_g2s(S.v[st] + (r - c.ta) * ROWF, A.value_pool + o, pb, &S.full[st], pol);
+                if (cursor_page(c, A, S, pi) >= 0) {
+                    bulk_g2s(S.k[st] + (r - c.ta) * ROWF, c.kb + static_cast<size_t>(r) * ROWF, pb,
+                             &S.full[st], pol);
+                    bulk_g2s(S.v[st] + (r - c.ta) * ROWF, c.vb + static_cast<size_t>(r) * ROWF, pb,
+                             &S.full[st], pol);
                 } else {
                     // bad page id (reported): the stage completes without
                     // this piece, its rows keep stale contents
@@ -512,7 +536,7 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
         mbar_init(&S.qfull[1], 1);
         mbar_init(&S.csync, NCW);
         fence_barrier_init();
-        cur.slot = 0;
+        cur.pst = 0;
         cursor_load<PAGED>(cur, A, S, s0, o0, s1, o1, /*table=*/A.kv_ready != 0);
         pol = l2_evict_first_policy();
     }
