@@ -128,13 +128,17 @@ size_t tle_decode_workspace_bytes(const tle_shape_t* shape, int n_seqs, int n_ct
 /* Flags of tle_decode_batch / tle_decode_batch_paged (a 0/1 `rotate` value
  * from older callers keeps its meaning). */
 #define TLE_DECODE_ROTATE 1   /* rope(q_s, k_s, pos_s) before attending            */
-/* The caller guarantees that the kernel launched just before this call on
- * the stream wrote none of the cached rows this call reads (rows < pos_s)
- * and no page table: the decode kernel then starts streaming them while
- * that kernel finishes (programmatic dependent launch), and waits for it
- * only before reading q/k/v and writing anything.  Holds in a forward pass,
- * where the previous kernel is the QKV projection; does not hold for a
- * prefill of the same layer issued just before on the same stream. */
+/* The caller guarantees that no kernel that may still be running when this
+ * call's kernel starts writes the cached rows this call reads (rows < pos_s)
+ * or a page table.  Under programmatic dependent launch that is the kernel
+ * launched just before this call and, in a chain of such launches, the ones
+ * before it that have not finished.  The decode kernel then starts streaming
+ * those rows while the previous kernels finish, and waits for them only
+ * before reading q/k/v and writing anything.  Holds in a forward pass (the
+ * kernels in flight are the projections and other layers' calls; a layer's
+ * rows < pos are written only by that layer's call of an earlier token) and
+ * in a loop over layers; does not hold for a prefill of the same layer
+ * issued just before on the same stream. */
 #define TLE_DECODE_KV_READY 2
 
 /* One decode step of layer `layer` for every sequence in the descriptor:
