@@ -14,6 +14,7 @@
 #include <thread>
 #include <vector>
 
+#include "fw_model.h"
 #include "ops.h"
 
 namespace {
@@ -98,6 +99,93 @@ void ref_decode_batch(int n_seqs, float* const* key_caches, float* const* value_
     for (int t = 1; t < n_threads; t++) th.emplace_back(worker);
     worker();
     for (auto& t : th) t.join();
+}
+
+// ---- the forward pass around attention (ops.h:39-143, 232-249) ----
+
+// ops.h:39
+float ref_fp16_to_f32(std::uint16_t h) { return fp16_to_f32(h); }
+
+// ops.h:64-66 (matmul throws on an unsupported type: -1 here)
+int ref_matmul(float* out, const void* W, const float* x, int rows, int cols, int type) {
+    try {
+        matmul(out, W, x, rows, cols, static_cast<ggml_type>(type));
+    } catch (...) {
+        return -1;
+    }
+    return 0;
+}
+
+// ops.h:95-96, 118, 130, 143
+void ref_rmsnorm(float* out, const float* x, const float* weight, int size, float eps) {
+    rmsnorm(out, x, weight, size, eps);
+}
+void ref_silu(float* x, int size) { silu(x, size); }
+void ref_elementwise_mul(float* a, const float* b, int size) { elementwise_mul(a, b, size); }
+void ref_vec_add(float* out, const float* x, int size) { vec_add(out, x, size); }
+
+// ops.h:232-235
+int ref_ffn_swiglu(float* out, const float* input, float* hb, float* hb2, const void* W_gate,
+                   const void* W_up, const void* W_down, int n_ff, int n_embd, int type) {
+    try {
+        ffn_swiglu(out, input, hb, hb2, W_gate, W_up, W_down, n_ff, n_embd,
+                   static_cast<ggml_type>(type));
+    } catch (...) {
+        return -1;
+    }
+    return 0;
+}
+
+// ops.h:249
+int ref_sample_argmax(const float* logits, int n_vocab) { return sample_argmax(logits, n_vocab); }
+
+void ref_set_num_threads(int n) { set_num_threads(n); }
+
+// forward() (src/forward.cpp:178-265) composed from the reference's own ops
+// in the same order, for one token at position pos.  The embedding lookup is
+// embed_token() (forward.cpp:35-60, static there) for F16/F32 tables through
+// the reference's fp16_to_f32.  Returns -1 on an unsupported format.
+int ref_forward(const fw_model_t* m, fw_state_t* s, int token, int pos) {
+    const int n_embd = m->n_embd, hd = m->n_embd / m->n_head, kv_dim = m->n_head_kv * hd;
+    llama_config_t cfg = make_cfg(m->n_layers, m->n_head, m->n_head_kv, hd, m->n_ctx,
+                                  m->rope_freq_base);
+    cfg.n_ff = static_cast<std::uint32_t>(m->n_ff);
+    cfg.n_vocab = static_cast<std::uint32_t>(m->n_vocab);
+    cfg.rms_norm_eps = m->rms_norm_eps;
+    try {
+        if (m->token_embd.type == 1) {
+            const auto* row = static_cast<const std::uint16_t*>(m->token_embd.data) +
+                              static_cast<size_t>(token) * n_embd;
+            for (int i = 0; i < n_embd; i++) s->x[i] = fp16_to_f32(row[i]);
+        } else if (m->token_embd.type == 0) {
+            const auto* row = static_cast<const float*>(m->token_embd.data) +
+                              static_cast<size_t>(token) * n_embd;
+            for (int i = 0; i < n_embd; i++) s->x[i] = row[i];
+        } else {
+            return -1;
+        }
+        for (int l = 0; l < m->n_layers; l++) {
+            const fw_layer_t& L = m->layers[l];
+            rmsnorm(s->xb, s->x, L.attn_norm, n_embd, cfg.rms_norm_eps);
+            matmul(s->q, L.wq.data, s->xb, n_embd, n_embd, static_cast<ggml_type>(L.wq.type));
+            matmul(s->k, L.wk.data, s->xb, kv_dim, n_embd, static_cast<ggml_type>(L.wk.type));
+            matmul(s->v, L.wv.data, s->xb, kv_dim, n_embd, static_cast<ggml_type>(L.wv.type));
+            rope(s->q, s->k, pos, hd, m->n_head, m->n_head_kv, cfg.rope_freq_base);
+            attention(s->xb2, s->q, s->k, s->v, s->key_cache, s->value_cache, s->att, l, pos, cfg);
+            matmul(s->xb, L.wo.data, s->xb2, n_embd, n_embd, static_cast<ggml_type>(L.wo.type));
+            vec_add(s->x, s->xb, n_embd);
+            rmsnorm(s->xb, s->x, L.ffn_norm, n_embd, cfg.rms_norm_eps);
+            ffn_swiglu(s->xb2, s->xb, s->hb, s->hb2, L.w_gate.data, L.w_up.data, L.w_down.data,
+                       m->n_ff, n_embd, static_cast<ggml_type>(L.w_gate.type));
+            vec_add(s->x, s->xb2, n_embd);
+        }
+        rmsnorm(s->x, s->x, m->output_norm, n_embd, cfg.rms_norm_eps);
+        const fw_weight_t& w = m->output.data ? m->output : m->token_embd;
+        matmul(s->logits, w.data, s->x, m->n_vocab, n_embd, static_cast<ggml_type>(w.type));
+    } catch (...) {
+        return -1;
+    }
+    return 0;
 }
 
 }  // extern "C"

@@ -14,7 +14,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def header_functions():
-    text = open(os.path.join(ROOT, "include", "tle_attn.h")).read()
+    text = "".join(open(os.path.join(ROOT, "include", h)).read()
+                   for h in ("tle_attn.h", "tle_forward.h"))
     return sorted(set(re.findall(r"\b(tle_[a-z_]+)\s*\(", text)))
 
 
@@ -34,7 +35,8 @@ def test_header_compiles_as_c():
     with tempfile.TemporaryDirectory() as d:
         src = os.path.join(d, "t.c")
         with open(src, "w") as f:
-            f.write('#include "tle_attn.h"\nint main(void){tle_shape_t s; (void)s; return 0;}\n')
+            f.write('#include "tle_attn.h"\n#include "tle_forward.h"\n'
+                    'int main(void){tle_shape_t s; tle_model_t m; (void)s; (void)m; return 0;}\n')
         r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
                             src, "-c", "-o", os.path.join(d, "t.o")], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr

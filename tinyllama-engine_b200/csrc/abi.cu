@@ -14,6 +14,7 @@
 
 #include "kernels.h"
 #include "tle_attn.h"
+#include "tle_forward.h"
 
 namespace {
 
@@ -635,3 +636,190 @@ extern "C" int tle_decode_batch_noalloc(const tle_shape_t* shape, const tle_seq_
     if (e != cudaSuccess) return cuda_error(e, "decode launch");
     return ok();
 }
+
+// ===================== forward pass around attention (tle_forward.h) =====================
+
+namespace {
+
+int check_weight(const void* W, int type, int cols, int* row_bytes, const char* what) {
+    if (!W || !aligned16(W)) return set_error(TLE_ERR_INVALID, "%s: weights must be non-null and 16-byte aligned", what);
+    if (cols <= 0 || cols > tle::kGemvMaxCols)
+        return set_error(TLE_ERR_UNSUPPORTED, "%s: cols %d outside [1, %d]", what, cols, tle::kGemvMaxCols);
+    const int rb = tle::weight_row_bytes(type, cols);
+    if (rb < 0) return set_error(TLE_ERR_UNSUPPORTED, "%s: weight type %d with %d cols is not supported", what, type, cols);
+    *row_bytes = rb;
+    return 0;
+}
+
+// Rows per warp: enough CTAs for two per SM on small matrices, fewer and
+// longer CTAs on big ones (the LM head), where each CTA's input staging
+// (and RMSNorm) is amortised over more rows.
+int rows_per_warp(int rows) {
+    const int per = rows / (2 * std::max(sm_count(), 1) * 8);
+    return std::max(1, std::min(8, per));
+}
+
+int gemv(int type, int epi, const tle::GemvSeg* segs, int n_seg, const uint8_t* W2, int cols,
+         const float* x, const float* norm_w, float eps, cudaStream_t st, const char* what) {
+    int rb = 0;
+    if (int rc = check_weight(segs[0].W, type, cols, &rb, what)) return rc;
+    tle::GemvArgs a{};
+    int rows = 0;
+    for (int i = 0; i < n_seg; ++i) {
+        a.seg[i] = segs[i];
+        rows += segs[i].rows;
+    }
+    a.n_seg = n_seg;
+    a.W2 = W2;
+    a.cols = cols;
+    a.row_bytes = rb;
+    a.rpw = rows_per_warp(rows);
+    a.x = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    cudaError_t e = tle::launch_gemv(type, epi, a, st);
+    if (e != cudaSuccess) return cuda_error(e, what);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tle_matmul(float* out, const void* W, const float* x, int rows, int cols, int type, void* stream) {
+    if (!out || !x) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (rows <= 0) return set_error(TLE_ERR_INVALID, "rows %d <= 0", rows);
+    tle::GemvSeg seg{static_cast<const uint8_t*>(W), out, rows, 0};
+    if (int rc = gemv(type, tle::kEpiStore, &seg, 1, nullptr, cols, x, nullptr, 0.f,
+                      static_cast<cudaStream_t>(stream), "matmul"))
+        return rc;
+    return ok();
+}
+
+int tle_rmsnorm(float* out, const float* x, const float* weight, int size, float eps, void* stream) {
+    if (!out || !x || !weight) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (size <= 0) return set_error(TLE_ERR_INVALID, "size %d <= 0", size);
+    cudaError_t e = tle::launch_rmsnorm(out, x, weight, size, eps, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "rmsnorm");
+    return ok();
+}
+
+int tle_vec_add(float* out, const float* x, int size, void* stream) {
+    if (!out || !x) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (size <= 0) return set_error(TLE_ERR_INVALID, "size %d <= 0", size);
+    cudaError_t e = tle::launch_vec_add(out, x, size, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "vec_add");
+    return ok();
+}
+
+int tle_ffn_swiglu(float* out, const float* input, float* hb, float* hb2, const void* W_gate,
+                   const void* W_up, const void* W_down, int n_ff, int n_embd, int type,
+                   void* stream) {
+    (void)hb2;
+    if (!out || !input || !hb || !W_up) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (n_ff <= 0 || n_embd <= 0) return set_error(TLE_ERR_INVALID, "bad n_ff/n_embd (%d, %d)", n_ff, n_embd);
+    int rb = 0;
+    if (int rc = check_weight(W_up, type, n_embd, &rb, "ffn_up")) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    tle::GemvSeg g{static_cast<const uint8_t*>(W_gate), hb, n_ff, 0};
+    if (int rc = gemv(type, tle::kEpiSwiGLU, &g, 1, static_cast<const uint8_t*>(W_up), n_embd, input,
+                      nullptr, 0.f, st, "ffn_gate/up"))
+        return rc;
+    tle::GemvSeg d{static_cast<const uint8_t*>(W_down), out, n_embd, 0};
+    if (int rc = gemv(type, tle::kEpiStore, &d, 1, nullptr, n_ff, hb, nullptr, 0.f, st, "ffn_down"))
+        return rc;
+    return ok();
+}
+
+int tle_sample_argmax(const float* logits, int n_vocab, int32_t* token, void* stream) {
+    if (!logits || !token) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (n_vocab <= 0) return set_error(TLE_ERR_INVALID, "n_vocab %d <= 0", n_vocab);
+    cudaError_t e = tle::launch_argmax(logits, n_vocab, token, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "argmax");
+    return ok();
+}
+
+size_t tle_forward_workspace_bytes(const tle_model_t* model) {
+    if (!model || model->n_ctx <= 0) return 0;
+    return partial_bytes(tle::kMaxCtas + 1);
+}
+
+int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token, int pos, void* stream) {
+    if (!m || !s || !token) return set_error(TLE_ERR_INVALID, "null model/state/token");
+    if (!m->layers || m->n_layers <= 0) return set_error(TLE_ERR_INVALID, "model has no layers");
+    tle_shape_t shape{m->n_layers, m->n_head, m->n_head_kv,
+                      m->n_head > 0 ? m->n_embd / m->n_head : 0, m->rope_freq_base};
+    if (int rc = check_shape(&shape)) return rc;
+    if (m->n_embd != m->n_head * shape.head_dim)
+        return set_error(TLE_ERR_UNSUPPORTED, "n_embd %d != n_head * 64", m->n_embd);
+    if (pos < 0 || pos >= m->n_ctx) return set_error(TLE_ERR_INVALID, "need 0 <= pos < n_ctx (pos=%d)", pos);
+    if (m->n_vocab <= 0 || m->n_ff <= 0) return set_error(TLE_ERR_INVALID, "bad n_vocab/n_ff");
+    if (!s->x || !s->xb2 || !s->q || !s->k || !s->v || !s->hb || !s->logits || !s->key_cache ||
+        !s->value_cache)
+        return set_error(TLE_ERR_INVALID, "null state buffer");
+    if (m->token_embd.type != TLE_W_F16 && m->token_embd.type != TLE_W_F32)
+        return set_error(TLE_ERR_UNSUPPORTED, "token_embd type %d (F16 or F32 supported)", m->token_embd.type);
+    if (!m->token_embd.data || !m->output_norm) return set_error(TLE_ERR_INVALID, "null global tensor");
+    const int n_embd = m->n_embd, kv_dim = m->n_head_kv * shape.head_dim, n_ff = m->n_ff;
+    const float eps = m->rms_norm_eps;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t* err = nullptr;
+    cudaError_t e = tle::error_word(&err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+
+    e = tle::launch_embed(m->token_embd.type, s->x, m->token_embd.data, token, m->n_vocab, n_embd, err, st);
+    if (e != cudaSuccess) return cuda_error(e, "embedding");
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& L = m->layers[l];
+        if (!L.attn_norm || !L.ffn_norm) return set_error(TLE_ERR_INVALID, "layer %d: null norm weight", l);
+        // rmsnorm + q, k, v (forward.cpp:184-196): one launch when the three share a format
+        tle::GemvSeg qkv[3] = {{static_cast<const uint8_t*>(L.attn_q.data), s->q, n_embd, 0},
+                               {static_cast<const uint8_t*>(L.attn_k.data), s->k, kv_dim, 0},
+                               {static_cast<const uint8_t*>(L.attn_v.data), s->v, kv_dim, 0}};
+        if (L.attn_q.type == L.attn_k.type && L.attn_q.type == L.attn_v.type) {
+            int rb = 0;
+            if (int rc = check_weight(L.attn_k.data, L.attn_k.type, n_embd, &rb, "attn_k")) return rc;
+            if (int rc = check_weight(L.attn_v.data, L.attn_v.type, n_embd, &rb, "attn_v")) return rc;
+            if (int rc = gemv(L.attn_q.type, tle::kEpiStore, qkv, 3, nullptr, n_embd, s->x, L.attn_norm,
+                              eps, st, "attn_qkv"))
+                return rc;
+        } else {
+            const tle_weight_t* w[3] = {&L.attn_q, &L.attn_k, &L.attn_v};
+            for (int i = 0; i < 3; ++i)
+                if (int rc = gemv(w[i]->type, tle::kEpiStore, &qkv[i], 1, nullptr, n_embd, s->x,
+                                  L.attn_norm, eps, st, "attn_q/k/v"))
+                    return rc;
+        }
+        // rope + attention (forward.cpp:198-208), appending row pos
+        if (int rc = single_decode(s->xb2, s->q, s->k, s->v, s->key_cache, s->value_cache, l, pos,
+                                   m->n_ctx, &shape, s->workspace, s->workspace_bytes, stream, 1))
+            return rc;
+        // output projection + residual (forward.cpp:210-214)
+        tle::GemvSeg wo{static_cast<const uint8_t*>(L.attn_output.data), s->x, n_embd, 0};
+        if (int rc = gemv(L.attn_output.type, tle::kEpiAdd, &wo, 1, nullptr, n_embd, s->xb2, nullptr,
+                          0.f, st, "attn_output"))
+            return rc;
+        // rmsnorm + SwiGLU (forward.cpp:216-227; all three read as the gate's type)
+        int rb = 0;
+        if (int rc = check_weight(L.ffn_up.data, L.ffn_gate.type, n_embd, &rb, "ffn_up")) return rc;
+        tle::GemvSeg gate{static_cast<const uint8_t*>(L.ffn_gate.data), s->hb, n_ff, 0};
+        if (int rc = gemv(L.ffn_gate.type, tle::kEpiSwiGLU, &gate, 1,
+                          static_cast<const uint8_t*>(L.ffn_up.data), n_embd, s->x, L.ffn_norm, eps, st,
+                          "ffn_gate/up"))
+            return rc;
+        // down projection + residual (forward.cpp:227-229)
+        tle::GemvSeg down{static_cast<const uint8_t*>(L.ffn_down.data), s->x, n_embd, 0};
+        if (int rc = gemv(L.ffn_gate.type, tle::kEpiAdd, &down, 1, nullptr, n_ff, s->hb, nullptr, 0.f, st,
+                          "ffn_down"))
+            return rc;
+    }
+    // final rmsnorm + LM head (forward.cpp:245-265)
+    const tle_weight_t& head = m->output.data ? m->output : m->token_embd;
+    tle::GemvSeg lm{static_cast<const uint8_t*>(head.data), s->logits, m->n_vocab, 0};
+    if (int rc = gemv(head.type, tle::kEpiStore, &lm, 1, nullptr, n_embd, s->x, m->output_norm, eps, st,
+                      "lm_head"))
+        return rc;
+    return ok();
+}
+
+}  // extern "C"

@@ -18,6 +18,7 @@ enum : uint32_t {
     kErrWaitMma = 0x103,    // waiter gave up on a tensor-core commit
     kErrDrain = 0x104,      // exit-time wait for in-flight copies gave up
     kErrBadPage = 0x105,    // paged decode: a page id outside the pool (access skipped)
+    kErrBadToken = 0x106,   // forward: a token id outside the vocabulary (zero embedding used)
     kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 

@@ -1,0 +1,496 @@
+// forward.cu -- the rest of TinyLlama's forward pass on the device: the
+// matrix-vector products of every GGUF weight format (fused with RMSNorm in
+// front and a residual add or SwiGLU behind), the embedding lookup and
+// greedy sampling.
+//
+// Reference semantics (src/ops.cpp): matmul() ops.cpp:959-981 with the
+// per-format paths F32 ops.cpp:251-262, F16 342-356, Q8_0 442-473, Q4_0
+// 616-655, Q6_K 882-948; rmsnorm() ops.cpp:1040-1054; silu() 1107-1113,
+// elementwise_mul() 1129-1146, vec_add() 1165-1184, ffn_swiglu() 1535-1564;
+// sample_argmax() 1587-1597; embed_token() forward.cpp:35-60.
+//
+// Design (B200): a decode step reads every weight once, so each product is
+// HBM-bound byte work.  The weights are read in place, in the reference's
+// GGUF block layout (no repacking: the pointers a GGUF loader hands out
+// work unchanged).  One CTA (8 warps) owns a tile of consecutive rows; each
+// warp computes whole rows, its lanes splitting a row's blocks (Q4_0/Q8_0:
+// 4 lanes per 32-weight block; Q6_K: lane = position l of the 256-weight
+// super-block; F16/F32: 16-byte vectors), and a warp shuffle reduces the
+// row.  The input vector sits in shared memory, normalised on the way in
+// when an RMSNorm precedes the product.  Every kernel is launched as a
+// programmatic dependent of the previous one: its CTAs issue a bulk L2
+// prefetch of their weight rows (weights are never written by a kernel) and
+// only then wait for the previous kernel, so the weight stream of one
+// product overlaps the tail of the one before.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tle {
+
+namespace {
+
+constexpr int GT = 256;        // threads per GEMV CTA
+constexpr int GW = GT / 32;    // warps per GEMV CTA
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint32_t ldg16(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+// 4-bit value n (0..15) minus 8, and an int8 stored as a byte, as floats:
+// 2^23 + v has v in its low mantissa bits, so one OR and one subtract do the
+// conversion exactly.
+__device__ __forceinline__ float nib_m8(uint32_t q, int shift) {
+    return __int_as_float(0x4B000000u | ((q >> shift) & 15u)) - 8388616.0f;
+}
+__device__ __forceinline__ float s8f(uint32_t q, int shift) {
+    return __int_as_float(0x4B000000u | (((q >> shift) & 0xFFu) ^ 0x80u)) - 8388736.0f;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Per-lane partial dot product of one weight row (GGUF layout) with xs.
+template <int T>
+__device__ __forceinline__ float row_dot(const uint8_t* __restrict__ row, const float* xs, int cols,
+                                         int lane);
+
+// F32 (ops.cpp:251-262): 4 consecutive weights per lane (one per lane
+// when rows are not 16-byte multiples).
+template <>
+__device__ __forceinline__ float row_dot<kWF32>(const uint8_t* __restrict__ row, const float* xs,
+                                                int cols, int lane) {
+    float acc = 0.f;
+    if (cols & 3) {
+        const float* w = reinterpret_cast<const float*>(row);
+        for (int c = lane; c < cols; c += 32) acc = fmaf(__ldg(w + c), xs[c], acc);
+        return acc;
+    }
+    const float4* w = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+    for (int c = lane; c < cols / 4; c += 32) {
+        const float4 a = __ldg(w + c);
+        const float4 x = *reinterpret_cast<const float4*>(xs + 4 * c);
+        acc = fmaf(a.x, x.x, acc);
+        acc = fmaf(a.y, x.y, acc);
+        acc = fmaf(a.z, x.z, acc);
+        acc = fmaf(a.w, x.w, acc);
+    }
+    return acc;
+}
+
+// F16 (ops.cpp:342-356): 8 consecutive weights per lane (one per lane
+// when rows are not 16-byte multiples).
+template <>
+__device__ __forceinline__ float row_dot<kWF16>(const uint8_t* __restrict__ row, const float* xs,
+                                                int cols, int lane) {
+    float acc = 0.f;
+    if (cols & 7) {
+        const unsigned short* w = reinterpret_cast<const unsigned short*>(row);
+        for (int c = lane; c < cols; c += 32) acc = fmaf(h2f(__ldg(w + c)), xs[c], acc);
+        return acc;
+    }
+    const uint4* w = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+    for (int c = lane; c < cols / 8; c += 32) {
+        const uint4 a = __ldg(w + c);
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + 8 * c);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + 8 * c + 4);
+        acc = fmaf(h2f(a.x & 0xFFFFu), x0.x, acc);
+        acc = fmaf(h2f(a.x >> 16), x0.y, acc);
+        acc = fmaf(h2f(a.y & 0xFFFFu), x0.z, acc);
+        acc = fmaf(h2f(a.y >> 16), x0.w, acc);
+        acc = fmaf(h2f(a.z & 0xFFFFu), x1.x, acc);
+        acc = fmaf(h2f(a.z >> 16), x1.y, acc);
+        acc = fmaf(h2f(a.w & 0xFFFFu), x1.z, acc);
+        acc = fmaf(h2f(a.w >> 16), x1.w, acc);
+    }
+    return acc;
+}
+
+// Q4_0 (ops.cpp:616-655): block = fp16 d + 16 bytes; byte j holds element
+// j (low nibble) and j + 16 (high nibble).  Lane t = lane & 3 of a block
+// takes bytes 4t..4t+3: elements 4t..4t+3 and 16+4t..16+4t+3.  Its 8-term
+// block partial is scaled by d like the reference's block sum.
+template <>
+__device__ __forceinline__ float row_dot<kWQ4_0>(const uint8_t* __restrict__ row, const float* xs,
+                                                 int cols, int lane) {
+    const int nb = cols >> 5;
+    const int t = lane & 3;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int b = lane >> 2; b < nb; b += 8) {
+        const uint8_t* blk = row + 18 * b;
+        const float d = h2f(static_cast<uint16_t>(ldg16(blk)));
+        const uint32_t q = ldg16(blk + 2 + 4 * t) | (ldg16(blk + 4 + 4 * t) << 16);
+        const float4 xl = *reinterpret_cast<const float4*>(xs + 32 * b + 4 * t);
+        const float4 xh = *reinterpret_cast<const float4*>(xs + 32 * b + 16 + 4 * t);
+        float s = nib_m8(q, 0) * xl.x;
+        s = fmaf(nib_m8(q, 4), xh.x, s);
+        s = fmaf(nib_m8(q, 8), xl.y, s);
+        s = fmaf(nib_m8(q, 12), xh.y, s);
+        s = fmaf(nib_m8(q, 16), xl.z, s);
+        s = fmaf(nib_m8(q, 20), xh.z, s);
+        s = fmaf(nib_m8(q, 24), xl.w, s);
+        s = fmaf(nib_m8(q, 28), xh.w, s);
+        acc = fmaf(d, s, acc);
+    }
+    return acc;
+}
+
+// Q8_0 (ops.cpp:442-473): block = fp16 d + 32 int8.  Lane t takes elements
+// 8t..8t+7 of each of its blocks.
+template <>
+__device__ __forceinline__ float row_dot<kWQ8_0>(const uint8_t* __restrict__ row, const float* xs,
+                                                 int cols, int lane) {
+    const int nb = cols >> 5;
+    const int t = lane & 3;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int b = lane >> 2; b < nb; b += 8) {
+        const uint8_t* blk = row + 34 * b;
+        const float d = h2f(static_cast<uint16_t>(ldg16(blk)));
+        const uint8_t* qs = blk + 2 + 8 * t;
+        const uint32_t q0 = ldg16(qs) | (ldg16(qs + 2) << 16);
+        const uint32_t q1 = ldg16(qs + 4) | (ldg16(qs + 6) << 16);
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + 32 * b + 8 * t);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + 32 * b + 8 * t + 4);
+        float s = s8f(q0, 0) * x0.x;
+        s = fmaf(s8f(q0, 8), x0.y, s);
+        s = fmaf(s8f(q0, 16), x0.z, s);
+        s = fmaf(s8f(q0, 24), x0.w, s);
+        s = fmaf(s8f(q1, 0), x1.x, s);
+        s = fmaf(s8f(q1, 8), x1.y, s);
+        s = fmaf(s8f(q1, 16), x1.z, s);
+        s = fmaf(s8f(q1, 24), x1.w, s);
+        acc = fmaf(d, s, acc);
+    }
+    return acc;
+}
+
+// Q6_K (ops.cpp:882-948): super-block of 256 = ql[128], qh[64], int8
+// scales[16], fp16 d.  Lane l takes position l of both halves: the four
+// 6-bit values built from ql[l], ql[l+32] and qh[l] of each half.
+template <>
+__device__ __forceinline__ float row_dot<kWQ6_K>(const uint8_t* __restrict__ row, const float* xs,
+                                                 int cols, int lane) {
+    const int nb = cols >> 8;
+    const int is = lane >> 4;
+    float acc = 0.f;
+    for (int b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + 210 * b;
+        const float d = h2f(static_cast<uint16_t>(ldg16(blk + 208)));
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t l0 = __ldg(blk + 64 * h + lane);
+            const uint32_t l1 = __ldg(blk + 64 * h + lane + 32);
+            const uint32_t hh = __ldg(blk + 128 + 32 * h + lane);
+            const float* X = xs + 256 * b + 128 * h;
+            const int q1 = static_cast<int>((l0 & 15u) | ((hh & 3u) << 4)) - 32;
+            const int q2 = static_cast<int>((l1 & 15u) | (((hh >> 2) & 3u) << 4)) - 32;
+            const int q3 = static_cast<int>((l0 >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
+            const int q4 = static_cast<int>((l1 >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
+            const int8_t* S = sc + 8 * h + is;
+            acc = fmaf(d * static_cast<float>(__ldg(S + 0)) * static_cast<float>(q1), X[lane], acc);
+            acc = fmaf(d * static_cast<float>(__ldg(S + 2)) * static_cast<float>(q2), X[lane + 32], acc);
+            acc = fmaf(d * static_cast<float>(__ldg(S + 4)) * static_cast<float>(q3), X[lane + 64], acc);
+            acc = fmaf(d * static_cast<float>(__ldg(S + 6)) * static_cast<float>(q4), X[lane + 96], acc);
+        }
+    }
+    return acc;
+}
+
+// Bulk prefetch into L2 of [p, p + bytes), trimmed inward to 16-byte
+// boundaries (a hint: the trimmed edges are simply not prefetched).
+__device__ __forceinline__ void prefetch_l2(const uint8_t* p, size_t bytes) {
+    uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
+    uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+    while (a < e) {
+        const uintptr_t left = e - a;
+        const uint32_t n = static_cast<uint32_t>(left < (uintptr_t(1) << 20) ? left : (uintptr_t(1) << 20));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+        a += n;
+    }
+}
+
+// One launch: rows of up to three matrices that share the input vector
+// (q, k and v of a layer), or gate and up rows for SwiGLU.
+template <int T, int EPI>
+__global__ void __launch_bounds__(GT) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float red[GW];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rows_per_cta = GW * a.rpw;
+
+    int s = 0;
+    while (s + 1 < a.n_seg && static_cast<int>(blockIdx.x) >= a.seg[s + 1].tile0) ++s;
+    const GemvSeg& seg = a.seg[s];
+    const int r0 = (static_cast<int>(blockIdx.x) - seg.tile0) * rows_per_cta;
+    const int r1 = min(r0 + rows_per_cta, seg.rows);
+
+    if (tid == 0) {
+        const size_t off = static_cast<size_t>(r0) * a.row_bytes;
+        const size_t len = static_cast<size_t>(r1 - r0) * a.row_bytes;
+        prefetch_l2(seg.W + off, len);
+        if (EPI == kEpiSwiGLU) prefetch_l2(a.W2 + off, len);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // The input vector, normalised (rmsnorm, ops.cpp:1040-1054: x * rms *
+    // weight with rms = 1 / sqrt(mean(x^2) + eps)) when a norm weight is
+    // given.
+    float rms = 1.f;
+    if (a.norm_w) {
+        float ss = 0.f;
+        for (int i = tid; i < a.cols; i += GT) {
+            const float v = a.x[i];
+            ss = fmaf(v, v, ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (warp == 0) {
+            float v = lane < GW ? red[lane] : 0.f;
+            v = warp_sum(v);
+            if (lane == 0) red[0] = 1.0f / sqrtf(v / static_cast<float>(a.cols) + a.eps);
+        }
+        __syncthreads();
+        rms = red[0];
+        for (int i = tid; i < a.cols; i += GT) xs[i] = a.x[i] * rms * a.norm_w[i];
+    } else {
+        for (int i = tid; i < a.cols; i += GT) xs[i] = a.x[i];
+    }
+    __syncthreads();
+
+    for (int k = 0; k < a.rpw; ++k) {
+        const int r = r0 + warp * a.rpw + k;
+        if (r >= r1) break;
+        const size_t off = static_cast<size_t>(r) * a.row_bytes;
+        const float y = warp_sum(row_dot<T>(seg.W + off, xs, a.cols, lane));
+        if (EPI == kEpiSwiGLU) {
+            const float u = warp_sum(row_dot<T>(a.W2 + off, xs, a.cols, lane));
+            // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
+            if (lane == 0) seg.out[r] = (y * (1.0f / (1.0f + expf(-y)))) * u;
+        } else if (EPI == kEpiAdd) {
+            if (lane == 0) seg.out[r] += y;
+        } else {
+            if (lane == 0) seg.out[r] = y;
+        }
+    }
+}
+
+// embed_token (forward.cpp:35-60): row `token` of the table, as fp32.  A
+// token outside [0, n_vocab) is reported (0x106) and gives a zero row.
+template <int T>
+__global__ void __launch_bounds__(256) embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ table,
+                                                     const int32_t* __restrict__ token, int n_vocab,
+                                                     int n_embd, uint32_t* err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int t = *token;
+    const bool ok = t >= 0 && t < n_vocab;
+    if (!ok && threadIdx.x == 0 && blockIdx.x == 0) record_error(err, kErrBadToken);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_embd; i += gridDim.x * blockDim.x) {
+        float v = 0.f;
+        if (ok) {
+            const size_t e = static_cast<size_t>(t) * n_embd + i;
+            v = (T == kWF16) ? h2f(__ldg(reinterpret_cast<const unsigned short*>(table) + e))
+                             : __ldg(reinterpret_cast<const float*>(table) + e);
+        }
+        x[i] = v;
+    }
+}
+
+// sample_argmax (ops.cpp:1587-1597): the first index of the maximum under
+// '>'.  A NaN never beats the running best, so NaNs after index 0 are
+// skipped; a NaN at index 0 makes the answer 0 (nothing compares greater).
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n,
+                                                      int32_t* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < n; i += 1024) {
+        float v = logits[i];
+        if (v != v) v = -INFINITY;           // NaN: never the maximum
+        if (bi == 0x7fffffff || v > bv) {    // first element of this thread, or strictly greater
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((tid & 31) == 0) {
+        sv[tid >> 5] = bv;
+        si[tid >> 5] = bi;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        bv = sv[tid];
+        bi = si[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (tid == 0) {
+            const float v0 = logits[0];
+            *out = (v0 != v0) ? 0 : bi;
+        }
+    }
+}
+
+// rmsnorm (ops.cpp:1040-1054) as its own launch (one CTA): out may alias x.
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(float* out, const float* x, const float* w,
+                                                       int n, float eps) {
+    __shared__ float red[32];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x;
+    float ss = 0.f;
+    for (int i = tid; i < n; i += 1024) ss = fmaf(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+        float v = warp_sum(red[tid]);
+        if (tid == 0) red[0] = 1.0f / sqrtf(v / static_cast<float>(n) + eps);
+    }
+    __syncthreads();
+    const float rms = red[0];
+    for (int i = tid; i < n; i += 1024) out[i] = x[i] * rms * w[i];
+}
+
+// vec_add (ops.cpp:1165-1184): out += x.
+__global__ void __launch_bounds__(256) vec_add_kernel(float* out, const float* x, int n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] += x[i];
+}
+
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       void** args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+template <int T, int EPI>
+cudaError_t launch_gemv_t(const GemvArgs& a, int n_tiles, cudaStream_t stream) {
+    static PerDeviceOnce once;
+    const size_t smem = static_cast<size_t>(a.cols) * sizeof(float);
+    cudaError_t e = once.run([&](int) {
+        return cudaFuncSetAttribute(gemv_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kGemvMaxCols * sizeof(float)));
+    });
+    if (e != cudaSuccess) return e;
+    GemvArgs copy = a;
+    void* args[] = {&copy};
+    return launch_pdl(reinterpret_cast<const void*>(gemv_kernel<T, EPI>), dim3(n_tiles), dim3(GT),
+                      smem, stream, args);
+}
+
+template <int EPI>
+cudaError_t launch_gemv_e(int type, const GemvArgs& a, int n_tiles, cudaStream_t stream) {
+    switch (type) {
+    case kWF32: return launch_gemv_t<kWF32, EPI>(a, n_tiles, stream);
+    case kWF16: return launch_gemv_t<kWF16, EPI>(a, n_tiles, stream);
+    case kWQ4_0: return launch_gemv_t<kWQ4_0, EPI>(a, n_tiles, stream);
+    case kWQ8_0: return launch_gemv_t<kWQ8_0, EPI>(a, n_tiles, stream);
+    case kWQ6_K: return launch_gemv_t<kWQ6_K, EPI>(a, n_tiles, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+int weight_row_bytes(int type, int cols) {
+    switch (type) {
+    case kWF32: return cols * 4;
+    case kWF16: return cols * 2;
+    case kWQ4_0: return cols % 32 ? -1 : cols / 32 * 18;
+    case kWQ8_0: return cols % 32 ? -1 : cols / 32 * 34;
+    case kWQ6_K: return cols % 256 ? -1 : cols / 256 * 210;
+    default: return -1;
+    }
+}
+
+cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream) {
+    const int rows_per_cta = GW * a.rpw;
+    int tiles = 0;
+    for (int s = 0; s < a.n_seg; ++s) {
+        a.seg[s].tile0 = tiles;
+        tiles += (a.seg[s].rows + rows_per_cta - 1) / rows_per_cta;
+    }
+    if (tiles == 0) return cudaSuccess;
+    switch (epi) {
+    case kEpiStore: return launch_gemv_e<kEpiStore>(type, a, tiles, stream);
+    case kEpiAdd: return launch_gemv_e<kEpiAdd>(type, a, tiles, stream);
+    case kEpiSwiGLU: return launch_gemv_e<kEpiSwiGLU>(type, a, tiles, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_embed(int type, float* x, const void* table, const int32_t* token, int n_vocab,
+                         int n_embd, uint32_t* err, cudaStream_t stream) {
+    const uint8_t* t = static_cast<const uint8_t*>(table);
+    void* args[] = {&x, &t, &token, &n_vocab, &n_embd, &err};
+    const int blocks = (n_embd + 255) / 256;
+    if (type == kWF16)
+        return launch_pdl(reinterpret_cast<const void*>(embed_kernel<kWF16>), dim3(blocks), dim3(256), 0,
+                          stream, args);
+    if (type == kWF32)
+        return launch_pdl(reinterpret_cast<const void*>(embed_kernel<kWF32>), dim3(blocks), dim3(256), 0,
+                          stream, args);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_argmax(const float* logits, int n, int32_t* out, cudaStream_t stream) {
+    void* args[] = {&logits, &n, &out};
+    return launch_pdl(reinterpret_cast<const void*>(argmax_kernel), dim3(1), dim3(1024), 0, stream, args);
+}
+
+cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps,
+                           cudaStream_t stream) {
+    void* args[] = {&out, &x, &w, &n, &eps};
+    return launch_pdl(reinterpret_cast<const void*>(rmsnorm_kernel), dim3(1), dim3(1024), 0, stream, args);
+}
+
+cudaError_t launch_vec_add(float* out, const float* x, int n, cudaStream_t stream) {
+    void* args[] = {&out, &x, &n};
+    const int blocks = min((n + 255) / 256, 1024);
+    return launch_pdl(reinterpret_cast<const void*>(vec_add_kernel), dim3(blocks), dim3(256), 0, stream,
+                      args);
+}
+
+}  // namespace tle

@@ -135,6 +135,42 @@ cudaError_t read_device_error(int clear, uint32_t* code);
 
 // Runs `configure` (kernel attributes) once per device, thread-safe; later
 // calls cost one atomic load.
+// ---- forward pass around attention (forward.cu) ----
+// Weight formats: the ggml type numbers (reference src/gguf.h:23-33).
+constexpr int kWF32 = 0, kWF16 = 1, kWQ4_0 = 2, kWQ8_0 = 8, kWQ6_K = 14;
+// What a GEMV does with row r's product y.
+constexpr int kEpiStore = 0;    // out[r] = y
+constexpr int kEpiAdd = 1;      // out[r] += y (residual)
+constexpr int kEpiSwiGLU = 2;   // out[r] = silu(gate_r) * up_r (gate rows seg[0].W, up rows W2)
+constexpr int kGemvMaxCols = 16384;   // input vector in shared memory (64 KB)
+
+struct GemvSeg {
+    const uint8_t* W;   // rows x cols, GGUF layout, row r at r * row_bytes
+    float* out;
+    int rows;
+    int tile0;          // first CTA of the segment (set by launch_gemv)
+};
+struct GemvArgs {
+    GemvSeg seg[3];
+    int n_seg;
+    const uint8_t* W2;      // SwiGLU: the up-projection rows (gate's layout)
+    int cols;
+    int row_bytes;
+    int rpw;                // rows per warp
+    const float* x;         // input [cols]
+    const float* norm_w;    // RMSNorm weight applied to x first (nullptr: none)
+    float eps;
+};
+// Bytes of one row of `cols` weights of format `type`; -1 if unsupported.
+int weight_row_bytes(int type, int cols);
+cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream);
+cudaError_t launch_embed(int type, float* x, const void* table, const int32_t* token, int n_vocab,
+                         int n_embd, uint32_t* err, cudaStream_t stream);
+cudaError_t launch_argmax(const float* logits, int n, int32_t* out, cudaStream_t stream);
+cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps,
+                           cudaStream_t stream);
+cudaError_t launch_vec_add(float* out, const float* x, int n, cudaStream_t stream);
+
 constexpr int kMaxDevices = 64;
 struct PerDeviceOnce {
     std::atomic<bool> done[kMaxDevices] = {};

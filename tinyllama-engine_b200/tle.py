@@ -41,6 +41,9 @@ EXPORTED = (
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
     "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
     "tle_decode_desc_paged", "tle_decode_batch_paged",
+    # include/tle_forward.h
+    "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
+    "tle_forward_workspace_bytes", "tle_forward",
 )
 
 
@@ -72,6 +75,34 @@ class PagePool(ctypes.Structure):
 class PagedSeq(ctypes.Structure):
     """tle_paged_seq_t: one sequence's device page table and decode position."""
     _fields_ = [("pages", ctypes.c_void_p), ("n_pages", ctypes.c_int32), ("pos", ctypes.c_int32)]
+
+
+class Weight(ctypes.Structure):
+    """tle_weight_t: a device tensor in GGUF layout and its ggml type."""
+    _fields_ = [("type", ctypes.c_int32), ("reserved", ctypes.c_int32), ("data", ctypes.c_void_p)]
+
+
+class Layer(ctypes.Structure):
+    """tle_layer_t: the tensors of one block (forward.cpp blk.l.*)."""
+    _fields_ = [(n, Weight) for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate",
+                                      "ffn_up", "ffn_down")] + \
+               [("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p)]
+
+
+class Model(ctypes.Structure):
+    """tle_model_t: llama_config_t fields and the global tensors."""
+    _fields_ = [(n, ctypes.c_int32) for n in ("n_layers", "n_embd", "n_head", "n_head_kv", "n_ff",
+                                               "n_vocab", "n_ctx")] + \
+               [("rope_freq_base", ctypes.c_float), ("rms_norm_eps", ctypes.c_float),
+                ("reserved", ctypes.c_int32), ("token_embd", Weight), ("output", Weight),
+                ("output_norm", ctypes.c_void_p), ("layers", ctypes.POINTER(Layer))]
+
+
+class State(ctypes.Structure):
+    """tle_state_t: RunState buffers in device memory."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("x", "xb", "xb2", "q", "k", "v", "hb", "hb2",
+                                                "logits", "key_cache", "value_cache",
+                                                "workspace")] + [("workspace_bytes", ctypes.c_size_t)]
 
 
 def tinyllama_shape(n_layers: int = 22) -> Shape:
@@ -112,6 +143,14 @@ def lib() -> ctypes.CDLL:
         L.tle_attention_lse.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), vp, sz, vp]
         L.tle_merge_lse.argtypes = [vp, vp, vp, i, vp]
         L.tle_decode_batch_noalloc.argtypes = [P(Shape), P(Seq), i, vp, vp, vp, vp, i, i, vp]
+        L.tle_matmul.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.tle_rmsnorm.argtypes = [vp, vp, vp, i, f, vp]
+        L.tle_vec_add.argtypes = [vp, vp, i, vp]
+        L.tle_ffn_swiglu.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, vp]
+        L.tle_sample_argmax.argtypes = [vp, i, vp, vp]
+        L.tle_forward_workspace_bytes.argtypes = [P(Model)]
+        L.tle_forward_workspace_bytes.restype = sz
+        L.tle_forward.argtypes = [P(Model), P(State), vp, i, vp]
         L.tle_decode_desc_paged.argtypes = [P(Shape), P(PagePool), P(PagedSeq), i, i, vp, sz, P(i)]
         L.tle_decode_batch_paged.argtypes = [P(Shape), P(PagePool), vp, i, i, vp, vp, vp, vp, i, i,
                                              vp, sz, vp]
@@ -449,3 +488,115 @@ def selftest_wait_timeout(limit_us: int = 20000, stream=None) -> None:
     """Launches a block whose bounded wait is planted to expire after
     limit_us (tle_selftest_wait_timeout); read the result with device_error."""
     _check(lib().tle_selftest_wait_timeout(int(limit_us), _stream(stream)))
+
+
+# ------------------------------------------------------------ forward pass
+def _wptr(t) -> int:
+    """Device pointer of a uint8 CUDA tensor holding GGUF-layout weights."""
+    import torch
+    if t.dtype != torch.uint8 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError("weights: need a contiguous uint8 CUDA tensor")
+    return int(t.data_ptr())
+
+
+def matmul(out, W, x, rows: int, cols: int, wtype: int, stream=None) -> None:
+    """ops.h:64-66 matmul on the device; W: uint8 CUDA tensor, GGUF layout."""
+    _want(out, rows, "out"); _want(x, cols, "x")
+    _check(lib().tle_matmul(_ptr(out), _wptr(W), _ptr(x), rows, cols, wtype, _stream(stream)))
+
+
+def rmsnorm(out, x, weight, eps: float = 1e-5, stream=None) -> None:
+    n = x.numel()
+    _want(out, n, "out"); _want(weight, n, "weight")
+    _check(lib().tle_rmsnorm(_ptr(out), _ptr(x), _ptr(weight), n, eps, _stream(stream)))
+
+
+def vec_add(out, x, stream=None) -> None:
+    n = out.numel()
+    _want(x, n, "x")
+    _check(lib().tle_vec_add(_ptr(out), _ptr(x), n, _stream(stream)))
+
+
+def ffn_swiglu(out, inp, hb, W_gate, W_up, W_down, n_ff: int, n_embd: int, wtype: int,
+               stream=None) -> None:
+    _want(out, n_embd, "out"); _want(inp, n_embd, "input"); _want(hb, n_ff, "hb")
+    _check(lib().tle_ffn_swiglu(_ptr(out), _ptr(inp), _ptr(hb), None, _wptr(W_gate),
+                                _wptr(W_up), _wptr(W_down), n_ff, n_embd, wtype, _stream(stream)))
+
+
+def sample_argmax(logits, token_out, stream=None) -> None:
+    """ops.h:249 on the device: writes the index into token_out (int32 CUDA)."""
+    import torch
+    _want(logits, 1, "logits")
+    if token_out.dtype != torch.int32 or not token_out.is_cuda:
+        raise ValueError("token_out: need an int32 CUDA tensor")
+    _check(lib().tle_sample_argmax(_ptr(logits), logits.numel(), _ptr(token_out), _stream(stream)))
+
+
+class DeviceModel:
+    """A model (tinyllama-engine_b200/synth.py SynthModel, GGUF layouts)
+    copied to device memory and described as a tle_model_t."""
+
+    _LAYER = (("attn_q", "attn_q"), ("attn_k", "attn_k"), ("attn_v", "attn_v"),
+              ("attn_output", "attn_output"), ("ffn_gate", "ffn_gate"), ("ffn_up", "ffn_up"),
+              ("ffn_down", "ffn_down"))
+
+    def __init__(self, model, device="cuda"):
+        import torch
+        self.src = model
+        dev = torch.device(device)
+        up = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+        self.keep = []
+
+        def w(W):
+            t = up(W.data)
+            self.keep.append(t)
+            return Weight(W.wtype, 0, t.data_ptr())
+
+        def f32(a):
+            t = up(a)
+            self.keep.append(t)
+            return t.data_ptr()
+
+        self.layers = (Layer * model.n_layers)()
+        for i, L in enumerate(model.layers):
+            for f, n in self._LAYER:
+                setattr(self.layers[i], f, w(L[n]))
+            self.layers[i].attn_norm = f32(L["attn_norm"])
+            self.layers[i].ffn_norm = f32(L["ffn_norm"])
+        out = w(model.output) if model.output is not None else Weight(0, 0, None)
+        self.desc = Model(model.n_layers, model.n_embd, model.n_head, model.n_head_kv, model.n_ff,
+                          model.n_vocab, model.n_ctx, model.rope_freq_base, model.rms_norm_eps, 0,
+                          w(model.token_embd), out, f32(model.output_norm), self.layers)
+
+
+class DeviceState:
+    """RunState (run_state.h) in device memory for a DeviceModel."""
+
+    def __init__(self, dm: DeviceModel, device="cuda"):
+        import torch
+        m = dm.src
+        z = lambda n: torch.zeros(n, dtype=torch.float32, device=device)  # noqa: E731
+        kv = m.kv_dim
+        self.t = {"x": z(m.n_embd), "xb": z(m.n_embd), "xb2": z(m.n_embd), "q": z(m.n_embd),
+                  "k": z(kv), "v": z(kv), "hb": z(m.n_ff), "hb2": z(m.n_ff),
+                  "logits": z(m.n_vocab), "key_cache": z(m.n_layers * m.n_ctx * kv),
+                  "value_cache": z(m.n_layers * m.n_ctx * kv)}
+        nbytes = lib().tle_forward_workspace_bytes(ctypes.byref(dm.desc))
+        self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        self.desc = State(**{k: v.data_ptr() for k, v in self.t.items()},
+                          workspace=self.workspace.data_ptr(), workspace_bytes=nbytes)
+
+    @property
+    def logits(self):
+        return self.t["logits"]
+
+
+def forward(dm: DeviceModel, ds: DeviceState, token, pos: int, stream=None) -> None:
+    """forward.h:16 on the device: token is an int32 CUDA tensor (its first
+    element is read); logits land in ds.logits."""
+    import torch
+    if token.dtype != torch.int32 or not token.is_cuda:
+        raise ValueError("token: need an int32 CUDA tensor")
+    _check(lib().tle_forward(ctypes.byref(dm.desc), ctypes.byref(ds.desc), _ptr(token), pos,
+                             _stream(stream)))
