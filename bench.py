@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--ctx-rows", type=int, default=4 * 1024 * 1024,
                     help="rows of the single sequence for --only ctxsplit")
     ap.add_argument("--only", choices=["prefill3", "decode4", "decode1", "ctxsplit", "decode5paged",
-                                       "decode4paged"], default=None,
+                                       "decode4paged", "generate2"], default=None,
                     help="run one secondary workload alone (--steps/--warmup apply) and print "
                          "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -210,7 +210,8 @@ def main():
         return
     if args.only:
         fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1,
-              "decode5paged": measure_paged5, "decode4paged": measure_paged4}[args.only]
+              "decode5paged": measure_paged5, "decode4paged": measure_paged4,
+              "generate2": measure_config2}[args.only]
         res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
         print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
                               warmup=max(3, args.warmup))), flush=True)
@@ -602,6 +603,132 @@ def measure_paged4(dev, peaks, steps=20, warmup=3, page_rows=256, shuffle=True):
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
             "gpu_launches": n_layers * steps}
+
+
+def cpu_forward_reference(model, tokens, n_threads):
+    """The reference's forward() (its own ops.cpp, composed in forward.cpp's
+    order by oracle/_ref) on the host: seconds per token over `tokens`."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    kind = "reference" if oracle.have_reference() else "port"
+    lib = oracle.reference() if kind == "reference" else oracle.port()
+    if kind == "reference":
+        lib._fn("set_num_threads", [ctypes_int()])(n_threads)
+    hf = oracle.HostForward(model)
+    t0 = time.perf_counter()
+    for pos, tok in enumerate(tokens):
+        lib.forward(hf, int(tok), pos)
+    dt = (time.perf_counter() - t0) / len(tokens)
+    if kind == "reference":
+        lib._fn("set_num_threads", [ctypes_int()])(1)
+    return dt, kind
+
+
+def ctypes_int():
+    import ctypes
+    return ctypes.c_int
+
+
+def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, cpu_tokens=3):
+    """Config 2: end-to-end greedy generation on the device, TinyLlama-1.1B
+    shapes with random Q4_0 weights (LM head Q4_0, fp16 embedding table,
+    RMSNorm weights 1.0): a 128-token prompt of random ids fed token by token
+    (as generate.cpp:56-59 does), then 256 tokens, each the argmax of the
+    previous logits, sampled on the device.  Every position runs as one
+    CUDA graph (embedding, 22 x [RMSNorm+q/k/v, rope+attention, output
+    projection+residual, RMSNorm+SwiGLU, down projection+residual], RMSNorm+LM
+    head, argmax) captured once; the token of step t+1 never leaves the
+    device.  Timed with CUDA events over whole generations."""
+    import numpy as np
+    import torch
+    import synth
+    import tle
+    n_ctx = prompt + gen
+    m = synth.make_model(seed=seed, n_layers=22, wtype=synth.Q4_0, output_type=synth.Q4_0,
+                         n_ctx=n_ctx)
+    dm = tle.DeviceModel(m, device=dev)
+    ds = tle.DeviceState(dm, device=dev)
+    ids = np.random.default_rng(seed).integers(0, m.n_vocab, prompt)
+    toks = torch.zeros(n_ctx + 1, dtype=torch.int32, device=dev)
+    toks[:prompt] = torch.from_numpy(ids.astype(np.int32)).to(dev)
+    side = torch.cuda.Stream(dev)
+
+    def step(pos, st):
+        tle.forward(dm, ds, toks[pos:pos + 1], pos, st)
+        if pos >= prompt - 1 and pos + 1 < n_ctx + 1:
+            tle.sample_argmax(ds.logits, toks[pos + 1:pos + 2], st)
+
+    # eager (host-launched) generation, also the warm-up
+    side.wait_stream(torch.cuda.current_stream(dev))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.cuda.stream(side):
+        for pos in range(n_ctx):
+            step(pos, side)
+        torch.cuda.synchronize(dev)
+        ev[0].record(side)
+        for pos in range(n_ctx):
+            if pos == prompt:
+                ev[1].record(side)
+            step(pos, side)
+        ev[2].record(side)
+    torch.cuda.synchronize(dev)
+    eager_prompt_ms, eager_gen_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    first = toks[prompt:].cpu().numpy().copy()
+
+    graphs = []
+    with torch.cuda.stream(side):
+        for pos in range(n_ctx):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                step(pos, side)
+            graphs.append(g)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    for pos in range(n_ctx):          # warm replay
+        graphs[pos].replay()
+    torch.cuda.synchronize(dev)
+    runs = max(1, steps)
+    pm, gm = [], []
+    for _ in range(runs):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        for pos in range(n_ctx):
+            if pos == prompt:
+                ev[1].record(stream)
+            graphs[pos].replay()
+        ev[2].record(stream)
+        torch.cuda.synchronize(dev)
+        pm.append(ev[0].elapsed_time(ev[1]))
+        gm.append(ev[1].elapsed_time(ev[2]))
+    same = bool(np.array_equal(first, toks[prompt:].cpu().numpy()))
+    if tle.device_error():
+        raise RuntimeError("device error during generation")
+    prompt_ms, gen_ms = statistics.median(pm), statistics.median(gm)
+    wbytes = m.weight_bytes_per_token()
+    tok_s = gen / (gen_ms / 1e3)
+    gbs = wbytes * tok_s / 1e9
+    cores = os.cpu_count() or 1
+    cpu_s, kind = cpu_forward_reference(m, ids[:cpu_tokens], cores)
+    del graphs
+    return {"workload": "config2: TinyLlama-1.1B shapes, random Q4_0 weights (LM head Q4_0, fp16 "
+                        "embeddings), 128-token random prompt + 256 greedy tokens, batch 1, "
+                        "all on the device (one CUDA graph per position)",
+            "metric": "generated tok/s", "value": round(tok_s, 1), "unit": "tok/s",
+            "ms_per_token": round(gen_ms / gen, 4), "prompt_ms": round(prompt_ms, 3),
+            "prompt_tok_s": round(prompt / (prompt_ms / 1e3), 1),
+            "eager_ms_per_token": round(eager_gen_ms / gen, 4),
+            "eager_prompt_ms": round(eager_prompt_ms, 3),
+            "tokens_identical_eager_vs_graph": same,
+            "weight_bytes_per_token": wbytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "note": "weight bytes per token x tok/s"},
+            "cpu_reference": {"kind": kind, "cores": cores,
+                              "tok_s": round(1.0 / cpu_s, 3),
+                              "sample": "%d prompt tokens through the 22-layer model" % cpu_tokens},
+            # per generated token: embedding, 22 x (q/k/v, decode, split-K merge,
+            # output projection, gate/up, down), LM head, argmax
+            "gpu_launches": (3 + 22 * 6) * gen * runs}
 
 
 def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):

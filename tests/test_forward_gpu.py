@@ -211,3 +211,44 @@ def test_forward_bad_token_is_reported(cuda):
     tle.forward(dm, ds, torch.tensor([3], dtype=torch.int32, device="cuda"), 1)
     assert np.all(np.isfinite(host(ds.logits)))
     assert tle.device_error() == 0
+
+
+def test_greedy_generation_device_fed_matches_synced_and_oracle(cuda):
+    """Greedy generation with the token of step t+1 written by the device
+    sampler and read by the next step's embedding, no host sync in between
+    (every launch a programmatic dependent of the one before): the same
+    tokens as a run synchronised after every step, and as the oracle's own
+    greedy loop (forward() then sample_argmax, generate.cpp:76-102)."""
+    import torch
+    import tle
+    prompt, gen = 6, 18
+    n = prompt + gen
+    m = synth.make_model(seed=11, n_layers=2, n_vocab=32000, n_ctx=n)
+    dm = tle.DeviceModel(m)
+    ids = np.random.default_rng(11).integers(0, m.n_vocab, prompt).astype(np.int32)
+
+    def generate(sync):
+        ds = tle.DeviceState(dm)
+        toks = torch.zeros(n + 1, dtype=torch.int32, device="cuda")
+        toks[:prompt] = torch.from_numpy(ids).cuda()
+        for pos in range(n):
+            tle.forward(dm, ds, toks[pos:pos + 1], pos)
+            if pos >= prompt - 1:
+                tle.sample_argmax(ds.logits, toks[pos + 1:pos + 2])
+            if sync:
+                torch.cuda.synchronize()
+        return host(toks)[prompt:n + 1]
+
+    fast, synced = generate(False), generate(True)
+    assert np.array_equal(fast, synced)
+    hf = oracle.HostForward(m)
+    P = oracle.port()
+    want, tok = [], int(ids[0])
+    for pos in range(n):
+        tok = int(ids[pos]) if pos < prompt else tok
+        P.forward(hf, tok, pos)
+        if pos >= prompt - 1:
+            tok = P.sample_argmax(hf.logits)
+            want.append(tok)
+    assert list(synced) == want
+    assert tle.device_error() == 0

@@ -146,6 +146,31 @@ TLE_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t
         : "memory");
 }
 
+// Loads of data another CTA or an earlier grid wrote, issued after the
+// wait (griddepcontrol.wait, an mbarrier, an acquire fence) that makes it
+// visible: L2 (.cg, never a stale L1 line) and volatile with a memory
+// clobber, so the compiler cannot schedule them above that wait (the
+// __ldcg/__ldg intrinsics are plain inline asm without a memory operand,
+// and a const __restrict__ load may be treated as invariant and hoisted).
+TLE_DEV float ld_cg(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+TLE_DEV float4 ld_cg4(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+TLE_DEV int32_t ld_cg_s32(const int32_t* p) {
+    int32_t v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // 4-byte asynchronous global -> shared copy (cp.async), and an arrival on
 // `bar` once this thread's earlier cp.async copies have landed.  The arrive
 // form without .noinc raises the barrier's pending count when it executes,

@@ -160,7 +160,7 @@ __device__ __forceinline__ int cursor_page(TileCursor& c, const DecodeArgs& A, D
         c.pst ^= 2;           // the next prefetch goes to the other slot
     } else {
         if (c.pst & 1) cp_async_wait_all();   // an unused prefetch must land before its slot is reused
-        id = __ldg(pages + pi);
+        id = ld_cg_s32(pages + pi);
     }
     c.pst &= ~1;
     id = check_page(A, id);
@@ -411,11 +411,11 @@ __device__ __forceinline__ int coalesced_head(int i, int lane) { return 2 * i + 
 __device__ __forceinline__ void load_partial(const DecodeArgs& A, int s, int c, int lane,
                                              float& m, float& l, float4 (&o)[16]) {
     const float* P = A.partials + static_cast<size_t>(s + c) * kPartialFloats;
-    m = __ldcg(P + NH * HD + lane);
-    l = __ldcg(P + NH * HD + NH + lane);
+    m = ld_cg(P + NH * HD + lane);
+    l = ld_cg(P + NH * HD + NH + lane);
     const float4* src = reinterpret_cast<const float4*>(P) + lane;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) o[i] = __ldcg(src + 32 * i);
+    for (int i = 0; i < 16; ++i) o[i] = ld_cg4(src + 32 * i);
 }
 
 // The last CTA of sequence s combines the partials of CTAs sc.lo..sc.hi (its
@@ -909,10 +909,10 @@ __global__ void __launch_bounds__(256) merge_kernel(const __grid_constant__ Deco
             a0[u] = a1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (c0 + u <= hi) {
                 const float* P = A.partials + static_cast<size_t>(s + c0 + u) * kPartialFloats;
-                mc[u] = __ldcg(P + NH * HD + h);
-                lc[u] = __ldcg(P + NH * HD + NH + h);
-                a0[u] = __ldcg(reinterpret_cast<const float4*>(P + h * HD + d0));
-                a1[u] = __ldcg(reinterpret_cast<const float4*>(P + h * HD + d0 + 4));
+                mc[u] = ld_cg(P + NH * HD + h);
+                lc[u] = ld_cg(P + NH * HD + NH + h);
+                a0[u] = ld_cg4(reinterpret_cast<const float4*>(P + h * HD + d0));
+                a1[u] = ld_cg4(reinterpret_cast<const float4*>(P + h * HD + d0 + 4));
             }
         }
         float mn = m_run;

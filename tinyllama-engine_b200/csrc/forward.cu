@@ -36,9 +36,6 @@ constexpr int GT = 256;        // threads per GEMV CTA
 constexpr int GW = GT / 32;    // warps per GEMV CTA
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-__device__ __forceinline__ uint32_t ldg16(const uint8_t* p) {
-    return __ldg(reinterpret_cast<const unsigned short*>(p));
-}
 // 4-bit value n (0..15) minus 8, and an int8 stored as a byte, as floats:
 // 2^23 + v has v in its low mantissa bits, so one OR and one subtract do the
 // conversion exactly.
@@ -56,25 +53,27 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // Per-lane partial dot product of one weight row (GGUF layout) with xs.
+// The row is in shared memory (a TMA-staged tile) or in global memory;
+// plain loads serve both (the compiler sees which space a pointer is in).
 template <int T>
-__device__ __forceinline__ float row_dot(const uint8_t* __restrict__ row, const float* xs, int cols,
-                                         int lane);
+__device__ __forceinline__ float row_dot(const uint8_t* row, const float* xs, int cols, int lane);
+
+__device__ __forceinline__ uint32_t ld16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 // F32 (ops.cpp:251-262): 4 consecutive weights per lane (one per lane
 // when rows are not 16-byte multiples).
 template <>
-__device__ __forceinline__ float row_dot<kWF32>(const uint8_t* __restrict__ row, const float* xs,
-                                                int cols, int lane) {
+__device__ __forceinline__ float row_dot<kWF32>(const uint8_t* row, const float* xs, int cols, int lane) {
     float acc = 0.f;
     if (cols & 3) {
         const float* w = reinterpret_cast<const float*>(row);
-        for (int c = lane; c < cols; c += 32) acc = fmaf(__ldg(w + c), xs[c], acc);
+        for (int c = lane; c < cols; c += 32) acc = fmaf(w[c], xs[c], acc);
         return acc;
     }
     const float4* w = reinterpret_cast<const float4*>(row);
 #pragma unroll 4
     for (int c = lane; c < cols / 4; c += 32) {
-        const float4 a = __ldg(w + c);
+        const float4 a = w[c];
         const float4 x = *reinterpret_cast<const float4*>(xs + 4 * c);
         acc = fmaf(a.x, x.x, acc);
         acc = fmaf(a.y, x.y, acc);
@@ -87,18 +86,17 @@ __device__ __forceinline__ float row_dot<kWF32>(const uint8_t* __restrict__ row,
 // F16 (ops.cpp:342-356): 8 consecutive weights per lane (one per lane
 // when rows are not 16-byte multiples).
 template <>
-__device__ __forceinline__ float row_dot<kWF16>(const uint8_t* __restrict__ row, const float* xs,
-                                                int cols, int lane) {
+__device__ __forceinline__ float row_dot<kWF16>(const uint8_t* row, const float* xs, int cols, int lane) {
     float acc = 0.f;
     if (cols & 7) {
-        const unsigned short* w = reinterpret_cast<const unsigned short*>(row);
-        for (int c = lane; c < cols; c += 32) acc = fmaf(h2f(__ldg(w + c)), xs[c], acc);
+        const uint16_t* w = reinterpret_cast<const uint16_t*>(row);
+        for (int c = lane; c < cols; c += 32) acc = fmaf(h2f(w[c]), xs[c], acc);
         return acc;
     }
     const uint4* w = reinterpret_cast<const uint4*>(row);
 #pragma unroll 4
     for (int c = lane; c < cols / 8; c += 32) {
-        const uint4 a = __ldg(w + c);
+        const uint4 a = w[c];
         const float4 x0 = *reinterpret_cast<const float4*>(xs + 8 * c);
         const float4 x1 = *reinterpret_cast<const float4*>(xs + 8 * c + 4);
         acc = fmaf(h2f(a.x & 0xFFFFu), x0.x, acc);
@@ -118,16 +116,15 @@ __device__ __forceinline__ float row_dot<kWF16>(const uint8_t* __restrict__ row,
 // takes bytes 4t..4t+3: elements 4t..4t+3 and 16+4t..16+4t+3.  Its 8-term
 // block partial is scaled by d like the reference's block sum.
 template <>
-__device__ __forceinline__ float row_dot<kWQ4_0>(const uint8_t* __restrict__ row, const float* xs,
-                                                 int cols, int lane) {
+__device__ __forceinline__ float row_dot<kWQ4_0>(const uint8_t* row, const float* xs, int cols, int lane) {
     const int nb = cols >> 5;
     const int t = lane & 3;
     float acc = 0.f;
 #pragma unroll 4
     for (int b = lane >> 2; b < nb; b += 8) {
         const uint8_t* blk = row + 18 * b;
-        const float d = h2f(static_cast<uint16_t>(ldg16(blk)));
-        const uint32_t q = ldg16(blk + 2 + 4 * t) | (ldg16(blk + 4 + 4 * t) << 16);
+        const float d = h2f(static_cast<uint16_t>(ld16(blk)));
+        const uint32_t q = ld16(blk + 2 + 4 * t) | (ld16(blk + 4 + 4 * t) << 16);
         const float4 xl = *reinterpret_cast<const float4*>(xs + 32 * b + 4 * t);
         const float4 xh = *reinterpret_cast<const float4*>(xs + 32 * b + 16 + 4 * t);
         float s = nib_m8(q, 0) * xl.x;
@@ -146,18 +143,17 @@ __device__ __forceinline__ float row_dot<kWQ4_0>(const uint8_t* __restrict__ row
 // Q8_0 (ops.cpp:442-473): block = fp16 d + 32 int8.  Lane t takes elements
 // 8t..8t+7 of each of its blocks.
 template <>
-__device__ __forceinline__ float row_dot<kWQ8_0>(const uint8_t* __restrict__ row, const float* xs,
-                                                 int cols, int lane) {
+__device__ __forceinline__ float row_dot<kWQ8_0>(const uint8_t* row, const float* xs, int cols, int lane) {
     const int nb = cols >> 5;
     const int t = lane & 3;
     float acc = 0.f;
 #pragma unroll 4
     for (int b = lane >> 2; b < nb; b += 8) {
         const uint8_t* blk = row + 34 * b;
-        const float d = h2f(static_cast<uint16_t>(ldg16(blk)));
+        const float d = h2f(static_cast<uint16_t>(ld16(blk)));
         const uint8_t* qs = blk + 2 + 8 * t;
-        const uint32_t q0 = ldg16(qs) | (ldg16(qs + 2) << 16);
-        const uint32_t q1 = ldg16(qs + 4) | (ldg16(qs + 6) << 16);
+        const uint32_t q0 = ld16(qs) | (ld16(qs + 2) << 16);
+        const uint32_t q1 = ld16(qs + 4) | (ld16(qs + 6) << 16);
         const float4 x0 = *reinterpret_cast<const float4*>(xs + 32 * b + 8 * t);
         const float4 x1 = *reinterpret_cast<const float4*>(xs + 32 * b + 8 * t + 4);
         float s = s8f(q0, 0) * x0.x;
@@ -177,33 +173,95 @@ __device__ __forceinline__ float row_dot<kWQ8_0>(const uint8_t* __restrict__ row
 // scales[16], fp16 d.  Lane l takes position l of both halves: the four
 // 6-bit values built from ql[l], ql[l+32] and qh[l] of each half.
 template <>
-__device__ __forceinline__ float row_dot<kWQ6_K>(const uint8_t* __restrict__ row, const float* xs,
-                                                 int cols, int lane) {
+__device__ __forceinline__ float row_dot<kWQ6_K>(const uint8_t* row, const float* xs, int cols, int lane) {
     const int nb = cols >> 8;
     const int is = lane >> 4;
     float acc = 0.f;
     for (int b = 0; b < nb; ++b) {
         const uint8_t* blk = row + 210 * b;
-        const float d = h2f(static_cast<uint16_t>(ldg16(blk + 208)));
+        const float d = h2f(static_cast<uint16_t>(ld16(blk + 208)));
         const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint32_t l0 = __ldg(blk + 64 * h + lane);
-            const uint32_t l1 = __ldg(blk + 64 * h + lane + 32);
-            const uint32_t hh = __ldg(blk + 128 + 32 * h + lane);
+            const uint32_t l0 = blk[64 * h + lane];
+            const uint32_t l1 = blk[64 * h + lane + 32];
+            const uint32_t hh = blk[128 + 32 * h + lane];
             const float* X = xs + 256 * b + 128 * h;
             const int q1 = static_cast<int>((l0 & 15u) | ((hh & 3u) << 4)) - 32;
             const int q2 = static_cast<int>((l1 & 15u) | (((hh >> 2) & 3u) << 4)) - 32;
             const int q3 = static_cast<int>((l0 >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
             const int q4 = static_cast<int>((l1 >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
             const int8_t* S = sc + 8 * h + is;
-            acc = fmaf(d * static_cast<float>(__ldg(S + 0)) * static_cast<float>(q1), X[lane], acc);
-            acc = fmaf(d * static_cast<float>(__ldg(S + 2)) * static_cast<float>(q2), X[lane + 32], acc);
-            acc = fmaf(d * static_cast<float>(__ldg(S + 4)) * static_cast<float>(q3), X[lane + 64], acc);
-            acc = fmaf(d * static_cast<float>(__ldg(S + 6)) * static_cast<float>(q4), X[lane + 96], acc);
+            acc = fmaf(d * static_cast<float>(S[0]) * static_cast<float>(q1), X[lane], acc);
+            acc = fmaf(d * static_cast<float>(S[2]) * static_cast<float>(q2), X[lane + 32], acc);
+            acc = fmaf(d * static_cast<float>(S[4]) * static_cast<float>(q3), X[lane + 64], acc);
+            acc = fmaf(d * static_cast<float>(S[6]) * static_cast<float>(q4), X[lane + 96], acc);
         }
     }
     return acc;
+}
+
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// Nibble values of bytes j, k of w (each byte holding one 4-bit value) as the
+// float pair (n_j - 8, n_k - 8): the byte permute builds 2^23 + n exactly,
+// one packed subtract removes 2^23 + 8.
+__device__ __forceinline__ uint64_t nib_pair(uint32_t w, int j, int k) {
+    const float a = __int_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | j));
+    const float b = __int_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | k));
+    return add2(pk2(a, b), pk2(-8388616.0f, -8388616.0f));
+}
+
+// Q4_0 rows from shared memory, R rows at once: each lane's slice of the
+// input vector is read once per block and used for all R rows (reading it
+// per row made the kernel shared-memory bound).  Lane t = lane & 3 of a
+// block takes bytes 4t..4t+3 (elements 4t..4t+3 low nibbles, 16+4t..
+// high nibbles); products as packed f32x2 FMAs, the 8-term block partial
+// scaled by d as the reference does per block.
+template <int R>
+__device__ __forceinline__ void rows_dot_q4(const uint8_t* const (&rows)[R], const float* xs, int b_lo,
+                                            int b_hi, int lane, float (&acc)[R]) {
+    const int t = lane & 3;
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = 0.f;
+#pragma unroll 2
+    for (int b = b_lo + (lane >> 2); b < b_hi; b += 8) {
+        const float4 xl = *reinterpret_cast<const float4*>(xs + 32 * b + 4 * t);
+        const float4 xh = *reinterpret_cast<const float4*>(xs + 32 * b + 16 + 4 * t);
+        const uint64_t x01 = pk2(xl.x, xl.y), x23 = pk2(xl.z, xl.w);
+        const uint64_t h01 = pk2(xh.x, xh.y), h23 = pk2(xh.z, xh.w);
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const uint8_t* blk = rows[i] + 18 * b;
+            const float d = h2f(static_cast<uint16_t>(ld16(blk)));
+            const uint32_t q = ld16(blk + 2 + 4 * t) | (ld16(blk + 4 + 4 * t) << 16);
+            const uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
+            uint64_t s2 = fma2(nib_pair(lo, 0, 1), x01, 0ull);
+            s2 = fma2(nib_pair(lo, 2, 3), x23, s2);
+            s2 = fma2(nib_pair(hi, 0, 1), h01, s2);
+            s2 = fma2(nib_pair(hi, 2, 3), h23, s2);
+            const float2 s = up2(s2);
+            acc[i] = fmaf(d, s.x + s.y, acc[i]);
+        }
+    }
 }
 
 // Bulk prefetch into L2 of [p, p + bytes), trimmed inward to 16-byte
@@ -219,40 +277,100 @@ __device__ __forceinline__ void prefetch_l2(const uint8_t* p, size_t bytes) {
     }
 }
 
+// Stages the input vector into xs with ordered L2 loads (it is the previous
+// kernel's output), eight 16-byte loads in flight per thread before any is
+// stored; returns this thread's share of sum(x^2).
+__device__ __forceinline__ float stage_x(float* xs, const float* x, int cols, int tid) {
+    float ss = 0.f;
+    if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int n4 = cols >> 2;
+        for (int base = tid; base < n4; base += GT * 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * GT;
+                if (i < n4) v[j] = ld_cg4(reinterpret_cast<const float4*>(x) + i);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * GT;
+                if (i < n4) {
+                    reinterpret_cast<float4*>(xs)[i] = v[j];
+                    ss = fmaf(v[j].x, v[j].x, ss);
+                    ss = fmaf(v[j].y, v[j].y, ss);
+                    ss = fmaf(v[j].z, v[j].z, ss);
+                    ss = fmaf(v[j].w, v[j].w, ss);
+                }
+            }
+        }
+    } else {
+        for (int base = tid; base < cols; base += GT * 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * GT;
+                if (i < cols) v[j] = ld_cg(x + i);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * GT;
+                if (i < cols) {
+                    xs[i] = v[j];
+                    ss = fmaf(v[j], v[j], ss);
+                }
+            }
+        }
+    }
+    return ss;
+}
+
 // One launch: rows of up to three matrices that share the input vector
-// (q, k and v of a layer), or gate and up rows for SwiGLU.
-template <int T, int EPI>
+// (q, k and v of a layer), or gate and up rows for SwiGLU.  TMA: the CTA's
+// rows are one contiguous span of the weights; a single 1-D bulk copy (two
+// for SwiGLU) brings them into shared memory, issued before the wait on
+// the previous kernel.  Otherwise (rows not 16-byte multiples) the rows are
+// read from global memory after an L2 prefetch.
+template <int T, int EPI, bool TMA>
 __global__ void __launch_bounds__(GT) gemv_kernel(const __grid_constant__ GemvArgs a) {
-    extern __shared__ __align__(16) float xs[];
+    extern __shared__ __align__(16) unsigned char gsm[];
     __shared__ float red[GW];
+    __shared__ float part[2][GW][4];   // Q4_0 path: per column chunk, per row group partial sums
+    __shared__ __align__(8) uint64_t wbar;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rows_per_cta = GW * a.rpw;
+    const int rows_per_cta = a.rpc;
+    float* xs = reinterpret_cast<float*>(gsm);
+    unsigned char* tile = gsm + a.xs_bytes;
+    unsigned char* tile2 = tile + a.tile_bytes;
 
     int s = 0;
     while (s + 1 < a.n_seg && static_cast<int>(blockIdx.x) >= a.seg[s + 1].tile0) ++s;
     const GemvSeg& seg = a.seg[s];
     const int r0 = (static_cast<int>(blockIdx.x) - seg.tile0) * rows_per_cta;
     const int r1 = min(r0 + rows_per_cta, seg.rows);
+    const size_t off0 = static_cast<size_t>(r0) * a.row_bytes;
+    const uint32_t span = static_cast<uint32_t>(r1 - r0) * static_cast<uint32_t>(a.row_bytes);
 
+    // Weights are never written by a kernel: fetch them before the wait.
     if (tid == 0) {
-        const size_t off = static_cast<size_t>(r0) * a.row_bytes;
-        const size_t len = static_cast<size_t>(r1 - r0) * a.row_bytes;
-        prefetch_l2(seg.W + off, len);
-        if (EPI == kEpiSwiGLU) prefetch_l2(a.W2 + off, len);
+        if (TMA) {
+            mbar_init(&wbar, 1);
+            fence_barrier_init();
+            mbar_arrive_expect_tx(&wbar, (EPI == kEpiSwiGLU ? 2u : 1u) * span);
+            bulk_g2s_plain(tile, seg.W + off0, span, &wbar);
+            if (EPI == kEpiSwiGLU) bulk_g2s_plain(tile2, a.W2 + off0, span, &wbar);
+        } else {
+            prefetch_l2(seg.W + off0, span);
+            if (EPI == kEpiSwiGLU) prefetch_l2(a.W2 + off0, span);
+        }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // The input vector, normalised (rmsnorm, ops.cpp:1040-1054: x * rms *
     // weight with rms = 1 / sqrt(mean(x^2) + eps)) when a norm weight is
     // given.
-    float rms = 1.f;
+    float ss = stage_x(xs, a.x, a.cols, tid);
     if (a.norm_w) {
-        float ss = 0.f;
-        for (int i = tid; i < a.cols; i += GT) {
-            const float v = a.x[i];
-            ss = fmaf(v, v, ss);
-        }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
@@ -262,27 +380,91 @@ __global__ void __launch_bounds__(GT) gemv_kernel(const __grid_constant__ GemvAr
             if (lane == 0) red[0] = 1.0f / sqrtf(v / static_cast<float>(a.cols) + a.eps);
         }
         __syncthreads();
-        rms = red[0];
-        for (int i = tid; i < a.cols; i += GT) xs[i] = a.x[i] * rms * a.norm_w[i];
-    } else {
-        for (int i = tid; i < a.cols; i += GT) xs[i] = a.x[i];
+        const float rms = red[0];
+        for (int i = tid; i < a.cols; i += GT) xs[i] = xs[i] * rms * a.norm_w[i];
     }
     __syncthreads();
+    bool ok = true;
+    if (TMA) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&wbar, 0));
+        if (!ok) {
+            if (lane == 0) record_error(a.err, kErrWaitFull);
+            // the copy may still be in flight: wait once more before the
+            // CTA (and its shared memory) goes away
+            mbar_wait(&wbar, 0);
+        }
+    }
 
-    for (int k = 0; k < a.rpw; ++k) {
+    if constexpr (T == kWQ4_0 && TMA) {
+        // Warps = (GW / ks) row groups of 4 rows x ks column chunks; SwiGLU
+        // runs a group's 4 gate and 4 up rows together (8 rows sharing the
+        // input reads).  Chunk partials are summed in chunk order.
+        constexpr int R = (EPI == kEpiSwiGLU) ? 8 : 4;
+        const int ks = a.ks;
+        const int g = warp / ks, kc = warp - g * ks;
+        const int nb = a.cols >> 5;
+        const int chunk = ((nb + ks - 1) / ks + 7) & ~7;
+        const int b_lo = kc * chunk, b_hi = min(nb, b_lo + chunk);
+        const int rb = r0 + 4 * g;
+        float acc[R];
+        if (ok && rb < r1) {
+            const uint8_t* rp[R];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = min(rb + i, r1 - 1) - r0;   // rows past r1 repeat the last one
+                rp[i] = tile + static_cast<size_t>(rr) * a.row_bytes;
+                if (EPI == kEpiSwiGLU) rp[i + 4] = tile2 + static_cast<size_t>(rr) * a.row_bytes;
+            }
+            rows_dot_q4<R>(rp, xs, b_lo, b_hi, lane, acc);
+#pragma unroll
+            for (int i = 0; i < R; ++i) acc[i] = warp_sum(acc[i]);
+            if (lane == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    part[0][warp][i] = acc[i];
+                    if (EPI == kEpiSwiGLU) part[1][warp][i] = acc[i + 4];
+                }
+            }
+        }
+        __syncthreads();
+        if (ok && tid < rows_per_cta) {
+            const int gg = tid >> 2, i = tid & 3;
+            const int r = r0 + tid;
+            if (r < r1) {
+                float y = 0.f, u = 0.f;
+                for (int c = 0; c < ks; ++c) {
+                    y += part[0][gg * ks + c][i];
+                    if (EPI == kEpiSwiGLU) u += part[1][gg * ks + c][i];
+                }
+                if (EPI == kEpiSwiGLU) {
+                    // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
+                    seg.out[r] = (y * (1.0f / (1.0f + expf(-y)))) * u;
+                } else if (EPI == kEpiAdd) {
+                    seg.out[r] = ld_cg(seg.out + r) + y;
+                } else {
+                    seg.out[r] = y;
+                }
+            }
+        }
+    } else {
+    for (int k = 0; ok && k < a.rpw; ++k) {
         const int r = r0 + warp * a.rpw + k;
         if (r >= r1) break;
-        const size_t off = static_cast<size_t>(r) * a.row_bytes;
-        const float y = warp_sum(row_dot<T>(seg.W + off, xs, a.cols, lane));
+        const uint8_t* wr = TMA ? tile + static_cast<size_t>(r - r0) * a.row_bytes
+                                : seg.W + static_cast<size_t>(r) * a.row_bytes;
+        const float y = warp_sum(row_dot<T>(wr, xs, a.cols, lane));
         if (EPI == kEpiSwiGLU) {
-            const float u = warp_sum(row_dot<T>(a.W2 + off, xs, a.cols, lane));
+            const uint8_t* ur = TMA ? tile2 + static_cast<size_t>(r - r0) * a.row_bytes
+                                    : a.W2 + static_cast<size_t>(r) * a.row_bytes;
+            const float u = warp_sum(row_dot<T>(ur, xs, a.cols, lane));
             // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
             if (lane == 0) seg.out[r] = (y * (1.0f / (1.0f + expf(-y)))) * u;
         } else if (EPI == kEpiAdd) {
-            if (lane == 0) seg.out[r] += y;
+            if (lane == 0) seg.out[r] = ld_cg(seg.out + r) + y;
         } else {
             if (lane == 0) seg.out[r] = y;
         }
+    }
     }
 }
 
@@ -290,11 +472,11 @@ __global__ void __launch_bounds__(GT) gemv_kernel(const __grid_constant__ GemvAr
 // token outside [0, n_vocab) is reported (0x106) and gives a zero row.
 template <int T>
 __global__ void __launch_bounds__(256) embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ table,
-                                                     const int32_t* __restrict__ token, int n_vocab,
-                                                     int n_embd, uint32_t* err) {
+                                                     const int32_t* token, int n_vocab, int n_embd,
+                                                     uint32_t* err) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int t = *token;
+    const int t = ld_cg_s32(token);   // the previous step's sampler may have written it
     const bool ok = t >= 0 && t < n_vocab;
     if (!ok && threadIdx.x == 0 && blockIdx.x == 0) record_error(err, kErrBadToken);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_embd; i += gridDim.x * blockDim.x) {
@@ -311,8 +493,7 @@ __global__ void __launch_bounds__(256) embed_kernel(float* __restrict__ x, const
 // sample_argmax (ops.cpp:1587-1597): the first index of the maximum under
 // '>'.  A NaN never beats the running best, so NaNs after index 0 are
 // skipped; a NaN at index 0 makes the answer 0 (nothing compares greater).
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n,
-                                                      int32_t* __restrict__ out) {
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int n, int32_t* out) {
     __shared__ float sv[32];
     __shared__ int si[32];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -320,12 +501,23 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     const int tid = threadIdx.x;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = tid; i < n; i += 1024) {
-        float v = logits[i];
-        if (v != v) v = -INFINITY;           // NaN: never the maximum
-        if (bi == 0x7fffffff || v > bv) {    // first element of this thread, or strictly greater
-            bv = v;
-            bi = i;
+    for (int base = tid; base < n; base += 1024 * 8) {
+        float vs[8];                         // eight loads in flight, then the scan
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * 1024;
+            vs[j] = i < n ? ld_cg(logits + i) : -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * 1024;
+            float v = vs[j];
+            if (i >= n) break;
+            if (v != v) v = -INFINITY;           // NaN: never the maximum
+            if (bi == 0x7fffffff || v > bv) {    // first element of this thread, or strictly greater
+                bv = v;
+                bi = i;
+            }
         }
     }
 #pragma unroll
@@ -355,7 +547,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
             }
         }
         if (tid == 0) {
-            const float v0 = logits[0];
+            const float v0 = ld_cg(logits);
             *out = (v0 != v0) ? 0 : bi;
         }
     }
@@ -369,7 +561,10 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(float* out, const float* 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x;
     float ss = 0.f;
-    for (int i = tid; i < n; i += 1024) ss = fmaf(x[i], x[i], ss);
+    for (int i = tid; i < n; i += 1024) {
+        const float v = ld_cg(x + i);
+        ss = fmaf(v, v, ss);
+    }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
@@ -379,7 +574,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(float* out, const float* 
     }
     __syncthreads();
     const float rms = red[0];
-    for (int i = tid; i < n; i += 1024) out[i] = x[i] * rms * w[i];
+    for (int i = tid; i < n; i += 1024) out[i] = ld_cg(x + i) * rms * w[i];
 }
 
 // vec_add (ops.cpp:1165-1184): out += x.
@@ -387,7 +582,7 @@ __global__ void __launch_bounds__(256) vec_add_kernel(float* out, const float* x
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-        out[i] += x[i];
+        out[i] = ld_cg(out + i) + ld_cg(x + i);
 }
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -405,19 +600,25 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-template <int T, int EPI>
-cudaError_t launch_gemv_t(const GemvArgs& a, int n_tiles, cudaStream_t stream) {
+template <int T, int EPI, bool TMA>
+cudaError_t launch_gemv_k(const GemvArgs& a, int n_tiles, cudaStream_t stream) {
     static PerDeviceOnce once;
-    const size_t smem = static_cast<size_t>(a.cols) * sizeof(float);
+    const size_t smem = a.xs_bytes + (EPI == kEpiSwiGLU ? 2 : 1) * a.tile_bytes;
     cudaError_t e = once.run([&](int) {
-        return cudaFuncSetAttribute(gemv_kernel<T, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kGemvMaxCols * sizeof(float)));
+        return cudaFuncSetAttribute(gemv_kernel<T, EPI, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kGemvMaxSmem);
     });
     if (e != cudaSuccess) return e;
     GemvArgs copy = a;
     void* args[] = {&copy};
-    return launch_pdl(reinterpret_cast<const void*>(gemv_kernel<T, EPI>), dim3(n_tiles), dim3(GT),
+    return launch_pdl(reinterpret_cast<const void*>(gemv_kernel<T, EPI, TMA>), dim3(n_tiles), dim3(GT),
                       smem, stream, args);
+}
+
+template <int T, int EPI>
+cudaError_t launch_gemv_t(const GemvArgs& a, int n_tiles, cudaStream_t stream) {
+    return a.tile_bytes ? launch_gemv_k<T, EPI, true>(a, n_tiles, stream)
+                        : launch_gemv_k<T, EPI, false>(a, n_tiles, stream);
 }
 
 template <int EPI>
@@ -446,13 +647,41 @@ int weight_row_bytes(int type, int cols) {
 }
 
 cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream) {
-    const int rows_per_cta = GW * a.rpw;
+    const int n_mats = (epi == kEpiSwiGLU) ? 2 : 1;
+    int rows = 0;
+    bool tma = (a.row_bytes % 16) == 0;   // tiles of whole rows start 16-byte aligned
+    for (int s = 0; s < a.n_seg; ++s) {
+        rows += a.seg[s].rows;
+        tma = tma && (reinterpret_cast<uintptr_t>(a.seg[s].W) & 15) == 0;
+    }
+    if (epi == kEpiSwiGLU) tma = tma && (reinterpret_cast<uintptr_t>(a.W2) & 15) == 0;
+    if (rows == 0) return cudaSuccess;
+    a.xs_bytes = (static_cast<int>(a.cols * sizeof(float)) + 15) & ~15;
+    auto fits = [&](int rpc) {
+        return a.xs_bytes + n_mats * static_cast<long>(rpc) * a.row_bytes <= kGemvMaxSmem;
+    };
+    a.ks = 1;
+    a.rpc = GW * a.rpw;
+    bool q4 = false;
+    if (type == kWQ4_0 && tma) {
+        // shared-memory Q4_0 path: groups of 4 rows, the columns split in
+        // ks chunks so that short matrices still spread over many warps
+        const int nb = a.cols >> 5;
+        const int ks = rows >= 16384 ? 1 : (nb >= 128 ? 4 : (nb >= 48 ? 2 : 1));
+        if (fits((GW / ks) * 4)) {
+            a.ks = ks;
+            a.rpc = (GW / ks) * 4;
+            q4 = true;
+        }
+    }
+    if (!q4) tma = tma && fits(a.rpc);
+    a.tile_bytes = tma ? a.rpc * a.row_bytes : 0;
     int tiles = 0;
     for (int s = 0; s < a.n_seg; ++s) {
         a.seg[s].tile0 = tiles;
-        tiles += (a.seg[s].rows + rows_per_cta - 1) / rows_per_cta;
+        tiles += (a.seg[s].rows + a.rpc - 1) / a.rpc;
     }
-    if (tiles == 0) return cudaSuccess;
+    if (uint32_t* w = nullptr; error_word(&w) == cudaSuccess) a.err = w;
     switch (epi) {
     case kEpiStore: return launch_gemv_e<kEpiStore>(type, a, tiles, stream);
     case kEpiAdd: return launch_gemv_e<kEpiAdd>(type, a, tiles, stream);

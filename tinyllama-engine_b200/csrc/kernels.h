@@ -143,6 +143,7 @@ constexpr int kEpiStore = 0;    // out[r] = y
 constexpr int kEpiAdd = 1;      // out[r] += y (residual)
 constexpr int kEpiSwiGLU = 2;   // out[r] = silu(gate_r) * up_r (gate rows seg[0].W, up rows W2)
 constexpr int kGemvMaxCols = 16384;   // input vector in shared memory (64 KB)
+constexpr int kGemvMaxSmem = 160 * 1024;   // input vector + TMA-staged weight rows per CTA
 
 struct GemvSeg {
     const uint8_t* W;   // rows x cols, GGUF layout, row r at r * row_bytes
@@ -156,10 +157,15 @@ struct GemvArgs {
     const uint8_t* W2;      // SwiGLU: the up-projection rows (gate's layout)
     int cols;
     int row_bytes;
-    int rpw;                // rows per warp
+    int rpw;                // rows per warp (generic path)
+    int rpc;                // (set by launch_gemv) rows per CTA
+    int ks;                 // (set by launch_gemv) column chunks per row group (shared-memory Q4_0 path)
     const float* x;         // input [cols]
     const float* norm_w;    // RMSNorm weight applied to x first (nullptr: none)
     float eps;
+    int xs_bytes;           // (set by launch_gemv) shared bytes of the input vector
+    int tile_bytes;         // (set by launch_gemv) TMA-staged rows per CTA; 0: rows read from global
+    uint32_t* err;          // device error word
 };
 // Bytes of one row of `cols` weights of format `type`; -1 if unsupported.
 int weight_row_bytes(int type, int cols);
