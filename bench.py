@@ -17,6 +17,11 @@ ranks (strong scaling: the 256-sequence total is fixed).
 compiled unmodified into oracle/_ref) on a bounded sample of the same
 workload on all host cores.
 
+Secondary lines (N=1, unless --no-secondary): prefill (config 3), batched
+ragged decode (config 4, contiguous and paged), single-sequence decode
+(config 1), paged config 5, and end-to-end greedy generation on the device
+(config 2: the whole forward pass, tle_forward.h).  `--only NAME` runs one.
+
 Prints ONE JSON line (rank 0).
 """
 from __future__ import annotations
@@ -383,7 +388,8 @@ def main():
                                  "decode_config4": measure_config4(dev, peaks),
                                  "decode_config1": measure_config1(dev, peaks),
                                  "decode_config4_paged": measure_paged4(dev, peaks),
-                                 "decode_config5_paged": measure_paged5(dev, peaks)}
+                                 "decode_config5_paged": measure_paged5(dev, peaks),
+                                 "generate_config2": measure_config2(dev, peaks, steps=3)}
         if world == 1 and not args.no_cpu_baseline:
             gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
             line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
