@@ -215,3 +215,53 @@ def test_decode_batch_rejects_unknown_flags():
     rc = tle.lib().tle_decode_batch(ctypes.byref(shape), p, 1, 1, p, p, p, p, 0, 4, p, 1 << 20, None)
     assert rc == tle.TLE_ERR_INVALID
     assert "flags" in tle.lib().tle_last_error().decode()
+
+
+# ------------------------------------------------- forward-pass arguments
+def test_matmul_rejects_bad_arguments_without_gpu():
+    """Checked before any device work (fake, never dereferenced pointers)."""
+    L = tle.lib()
+    p = 0x200000
+    assert L.tle_matmul(p, p, p, 0, 64, tle_w("Q4_0"), None) == tle.TLE_ERR_INVALID       # rows 0
+    assert L.tle_matmul(p, p, p, 8, 33, tle_w("Q4_0"), None) == tle.TLE_ERR_UNSUPPORTED   # cols % 32
+    assert L.tle_matmul(p, p, p, 8, 300, tle_w("Q6_K"), None) == tle.TLE_ERR_UNSUPPORTED  # cols % 256
+    assert L.tle_matmul(p, p, p, 8, 64, 3, None) == tle.TLE_ERR_UNSUPPORTED               # Q4_1
+    assert L.tle_matmul(p, p + 2, p, 8, 64, tle_w("Q4_0"), None) == tle.TLE_ERR_INVALID   # unaligned W
+    assert L.tle_matmul(p, p, p, 8, 16385, tle_w("F32"), None) == tle.TLE_ERR_UNSUPPORTED # too wide
+    assert "cols" in L.tle_last_error().decode()
+
+
+def tle_w(name):
+    return {"F32": 0, "F16": 1, "Q4_0": 2, "Q8_0": 8, "Q6_K": 14}[name]
+
+
+def fake_model(**kw):
+    layers = (tle.Layer * 2)()
+    p = 0x400000
+    for i in range(2):
+        for f in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+            setattr(layers[i], f, tle.Weight(2, 0, p))
+        layers[i].attn_norm = p
+        layers[i].ffn_norm = p
+    args = dict(n_layers=2, n_embd=2048, n_head=32, n_head_kv=4, n_ff=5632, n_vocab=32000,
+                n_ctx=64, rope_freq_base=10000.0, rms_norm_eps=1e-5, reserved=0,
+                token_embd=tle.Weight(1, 0, p), output=tle.Weight(2, 0, p), output_norm=p,
+                layers=layers)
+    args.update(kw)
+    return tle.Model(**args), layers
+
+
+def test_forward_rejects_bad_models_without_gpu():
+    L = tle.lib()
+    p = 0x400000
+    st = tle.State(*([p] * 12), workspace_bytes=1 << 20)
+    m, keep = fake_model(n_head=16)                       # attention kernels need 32 heads
+    assert L.tle_forward(ctypes.byref(m), ctypes.byref(st), p, 0, None) == tle.TLE_ERR_UNSUPPORTED
+    m, keep = fake_model()
+    assert L.tle_forward(ctypes.byref(m), ctypes.byref(st), p, 64, None) == tle.TLE_ERR_INVALID  # pos
+    m, keep = fake_model(token_embd=tle.Weight(2, 0, p))  # Q4_0 embedding table
+    assert L.tle_forward(ctypes.byref(m), ctypes.byref(st), p, 0, None) == tle.TLE_ERR_UNSUPPORTED
+    m, keep = fake_model()
+    assert L.tle_forward(None, ctypes.byref(st), p, 0, None) == tle.TLE_ERR_INVALID
+    assert L.tle_forward(ctypes.byref(m), ctypes.byref(st), None, 0, None) == tle.TLE_ERR_INVALID
+    assert L.tle_forward_workspace_bytes(ctypes.byref(m)) > 0
