@@ -27,7 +27,7 @@ _build:
 _build/%.o: $(CSRC)/%.cu $(CSRC)/common.cuh $(CSRC)/kernels.h include/tle_attn.h include/tle_forward.h | _build
 	$(NVCC) $(NVFLAGS) -c $< -o $@
 
-_build/host_%.o: $(HOST)/%.cpp $(HOST)/ops_gpu.h include/tle_attn.h | _build
+_build/host_%.o: $(HOST)/%.cpp $(HOST)/ops_gpu.h include/tle_attn.h include/tle_forward.h | _build
 	$(CXX) -std=c++20 -O2 -g -Wall -Wextra -fPIC -Iinclude -I$(CUDA_HOME)/include -c $< -o $@
 
 $(LIB): $(CU_OBJS) $(HOST_OBJS)
@@ -38,7 +38,7 @@ oracle:
 
 cpptest: tests/cpp/test_ops_gpu
 
-tests/cpp/test_ops_gpu: $(LIB) tests/cpp/test_ops_gpu.cpp $(HOST)/ops_gpu.h
+tests/cpp/test_ops_gpu: $(LIB) tests/cpp/test_ops_gpu.cpp $(HOST)/ops_gpu.h include/tle_forward.h
 	g++ -std=c++20 -O2 -Wall -Iinclude -I$(HOST) tests/cpp/test_ops_gpu.cpp \
 	    -L$(PKG) -ltle_attn -Wl,-rpath,'$$ORIGIN/../../$(PKG)' -o tests/cpp/test_ops_gpu
 

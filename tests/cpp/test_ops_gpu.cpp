@@ -1,10 +1,14 @@
 // test_ops_gpu.cpp -- the reference's attention and rope test groups
-// (src/test_ops.cpp:295-546) run through the C++ layer of this library
+// (src/test_ops.cpp:295-546) and its matmul (all formats), rmsnorm, vec_add,
+// ffn_swiglu and argmax groups (test_ops.cpp:42-127, 202-268, 583-596,
+// 638-918) run through the C++ layer of this library
 // (tinyllama-engine_b200/host/ops_gpu.h), i.e. the call surface a forward.cpp
 // built on device buffers uses.  Same check()/approx_equal() conventions and
 // the same exit status contract (non-zero on failure) as the reference suite.
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <iostream>
 #include <vector>
 
@@ -208,6 +212,103 @@ void test_errors() {
     check("unsupported head count throws", threw);
 }
 
+// A device copy of host bytes (weights in GGUF layout).
+struct DevBytes {
+    void* p = nullptr;
+    template <class T>
+    explicit DevBytes(const std::vector<T>& h) : p(tle::device_alloc_bytes(h.size() * sizeof(T))) {
+        tle::copy_bytes_to_device(p, h.data(), h.size() * sizeof(T));
+    }
+    ~DevBytes() { tle::device_free(p); }
+};
+
+std::vector<float> matmul_dev(const void* W, std::size_t bytes, const std::vector<float>& x, int rows,
+                              int cols, int type) {
+    std::vector<unsigned char> w(static_cast<const unsigned char*>(W),
+                                 static_cast<const unsigned char*>(W) + bytes);
+    DevBytes dw(w);
+    Dev dx(x.size()), out(rows);
+    dx.put(x);
+    tle::matmul_gpu(out.p, dw.p, dx.p, rows, cols, type);
+    return out.get();
+}
+
+struct BlockQ8 { std::uint16_t d; std::int8_t qs[32]; };
+struct BlockQ4 { std::uint16_t d; std::uint8_t qs[16]; };
+struct BlockQ6 { std::uint8_t ql[128]; std::uint8_t qh[64]; std::int8_t scales[16]; std::uint16_t d; };
+static_assert(sizeof(BlockQ8) == 34 && sizeof(BlockQ4) == 18 && sizeof(BlockQ6) == 210, "GGUF blocks");
+
+void test_matmul() {
+    std::cout << "\n=== matmul (device, test_ops.cpp:42-89, 548-576, 638-918) ===\n";
+    float W[] = {1, 2, 3, 4, 5, 6};
+    auto o = matmul_dev(W, sizeof W, {1, 1, 1}, 2, 3, TLE_W_F32);
+    check("f32 row 0 = 6.0", approx_equal(o[0], 6.0f));
+    check("f32 row 1 = 15.0", approx_equal(o[1], 15.0f));
+    std::uint16_t Wh[] = {0x4000, 0x0000, 0x0000, 0x4200};
+    o = matmul_dev(Wh, sizeof Wh, {5.0f, 7.0f}, 2, 2, TLE_W_F16);
+    check("f16 row 0 = 10.0", approx_equal(o[0], 10.0f));
+    check("f16 row 1 = 21.0", approx_equal(o[1], 21.0f));
+    std::vector<float> I(256 * 256, 0.0f), x(256);
+    for (int i = 0; i < 256; i++) { I[i * 256 + i] = 1.0f; x[i] = static_cast<float>(i); }
+    o = matmul_dev(I.data(), I.size() * 4, x, 256, 256, TLE_W_F32);
+    bool ok = true;
+    for (int i = 0; i < 256; i++) ok = ok && approx_equal(o[i], x[i]);
+    check("256x256 identity", ok);
+    std::vector<float> ones32(32, 1.0f);
+    BlockQ8 b8{};
+    b8.d = 0x3C00;
+    for (auto& q : b8.qs) q = 2;
+    check("q8_0 d=1 qs=2 -> 64", approx_equal(matmul_dev(&b8, sizeof b8, ones32, 1, 32, TLE_W_Q8_0)[0], 64.0f, 0.1f));
+    b8.d = 0x3800;
+    for (int i = 0; i < 32; i++) b8.qs[i] = static_cast<std::int8_t>(i);
+    check("q8_0 d=0.5 qs=0..31 -> 248", approx_equal(matmul_dev(&b8, sizeof b8, ones32, 1, 32, TLE_W_Q8_0)[0], 248.0f, 0.5f));
+    BlockQ4 b4{};
+    b4.d = 0x3C00;
+    std::memset(b4.qs, 0x99, 16);
+    check("q4_0 nibbles 9 -> 32", approx_equal(matmul_dev(&b4, sizeof b4, ones32, 1, 32, TLE_W_Q4_0)[0], 32.0f, 0.5f));
+    b4.d = 0x4000;
+    std::memset(b4.qs, 0x88, 16);
+    check("q4_0 nibbles 8 -> 0", approx_equal(matmul_dev(&b4, sizeof b4, ones32, 1, 32, TLE_W_Q4_0)[0], 0.0f, 0.5f));
+    BlockQ6 b6[2]{};
+    for (auto& b : b6) {
+        b.d = 0x4000;
+        for (auto& s6 : b.scales) s6 = 1;
+    }
+    auto o6 = matmul_dev(b6, sizeof b6, std::vector<float>(256, 1.0f), 2, 256, TLE_W_Q6_K);
+    check("q6_k 2-row d=2 -> -16384", approx_equal(o6[0], -16384.0f, 1.0f) && approx_equal(o6[1], -16384.0f, 1.0f));
+}
+
+void test_norm_add_ffn_argmax() {
+    std::cout << "\n=== rmsnorm / vec_add / ffn_swiglu / argmax (device) ===\n";
+    Dev x(2), w(2), out(2);
+    x.put({3.0f, 4.0f});
+    w.put({2.0f, 0.5f});
+    tle::rmsnorm_gpu(out.p, x.p, w.p, 2, 0.0f);
+    auto o = out.get();
+    const float r = 1.0f / std::sqrt(12.5f);
+    check("rmsnorm weight scaling", approx_equal(o[0], 3.0f * r * 2.0f) && approx_equal(o[1], 4.0f * r * 0.5f));
+    Dev a(3), b(3);
+    a.put({1, 2, 3});
+    b.put({10, 20, 30});
+    tle::vec_add_gpu(a.p, b.p, 3);
+    o = a.get();
+    check("[1,2,3] + [10,20,30]", approx_equal(o[0], 11) && approx_equal(o[1], 22) && approx_equal(o[2], 33));
+    std::vector<float> Wg = {1, 0, 0, 1, 1, 1}, Wu = {1, 1, 0, 1, 1, 0}, Wd = {1, 0, 1, 0, 1, 0};
+    DevBytes dg(Wg), du(Wu), dd(Wd);
+    Dev in(2), hb(3), hb2(3), fo(2);
+    in.put({1.0f, 2.0f});
+    tle::ffn_swiglu_gpu(fo.p, in.p, hb.p, hb2.p, dg.p, du.p, dd.p, 3, 2, TLE_W_F32);
+    o = fo.get();
+    auto silu = [](float v) { return v / (1.0f + std::exp(-v)); };
+    check("ffn out[0]", approx_equal(o[0], silu(1) * 3 + silu(3), 1e-3f));
+    check("ffn out[1]", approx_equal(o[1], silu(2) * 2, 1e-3f));
+    Dev lg(4);
+    lg.put({1.0f, 5.0f, 3.0f, 2.0f});
+    check("argmax picks index 1", tle::sample_argmax_gpu(lg.p, 4) == 1);
+    lg.put({-1.0f, -5.0f, -0.5f, -2.0f});
+    check("argmax all negatives picks index 2", tle::sample_argmax_gpu(lg.p, 4) == 2);
+}
+
 }  // namespace
 
 int main() {
@@ -215,6 +316,8 @@ int main() {
         test_attention();
         test_rope();
         test_errors();
+        test_matmul();
+        test_norm_add_ffn_argmax();
         tle::device_sync();
     } catch (const std::exception& e) {
         std::cerr << "error: " << e.what() << "\n";

@@ -1,5 +1,7 @@
 """Runs tests/cpp/test_ops_gpu: the reference suite's attention and rope
-groups (src/test_ops.cpp:295-546) through the C++20 ops_gpu.h layer."""
+groups (src/test_ops.cpp:295-546) and its matmul / rmsnorm / vec_add /
+ffn_swiglu / argmax groups (test_ops.cpp:42-127, 202-268, 583-596,
+638-918) through the C++20 ops_gpu.h layer."""
 import os
 import subprocess
 

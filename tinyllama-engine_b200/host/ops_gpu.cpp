@@ -42,6 +42,56 @@ void rope_attention_gpu(float* out, const float* q, const float* k, const float*
                              attention_workspace_floats(cfg) * sizeof(float), stream));
 }
 
+void matmul_gpu(float* out, const void* W, const float* x, int rows, int cols, int type, void* stream) {
+    check(tle_matmul(out, W, x, rows, cols, type, stream));
+}
+
+void rmsnorm_gpu(float* out, const float* x, const float* weight, int size, float eps, void* stream) {
+    check(tle_rmsnorm(out, x, weight, size, eps, stream));
+}
+
+void vec_add_gpu(float* out, const float* x, int size, void* stream) {
+    check(tle_vec_add(out, x, size, stream));
+}
+
+void ffn_swiglu_gpu(float* out, const float* input, float* hb, float* hb2, const void* W_gate,
+                    const void* W_up, const void* W_down, int n_ff, int n_embd, int type,
+                    void* stream) {
+    check(tle_ffn_swiglu(out, input, hb, hb2, W_gate, W_up, W_down, n_ff, n_embd, type, stream));
+}
+
+int sample_argmax_gpu(const float* logits, int n_vocab, void* stream) {
+    int32_t* d = static_cast<int32_t*>(device_alloc_bytes(sizeof(int32_t)));
+    int32_t h = 0;
+    try {
+        check(tle_sample_argmax(logits, n_vocab, d, stream));
+        cuda_check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "sync");
+        copy_bytes_to_host(&h, d, sizeof h);
+    } catch (...) {
+        device_free(d);
+        throw;
+    }
+    device_free(d);
+    return h;
+}
+
+void forward_gpu(const tle_model_t& model, const tle_state_t& state, const int32_t* token, int pos,
+                 void* stream) {
+    check(tle_forward(&model, &state, token, pos, stream));
+}
+
+void* device_alloc_bytes(std::size_t n) {
+    void* p = nullptr;
+    cuda_check(cudaMalloc(&p, std::max<std::size_t>(n, 1)), "cudaMalloc");
+    return p;
+}
+void copy_bytes_to_device(void* dst, const void* src, std::size_t n) {
+    cuda_check(cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+}
+void copy_bytes_to_host(void* dst, const void* src, std::size_t n) {
+    cuda_check(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+}
+
 float* device_alloc_floats(std::size_t n) {
     void* p = nullptr;
     cuda_check(cudaMalloc(&p, std::max<std::size_t>(n, 1) * sizeof(float)), "cudaMalloc");

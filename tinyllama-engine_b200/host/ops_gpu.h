@@ -7,6 +7,10 @@
 //             layer, pos, cfg)
 //   rope + attention (forward.cpp:192-208)      tle::rope_attention_gpu(...)
 //   RunState (run_state.h:27-182)               tle::DeviceRunState
+//   matmul(out, W, x, rows, cols, type)         tle::matmul_gpu(...)      ops.h:64-66
+//   rmsnorm / vec_add / ffn_swiglu              tle::rmsnorm_gpu, ...     ops.h:95-96, 143, 232-235
+//   sample_argmax(logits, n_vocab)              tle::sample_argmax_gpu    ops.h:249
+//   forward(model, state, token, pos)           tle::forward_gpu          forward.h:16
 //
 // All pointers are device pointers.  Errors throw std::runtime_error, the
 // reference's convention (e.g. ops.cpp:978-979, forward.cpp:143-145).
@@ -16,9 +20,11 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "tle_attn.h"
+#include "tle_forward.h"
 
 namespace tle {
 
@@ -78,8 +84,42 @@ void rope_attention_gpu(float* out, const float* q, const float* k, const float*
                         float* key_cache, float* value_cache, float* att, int layer, int pos,
                         const AttnConfig& cfg, void* stream = nullptr);
 
+// ---- the forward pass around attention (tle_forward.h) ----
+// Weights are device copies of the GGUF tensor bytes; `type` is the ggml
+// type (the reference's ggml_type enum converts implicitly through the
+// template overloads).
+void matmul_gpu(float* out, const void* W, const float* x, int rows, int cols, int type,
+                void* stream = nullptr);
+void rmsnorm_gpu(float* out, const float* x, const float* weight, int size, float eps,
+                 void* stream = nullptr);
+void vec_add_gpu(float* out, const float* x, int size, void* stream = nullptr);
+void ffn_swiglu_gpu(float* out, const float* input, float* hb, float* hb2, const void* W_gate,
+                    const void* W_up, const void* W_down, int n_ff, int n_embd, int type,
+                    void* stream = nullptr);
+// ops.h:249 returns the token on the host (synchronises); the tle_sample_argmax
+// C call leaves it in device memory for a device-fed loop.
+int sample_argmax_gpu(const float* logits, int n_vocab, void* stream = nullptr);
+template <class E, class = std::enable_if_t<std::is_enum_v<E>>>
+void matmul_gpu(float* out, const void* W, const float* x, int rows, int cols, E type,
+                void* stream = nullptr) {
+    matmul_gpu(out, W, x, rows, cols, static_cast<int>(type), stream);
+}
+template <class E, class = std::enable_if_t<std::is_enum_v<E>>>
+void ffn_swiglu_gpu(float* out, const float* input, float* hb, float* hb2, const void* W_gate,
+                    const void* W_up, const void* W_down, int n_ff, int n_embd, E type,
+                    void* stream = nullptr) {
+    ffn_swiglu_gpu(out, input, hb, hb2, W_gate, W_up, W_down, n_ff, n_embd, static_cast<int>(type),
+                   stream);
+}
+// forward.h:16 for the token *token (device int32) at position pos.
+void forward_gpu(const tle_model_t& model, const tle_state_t& state, const int32_t* token, int pos,
+                 void* stream = nullptr);
+
 // Device-memory helpers so C++ callers need no CUDA headers of their own.
 float* device_alloc_floats(std::size_t n);
+void* device_alloc_bytes(std::size_t n);
+void copy_bytes_to_device(void* dst, const void* src, std::size_t n);
+void copy_bytes_to_host(void* dst, const void* src, std::size_t n);
 void device_free(void* p);
 void copy_to_device(float* dst, const float* src, std::size_t n);
 void copy_to_host(float* dst, const float* src, std::size_t n);
