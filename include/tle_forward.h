@@ -62,6 +62,23 @@ int tle_ffn_swiglu(float* out, const float* input, float* hb, float* hb2, const 
  * '>' scan; a NaN at index 0 gives 0. */
 int tle_sample_argmax(const float* logits, int n_vocab, int32_t* token, void* stream);
 
+/* sample_temperature ops.h:262 and sample_top_p ops.h:278 with the uniform
+ * draw r in [0, 1) passed in (the reference draws it from its own unseeded
+ * std::mt19937, ops.cpp:1571; pass dist(rng) from any generator).  As in the
+ * reference the logits are scaled by 1/temperature when temperature != 1
+ * and > 0 and overwritten with their softmax; the token is written to
+ * *token (device int32).  Temperature: the first index whose running
+ * probability sum exceeds r (n_vocab - 1 if none).  Top-p: the most probable
+ * tokens, sorted by probability (ties by index), up to a cumulative sum
+ * >= top_p; r scaled by that sum picks among them in that order.  The
+ * reference sorts only its 100 most probable tokens (std::partial_sort)
+ * and walks any longer nucleus in an unspecified order; here up to 2048
+ * tokens are sorted and a nucleus is cut at 2048.  n_vocab <= 40960. */
+int tle_sample_temperature(float* logits, int n_vocab, float temperature, float r, int32_t* token,
+                           void* stream);
+int tle_sample_top_p(float* logits, int n_vocab, float temperature, float top_p, float r,
+                     int32_t* token, void* stream);
+
 /* ---- forward() ---- */
 
 typedef struct {

@@ -240,6 +240,88 @@ int oracle_sample_argmax(const float *logits, int n_vocab)
     return best;
 }
 
+/* softmax(): ops.cpp:1072-1091 (max, exp and sum, multiply by 1/sum). */
+int oracle_softmax_inplace(float *x, int size)
+{
+    float max_val = x[0];
+    for (int i = 1; i < size; i++)
+        if (x[i] > max_val) max_val = x[i];
+    float sum = 0.0f;
+    for (int i = 0; i < size; i++) {
+        x[i] = expf(x[i] - max_val);
+        sum += x[i];
+    }
+    float inv_sum = 1.0f / sum;
+    for (int i = 0; i < size; i++) x[i] *= inv_sum;
+    return 0;
+}
+
+/* sample_temperature(): ops.cpp:1624-1651 with the uniform draw r passed in
+ * (the reference draws it from an unseeded mt19937, ops.cpp:1571-1574,
+ * 1642-1643).  Scales logits by 1/T when T != 1 and T > 0, softmax in place,
+ * then the first index whose running sum exceeds r; n_vocab - 1 if none. */
+int oracle_sample_temperature(float *logits, int n_vocab, float temperature, float r)
+{
+    if (temperature != 1.0f && temperature > 0.0f) {
+        float inv_temp = 1.0f / temperature;
+        for (int i = 0; i < n_vocab; i++) logits[i] *= inv_temp;
+    }
+    oracle_softmax_inplace(logits, n_vocab);
+    float cumsum = 0.0f;
+    for (int i = 0; i < n_vocab; i++) {
+        cumsum += logits[i];
+        if (cumsum > r) return i;
+    }
+    return n_vocab - 1;
+}
+
+/* sample_top_p(): ops.cpp:1677-1722 with r passed in.  The reference sorts
+ * the min(n, 100) most probable indices (std::partial_sort, descending; the
+ * rest stay in an unspecified order); here all indices are sorted by
+ * (probability descending, index ascending), which is the reference's order
+ * whenever the nucleus has at most 100 tokens and no tied probabilities. */
+static const float *g_sort_p;
+static int cmp_desc(const void *a, const void *b)
+{
+    int i = *(const int *)a, j = *(const int *)b;
+    float pi = g_sort_p[i], pj = g_sort_p[j];
+    if (pi > pj) return -1;
+    if (pi < pj) return 1;
+    return (i > j) - (i < j);
+}
+int oracle_sample_top_p(float *logits, int n_vocab, float temperature, float top_p, float r)
+{
+    if (temperature != 1.0f && temperature > 0.0f) {
+        float inv_temp = 1.0f / temperature;
+        for (int i = 0; i < n_vocab; i++) logits[i] *= inv_temp;
+    }
+    oracle_softmax_inplace(logits, n_vocab);
+    int *idx = (int *)malloc(sizeof(int) * (size_t)n_vocab);
+    if (!idx) return -1;
+    for (int i = 0; i < n_vocab; i++) idx[i] = i;
+    g_sort_p = logits;
+    qsort(idx, (size_t)n_vocab, sizeof(int), cmp_desc);
+    float cumsum = 0.0f;
+    int cutoff = 0;
+    for (int i = 0; i < n_vocab; i++) {
+        cumsum += logits[idx[i]];
+        cutoff = i + 1;
+        if (cumsum >= top_p) break;
+    }
+    float rr = r * cumsum;
+    float running = 0.0f;
+    int tok = idx[0];
+    for (int i = 0; i < cutoff; i++) {
+        running += logits[idx[i]];
+        if (running > rr) {
+            tok = idx[i];
+            break;
+        }
+    }
+    free(idx);
+    return tok;
+}
+
 /* ------------------------------------------------------------ forward() */
 
 #include "fw_model.h"

@@ -156,6 +156,21 @@ class _Lib:
     def sample_argmax(self, logits) -> int:
         return int(self._fn("sample_argmax", [_f, _i], _i)(_fp(logits), logits.size))
 
+    # ops.h:262 / 278 with the uniform draw r given (port only: the reference
+    # draws r from its own unseeded generator, see sample_top_p_reference)
+    def sample_temperature(self, logits, temperature, r) -> int:
+        f = self._fn("sample_temperature", [_f, _i, ctypes.c_float, ctypes.c_float], _i)
+        return int(f(_fp(logits), logits.size, temperature, r))
+
+    def sample_top_p(self, logits, temperature, top_p, r) -> int:
+        f = self._fn("sample_top_p", [_f, _i, ctypes.c_float, ctypes.c_float, ctypes.c_float], _i)
+        return int(f(_fp(logits), logits.size, temperature, top_p, r))
+
+    # the reference's own sample_top_p (its internal random draw)
+    def sample_top_p_reference(self, logits, temperature, top_p) -> int:
+        f = self._fn("sample_top_p", [_f, _i, ctypes.c_float, ctypes.c_float], _i)
+        return int(f(_fp(logits), logits.size, temperature, top_p))
+
     # forward.cpp:178-265 on a HostForward (logits in hf.logits)
     def forward(self, hf: "HostForward", token: int, pos: int):
         f = self._fn("forward", [ctypes.POINTER(FwModel), ctypes.POINTER(FwState), _i, _i], _i)

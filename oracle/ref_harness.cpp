@@ -141,6 +141,15 @@ int ref_sample_argmax(const float* logits, int n_vocab) { return sample_argmax(l
 
 void ref_set_num_threads(int n) { set_num_threads(n); }
 
+// ops.h:262, 278 as the reference runs them: the uniform draw comes from its
+// own unseeded generator (ops.cpp:1571), so these are nondeterministic.
+int ref_sample_temperature(float* logits, int n_vocab, float temperature) {
+    return sample_temperature(logits, n_vocab, temperature);
+}
+int ref_sample_top_p(float* logits, int n_vocab, float temperature, float top_p) {
+    return sample_top_p(logits, n_vocab, temperature, top_p);
+}
+
 // forward() (src/forward.cpp:178-265) composed from the reference's own ops
 // in the same order, for one token at position pos.  The embedding lookup is
 // embed_token() (forward.cpp:35-60, static there) for F16/F32 tables through

@@ -307,6 +307,24 @@ void test_norm_add_ffn_argmax() {
     check("argmax picks index 1", tle::sample_argmax_gpu(lg.p, 4) == 1);
     lg.put({-1.0f, -5.0f, -0.5f, -2.0f});
     check("argmax all negatives picks index 2", tle::sample_argmax_gpu(lg.p, 4) == 2);
+    // test_ops.cpp:598-633
+    Dev s5(5);
+    bool valid = true;
+    for (int trial = 0; trial < 10; trial++) {
+        s5.put({1.0f, 10.0f, 2.0f, 0.5f, 0.1f});
+        const int t = tle::sample_temperature_gpu(s5.p, 5, 1.0f);
+        valid = valid && t >= 0 && t < 5;
+        s5.put({1.0f, 10.0f, 2.0f, 0.5f, 0.1f});
+        const int u = tle::sample_top_p_gpu(s5.p, 5, 0.8f, 0.9f);
+        valid = valid && u >= 0 && u < 5;
+    }
+    check("temperature / top-p sampling: valid token IDs", valid);
+    int top_count = 0;
+    for (int trial = 0; trial < 20; trial++) {
+        s5.put({0.0f, 100.0f, 0.0f, 0.0f, 0.0f});
+        if (tle::sample_top_p_gpu(s5.p, 5, 0.5f, 0.1f) == 1) top_count++;
+    }
+    check("top-p with dominant logit picks it consistently", top_count >= 18);
 }
 
 }  // namespace

@@ -252,3 +252,67 @@ def test_greedy_generation_device_fed_matches_synced_and_oracle(cuda):
             want.append(tok)
     assert list(synced) == want
     assert tle.device_error() == 0
+
+
+def _probs(logits, temperature):
+    x = logits.astype(np.float32).copy()
+    if temperature != 1.0 and temperature > 0:
+        x *= np.float32(1.0) / np.float32(temperature)
+    e = np.exp(x - x.max(), dtype=np.float32)
+    return e / e.sum(dtype=np.float32)
+
+
+@pytest.mark.parametrize("scale,temperature", [(1.0, 1.0), (3.0, 0.7), (0.2, 1.5)])
+def test_temperature_sampling_matches_oracle(cuda, scale, temperature):
+    """With the same uniform draw r the device picks the oracle's token.  The
+    draws sit in the middle of a token's cumulative-probability interval
+    (sequential fp32 sums, as the reference's), away from the summation-
+    order differences; the logits are left as the probabilities, like the
+    reference."""
+    import torch
+    import tle
+    rng = np.random.default_rng(int(scale * 10))
+    lg = (rng.standard_normal(32000) * scale).astype(np.float32)
+    p = _probs(lg, temperature)
+    c = np.cumsum(p, dtype=np.float32)
+    P = oracle.port()
+    picks = [int(i) for i in np.argsort(-p)[:6]] + [int(x) for x in rng.integers(0, 32000, 6)]
+    tested = 0
+    for i in picks:
+        lo = float(c[i - 1]) if i else 0.0
+        if float(c[i]) - lo < 2e-5 or float(c[i]) >= 1.0:
+            continue
+        r = (lo + float(c[i])) / 2
+        want = P.sample_temperature(lg.copy(), temperature, r)
+        dl = dev(lg)
+        t = torch.zeros(1, dtype=torch.int32, device="cuda")
+        tle.sample_temperature(dl, t, temperature, r)
+        assert int(host(t)[0]) == want, (i, want)
+        assert np.allclose(host(dl), p, rtol=1e-5, atol=1e-9)
+        tested += 1
+    assert tested >= 3
+
+
+@pytest.mark.parametrize("scale,top_p", [(6.0, 0.9), (4.5, 0.9), (3.0, 0.5), (9.0, 0.95)])
+def test_top_p_sampling_matches_oracle(cuda, scale, top_p):
+    import torch
+    import tle
+    rng = np.random.default_rng(int(scale * 100))
+    lg = (rng.standard_normal(32000) * scale).astype(np.float32)
+    temperature = 0.8
+    p = _probs(lg, temperature)
+    order = np.argsort(-p, kind="stable")
+    cs = np.cumsum(p[order].astype(np.float64))
+    m = int(np.searchsorted(cs, top_p) + 1)
+    total = cs[m - 1]
+    P = oracle.port()
+    for k in range(min(m, 5)):
+        lo = cs[k - 1] if k else 0.0
+        if cs[k] - lo < 1e-4 * total:
+            continue
+        r = float((lo + cs[k]) / 2 / total)
+        want = P.sample_top_p(lg.copy(), temperature, top_p, r)
+        t = torch.zeros(1, dtype=torch.int32, device="cuda")
+        tle.sample_top_p(dev(lg), t, temperature, top_p, r)
+        assert int(host(t)[0]) == want, (k, m, want)
+        assert want == int(order[k])

@@ -126,3 +126,45 @@ def test_forward_bit_exact_vs_reference(wtype, out_type):
         assert np.all(np.isfinite(hp.logits))
         assert np.array_equal(hp.logits, hr.logits), pos
     assert np.array_equal(hp.bufs["key_cache"], hr.bufs["key_cache"])
+
+
+def _probs(logits, temperature):
+    x = logits.astype(np.float32).copy()
+    if temperature != 1.0 and temperature > 0:
+        x *= np.float32(1.0) / np.float32(temperature)
+    e = np.exp(x - x.max(), dtype=np.float32)
+    return e / e.sum(dtype=np.float32)
+
+
+def test_sampling_known_answers_and_reference_draws():
+    """test_ops.cpp:598-633: temperature and top-p give valid ids, and top-p
+    with a dominant logit keeps picking it; the oracle (uniform draw passed
+    in) agrees with the reference's own draws: every reference top-p token
+    lies in the oracle's nucleus (nuclei of at most 100 tokens, which the
+    reference sorts fully)."""
+    P = oracle.port()
+    rng = np.random.default_rng(9)
+    for r in rng.random(10):
+        tok = P.sample_temperature(np.array([1.0, 10.0, 2.0, 0.5, 0.1], np.float32), 1.0, float(r))
+        assert 0 <= tok < 5                                        # test_ops.cpp:601-610
+        tok = P.sample_top_p(np.array([1.0, 10.0, 2.0, 0.5, 0.1], np.float32), 0.8, 0.9, float(r))
+        assert 0 <= tok < 5                                        # test_ops.cpp:613-621
+        dom = np.array([0.0, 100.0, 0.0, 0.0, 0.0], np.float32)
+        assert P.sample_top_p(dom, 0.5, 0.1, float(r)) == 1       # test_ops.cpp:624-633
+    lg = np.array([1.0, 2.0, 3.0], np.float32)
+    p = _probs(lg, 1.0)
+    assert P.sample_temperature(lg.copy(), 1.0, float(p[0] / 2)) == 0
+    assert P.sample_temperature(lg.copy(), 1.0, float(p[0] + p[1] / 2)) == 1
+    assert P.sample_temperature(lg.copy(), 1.0, 0.99999) == 2
+    if not oracle.have_reference():
+        return
+    R = oracle.reference()
+    for scale in (4.5, 6.0):
+        lg = rng.standard_normal(32000).astype(np.float32) * scale
+        p = _probs(lg, 0.8)
+        order = np.argsort(-p, kind="stable")
+        m = int(np.searchsorted(np.cumsum(p[order]), 0.9) + 1)
+        assert m <= 100
+        nucleus = set(order[:m].tolist())
+        for _ in range(100):
+            assert R.sample_top_p_reference(lg.copy(), 0.8, 0.9) in nucleus

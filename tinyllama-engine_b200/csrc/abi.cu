@@ -739,6 +739,34 @@ int tle_sample_argmax(const float* logits, int n_vocab, int32_t* token, void* st
     return ok();
 }
 
+}  // extern "C"
+
+namespace {
+int sample_common(float* logits, int n_vocab, float temperature, float top_p, float r, bool use_top_p,
+                  int32_t* token, void* stream) {
+    if (!logits || !token) return set_error(TLE_ERR_INVALID, "null pointer argument");
+    if (n_vocab <= 0 || n_vocab > tle::kSampleMaxVocab)
+        return set_error(TLE_ERR_UNSUPPORTED, "n_vocab %d outside [1, %d]", n_vocab, tle::kSampleMaxVocab);
+    if (!(r >= 0.0f && r < 1.0f)) return set_error(TLE_ERR_INVALID, "r must be in [0, 1)");
+    cudaError_t e = tle::launch_sample(logits, n_vocab, temperature, top_p, r, use_top_p, token,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "sample");
+    return ok();
+}
+}  // namespace
+
+extern "C" {
+
+int tle_sample_temperature(float* logits, int n_vocab, float temperature, float r, int32_t* token,
+                           void* stream) {
+    return sample_common(logits, n_vocab, temperature, 1.0f, r, false, token, stream);
+}
+
+int tle_sample_top_p(float* logits, int n_vocab, float temperature, float top_p, float r,
+                     int32_t* token, void* stream) {
+    return sample_common(logits, n_vocab, temperature, top_p, r, true, token, stream);
+}
+
 size_t tle_forward_workspace_bytes(const tle_model_t* model) {
     if (!model || model->n_ctx <= 0) return 0;
     return partial_bytes(tle::kMaxCtas + 1);

@@ -553,6 +553,232 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int n
     }
 }
 
+// sample_temperature / sample_top_p (ops.cpp:1624-1722) with the uniform
+// draw r given.  One CTA: the row is scaled by 1/T (when T != 1 and T > 0),
+// turned into probabilities (softmax ops.cpp:1072-1091: max, exp, times
+// 1/sum) in shared memory and written back over the logits as the
+// reference does.  Temperature: thread t owns the contiguous chunk t of the
+// row; chunk sums, a block scan, then the owner of the first crossing of r
+// walks its chunk in index order (n - 1 if the sum never exceeds r).  Top-p:
+// the largest threshold whose tail mass reaches top_p (binary search on
+// the float bits), the tokens at or above it (at most kTopPMax, the most
+// probable kept when more) bitonic-sorted by (probability descending, index
+// ascending), then one thread walks them as the reference walks its
+// partially sorted order: cumulative sum to top_p, r scaled by it, first
+// running sum above it.
+constexpr int kSampleThreads = 1024;
+constexpr int kTopPMax = 2048;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float w = warp_sum(red[threadIdx.x]);
+        if (threadIdx.x == 0) red[0] = w;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+template <bool TOP_P>
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(float* logits, int n, float temperature,
+                                                                float top_p, float r, int32_t* out) {
+    extern __shared__ __align__(16) float sp[];     // [n] probabilities, then top-p candidates
+    __shared__ float red[32];
+    __shared__ int best;
+    __shared__ int cnt;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x;
+    const bool scale = temperature != 1.0f && temperature > 0.0f;
+    const float inv_temp = scale ? 1.0f / temperature : 1.0f;
+    float mx = -INFINITY;
+    for (int base = tid; base < n; base += kSampleThreads * 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * kSampleThreads;
+            v[j] = i < n ? ld_cg(logits + i) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = base + j * kSampleThreads;
+            if (i < n) {
+                const float x = scale ? v[j] * inv_temp : v[j];
+                sp[i] = x;
+                mx = fmaxf(mx, x);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid < 32) {
+        float w = red[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+        if (tid == 0) red[0] = w;
+    }
+    __syncthreads();
+    mx = red[0];
+    float sum = 0.f;
+    for (int i = tid; i < n; i += kSampleThreads) {
+        const float e = expf(sp[i] - mx);
+        sp[i] = e;
+        sum += e;
+    }
+    sum = block_sum(sum, red);
+    const float inv_sum = 1.0f / sum;
+    for (int i = tid; i < n; i += kSampleThreads) {
+        const float p = sp[i] * inv_sum;
+        sp[i] = p;
+        logits[i] = p;
+    }
+    __syncthreads();
+
+    if (!TOP_P) {
+        const int per = (n + kSampleThreads - 1) / kSampleThreads;
+        const int c0 = min(n, tid * per), c1 = min(n, c0 + per);
+        float cs = 0.f;
+        for (int i = c0; i < c1; ++i) cs += sp[i];
+        // inclusive block scan of the chunk sums (warp shuffles, then one
+        // warp over the warp totals)
+        float incl = cs;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, incl, o);
+            if ((tid & 31) >= o) incl += y;
+        }
+        if ((tid & 31) == 31) red[tid >> 5] = incl;
+        if (tid == 0) best = n - 1;
+        __syncthreads();
+        if (tid < 32) {
+            float w = red[tid];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, w, o);
+                if (tid >= o) w += y;
+            }
+            red[tid] = w;
+        }
+        __syncthreads();
+        const float prefix = incl - cs + ((tid >> 5) ? red[(tid >> 5) - 1] : 0.f);
+        if (c1 > c0 && prefix + cs > r) {
+            float running = prefix;
+            int found = c1 - 1;
+            for (int i = c0; i < c1; ++i) {
+                running += sp[i];
+                if (running > r) {
+                    found = i;
+                    break;
+                }
+            }
+            atomicMin(&best, found);
+        }
+        __syncthreads();
+        if (tid == 0) *out = best;
+        return;
+    }
+
+    // top-p: the largest t (float bits; probabilities are >= 0) whose tail
+    // mass sum(p >= t) reaches top_p
+    float* cp = sp + ((n + 3) & ~3);
+    int* ci = reinterpret_cast<int*>(cp + kTopPMax);
+    unsigned lo = 0u, hi = __float_as_uint(1.0f);
+    while (lo < hi) {
+        const unsigned mid = lo + (hi - lo + 1) / 2;
+        const float t = __uint_as_float(mid);
+        float m = 0.f;
+        for (int i = tid; i < n; i += kSampleThreads)
+            if (sp[i] >= t) m += sp[i];
+        m = block_sum(m, red);
+        if (m >= top_p) lo = mid; else hi = mid - 1;
+    }
+    // at most kTopPMax candidates: raise the threshold while there are more
+    unsigned t_bits = lo;
+    for (;;) {
+        const float t = __uint_as_float(t_bits);
+        float c = 0.f;
+        for (int i = tid; i < n; i += kSampleThreads) c += (sp[i] >= t) ? 1.f : 0.f;
+        c = block_sum(c, red);
+        if (c <= kTopPMax) break;
+        unsigned a = t_bits + 1, b = __float_as_uint(1.0f);   // smallest bits with count <= max
+        while (a < b) {
+            const unsigned mid = a + (b - a) / 2;
+            const float tm = __uint_as_float(mid);
+            float cm = 0.f;
+            for (int i = tid; i < n; i += kSampleThreads) cm += (sp[i] >= tm) ? 1.f : 0.f;
+            cm = block_sum(cm, red);
+            if (cm <= kTopPMax) b = mid; else a = mid + 1;
+        }
+        t_bits = a;
+    }
+    if (tid == 0) cnt = 0;
+    __syncthreads();
+    const float t = __uint_as_float(t_bits);
+    for (int i = tid; i < n; i += kSampleThreads)
+        if (sp[i] >= t) {
+            const int k = atomicAdd(&cnt, 1);
+            if (k < kTopPMax) {
+                cp[k] = sp[i];
+                ci[k] = i;
+            }
+        }
+    __syncthreads();
+    const int m = min(cnt, kTopPMax);
+    int P2 = 1;
+    while (P2 < m) P2 <<= 1;
+    for (int k = m + tid; k < P2; k += kSampleThreads) {
+        cp[k] = -1.f;
+        ci[k] = 0x7fffffff;
+    }
+    __syncthreads();
+    // bitonic sort: probability descending, then index ascending
+    for (int size = 2; size <= P2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int k = tid; k < P2; k += kSampleThreads) {
+                const int j = k ^ stride;
+                if (j > k) {
+                    const bool desc = (k & size) == 0;
+                    const float pk = cp[k], pj = cp[j];
+                    const int ik = ci[k], ij = ci[j];
+                    const bool k_first = pk > pj || (pk == pj && ik < ij);
+                    if (desc != k_first) {
+                        cp[k] = pj;
+                        cp[j] = pk;
+                        ci[k] = ij;
+                        ci[j] = ik;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (tid == 0) {
+        float cumsum = 0.f;
+        int cutoff = 0;
+        for (int k = 0; k < m; ++k) {
+            cumsum += cp[k];
+            cutoff = k + 1;
+            if (cumsum >= top_p) break;
+        }
+        const float rr = r * cumsum;
+        float running = 0.f;
+        int tok = ci[0];
+        for (int k = 0; k < cutoff; ++k) {
+            running += cp[k];
+            if (running > rr) {
+                tok = ci[k];
+                break;
+            }
+        }
+        *out = tok;
+    }
+}
+
 // rmsnorm (ops.cpp:1040-1054) as its own launch (one CTA): out may alias x.
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(float* out, const float* x, const float* w,
                                                        int n, float eps) {
@@ -707,6 +933,24 @@ cudaError_t launch_embed(int type, float* x, const void* table, const int32_t* t
 cudaError_t launch_argmax(const float* logits, int n, int32_t* out, cudaStream_t stream) {
     void* args[] = {&logits, &n, &out};
     return launch_pdl(reinterpret_cast<const void*>(argmax_kernel), dim3(1), dim3(1024), 0, stream, args);
+}
+
+cudaError_t launch_sample(float* logits, int n, float temperature, float top_p, float r, bool use_top_p,
+                          int32_t* out, cudaStream_t stream) {
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([&](int) {
+        cudaError_t x = cudaFuncSetAttribute(sample_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSampleMaxSmem);
+        if (x != cudaSuccess) return x;
+        return cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kSampleMaxSmem);
+    });
+    if (e != cudaSuccess) return e;
+    const size_t smem = (static_cast<size_t>((n + 3) & ~3) + (use_top_p ? 2 * kTopPMax : 0)) * 4;
+    void* args[] = {&logits, &n, &temperature, &top_p, &r, &out};
+    return launch_pdl(use_top_p ? reinterpret_cast<const void*>(sample_kernel<true>)
+                                : reinterpret_cast<const void*>(sample_kernel<false>),
+                      dim3(1), dim3(kSampleThreads), smem, stream, args);
 }
 
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps,

@@ -173,6 +173,11 @@ cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream);
 cudaError_t launch_embed(int type, float* x, const void* table, const int32_t* token, int n_vocab,
                          int n_embd, uint32_t* err, cudaStream_t stream);
 cudaError_t launch_argmax(const float* logits, int n, int32_t* out, cudaStream_t stream);
+// Temperature or top-p sampling of one row with the uniform draw r.
+constexpr int kSampleMaxVocab = 40960;
+constexpr int kSampleMaxSmem = (kSampleMaxVocab + 2 * 2048) * 4;
+cudaError_t launch_sample(float* logits, int n, float temperature, float top_p, float r, bool use_top_p,
+                          int32_t* out, cudaStream_t stream);
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps,
                            cudaStream_t stream);
 cudaError_t launch_vec_add(float* out, const float* x, int n, cudaStream_t stream);

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <random>
 #include <utility>
 
 namespace tle {
@@ -73,6 +74,42 @@ int sample_argmax_gpu(const float* logits, int n_vocab, void* stream) {
     }
     device_free(d);
     return h;
+}
+
+namespace {
+std::mt19937& layer_rng() {
+    static std::mt19937 rng(std::random_device{}());
+    return rng;
+}
+template <class F>
+int sample_to_host(F&& launch, void* stream) {
+    int32_t* d = static_cast<int32_t*>(device_alloc_bytes(sizeof(int32_t)));
+    int32_t h = 0;
+    try {
+        check(launch(d));
+        cuda_check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "sync");
+        copy_bytes_to_host(&h, d, sizeof h);
+    } catch (...) {
+        device_free(d);
+        throw;
+    }
+    device_free(d);
+    return h;
+}
+}  // namespace
+
+int sample_temperature_gpu(float* logits, int n_vocab, float temperature, void* stream) {
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    const float r = dist(layer_rng());
+    return sample_to_host(
+        [&](int32_t* d) { return tle_sample_temperature(logits, n_vocab, temperature, r, d, stream); }, stream);
+}
+
+int sample_top_p_gpu(float* logits, int n_vocab, float temperature, float top_p, void* stream) {
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    const float r = dist(layer_rng());
+    return sample_to_host(
+        [&](int32_t* d) { return tle_sample_top_p(logits, n_vocab, temperature, top_p, r, d, stream); }, stream);
 }
 
 void forward_gpu(const tle_model_t& model, const tle_state_t& state, const int32_t* token, int pos,

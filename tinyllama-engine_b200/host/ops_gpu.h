@@ -10,6 +10,7 @@
 //   matmul(out, W, x, rows, cols, type)         tle::matmul_gpu(...)      ops.h:64-66
 //   rmsnorm / vec_add / ffn_swiglu              tle::rmsnorm_gpu, ...     ops.h:95-96, 143, 232-235
 //   sample_argmax(logits, n_vocab)              tle::sample_argmax_gpu    ops.h:249
+//   sample_temperature / sample_top_p           tle::sample_*_gpu         ops.h:262, 278
 //   forward(model, state, token, pos)           tle::forward_gpu          forward.h:16
 //
 // All pointers are device pointers.  Errors throw std::runtime_error, the
@@ -99,6 +100,13 @@ void ffn_swiglu_gpu(float* out, const float* input, float* hb, float* hb2, const
 // ops.h:249 returns the token on the host (synchronises); the tle_sample_argmax
 // C call leaves it in device memory for a device-fed loop.
 int sample_argmax_gpu(const float* logits, int n_vocab, void* stream = nullptr);
+// ops.h:262 / 278: the uniform draw comes from a std::mt19937 this layer
+// holds, seeded by std::random_device like the reference's get_rng()
+// (ops.cpp:1571-1574), drawn with std::uniform_real_distribution<float>;
+// logits become probabilities; the token is returned on the host.
+int sample_temperature_gpu(float* logits, int n_vocab, float temperature, void* stream = nullptr);
+int sample_top_p_gpu(float* logits, int n_vocab, float temperature, float top_p,
+                     void* stream = nullptr);
 template <class E, class = std::enable_if_t<std::is_enum_v<E>>>
 void matmul_gpu(float* out, const void* W, const float* x, int rows, int cols, E type,
                 void* stream = nullptr) {

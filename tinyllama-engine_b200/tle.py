@@ -43,7 +43,7 @@ EXPORTED = (
     "tle_decode_desc_paged", "tle_decode_batch_paged",
     # include/tle_forward.h
     "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
-    "tle_forward_workspace_bytes", "tle_forward",
+    "tle_forward_workspace_bytes", "tle_forward", "tle_sample_temperature", "tle_sample_top_p",
 )
 
 
@@ -151,6 +151,8 @@ def lib() -> ctypes.CDLL:
         L.tle_forward_workspace_bytes.argtypes = [P(Model)]
         L.tle_forward_workspace_bytes.restype = sz
         L.tle_forward.argtypes = [P(Model), P(State), vp, i, vp]
+        L.tle_sample_temperature.argtypes = [vp, i, f, f, vp, vp]
+        L.tle_sample_top_p.argtypes = [vp, i, f, f, f, vp, vp]
         L.tle_decode_desc_paged.argtypes = [P(Shape), P(PagePool), P(PagedSeq), i, i, vp, sz, P(i)]
         L.tle_decode_batch_paged.argtypes = [P(Shape), P(PagePool), vp, i, i, vp, vp, vp, vp, i, i,
                                              vp, sz, vp]
@@ -531,6 +533,20 @@ def sample_argmax(logits, token_out, stream=None) -> None:
     if token_out.dtype != torch.int32 or not token_out.is_cuda:
         raise ValueError("token_out: need an int32 CUDA tensor")
     _check(lib().tle_sample_argmax(_ptr(logits), logits.numel(), _ptr(token_out), _stream(stream)))
+
+
+def sample_temperature(logits, token_out, temperature: float, r: float, stream=None) -> None:
+    """ops.h:262 on the device with the uniform draw r; logits become probabilities."""
+    _want(logits, 1, "logits")
+    _check(lib().tle_sample_temperature(_ptr(logits), logits.numel(), temperature, r,
+                                        _ptr(token_out), _stream(stream)))
+
+
+def sample_top_p(logits, token_out, temperature: float, top_p: float, r: float, stream=None) -> None:
+    """ops.h:278 on the device with the uniform draw r; logits become probabilities."""
+    _want(logits, 1, "logits")
+    _check(lib().tle_sample_top_p(_ptr(logits), logits.numel(), temperature, top_p, r,
+                                  _ptr(token_out), _stream(stream)))
 
 
 class DeviceModel:
