@@ -265,3 +265,16 @@ def test_forward_rejects_bad_models_without_gpu():
     assert L.tle_forward(None, ctypes.byref(st), p, 0, None) == tle.TLE_ERR_INVALID
     assert L.tle_forward(ctypes.byref(m), ctypes.byref(st), None, 0, None) == tle.TLE_ERR_INVALID
     assert L.tle_forward_workspace_bytes(ctypes.byref(m)) > 0
+
+
+def test_sampling_rejects_bad_arguments_without_gpu():
+    """Checked before any device work (fake, never dereferenced pointers)."""
+    L = tle.lib()
+    p = 0x200000
+    assert L.tle_sample_temperature(p, 0, 1.0, 0.5, p, None) == tle.TLE_ERR_UNSUPPORTED     # empty row
+    assert L.tle_sample_temperature(p, 50000, 1.0, 0.5, p, None) == tle.TLE_ERR_UNSUPPORTED  # > 40960
+    assert L.tle_sample_top_p(p, 32000, 1.0, 0.9, 1.0, p, None) == tle.TLE_ERR_INVALID      # r == 1
+    assert L.tle_sample_top_p(p, 32000, 1.0, 0.9, -0.1, p, None) == tle.TLE_ERR_INVALID
+    assert L.tle_sample_temperature(p, 32000, 1.0, float("nan"), p, None) == tle.TLE_ERR_INVALID
+    assert "r must be" in L.tle_last_error().decode()
+    assert L.tle_sample_top_p(None, 32000, 1.0, 0.9, 0.5, p, None) == tle.TLE_ERR_INVALID
