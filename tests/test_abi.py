@@ -278,3 +278,24 @@ def test_sampling_rejects_bad_arguments_without_gpu():
     assert L.tle_sample_temperature(p, 32000, 1.0, float("nan"), p, None) == tle.TLE_ERR_INVALID
     assert "r must be" in L.tle_last_error().decode()
     assert L.tle_sample_top_p(None, 32000, 1.0, 0.9, 0.5, p, None) == tle.TLE_ERR_INVALID
+
+
+def test_paged_cache_allocator_host_logic():
+    """PagedKVCache's free list (host side; built on the CPU here): pages
+    come out in pool order, exhaustion raises, freed pages are reused, and
+    page counts round up."""
+    import torch
+    pc = tle.PagedKVCache(6, 32, tle.tinyllama_shape(1), device="cpu")
+    assert pc.key_pool.shape == (1, 6, 32, 256)
+    assert pc.pages_for(1) == 1 and pc.pages_for(32) == 1 and pc.pages_for(33) == 2
+    a = pc.alloc(4)
+    assert a == [0, 1, 2, 3]
+    with pytest.raises(MemoryError):
+        pc.alloc(3)
+    pc.free(a[:2])
+    b = pc.alloc(4)
+    assert sorted(b) == [0, 1, 4, 5]
+    t = pc.table(b)
+    assert t.dtype == torch.int32 and t.tolist() == b
+    pool = pc.pool()
+    assert pool.n_pages == 6 and pool.page_rows == 32
