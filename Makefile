@@ -14,7 +14,7 @@ LIB := $(PKG)/libtle_attn.so
 ARCH := -gencode arch=compute_100a,code=sm_100a
 NVFLAGS := -std=c++20 -O3 $(ARCH) -lineinfo -Xcompiler -fPIC -Xcompiler -Wall \
            --expt-relaxed-constexpr -Iinclude -I$(CSRC)
-CU_SRCS := $(CSRC)/decode.cu $(CSRC)/prefill.cu $(CSRC)/forward.cu $(CSRC)/abi.cu
+CU_SRCS := $(CSRC)/decode.cu $(CSRC)/prefill.cu $(CSRC)/forward.cu $(CSRC)/gemm.cu $(CSRC)/abi.cu
 HOST_SRCS := $(HOST)/ops_gpu.cpp
 CU_OBJS := $(patsubst $(CSRC)/%.cu,_build/%.o,$(CU_SRCS))
 HOST_OBJS := $(patsubst $(HOST)/%.cpp,_build/host_%.o,$(HOST_SRCS))
@@ -24,7 +24,7 @@ all: $(LIB) oracle cpptest
 _build:
 	mkdir -p _build
 
-_build/%.o: $(CSRC)/%.cu $(CSRC)/common.cuh $(CSRC)/kernels.h include/tle_attn.h include/tle_forward.h | _build
+_build/%.o: $(CSRC)/%.cu $(CSRC)/common.cuh $(CSRC)/tcgen05.cuh $(CSRC)/kernels.h include/tle_attn.h include/tle_forward.h | _build
 	$(NVCC) $(NVFLAGS) -c $< -o $@
 
 _build/host_%.o: $(HOST)/%.cpp $(HOST)/ops_gpu.h include/tle_attn.h include/tle_forward.h | _build

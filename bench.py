@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--ctx-rows", type=int, default=4 * 1024 * 1024,
                     help="rows of the single sequence for --only ctxsplit")
     ap.add_argument("--only", choices=["prefill3", "decode4", "decode1", "ctxsplit", "decode5paged",
-                                       "decode4paged", "generate2"], default=None,
+                                       "decode4paged", "generate2", "prompt2"], default=None,
                     help="run one secondary workload alone (--steps/--warmup apply) and print "
                          "its line; for profiling")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -216,7 +216,7 @@ def main():
     if args.only:
         fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1,
               "decode5paged": measure_paged5, "decode4paged": measure_paged4,
-              "generate2": measure_config2}[args.only]
+              "generate2": measure_config2, "prompt2": measure_prompt2}[args.only]
         res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
         print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
                               warmup=max(3, args.warmup))), flush=True)
@@ -735,6 +735,49 @@ def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, 
             # per generated token: embedding, 22 x (q/k/v, decode, split-K merge,
             # output projection, gate/up, down), LM head, argmax
             "gpu_launches": (3 + 22 * 6) * gen * runs}
+
+
+def measure_prompt2(dev, peaks, steps=5, warmup=3, prompts=(128, 2048), seed=2):
+    """Config 2's model with its prompt through the batched prompt pass
+    (tle_prompt_forward: every product over all prompt tokens on the tensor
+    cores, fp16 weight copy made once beforehand) instead of one forward()
+    per prompt token; also a 2048-token prompt.  A step is one whole prompt
+    pass (embedding, 22 layers, LM head of the last token), timed with CUDA
+    events.  Roofline: the fp16 weight copy must be read once per pass
+    (HBM) and the products cost 2 x tokens x weights flops (tensor)."""
+    import numpy as np
+    import torch
+    import synth
+    import tle
+    m = synth.make_model(seed=seed, n_layers=22, wtype=synth.Q4_0, output_type=synth.Q4_0,
+                         n_ctx=max(prompts))
+    dm = tle.DeviceModel(m, device=dev)
+    ds = tle.DeviceState(dm, device=dev)
+    pw = tle.PromptWeights(dm)
+    stream = torch.cuda.current_stream(dev)
+    lin = sum(m.layers[0][n].rows * m.layers[0][n].cols for n in synth.LAYER_WEIGHTS)
+    out = {}
+    for S in prompts:
+        ids = np.random.default_rng(seed + S).integers(0, m.n_vocab, S).astype(np.int32)
+        toks = torch.from_numpy(ids).to(dev)
+        scratch = tle.prompt_scratch(dm, S, 0, dev)
+        ms = _time_steps(lambda: tle.prompt_forward(dm, ds, pw, toks, 0, scratch, stream),
+                         steps, warmup, stream)
+        if tle.device_error():
+            raise RuntimeError("device error during the prompt pass")
+        flops = 22 * (2.0 * S * lin + 4.0 * 64 * 32 * S * (S + 1) / 2)
+        wbytes = 22 * 2 * lin
+        out[str(S)] = {"ms": round(ms, 4), "tok_s": round(S / (ms / 1e3), 1),
+                       "tflops": round(flops / (ms / 1e3) / 1e12, 2),
+                       "frac_tensor": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+                       "fp16_weight_gbs": round(wbytes / (ms / 1e3) / 1e9, 1),
+                       "frac_hbm": round(wbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+    per_pass = 1 + 22 * 9 + 1
+    return {"workload": "config2 model (TinyLlama-1.1B shapes, random Q4_0) prompt through "
+                        "tle_prompt_forward, %s tokens" % "/".join(str(p) for p in prompts),
+            "metric": "prompt tok/s", "value": out[str(prompts[0])]["tok_s"], "unit": "tok/s",
+            "dtype": "f16 products, fp32 accumulation", "prompts": out,
+            "gpu_launches": per_pass * steps * len(prompts)}
 
 
 def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):

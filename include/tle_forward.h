@@ -130,6 +130,38 @@ size_t tle_forward_workspace_bytes(const tle_model_t* model);
 int tle_forward(const tle_model_t* model, const tle_state_t* state, const int32_t* token, int pos,
                 void* stream);
 
+/* ---- batched prompt ----
+ * The reference feeds a prompt one token at a time (generate.cpp:52-59: one
+ * forward() per prompt token).  tle_prompt_forward runs those forward()
+ * calls for n_tokens tokens at once, layer by layer: every product is one
+ * matrix product over all the tokens on the tcgen05 tensor cores (fp16
+ * operands, fp32 accumulation), the attention is tle_prefill's.  The
+ * products read an fp16 copy of the linear weights made once by
+ * tle_prompt_pack_weights. */
+
+/* Bytes of the fp16 weight copy: per layer, in order, q/k/v rows
+ * [n_embd + 2*kv_dim][n_embd], output [n_embd][n_embd], gate then up rows
+ * [2*n_ff][n_embd], down [n_embd][n_ff].  0 if the model is unsupported
+ * (tle_last_error says why): n_head 32, n_head_kv 4, head_dim 64, n_ff a
+ * multiple of 128. */
+size_t tle_prompt_weights_bytes(const tle_model_t* model);
+/* Writes the fp16 copy into dst (device, 16-byte aligned, at least
+ * tle_prompt_weights_bytes): each weight dequantised as the reference does
+ * (every TLE_W_* format; the feed-forward weights read as ffn_gate's type,
+ * forward.cpp:224-227) and rounded to nearest fp16. */
+int tle_prompt_pack_weights(const tle_model_t* model, void* dst, size_t dst_bytes, void* stream);
+/* Scratch of tle_prompt_forward for n_tokens prompt tokens at pos0. */
+size_t tle_prompt_scratch_bytes(const tle_model_t* model, int n_tokens, int pos0);
+/* forward() for tokens[0..n_tokens) (device int32) at positions pos0.. in
+ * one pass: appends rows pos0 .. pos0+n_tokens-1 of every layer's cache and
+ * leaves the last token's logits in state->logits and its final residual
+ * in state->x, as the reference's prompt loop does.  scratch: device,
+ * 1024-byte aligned, tle_prompt_scratch_bytes.  Tokens outside [0, n_vocab)
+ * are reported through tle_device_error (0x106) and embed as zeros. */
+int tle_prompt_forward(const tle_model_t* model, const void* packed, const tle_state_t* state,
+                       const int32_t* tokens, int n_tokens, int pos0, void* scratch,
+                       size_t scratch_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

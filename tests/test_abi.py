@@ -267,6 +267,46 @@ def test_forward_rejects_bad_models_without_gpu():
     assert L.tle_forward_workspace_bytes(ctypes.byref(m)) > 0
 
 
+def test_prompt_sizes_and_argument_checks_without_gpu():
+    """Batched prompt: the fp16 weight copy and scratch sizes follow the
+    documented layouts, and bad arguments are refused before any device
+    work (fake, never dereferenced pointers)."""
+    L = tle.lib()
+    p = 0x400000
+    m, keep = fake_model(n_ctx=512)
+    e, kv, ff = 2048, 256, 5632
+    layer_halves = (e + 2 * kv) * e + e * e + 2 * ff * e + e * ff
+    assert L.tle_prompt_weights_bytes(ctypes.byref(m)) == 2 * 2 * layer_halves
+
+    def a(n):
+        return (n + 1023) // 1024 * 1024
+    for S, pos0 in ((1, 0), (200, 0), (128, 300)):
+        sp = (S + 127) // 128 * 128
+        attn_ws = L.tle_prefill_workspace_bytes(ctypes.byref(tle.tinyllama_shape(2)), S, pos0)
+        want = (2 * a(S * e * 4) + 2 * a(S * kv * 4) + a(S * e * 4) + 2 * a(sp * e * 2) + a(sp * ff * 2)
+                + a(attn_ws))
+        assert L.tle_prompt_scratch_bytes(ctypes.byref(m), S, pos0) == want, (S, pos0)
+
+    bad, keep2 = fake_model(n_ff=5600)                     # not a multiple of the 128-row tile
+    assert L.tle_prompt_weights_bytes(ctypes.byref(bad)) == 0
+    assert "n_ff" in L.tle_last_error().decode()
+    bad, keep2 = fake_model(n_head=16)
+    assert L.tle_prompt_scratch_bytes(ctypes.byref(bad), 8, 0) == 0
+
+    st = tle.State(*([p] * 12), workspace_bytes=0)
+    big = 1 << 40
+    fwd = L.tle_prompt_forward
+    assert fwd(ctypes.byref(m), p, ctypes.byref(st), p, 0, 0, p, big, None) == tle.TLE_ERR_INVALID
+    assert fwd(ctypes.byref(m), p, ctypes.byref(st), p, 500, 13, p, big, None) == tle.TLE_ERR_INVALID
+    assert fwd(ctypes.byref(m), p, ctypes.byref(st), p, 8, 0, p + 512, big, None) == tle.TLE_ERR_INVALID
+    assert fwd(ctypes.byref(m), p, ctypes.byref(st), p, 8, 0, p, 1024, None) == tle.TLE_ERR_WORKSPACE
+    assert fwd(ctypes.byref(m), None, ctypes.byref(st), p, 8, 0, p, big, None) == tle.TLE_ERR_INVALID
+    q4_table, keep3 = fake_model(n_ctx=512, token_embd=tle.Weight(2, 0, p))
+    assert fwd(ctypes.byref(q4_table), p, ctypes.byref(st), p, 8, 0, p, big, None) == tle.TLE_ERR_UNSUPPORTED
+    assert L.tle_prompt_pack_weights(ctypes.byref(m), None, big, None) == tle.TLE_ERR_INVALID
+    assert L.tle_prompt_pack_weights(ctypes.byref(m), p, 1024, None) == tle.TLE_ERR_WORKSPACE
+
+
 def test_sampling_rejects_bad_arguments_without_gpu():
     """Checked before any device work (fake, never dereferenced pointers)."""
     L = tle.lib()

@@ -851,3 +851,270 @@ int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token
 }
 
 }  // extern "C"
+
+// ===================== batched prompt (tle_forward.h) =====================
+
+namespace {
+
+constexpr size_t kSegAlign = 1024;
+size_t align_up(size_t n) { return (n + kSegAlign - 1) / kSegAlign * kSegAlign; }
+
+// Element offsets (fp16) of one layer's weights in the packed copy.
+struct PackedLayer {
+    size_t qkv, o, gu, down, total;
+};
+PackedLayer packed_layer(const tle_model_t* m) {
+    const size_t e = static_cast<size_t>(m->n_embd), kv = static_cast<size_t>(m->n_head_kv) * tle::kHeadDim,
+                 ff = static_cast<size_t>(m->n_ff);
+    PackedLayer p;
+    p.qkv = 0;
+    p.o = p.qkv + (e + 2 * kv) * e;
+    p.gu = p.o + e * e;
+    p.down = p.gu + 2 * ff * e;
+    p.total = p.down + e * ff;
+    return p;
+}
+
+// Byte offsets of tle_prompt_forward's scratch (each segment 1024-aligned).
+struct PromptScratch {
+    size_t x, q, k, v, att, xb16, att16, h16, attn_ws, total;
+    int s_pad;
+};
+PromptScratch prompt_scratch(const tle_model_t* m, int n_tokens, int pos0) {
+    const size_t S = static_cast<size_t>(n_tokens), e = static_cast<size_t>(m->n_embd),
+                 kv = static_cast<size_t>(m->n_head_kv) * tle::kHeadDim, ff = static_cast<size_t>(m->n_ff);
+    PromptScratch p{};
+    p.s_pad = (n_tokens + tle::kGemmTileTokens - 1) / tle::kGemmTileTokens * tle::kGemmTileTokens;
+    const size_t sp = static_cast<size_t>(p.s_pad);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off += align_up(bytes);
+        return at;
+    };
+    p.x = take(S * e * 4);
+    p.q = take(S * e * 4);
+    p.k = take(S * kv * 4);
+    p.v = take(S * kv * 4);
+    p.att = take(S * e * 4);
+    p.xb16 = take(sp * e * 2);
+    p.att16 = take(sp * e * 2);
+    p.h16 = take(sp * ff * 2);
+    p.attn_ws = take(tle::prefill_workspace_bytes(n_tokens, pos0));
+    p.total = off;
+    return p;
+}
+
+// The model shapes the batched prompt supports; 0 or a TLE_* error.
+int check_prompt_model(const tle_model_t* m) {
+    if (!m) return set_error(TLE_ERR_INVALID, "model is NULL");
+    if (!m->layers || m->n_layers <= 0) return set_error(TLE_ERR_INVALID, "model has no layers");
+    tle_shape_t shape{m->n_layers, m->n_head, m->n_head_kv, m->n_head > 0 ? m->n_embd / m->n_head : 0,
+                      m->rope_freq_base};
+    if (int rc = check_shape(&shape)) return rc;
+    if (m->n_embd != m->n_head * tle::kHeadDim)
+        return set_error(TLE_ERR_UNSUPPORTED, "n_embd %d != n_head * 64", m->n_embd);
+    if (m->n_ff <= 0 || m->n_ff % tle::kGemmTileRows)
+        return set_error(TLE_ERR_UNSUPPORTED, "n_ff %d is not a positive multiple of %d", m->n_ff,
+                         tle::kGemmTileRows);
+    if (m->n_vocab <= 0 || m->n_ctx <= 0) return set_error(TLE_ERR_INVALID, "bad n_vocab/n_ctx");
+    const int kv = m->n_head_kv * tle::kHeadDim;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& L = m->layers[l];
+        const struct {
+            const tle_weight_t* w;
+            int type, cols;
+            const char* name;
+        } ws[7] = {{&L.attn_q, L.attn_q.type, m->n_embd, "attn_q"},
+                   {&L.attn_k, L.attn_k.type, m->n_embd, "attn_k"},
+                   {&L.attn_v, L.attn_v.type, m->n_embd, "attn_v"},
+                   {&L.attn_output, L.attn_output.type, m->n_embd, "attn_output"},
+                   {&L.ffn_gate, L.ffn_gate.type, m->n_embd, "ffn_gate"},
+                   {&L.ffn_up, L.ffn_gate.type, m->n_embd, "ffn_up"},
+                   {&L.ffn_down, L.ffn_gate.type, m->n_ff, "ffn_down"}};
+        for (const auto& w : ws) {
+            if (!w.w->data) return set_error(TLE_ERR_INVALID, "layer %d: %s is NULL", l, w.name);
+            if (tle::weight_row_bytes(w.type, w.cols) < 0)
+                return set_error(TLE_ERR_UNSUPPORTED, "layer %d: %s type %d with %d cols is not supported", l,
+                                 w.name, w.type, w.cols);
+        }
+        if (!L.attn_norm || !L.ffn_norm) return set_error(TLE_ERR_INVALID, "layer %d: null norm weight", l);
+    }
+    (void)kv;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tle_prompt_weights_bytes(const tle_model_t* model) {
+    if (check_prompt_model(model)) return 0;
+    return packed_layer(model).total * 2 * static_cast<size_t>(model->n_layers);
+}
+
+int tle_prompt_pack_weights(const tle_model_t* m, void* dst, size_t dst_bytes, void* stream) {
+    if (int rc = check_prompt_model(m)) return rc;
+    if (!dst || !aligned16(dst)) return set_error(TLE_ERR_INVALID, "dst must be non-null and 16-byte aligned");
+    const PackedLayer P = packed_layer(m);
+    const size_t need = P.total * 2 * static_cast<size_t>(m->n_layers);
+    if (dst_bytes < need) return set_error(TLE_ERR_WORKSPACE, "dst %zu bytes < %zu needed", dst_bytes, need);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int e = m->n_embd, kv = m->n_head_kv * tle::kHeadDim, ff = m->n_ff;
+    const size_t ee = static_cast<size_t>(e);
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& L = m->layers[l];
+        uint16_t* base = static_cast<uint16_t*>(dst) + P.total * static_cast<size_t>(l);
+        const struct {
+            const tle_weight_t* w;
+            int type, rows, cols;
+            size_t at;
+        } parts[7] = {{&L.attn_q, L.attn_q.type, e, e, P.qkv},
+                      {&L.attn_k, L.attn_k.type, kv, e, P.qkv + ee * e},
+                      {&L.attn_v, L.attn_v.type, kv, e, P.qkv + (ee + kv) * e},
+                      {&L.attn_output, L.attn_output.type, e, e, P.o},
+                      {&L.ffn_gate, L.ffn_gate.type, ff, e, P.gu},
+                      {&L.ffn_up, L.ffn_gate.type, ff, e, P.gu + static_cast<size_t>(ff) * e},
+                      {&L.ffn_down, L.ffn_gate.type, e, ff, P.down}};
+        for (const auto& p : parts) {
+            cudaError_t err = tle::launch_pack_f16(p.type, base + p.at, p.w->data, p.rows, p.cols, st);
+            if (err != cudaSuccess) return cuda_error(err, "pack weights");
+        }
+    }
+    return ok();
+}
+
+size_t tle_prompt_scratch_bytes(const tle_model_t* model, int n_tokens, int pos0) {
+    if (check_prompt_model(model) || n_tokens <= 0 || pos0 < 0) return 0;
+    return prompt_scratch(model, n_tokens, pos0).total;
+}
+
+int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state_t* s, const int32_t* tokens,
+                       int n_tokens, int pos0, void* scratch, size_t scratch_bytes, void* stream) {
+    if (int rc = check_prompt_model(m)) return rc;
+    if (!packed || !s || !tokens || !scratch) return set_error(TLE_ERR_INVALID, "null packed/state/tokens/scratch");
+    if (!aligned16(packed)) return set_error(TLE_ERR_INVALID, "packed weights must be 16-byte aligned");
+    if (n_tokens <= 0 || n_tokens > 65535 || pos0 < 0 || static_cast<int64_t>(pos0) + n_tokens > m->n_ctx)
+        return set_error(TLE_ERR_INVALID, "need 0 < n_tokens <= 65535 and 0 <= pos0, pos0 + n_tokens <= n_ctx");
+    if (!s->x || !s->logits || !s->key_cache || !s->value_cache) return set_error(TLE_ERR_INVALID, "null state buffer");
+    if (!aligned16(s->key_cache) || !aligned16(s->value_cache) || !aligned16(s->x))
+        return set_error(TLE_ERR_INVALID, "state buffers must be 16-byte aligned");
+    if (m->token_embd.type != TLE_W_F16 && m->token_embd.type != TLE_W_F32)
+        return set_error(TLE_ERR_UNSUPPORTED, "token_embd type %d (F16 or F32 supported)", m->token_embd.type);
+    if (!m->token_embd.data || !m->output_norm) return set_error(TLE_ERR_INVALID, "null global tensor");
+    if ((reinterpret_cast<uintptr_t>(scratch) & (kSegAlign - 1)) != 0)
+        return set_error(TLE_ERR_INVALID, "scratch must be 1024-byte aligned");
+    const PromptScratch W = prompt_scratch(m, n_tokens, pos0);
+    if (scratch_bytes < W.total)
+        return set_error(TLE_ERR_WORKSPACE, "scratch %zu bytes < %zu needed", scratch_bytes, W.total);
+    const PackedLayer P = packed_layer(m);
+    const int e = m->n_embd, kv = m->n_head_kv * tle::kHeadDim, ff = m->n_ff, S = n_tokens;
+    const float eps = m->rms_norm_eps;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned char* ws = static_cast<unsigned char*>(scratch);
+    float* X = reinterpret_cast<float*>(ws + W.x);
+    float* Q = reinterpret_cast<float*>(ws + W.q);
+    float* K = reinterpret_cast<float*>(ws + W.k);
+    float* V = reinterpret_cast<float*>(ws + W.v);
+    float* ATT = reinterpret_cast<float*>(ws + W.att);
+    uint16_t* XB16 = reinterpret_cast<uint16_t*>(ws + W.xb16);
+    uint16_t* ATT16 = reinterpret_cast<uint16_t*>(ws + W.att16);
+    uint16_t* H16 = reinterpret_cast<uint16_t*>(ws + W.h16);
+    uint32_t* err = nullptr;
+    cudaError_t ce = tle::error_word(&err);
+    if (ce != cudaSuccess) return cuda_error(ce, "device error word");
+
+    ce = tle::launch_embed_rows(m->token_embd.type, X, m->token_embd.data, tokens, S, m->n_vocab, e, err, st);
+    if (ce != cudaSuccess) return cuda_error(ce, "embedding");
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& L = m->layers[l];
+        const uint16_t* Wl = static_cast<const uint16_t*>(packed) + P.total * static_cast<size_t>(l);
+        // rmsnorm + q/k/v for all tokens (forward.cpp:184-196)
+        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.attn_norm, e, eps, S, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "attn_norm");
+        tle::GemmLaunch g{};
+        g.W = Wl + P.qkv;
+        g.w_rows = e + 2 * kv;
+        g.X = XB16;
+        g.n_tokens = S;
+        g.K = e;
+        g.tile_rows = g.w_rows;
+        g.seg[0] = {0, e, Q};
+        g.seg[1] = {e, kv, K};
+        g.seg[2] = {e + kv, kv, V};
+        g.n_seg = 3;
+        g.err = err;
+        ce = tle::launch_gemm_f16(tle::kEpiStore, g, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "attn_qkv");
+        // rope + attention of every token (forward.cpp:198-208), appending rows pos0..
+        tle::PrefillArgs a{};
+        a.q = Q;
+        a.k = K;
+        a.v = V;
+        a.out = ATT;
+        a.key_cache = s->key_cache;
+        a.value_cache = s->value_cache;
+        a.layer = l;
+        a.pos0 = pos0;
+        a.n_tokens = S;
+        a.n_ctx = m->n_ctx;
+        a.workspace = ws + W.attn_ws;
+        a.err = err;
+        a.f16 = 1;   // fp16 operands: the errors of one layer's attention feed the next layer
+        fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, m->rope_freq_base);
+        ce = tle::launch_prefill(a, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "attention");
+        // output projection + residual (forward.cpp:210-214)
+        ce = tle::launch_to_f16(ATT16, ATT, static_cast<size_t>(S) * e, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "attention output");
+        g = tle::GemmLaunch{};
+        g.W = Wl + P.o;
+        g.w_rows = e;
+        g.X = ATT16;
+        g.n_tokens = S;
+        g.K = e;
+        g.tile_rows = e;
+        g.seg[0] = {0, e, X};
+        g.n_seg = 1;
+        g.err = err;
+        ce = tle::launch_gemm_f16(tle::kEpiAdd, g, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "attn_output");
+        // rmsnorm + gate/up + SwiGLU (forward.cpp:216-227)
+        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.ffn_norm, e, eps, S, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "ffn_norm");
+        g = tle::GemmLaunch{};
+        g.W = Wl + P.gu;
+        g.w_rows = 2 * ff;
+        g.X = XB16;
+        g.n_tokens = S;
+        g.K = e;
+        g.tile_rows = ff;
+        g.h_out = H16;
+        g.err = err;
+        ce = tle::launch_gemm_f16(tle::kEpiSwiGLU, g, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "ffn_gate/up");
+        // down projection + residual (forward.cpp:227-229)
+        g = tle::GemmLaunch{};
+        g.W = Wl + P.down;
+        g.w_rows = e;
+        g.X = H16;
+        g.n_tokens = S;
+        g.K = ff;
+        g.tile_rows = e;
+        g.seg[0] = {0, e, X};
+        g.n_seg = 1;
+        g.err = err;
+        ce = tle::launch_gemm_f16(tle::kEpiAdd, g, st);
+        if (ce != cudaSuccess) return cuda_error(ce, "ffn_down");
+    }
+    // the last token's residual, final rmsnorm + LM head (forward.cpp:245-265)
+    ce = cudaMemcpyAsync(s->x, X + static_cast<size_t>(S - 1) * e, sizeof(float) * e, cudaMemcpyDeviceToDevice, st);
+    if (ce != cudaSuccess) return cuda_error(ce, "last residual");
+    const tle_weight_t& head = m->output.data ? m->output : m->token_embd;
+    tle::GemvSeg lm{static_cast<const uint8_t*>(head.data), s->logits, m->n_vocab, 0};
+    if (int rc = gemv(head.type, tle::kEpiStore, &lm, 1, nullptr, e, s->x, m->output_norm, eps, st, "lm_head"))
+        return rc;
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,431 @@
+// gemm.cu -- the batched prompt: every product of forward() for S prompt
+// tokens at once, on the tcgen05 tensor cores.
+//
+// Reference semantics: generate.cpp:52-59 feeds the prompt one token at a
+// time through forward() (forward.cpp:178-265), so each weight matrix meets
+// one vector per call (matmul, ops.cpp:959-981).  For S prompt tokens the
+// products of one layer are the matrix products Y[S][rows] = X[S][cols] W^T
+// of the same weights with S inputs.
+//
+// B200 design:
+//  * The weights are dequantised once into an fp16 copy (launch_pack_f16:
+//    the reference's dequantised value of every GGUF format, rounded to
+//    fp16; 2 bytes a weight, ~1.9 GB for TinyLlama-1.1B, kept resident in
+//    HBM next to the GGUF bytes the decode path reads).
+//  * gemm_f16_kernel: one CTA per (128 weight rows, 128 tokens) tile.  A
+//    producer warp streams 64-wide K slices of the weight tile (TMA, 128-byte
+//    swizzle) and of the token tile into a ring of shared-memory stages; one
+//    thread of the MMA warp issues tcgen05.mma kind::f16 (M = 128 weight
+//    rows = TMEM lanes, N = 128 tokens = TMEM columns, fp32 accumulation in
+//    TMEM); the four warps read the accumulator back (one weight row per
+//    thread) and apply the epilogue the token-at-a-time path fuses into its
+//    GEMV: store into q/k/v, residual add, or SwiGLU of a gate and an up
+//    accumulator (two per CTA) written as fp16 for the down product.
+//  * Small kernels around it: the embedding rows, RMSNorm of S rows into the
+//    fp16 operand, and the fp16 copy of the attention output.
+// Operands enter the tensor cores as fp16 (11-bit significand) with fp32
+// accumulation; the attention in between is tle_prefill's (bf16 operands).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace tle {
+
+namespace {
+
+constexpr int GM = kGemmTileRows;     // 128 weight rows: TMEM lanes
+constexpr int GN = kGemmTileTokens;   // 128 tokens: TMEM columns per accumulator
+constexpr int GK = kGemmTileK;        // 64 fp16 = one 128-byte swizzle row
+constexpr int kGemmThreads = 128;
+constexpr uint32_t kTileBytes = GM * GK * 2;   // 16 KB, the same for a token tile
+static_assert(GM == GN, "weight and token tiles share one tensor-map box");
+constexpr uint32_t kIdesc = idesc_f16_f32(GM, GN);
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// Bounded wait; after the first expiry in a thread every later wait of that
+// thread returns at once.
+__device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                             uint32_t code, bool& failed) {
+    if (failed) return;
+    if (!mbar_wait(bar, parity)) {
+        record_error(err, code);
+        failed = true;
+    }
+}
+
+template <int NACC, int STAGES>
+struct GemmSmem {
+    uint16_t a[STAGES][NACC][GM * GK];   // weight slices (gate, up), SW128 K-major
+    uint16_t b[STAGES][GN * GK];         // token slices
+    uint64_t full[STAGES];               // the stage's copies landed
+    uint64_t empty[STAGES];              // the stage's MMAs completed
+    uint64_t acc_full;                   // the last MMA completed
+    uint32_t tmem_base;
+};
+template <int EPI>
+struct GemmCfg {
+    static constexpr int NACC = EPI == kEpiSwiGLU ? 2 : 1;
+    static constexpr int STAGES = NACC == 2 ? 4 : 6;
+    static constexpr uint32_t kCols = NACC * GN;   // TMEM columns (128 or 256)
+    using Smem = GemmSmem<NACC, STAGES>;
+    static constexpr int kSmemBytes = static_cast<int>(sizeof(Smem)) + 1024;   // + alignment slack
+};
+
+struct GemmArgs {
+    CUtensorMap tm_w;   // fp16 [w_rows][K], box {64, 128}
+    CUtensorMap tm_x;   // fp16 [S_pad][K], box {64, 128}
+    int K;
+    int n_tokens;
+    int up_row0;        // SwiGLU: first up row in tm_w (= n_ff)
+    int n_seg;
+    int seg_row0[3];
+    int seg_rows[3];
+    float* seg_out[3];
+    uint16_t* h_out;    // SwiGLU: [S_pad][up_row0]
+    uint32_t* err;
+};
+
+// Warp roles (128 threads, one CTA per SM by shared memory):
+//   warp 0: TMA producer (one lane issues), warp 1: MMA issuer (one elected
+//   lane); then all four warps run the epilogue, warp w on TMEM lanes
+//   32w..32w+31 (the lanes a warp may access are fixed by its rank mod 4).
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_constant__ GemmArgs A) {
+    using C = GemmCfg<EPI>;
+    constexpr int NACC = C::NACC;
+    constexpr int ST = C::STAGES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // SW128 atoms need 1024-byte aligned tiles (the launch adds 1 KB of slack)
+    typename C::Smem& S = *reinterpret_cast<typename C::Smem*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * GM;
+    const int t0 = blockIdx.y * GN;
+    const int nk = A.K / GK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        mbar_init(&S.acc_full, 1);
+        fence_barrier_init();
+        prefetch_tmap(&A.tm_w);
+        prefetch_tmap(&A.tm_x);
+    }
+    if (warp == 0) {
+        tmem_alloc(&S.tmem_base, C::kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+    bool failed = false;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % ST;
+            if (kb >= ST) wait_or_flag(&S.empty[s], ((kb / ST) - 1) & 1, A.err, kErrWaitEmpty, failed);
+            failed = __any_sync(0xffffffffu, failed);   // the warp stops as one
+            if (failed) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&S.full[s], (NACC + 1) * kTileBytes);
+                tma_load_2d(S.a[s][0], &A.tm_w, kb * GK, m0, &S.full[s]);
+                if (NACC == 2) tma_load_2d(S.a[s][NACC - 1], &A.tm_w, kb * GK, A.up_row0 + m0, &S.full[s]);
+                tma_load_2d(S.b[s], &A.tm_x, kb * GK, t0, &S.full[s]);
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer --------------------------------
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % ST;
+            wait_or_flag(&S.full[s], (kb / ST) & 1, A.err, kErrWaitFull, failed);
+            failed = __any_sync(0xffffffffu, failed);
+            if (failed) break;
+            tc_fence_after();
+            if (elect_one()) {
+                const uint64_t db = sw128_desc(smem_u32(S.b[s]));
+#pragma unroll
+                for (int acc = 0; acc < NACC; ++acc) {
+                    const uint64_t da = sw128_desc(smem_u32(S.a[s][acc]));
+#pragma unroll
+                    for (int kk = 0; kk < GK / 16; ++kk)   // 16 fp16 = 32 bytes = 2 descriptor units
+                        umma_bf16(tmem + acc * GN, da + 2 * kk, db + 2 * kk, kIdesc,
+                                  (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&S.empty[s]);
+                if (kb == nk - 1) umma_commit(&S.acc_full);
+            }
+            __syncwarp();
+        }
+    }
+
+    // ------------------------------ epilogue (all warps) ------------------------------
+    wait_or_flag(&S.acc_full, 0, A.err, kErrWaitMma, failed);
+    tc_fence_after();
+    const int r = m0 + 32 * warp + lane;   // this thread's weight row
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    float* seg_out = nullptr;
+    int seg_ld = 0;
+    if (EPI != kEpiSwiGLU) {
+        // a tile lies inside one segment (the launcher checks it)
+        int si = 0;
+        for (int i = 1; i < A.n_seg; ++i)
+            if (m0 >= A.seg_row0[i]) si = i;
+        seg_ld = A.seg_rows[si];
+        seg_out = A.seg_out[si] + (r - A.seg_row0[si]);
+    }
+#pragma unroll 1
+    for (int c = 0; c < GN / 32; ++c) {
+        float v[32];
+        float u[32];
+        tmem_ld32(trow + 32 * c, v);
+        if (NACC == 2) tmem_ld32(trow + GN + 32 * c, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int t = t0 + 32 * c + j;
+            if (t >= A.n_tokens) break;
+            if (EPI == kEpiStore) {
+                seg_out[static_cast<size_t>(t) * seg_ld] = v[j];
+            } else if (EPI == kEpiAdd) {
+                float* p = seg_out + static_cast<size_t>(t) * seg_ld;
+                *p = *p + v[j];
+            } else {
+                // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
+                const float g = v[j];
+                A.h_out[static_cast<size_t>(t) * A.up_row0 + r] = f2h((g * (1.0f / (1.0f + expf(-g)))) * u[j]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kCols);
+    }
+}
+
+// ---- fp16 copy of a GGUF weight ---------------------------------------------
+// Element e of a row, dequantised as the reference does (gguf block layouts,
+// ops.cpp Q4_0 616-655, Q8_0 442-473, Q6_K 882-948): the products are exact
+// in fp32, so the only rounding is the final one to fp16.
+template <int T>
+__device__ __forceinline__ float deq(const uint8_t* row, int e);
+template <>
+__device__ __forceinline__ float deq<kWF32>(const uint8_t* row, int e) {
+    return reinterpret_cast<const float*>(row)[e];
+}
+template <>
+__device__ __forceinline__ float deq<kWF16>(const uint8_t* row, int e) {
+    return h2f(reinterpret_cast<const uint16_t*>(row)[e]);
+}
+template <>
+__device__ __forceinline__ float deq<kWQ4_0>(const uint8_t* row, int e) {
+    const uint8_t* blk = row + 18 * (e >> 5);
+    const int j = e & 31;
+    const float d = h2f(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+    const int q = blk[2 + (j & 15)];
+    const int n = (j < 16) ? (q & 15) : (q >> 4);
+    return static_cast<float>(n - 8) * d;
+}
+template <>
+__device__ __forceinline__ float deq<kWQ8_0>(const uint8_t* row, int e) {
+    const uint8_t* blk = row + 34 * (e >> 5);
+    const float d = h2f(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+    return static_cast<float>(static_cast<int8_t>(blk[2 + (e & 31)])) * d;
+}
+template <>
+__device__ __forceinline__ float deq<kWQ6_K>(const uint8_t* row, int e) {
+    // super-block of 256: half h, quarter i of the half, position l
+    const uint8_t* blk = row + 210 * (e >> 8);
+    const int r = e & 255;
+    const int h = r >> 7, i = (r >> 5) & 3, l = r & 31;
+    const uint32_t ql = blk[64 * h + l + 32 * (i & 1)];
+    const uint32_t qh = blk[128 + 32 * h + l];
+    const int q = static_cast<int>(((i < 2) ? (ql & 15u) : (ql >> 4)) | (((qh >> (2 * i)) & 3u) << 4)) - 32;
+    const float d = h2f(static_cast<uint16_t>(blk[208] | (blk[209] << 8)));
+    const int8_t sc = static_cast<int8_t>(blk[192 + 8 * h + (l >> 4) + 2 * i]);
+    return d * static_cast<float>(sc) * static_cast<float>(q);
+}
+
+template <int T>
+__global__ void __launch_bounds__(256) pack_f16_kernel(uint16_t* __restrict__ dst, const uint8_t* __restrict__ W,
+                                                       int rows, int cols, int row_bytes) {
+    const size_t n = static_cast<size_t>(rows) * cols;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t rr = i / static_cast<size_t>(cols);
+        const int e = static_cast<int>(i - rr * static_cast<size_t>(cols));
+        dst[i] = f2h(deq<T>(W + rr * static_cast<size_t>(row_bytes), e));
+    }
+}
+
+// ---- RMSNorm of S rows into the fp16 operand (ops.cpp:1040-1054 per row) ----
+__global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
+                                                               const float* __restrict__ w, int n, float eps) {
+    __shared__ float red[8];
+    __shared__ float rms;
+    const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+    uint16_t* orow = out + static_cast<size_t>(blockIdx.x) * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t += red[i];
+        rms = 1.0f / sqrtf(t / static_cast<float>(n) + eps);
+    }
+    __syncthreads();
+    const float s = rms;
+    for (int i = threadIdx.x; i < n; i += 256) orow[i] = f2h(xr[i] * s * w[i]);
+}
+
+__global__ void __launch_bounds__(256) to_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
+                                                     size_t n) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        out[i] = f2h(x[i]);
+}
+
+// embed_token (forward.cpp:35-60) for S tokens: block (x, t) writes a slice
+// of row t.  A token outside [0, n_vocab) is reported (0x106) and gives zeros.
+template <int T>
+__global__ void __launch_bounds__(256) embed_rows_kernel(float* __restrict__ x, const uint8_t* __restrict__ table,
+                                                         const int32_t* __restrict__ tokens, int n_vocab,
+                                                         int n_embd, uint32_t* err) {
+    const int t = blockIdx.y;
+    const int tok = tokens[t];
+    const bool ok = tok >= 0 && tok < n_vocab;
+    if (!ok && threadIdx.x == 0 && blockIdx.x == 0) record_error(err, kErrBadToken);
+    float* xr = x + static_cast<size_t>(t) * n_embd;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_embd; i += gridDim.x * blockDim.x) {
+        float v = 0.f;
+        if (ok) {
+            const size_t e = static_cast<size_t>(tok) * n_embd + i;
+            v = (T == kWF16) ? h2f(reinterpret_cast<const uint16_t*>(table)[e])
+                             : reinterpret_cast<const float*>(table)[e];
+        }
+        xr[i] = v;
+    }
+}
+
+template <int EPI>
+cudaError_t launch_gemm_e(const GemmArgs& a, dim3 grid, cudaStream_t stream) {
+    using C = GemmCfg<EPI>;
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([&](int) {
+        return cudaFuncSetAttribute(gemm_f16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::kSmemBytes);
+    });
+    if (e != cudaSuccess) return e;
+    gemm_f16_kernel<EPI><<<grid, kGemmThreads, C::kSmemBytes, stream>>>(a);
+    return cudaGetLastError();
+}
+
+inline int grid_for(size_t n) {
+    const size_t b = (n + 255) / 256;
+    return static_cast<int>(b < 148 * 16 ? (b ? b : 1) : 148 * 16);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream) {
+    if (g.K <= 0 || g.K % GK || g.tile_rows <= 0 || g.tile_rows % GM || g.n_tokens <= 0)
+        return cudaErrorInvalidValue;
+    if (epi == kEpiSwiGLU ? (g.w_rows != 2 * g.tile_rows || !g.h_out) : (g.w_rows != g.tile_rows))
+        return cudaErrorInvalidValue;
+    GemmArgs a{};
+    const int s_pad = (g.n_tokens + GN - 1) / GN * GN;
+    cudaError_t e = make_tmap_16b(&a.tm_w, const_cast<uint16_t*>(g.W), static_cast<uint64_t>(g.K),
+                                  static_cast<uint64_t>(g.w_rows), GM, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (e != cudaSuccess) return e;
+    e = make_tmap_16b(&a.tm_x, const_cast<uint16_t*>(g.X), static_cast<uint64_t>(g.K),
+                      static_cast<uint64_t>(s_pad), GN, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (e != cudaSuccess) return e;
+    a.K = g.K;
+    a.n_tokens = g.n_tokens;
+    a.up_row0 = g.tile_rows;
+    a.h_out = g.h_out;
+    a.err = g.err;
+    if (epi != kEpiSwiGLU) {
+        // segments: in row order, tile-aligned, covering [0, w_rows)
+        if (g.n_seg < 1 || g.n_seg > 3) return cudaErrorInvalidValue;
+        int next = 0;
+        for (int i = 0; i < g.n_seg; ++i) {
+            if (g.seg[i].row0 != next || g.seg[i].rows <= 0 || g.seg[i].rows % GM || !g.seg[i].out)
+                return cudaErrorInvalidValue;
+            next += g.seg[i].rows;
+            a.seg_row0[i] = g.seg[i].row0;
+            a.seg_rows[i] = g.seg[i].rows;
+            a.seg_out[i] = g.seg[i].out;
+        }
+        if (next != g.w_rows) return cudaErrorInvalidValue;
+        a.n_seg = g.n_seg;
+    }
+    const dim3 grid(g.tile_rows / GM, s_pad / GN);
+    switch (epi) {
+        case kEpiStore: return launch_gemm_e<kEpiStore>(a, grid, stream);
+        case kEpiAdd: return launch_gemm_e<kEpiAdd>(a, grid, stream);
+        case kEpiSwiGLU: return launch_gemm_e<kEpiSwiGLU>(a, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_pack_f16(int type, uint16_t* dst, const void* W, int rows, int cols, cudaStream_t stream) {
+    const int rb = weight_row_bytes(type, cols);
+    if (rb <= 0 || rows <= 0) return cudaErrorInvalidValue;
+    const int grid = grid_for(static_cast<size_t>(rows) * cols);
+    const uint8_t* w = static_cast<const uint8_t*>(W);
+    switch (type) {
+        case kWF32: pack_f16_kernel<kWF32><<<grid, 256, 0, stream>>>(dst, w, rows, cols, rb); break;
+        case kWF16: pack_f16_kernel<kWF16><<<grid, 256, 0, stream>>>(dst, w, rows, cols, rb); break;
+        case kWQ4_0: pack_f16_kernel<kWQ4_0><<<grid, 256, 0, stream>>>(dst, w, rows, cols, rb); break;
+        case kWQ8_0: pack_f16_kernel<kWQ8_0><<<grid, 256, 0, stream>>>(dst, w, rows, cols, rb); break;
+        case kWQ6_K: pack_f16_kernel<kWQ6_K><<<grid, 256, 0, stream>>>(dst, w, rows, cols, rb); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows_f16(uint16_t* out, const float* x, const float* w, int n, float eps,
+                                    int n_tokens, cudaStream_t stream) {
+    if (n <= 0 || n_tokens <= 0) return cudaErrorInvalidValue;
+    rmsnorm_rows_f16_kernel<<<n_tokens, 256, 0, stream>>>(out, x, w, n, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    to_f16_kernel<<<grid_for(n), 256, 0, stream>>>(out, x, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed_rows(int type, float* x, const void* table, const int32_t* tokens, int n_tokens,
+                              int n_vocab, int n_embd, uint32_t* err, cudaStream_t stream) {
+    if (n_tokens <= 0 || n_embd <= 0 || n_tokens > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((n_embd + 255) / 256, n_tokens);
+    const uint8_t* tb = static_cast<const uint8_t*>(table);
+    if (type == kWF16)
+        embed_rows_kernel<kWF16><<<grid, 256, 0, stream>>>(x, tb, tokens, n_vocab, n_embd, err);
+    else if (type == kWF32)
+        embed_rows_kernel<kWF32><<<grid, 256, 0, stream>>>(x, tb, tokens, n_vocab, n_embd, err);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+}  // namespace tle

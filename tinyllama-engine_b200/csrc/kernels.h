@@ -126,6 +126,7 @@ struct PrefillArgs {
     int n_ctx;
     void* workspace;
     uint32_t* err;        // device error word
+    int f16;              // tensor-core operands fp16 (batched prompt) instead of bf16 (tle_prefill)
     float inv_freq[kHeadDim / 2];
 };
 size_t prefill_workspace_bytes(int n_tokens, int pos0);
@@ -181,6 +182,42 @@ cudaError_t launch_sample(float* logits, int n, float temperature, float top_p, 
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps,
                            cudaStream_t stream);
 cudaError_t launch_vec_add(float* out, const float* x, int n, cudaStream_t stream);
+
+// ---- batched prompt forward (gemm.cu) ----
+// Y[t][r] = sum_k W[r][k] X[t][k] on the tensor cores, W and X fp16
+// row-major, fp32 accumulation; tiles of 128 weight rows x 128 tokens.
+constexpr int kGemmTileRows = 128;
+constexpr int kGemmTileTokens = 128;
+constexpr int kGemmTileK = 64;
+struct GemmSegment {
+    int row0;     // first weight row of the segment
+    int rows;     // its rows (a multiple of kGemmTileRows)
+    float* out;   // [n_tokens][rows]: out[t][r - row0]
+};
+struct GemmLaunch {
+    const uint16_t* W;   // fp16 [w_rows][K]
+    int w_rows;
+    const uint16_t* X;   // fp16 [round_up(n_tokens, 128)][K] (pad rows are read, their results dropped)
+    int n_tokens;
+    int K;               // a multiple of kGemmTileK
+    int tile_rows;       // output rows: w_rows (store/add), n_ff (SwiGLU: gate rows 0.., up rows n_ff..)
+    GemmSegment seg[3];  // store/add outputs by weight row
+    int n_seg;
+    uint16_t* h_out;     // SwiGLU: fp16 [round_up(n_tokens, 128)][tile_rows]
+    uint32_t* err;
+};
+cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream);
+// fp16 copy of a GGUF weight (rows x cols of `type`): dst[r][c] = the
+// reference's dequantised value, rounded to nearest fp16.
+cudaError_t launch_pack_f16(int type, uint16_t* dst, const void* W, int rows, int cols, cudaStream_t stream);
+// out[t][:] = fp16(rmsnorm(x[t][:]) * w) for t < n_tokens.
+cudaError_t launch_rmsnorm_rows_f16(uint16_t* out, const float* x, const float* w, int n, float eps,
+                                    int n_tokens, cudaStream_t stream);
+// out[i] = fp16(x[i]), i < n.
+cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, cudaStream_t stream);
+// x[t][:] = row tokens[t] of the table (F16 or F32), t < n_tokens.
+cudaError_t launch_embed_rows(int type, float* x, const void* table, const int32_t* tokens, int n_tokens,
+                             int n_vocab, int n_embd, uint32_t* err, cudaStream_t stream);
 
 constexpr int kMaxDevices = 64;
 struct PerDeviceOnce {

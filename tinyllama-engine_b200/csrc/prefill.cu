@@ -25,9 +25,14 @@
 //     The next item's first scores are computed during this item's epilogue,
 //     which stages O through the dead Q buffer for coalesced stores.  Q, K,
 //     V and P enter the MMA as bf16 with fp32 accumulation (the north-star
-//     prefill contract, tolerance 2e-2).
+//     prefill contract, tolerance 2e-2).  Both kernels are templates on the
+//     16-bit type: the batched prompt (gemm.cu) runs them with fp16
+//     operands, 3 more significand bits, because there the attention
+//     output of one layer feeds the next (|q/8|, |k|, |v| and P <= 2^8 stay
+//     far inside fp16's range for this model family).
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <math.h>
 
 #include <mutex>
@@ -92,6 +97,17 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&b);
 }
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// The 16-bit operand type of one instantiation: bf16 (tle_prefill) or fp16
+// (the batched prompt, whose errors compound over layers).
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+    if constexpr (F16) return pack_f16(lo, hi);
+    else return pack_bf16(lo, hi);
+}
 
 // blockIdx.y == 0: one token per warp, lane = rotation pair p.  One sincosf
 //   per (token, pair) serves the 32 query heads and 4 key heads: rotated
@@ -101,6 +117,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 //   tokens, zero pad) are transposed through shared memory into Vt, and the
 //   new tokens' v rows are appended to the cache; Kb rows of the cache prefix
 //   (bf16 of the cached rotated k) and of the pad (zero).
+template <bool F16>
 __global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __grid_constant__ PrepArgs A) {
     __shared__ __align__(16) uint16_t vtile[kVtRows * kVtPitch];   // bf16 bits
     // The attention launch may start now (programmatic dependent launch): it
@@ -135,7 +152,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __g
         for (int h = 0; h < NH; ++h) {
             const float2 x = xq[h];
             qb32[(static_cast<size_t>(h) * A.S_pad + i) * (HD / 2) + lane] =
-                pack_bf16((x.x * cs - x.y * sn) * kQScale, (x.x * sn + x.y * cs) * kQScale);
+                pack16<F16>((x.x * cs - x.y * sn) * kQScale, (x.x * sn + x.y * cs) * kQScale);
         }
         float2* kcr = reinterpret_cast<float2*>(A.kc + static_cast<size_t>(pos) * NKV * HD);
         uint32_t* kb32 = reinterpret_cast<uint32_t*>(A.kb);
@@ -144,7 +161,7 @@ __global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __g
             const float2 x = xk[g];
             const float2 y = make_float2(x.x * cs - x.y * sn, x.x * sn + x.y * cs);
             kcr[g * (HD / 2) + lane] = y;                                     // append (ops.cpp:1370)
-            kb32[(static_cast<size_t>(g) * A.R_pad + pos) * (HD / 2) + lane] = pack_bf16(y.x, y.y);
+            kb32[(static_cast<size_t>(g) * A.R_pad + pos) * (HD / 2) + lane] = pack16<F16>(y.x, y.y);
         }
         return;
     }
@@ -173,14 +190,14 @@ __global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __g
         if (r >= A.pos0 && r < A.R)   // append v of the new tokens (ops.cpp:1371)
             reinterpret_cast<float4*>(A.vc + static_cast<size_t>(r) * NKV * HD)[c4] = vv[u];
         *reinterpret_cast<uint2*>(&vtile[rr * kVtPitch + 4 * c4]) =
-            make_uint2(pack_bf16(vv[u].x, vv[u].y), pack_bf16(vv[u].z, vv[u].w));
+            make_uint2(pack16<F16>(vv[u].x, vv[u].y), pack16<F16>(vv[u].z, vv[u].w));
         // Kb rows outside [pos0, R): bf16 of the cached prefix, zero pad
         if (r < A.pos0 || r >= A.R) {
             float4 kk = make_float4(0.f, 0.f, 0.f, 0.f);
             if (r < A.pos0) kk = reinterpret_cast<const float4*>(A.kc + static_cast<size_t>(r) * NKV * HD)[c4];
             const int g = c4 / (HD / 4), d4 = c4 % (HD / 4);
             *reinterpret_cast<uint2*>(A.kb + (static_cast<size_t>(g) * A.R_pad + r) * HD + 4 * d4) =
-                make_uint2(pack_bf16(kk.x, kk.y), pack_bf16(kk.z, kk.w));
+                make_uint2(pack16<F16>(kk.x, kk.y), pack16<F16>(kk.z, kk.w));
         }
     }
     __syncthreads();
@@ -342,7 +359,10 @@ __device__ __forceinline__ Item item_at(const AttnArgs& A, int idx) {
     return it;
 }
 
+template <bool F16>
 __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __grid_constant__ AttnArgs A) {
+    constexpr uint32_t kIdS = F16 ? idesc_f16_f32(BM, BN) : kIdescS;
+    constexpr uint32_t kIdO = F16 ? idesc_f16_f32(BM, HD) : kIdescO;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // SW128 atoms need 1024-byte aligned tiles (the launch adds 1 KB of slack)
     AttnSmem& S = *reinterpret_cast<AttnSmem*>(
@@ -449,7 +469,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
                     const uint64_t dq = sw128_desc(smem_u32(S.q[b][i]));
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk)
-                        umma_bf16(tS, dq + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdescS, kk > 0);
+                        umma_bf16(tS, dq + 2 * kk, dk0 + st * kStageK + 2 * kk, kIdS, kk > 0);
                     umma_commit(&S.s_full[i]);
                     if (n == n_kv - 1) umma_commit(&S.q_free[b]);   // last read of Q buffer b
                 }
@@ -463,7 +483,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk)
                         umma_bf16_tmem_a(tO, tP + 8 * kk,
-                                         dv0 + st * kStageV + (kk >> 2) * kHalfV + 2 * (kk & 3), kIdescO,
+                                         dv0 + st * kStageV + (kk >> 2) * kHalfV + 2 * (kk & 3), kIdO,
                                          (n > 0 || kk > 0) ? 1u : 0u);
                     umma_commit(&S.p_free[i]);
                     umma_commit(&S.kv_empty[st]);
@@ -579,7 +599,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
 #pragma unroll
                 for (int e = 0; e < BN / 2; ++e) {
                     lsum2[e & 3] = fadd2(lsum2[e & 3], f2(s[2 * e], s[2 * e + 1]));
-                    pk[e] = pack_bf16(s[2 * e], s[2 * e + 1]);
+                    pk[e] = pack16<F16>(s[2 * e], s[2 * e + 1]);
                 }
                 float lsum0, lsum1;
                 f2_split(fadd2(fadd2(lsum2[0], lsum2[1]), fadd2(lsum2[2], lsum2[3])), lsum0, lsum1);
@@ -696,6 +716,11 @@ cudaError_t make_map(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, u
 
 }  // namespace
 
+cudaError_t make_tmap_16b(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                          CUtensorMapDataType dtype) {
+    return make_map(m, base, cols, rows, box_rows, dtype);
+}
+
 size_t prefill_workspace_bytes(int n_tokens, int pos0) {
     if (n_tokens <= 0 || pos0 < 0) return 0;
     return layout_for(n_tokens, pos0).total;
@@ -721,17 +746,20 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     for (int i = 0; i < HD / 2; ++i) p.inv_freq[i] = a.inv_freq[i];
     {
         const int gx = std::max((L.S_pad + kPrepTokensPerBlock - 1) / kPrepTokensPerBlock, L.R_pad / kVtRows);
-        prefill_prep_kernel<<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
+        if (a.f16)
+            prefill_prep_kernel<true><<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
+        else
+            prefill_prep_kernel<false><<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     AttnArgs t{};
-    cudaError_t e = make_map(&t.tm_q, p.qb, HD, static_cast<uint64_t>(NH) * L.S_pad, BM);
+    const CUtensorMapDataType dt = a.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    cudaError_t e = make_map(&t.tm_q, p.qb, HD, static_cast<uint64_t>(NH) * L.S_pad, BM, dt);
     if (e != cudaSuccess) return e;
-    e = make_map(&t.tm_k, p.kb, HD, static_cast<uint64_t>(NKV) * L.R_pad, BN);
+    e = make_map(&t.tm_k, p.kb, HD, static_cast<uint64_t>(NKV) * L.R_pad, BN, dt);
     if (e != cudaSuccess) return e;
-    e = make_map(&t.tm_vt, p.vt, static_cast<uint64_t>(L.R_pad), static_cast<uint64_t>(NKV) * HD, 64,
-                 CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    e = make_map(&t.tm_vt, p.vt, static_cast<uint64_t>(L.R_pad), static_cast<uint64_t>(NKV) * HD, 64, dt);
     if (e != cudaSuccess) return e;
     t.out = a.out;
     t.pos0 = a.pos0;
@@ -749,11 +777,16 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         // setmaxnreg.inc waits until the block's launch registers cover the
         // split; refuse to launch (instead of hanging) if the compiled kernel
         // was given fewer registers than the split assumes.
-        cudaFuncAttributes fa{};
-        cudaError_t r = cudaFuncGetAttributes(&fa, prefill_attn_kernel);
-        if (r != cudaSuccess) return r;
-        if (fa.numRegs < kLaunchRegs) return cudaErrorInvalidConfiguration;
-        return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        for (const void* fn : {reinterpret_cast<const void*>(prefill_attn_kernel<false>),
+                               reinterpret_cast<const void*>(prefill_attn_kernel<true>)}) {
+            cudaFuncAttributes fa{};
+            cudaError_t r = cudaFuncGetAttributes(&fa, fn);
+            if (r != cudaSuccess) return r;
+            if (fa.numRegs < kLaunchRegs) return cudaErrorInvalidConfiguration;
+            r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (r != cudaSuccess) return r;
+        }
+        return cudaSuccess;
     });
     if (e != cudaSuccess) return e;
     // Programmatic dependent launch: the attention grid may start while the
@@ -772,7 +805,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, t);
+    if (a.f16) return cudaLaunchKernelEx(&cfg, prefill_attn_kernel<true>, t);
+    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel<false>, t);
 }
 
 }  // namespace tle

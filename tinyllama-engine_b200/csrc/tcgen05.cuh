@@ -72,7 +72,15 @@ constexpr uint32_t idesc_bf16_f32(int M, int N) {
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+// Instruction descriptor, kind::f16: D fp32, A/B fp16 (format 0), both
+// K-major; same fields as idesc_bf16_f32.
+constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.  kind::f16: the
+// operand type (bf16 or fp16, the same for A and B) is the instruction
+// descriptor's.
 TLE_DEV void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                        uint32_t accumulate) {
     asm volatile(
@@ -175,5 +183,11 @@ TLE_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64
 TLE_DEV void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+
+// Host: 2-D tensor map over a row-major [rows][cols] array of 16-bit
+// elements (bf16 or fp16), box {64, box_rows}, 128-byte swizzle (the UMMA
+// K-major SW128 layout), no out-of-bounds fill needed by the callers.
+cudaError_t make_tmap_16b(CUtensorMap* m, void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                          CUtensorMapDataType dtype);
 
 }  // namespace tle

@@ -44,6 +44,8 @@ EXPORTED = (
     # include/tle_forward.h
     "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
     "tle_forward_workspace_bytes", "tle_forward", "tle_sample_temperature", "tle_sample_top_p",
+    "tle_prompt_weights_bytes", "tle_prompt_pack_weights", "tle_prompt_scratch_bytes",
+    "tle_prompt_forward",
 )
 
 
@@ -156,6 +158,12 @@ def lib() -> ctypes.CDLL:
         L.tle_decode_desc_paged.argtypes = [P(Shape), P(PagePool), P(PagedSeq), i, i, vp, sz, P(i)]
         L.tle_decode_batch_paged.argtypes = [P(Shape), P(PagePool), vp, i, i, vp, vp, vp, vp, i, i,
                                              vp, sz, vp]
+        L.tle_prompt_weights_bytes.argtypes = [P(Model)]
+        L.tle_prompt_weights_bytes.restype = sz
+        L.tle_prompt_pack_weights.argtypes = [P(Model), vp, sz, vp]
+        L.tle_prompt_scratch_bytes.argtypes = [P(Model), i, i]
+        L.tle_prompt_scratch_bytes.restype = sz
+        L.tle_prompt_forward.argtypes = [P(Model), vp, P(State), vp, i, i, vp, sz, vp]
         _lib = L
     return _lib
 
@@ -606,6 +614,50 @@ class DeviceState:
     @property
     def logits(self):
         return self.t["logits"]
+
+
+class PromptWeights:
+    """The fp16 copy of a DeviceModel's linear weights that the batched
+    prompt reads (tle_prompt_pack_weights), made once on the device."""
+
+    def __init__(self, dm: DeviceModel, stream=None):
+        import torch
+        nbytes = lib().tle_prompt_weights_bytes(ctypes.byref(dm.desc))
+        if nbytes == 0:
+            _check(TLE_ERR_UNSUPPORTED)
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        _check(lib().tle_prompt_pack_weights(ctypes.byref(dm.desc), _ptr(self.buf), nbytes,
+                                             _stream(stream)))
+
+
+def prompt_scratch(dm: DeviceModel, n_tokens: int, pos0: int = 0, device="cuda"):
+    """A 1024-byte aligned uint8 CUDA tensor of tle_prompt_scratch_bytes (the
+    caching allocator hands out 512-byte aligned blocks, so this
+    over-allocates by 1 KB and offsets)."""
+    import torch
+    need = lib().tle_prompt_scratch_bytes(ctypes.byref(dm.desc), n_tokens, pos0)
+    if need == 0:
+        _check(TLE_ERR_INVALID)
+    raw = torch.empty(need + 1024, dtype=torch.uint8, device=device)
+    off = (-raw.data_ptr()) % 1024
+    return raw[off:off + need]
+
+
+def prompt_forward(dm: DeviceModel, ds: DeviceState, pw: PromptWeights, tokens, pos0: int = 0,
+                   scratch=None, stream=None) -> None:
+    """generate.cpp:52-59's prompt loop (forward() for tokens[i] at pos0 + i)
+    as one batched pass: tokens is an int32 CUDA tensor; the caches get rows
+    pos0.., ds.logits the last token's logits.  scratch: from prompt_scratch
+    (allocated here when None)."""
+    import torch
+    if tokens.dtype != torch.int32 or not tokens.is_cuda or not tokens.is_contiguous():
+        raise ValueError("tokens: need a contiguous int32 CUDA tensor")
+    n = tokens.numel()
+    if scratch is None:
+        scratch = prompt_scratch(dm, n, pos0, tokens.device)
+    _check(lib().tle_prompt_forward(ctypes.byref(dm.desc), _ptr(pw.buf), ctypes.byref(ds.desc),
+                                    _ptr(tokens), n, pos0, _ptr(scratch),
+                                    scratch.numel() * scratch.element_size(), _stream(stream)))
 
 
 def forward(dm: DeviceModel, ds: DeviceState, token, pos: int, stream=None) -> None:
