@@ -8,13 +8,17 @@ value is exact in fp32 and rounds once to fp16, as numpy rounds it.  The
 products take fp16 operands (weights, normalised inputs, attention output,
 SwiGLU output) with fp32 accumulation and the attention fp16 Q, K, V and P,
 so results differ from the fp32 oracle by the rounding of those inputs
-(2^-11 relative each).  A float64 model of exactly those roundings on these
-cases gives cache-row errors of at most 3.3e-4 x max|row| in layer 0 and
-6.8e-3 in layer 1 (the layer-0 attention error feeds layer 1), and logits
-errors of 1e-4 (Q4_0), 9e-4 (Q8_0) and 1.4e-4 (F16) x max|logit|; the
-bounds below are about 5x those.  The Q6_K model (large random weights,
-near-one-hot attention) amplifies them to 3 % of the logits, so for Q6_K
-only the layer-0 cache rows and the weight copy are checked.
+(2^-11 relative each).  A float64 model of exactly those roundings, run on
+the models and tokens of these cases, gives cache-row errors of at most
+3.2e-4 x max|row| in layer 0 and 4.9e-3 in layer 1 (the layer-0 attention
+error feeds layer 1), and logits errors of 2.0e-3 (Q4_0, 2 layers,
+200 tokens), 1.0e-4 (Q4_0 in two chunks), 5.2e-4 (Q8_0) and 8.2e-5 (F16)
+x max|logit|.  The random models' attention is close to one-hot, so the
+fp16 rounding of q and k moves the layer-1 attention output by tens of
+percent on some rows, and the logits error depends on the seed.  The bounds
+below are about 5x the modelled errors of each case.  The Q6_K model (large
+random weights) amplifies them to 1.2 % of the logits, so for Q6_K only the
+cache rows and the weight copy are checked.
 """
 import os
 import sys
@@ -29,15 +33,10 @@ sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(
                                 "tinyllama-engine_b200"))
 import synth  # noqa: E402
 
-# The first GPU run of these kernels is made by hand before they join the
-# round-end suite: TLE_RUN_PROMPT_GPU=1 selects them.
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TLE_RUN_PROMPT_GPU") != "1",
-                                 reason="batched prompt: first supervised GPU run pending")]
+pytestmark = pytest.mark.gpu
 
 LAYER0_TOL = 2e-3
 LAYER1_TOL = 3e-2
-LOGIT_TOL = {Q4_0: 1e-3, Q8_0: 5e-3, F16: 1e-3}
 
 
 def host(t):
@@ -81,7 +80,7 @@ def test_weight_copy_is_bit_exact(cuda, wtype):
     assert off == got.size
 
 
-def check_prompt(m, tokens, wtype, chunks=None):
+def check_prompt(m, tokens, logit_tol, chunks=None):
     import torch
     import tle
     dm = tle.DeviceModel(m)
@@ -106,8 +105,8 @@ def check_prompt(m, tokens, wtype, chunks=None):
         assert rel(vc[l], vw[l]) <= tol, ("v", l, rel(vc[l], vw[l]))
     got = host(ds.logits)
     assert np.all(np.isfinite(got))
-    if wtype in LOGIT_TOL:
-        t = LOGIT_TOL[wtype]
+    if logit_tol is not None:
+        t = logit_tol
         assert rel(got, want) <= t, rel(got, want)
         top2 = np.sort(want)[-2:]
         if top2[1] - top2[0] > 2 * t * np.max(np.abs(want)):
@@ -116,15 +115,15 @@ def check_prompt(m, tokens, wtype, chunks=None):
     return dm, ds, hf
 
 
-@pytest.mark.parametrize("wtype,n_layers,vocab,S,out_type", [
-    (Q4_0, 2, 2048, 200, Q4_0), (Q8_0, 1, 1024, 64, None), (F16, 1, 1024, 64, F16),
-    (Q6_K, 1, 1024, 64, Q6_K),
+@pytest.mark.parametrize("wtype,n_layers,vocab,S,out_type,logit_tol", [
+    (Q4_0, 2, 2048, 200, Q4_0, 1e-2), (Q8_0, 1, 1024, 64, None, 3e-3), (F16, 1, 1024, 64, F16, 5e-4),
+    (Q6_K, 1, 1024, 64, Q6_K, None),
 ])
-def test_prompt_matches_token_at_a_time_oracle(cuda, wtype, n_layers, vocab, S, out_type):
+def test_prompt_matches_token_at_a_time_oracle(cuda, wtype, n_layers, vocab, S, out_type, logit_tol):
     m = synth.make_model(seed=31 + wtype, n_layers=n_layers, wtype=wtype, output_type=out_type,
                          n_vocab=vocab, n_ctx=256, n_ff=512)
     tokens = np.random.default_rng(7).integers(0, vocab, S)
-    check_prompt(m, tokens, wtype)
+    check_prompt(m, tokens, logit_tol)
 
 
 def test_prompt_in_chunks_then_decode(cuda):
@@ -136,11 +135,11 @@ def test_prompt_in_chunks_then_decode(cuda):
     m = synth.make_model(seed=35, n_layers=2, wtype=Q4_0, output_type=Q4_0, n_vocab=2048, n_ctx=256,
                          n_ff=512)
     tokens = np.random.default_rng(8).integers(0, 2048, 133)
-    dm, ds, hf = check_prompt(m, tokens, Q4_0, chunks=[72, 61])
+    dm, ds, hf = check_prompt(m, tokens, 5e-4, chunks=[72, 61])
     nxt = 1234
     tle.forward(dm, ds, torch.tensor([nxt], dtype=torch.int32, device="cuda"), len(tokens))
     want = oracle.port().forward(hf, nxt, len(tokens))
-    assert rel(host(ds.logits), want) <= LOGIT_TOL[Q4_0] * 5
+    assert rel(host(ds.logits), want) <= 2.5e-3
 
 
 def test_prompt_single_token_and_bad_token(cuda):
@@ -150,7 +149,7 @@ def test_prompt_single_token_and_bad_token(cuda):
     import tle
     m = synth.make_model(seed=36, n_layers=1, wtype=Q4_0, output_type=Q4_0, n_vocab=512, n_ctx=32,
                          n_ff=512)
-    check_prompt(m, [5], Q4_0)
+    check_prompt(m, [5], 1e-3)
     dm = tle.DeviceModel(m)
     ds = tle.DeviceState(dm)
     pw = tle.PromptWeights(dm)
