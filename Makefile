@@ -10,6 +10,8 @@ PKG := tinyllama-engine_b200
 CSRC := $(PKG)/csrc
 HOST := $(PKG)/host
 LIB := $(PKG)/libtle_attn.so
+# Reference checkout for oracle/_ref: by default the one beside this repository.
+REF ?= $(abspath $(CURDIR)/../reference)
 
 ARCH := -gencode arch=compute_100a,code=sm_100a
 NVFLAGS := -std=c++20 -O3 $(ARCH) -lineinfo -Xcompiler -fPIC -Xcompiler -Wall \
@@ -34,7 +36,7 @@ $(LIB): $(CU_OBJS) $(HOST_OBJS)
 	$(NVCC) $(ARCH) -shared $^ -o $@
 
 oracle:
-	$(MAKE) -C oracle
+	$(MAKE) -C oracle REF=$(REF)
 
 cpptest: tests/cpp/test_ops_gpu
 

@@ -8,10 +8,15 @@ the 126 MB L2, so no flush is needed).  A step is one fused
 rope + append + GQA decode-attention call for every sequence
 (tle_decode_batch), i.e. attention() of src/ops.cpp:1317 for 256 sequences.
 
-Multi-GPU (torchrun, one process per GPU): sequences are partitioned by
-length (tle_partition_lpt), every rank decodes its shard from its own HBM,
-then the outputs are all-gathered over NCCL; the step time is the max over
-ranks (strong scaling: the 256-sequence total is fixed).
+Multi-GPU (torchrun, one process per GPU): the 256 equal sequences are cut
+into contiguous equal blocks (shard.plan), every rank decodes its block from
+its own HBM straight into its slot of the all-gather buffer, and the NCCL
+all-gather of step i (already in sequence order) runs on its own stream while
+step i+1 decodes into a second buffer; the step time is the max over ranks
+(strong scaling: the 256-sequence total is fixed).  The same line carries
+config 4 at the job's GPU count (`decode_config4`: 64 ragged sequences
+LPT-partitioned, 22 layers per step, one all-gather of every layer's
+outputs per step).
 
 `--impl reference` times the reference's own CPU attention (src/ops.cpp
 compiled unmodified into oracle/_ref) on a bounded sample of the same
@@ -180,6 +185,14 @@ def cpu_model():
 
 
 # ------------------------------------------------------------- GPU arm
+def main_config(args):
+    """`config` of the headline line, the same dict in both arms."""
+    n = args.gpus
+    return {"workload": WORKLOAD, "n_seqs": args.seqs, "ctx": args.ctx, "layers_timed": 1,
+            "l2": "inputs larger than L2 (17.2 GB of K+V per step)",
+            "parallelism": "sequence partition over %d GPUs + NCCL all-gather" % n if n > 1 else "1 GPU"}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -196,14 +209,13 @@ def main():
                 "n_gpus": args.gpus, "steps": runs, "warmup": args.warmup,
                 "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
-                "config": {"workload": WORKLOAD, "n_seqs": args.seqs, "ctx": args.ctx},
+                "config": main_config(args),
                 "cpu_baseline": dict(desc, value=round(gbs, 3), unit="GB/s"),
                 "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
 
-    import numpy as np
     import torch
     import torch.distributed as dist
     import tle
@@ -223,173 +235,62 @@ def main():
         return
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
-
-    # ---- shard the sequences (LPT by length; all equal here) ----
-    import shard
-    plan = shard.plan([args.ctx] * args.seqs, world)
-    mine = plan.mine(rank)
-    n = len(mine)
-    max_local = plan.max_local
-
-    # ---- device-resident state (KV caches of my sequences) ----
-    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
-    kc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
-    vc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
-    caches = [(kc[i], vc[i], args.ctx) for i in range(n)]
-    shape = tle.tinyllama_shape(1)
-    batch = tle.DecodeBatch(caches, [args.ctx - 1] * n, shape)
-    hq = torch.randn((max_local, QD), generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
-    hk = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(8 + rank)).pin_memory()
-    hv = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
-    q = hq.to(dev); k = hk.to(dev); v = hv.to(dev)
-    out = torch.zeros((max_local, QD), device=dev)
-    gather = shard.OutputGather(plan, QD, dev)
-    hout = torch.zeros((args.seqs, QD)).pin_memory()
-    stream = torch.cuda.current_stream(dev)
-
-    def decode_only():
-        batch.run(q, k, v, out, 0, rotate=True, stream=stream)
-
-    def step():
-        decode_only()
-        return gather(out)   # NCCL all-gather + reorder (world > 1)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    barrier()
-
+    peaks = load_peaks()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-
-    # ---- device-timed region: K steps (decode + NCCL gather) ----
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    barrier()
-    ev[0].record(stream)
-    for i in range(args.steps):
-        kev[i][0].record(stream)
-        decode_only()
-        kev[i][1].record(stream)
-        gather(out)
-    ev[1].record(stream)
-    barrier()
-    t_ms = ev[0].elapsed_time(ev[1])
-    k_ms = [a.elapsed_time(b) for a, b in kev]
-
-    # ---- end-to-end through the public API with host buffers ----
-    # Every step copies its q/k/v from pinned host memory and reads its
-    # output back; the copies run on their own streams (one per direction),
-    # double-buffered, so step i+1's inputs and step i-1's outputs move while
-    # step i computes (the serving pattern).  The per-step descriptor upload
-    # (positions) stays on the compute stream, ordered after the previous
-    # kernel.
-    cstream = torch.cuda.Stream(dev)     # host -> device
-    dstream = torch.cuda.Stream(dev)     # device -> host
-    qb = [torch.empty_like(q) for _ in range(2)]
-    kb = [torch.empty_like(k) for _ in range(2)]
-    vb = [torch.empty_like(v) for _ in range(2)]
-    ob = [out, torch.zeros_like(out)]
-    hout2 = [hout, torch.zeros_like(hout).pin_memory()]
-    h2d_done = [torch.cuda.Event() for _ in range(2)]
-    comp_done = [torch.cuda.Event() for _ in range(2)]
-    d2h_done = [torch.cuda.Event() for _ in range(2)]
-    barrier()
-    e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    e2[0].record(stream)
-    cstream.wait_event(e2[0])
-    dstream.wait_event(e2[0])
-    for i in range(args.steps):
-        b = i & 1
-        with torch.cuda.stream(cstream):
-            if i >= 2:
-                cstream.wait_event(comp_done[b])      # step i-2 finished reading buffers b
-            qb[b].copy_(hq, non_blocking=True)
-            kb[b].copy_(hk, non_blocking=True)
-            vb[b].copy_(hv, non_blocking=True)
-            h2d_done[b].record(cstream)
-        stream.wait_event(h2d_done[b])
-        batch.upload(stream)                          # per-step descriptor (positions)
-        if i >= 2:
-            stream.wait_event(d2h_done[b])            # ob[b] of step i-2 read back
-        batch.run(qb[b], kb[b], vb[b], ob[b], 0, rotate=True, stream=stream)
-        res = gather(ob[b])
-        res.record_stream(dstream)
-        comp_done[b].record(stream)
-        with torch.cuda.stream(dstream):
-            dstream.wait_event(comp_done[b])
-            hout2[b].copy_(res, non_blocking=True)
-            d2h_done[b].record(dstream)
-    stream.wait_stream(cstream)
-    stream.wait_stream(dstream)
-    e2[1].record(stream)
-    barrier()
-    e2e_ms = e2[0].elapsed_time(e2[1])
+    r5 = run_config5(args, dev, rank, world, barrier)
     clk = clocks.stop()
+    r4 = run_config4_sharded(dev, rank, world, barrier, peaks)
     err_code = tle.device_error()
     if err_code:
         raise RuntimeError(f"device error word 0x{err_code:x}")
 
-    # ---- max over ranks ----
-    vals = torch.tensor([t_ms, e2e_ms, statistics.mean(k_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, kernel_ms = [float(x) for x in vals.cpu()]
-
-    total_bytes = args.seqs * args.ctx * ROW_BYTES
-    step_s = t_ms / 1e3 / args.steps
-    value = total_bytes / step_s / 1e9
-    e2e_value = total_bytes / (e2e_ms / 1e3 / args.steps) / 1e9
-
     if rank == 0:
-        peaks = load_peaks()
-        local_bytes = n * args.ctx * ROW_BYTES
-        achieved = local_bytes / (kernel_ms / 1e3) / 1e9
+        total_bytes = args.seqs * args.ctx * ROW_BYTES
+        step_s = r5["t_ms"] / 1e3 / args.steps
+        value = total_bytes / step_s / 1e9
+        e2e_value = total_bytes / (r5["e2e_ms"] / 1e3 / args.steps) / 1e9
+        achieved = r5["local_bytes"] / (r5["kernel_ms"] / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup),
-            "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "ms_per_step": round(r5["t_ms"] / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic N(0,1) fp32, seeded (no dataset)",
-            "config": {"workload": WORKLOAD, "n_seqs": args.seqs, "ctx": args.ctx,
-                       "layers_timed": 1, "l2": "inputs larger than L2 (17.2 GB KV per step)",
-                       "parallelism": f"sequence partition over {world} GPU(s) + NCCL all-gather"
-                       if world > 1 else "1 GPU"},
+            "config": main_config(args),
             "tok_s_attn_22_layers": round(args.seqs / (step_s * 22), 1),
-            "pct_hbm_peak": round(100 * achieved / peaks["hbm_gbs"], 1),
+            "frac_per_gpu": round(value / world / peaks["hbm_gbs"], 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"],
-                         "traffic": profile_traffic(local_bytes),
-                         "kernel": "tle_decode_batch (decode_kernel, split-K merge fused), rank 0",
-                         "algorithmic_bytes_per_launch": local_bytes,
-                         "kernel_ms": round(kernel_ms, 4)},
+                         "traffic": profile_traffic(r5["local_bytes"]),
+                         "kernel": "decode_kernel (tle_decode_batch, split-K merge fused), rank 0",
+                         "algorithmic_bytes_per_launch": r5["local_bytes"],
+                         "kernel_ms": round(r5["kernel_ms"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": int(hq[:n].numel() * 4 + hk[:n].numel() * 4
-                                              + hv[:n].numel() * 4 + batch.desc_bytes),
-                    "d2h_bytes_per_step": int(args.seqs * QD * 4),
-                    "ms_per_step": round(e2e_ms / args.steps, 4),
-                    "path": "tle.DecodeBatch.run (C ABI tle_decode_batch) with pinned host q/k/v "
-                            "in and host out back every step; copies on their own streams, "
-                            "double-buffered, overlapping the neighbouring steps' kernels"},
+                    "h2d_bytes_per_step": r5["h2d_bytes"], "d2h_bytes_per_step": r5["d2h_bytes"],
+                    "ms_per_step": round(r5["e2e_ms"] / args.steps, 4)},
+            "decode_config4": r4,
             "gpu_launches": args.steps,   # one decode_kernel per tle_decode_batch call
             "clocks": clk,
         }
         if world == 1 and not args.no_secondary:
-            line["secondary"] = {"prefill_config3": measure_prefill(dev, peaks),
-                                 "decode_config4": measure_config4(dev, peaks),
-                                 "decode_config1": measure_config1(dev, peaks),
-                                 "decode_config4_paged": measure_paged4(dev, peaks),
-                                 "decode_config5_paged": measure_paged5(dev, peaks),
-                                 "generate_config2": measure_config2(dev, peaks, steps=3)}
+            line["secondary"] = {
+                "prefill_config3": compact(measure_prefill(dev, peaks)),
+                "decode_config4_n1": compact(measure_config4(dev, peaks)),
+                "decode_config1": compact(measure_config1(dev, peaks)),
+                "decode_config4_paged": compact(measure_paged4(dev, peaks)),
+                "decode_config5_paged": compact(measure_paged5(dev, peaks)),
+                "generate_config2": compact(measure_config2(dev, peaks, steps=3)),
+                "prompt_config2": compact(measure_prompt2(dev, peaks, steps=3))}
         if world == 1 and not args.no_cpu_baseline:
             gbs, med, runs, desc = cpu_reference_run(args.seqs, args.ctx, 1000, 1, args.cpu_seconds)
             line["cpu_baseline"] = dict(desc, value=round(gbs, 3), unit="GB/s")
@@ -398,6 +299,259 @@ def main():
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def compact(d):
+    """The few fields of a secondary workload that the one-line record keeps
+    (the full record: `bench.py --only NAME`)."""
+    out = {"value": d.get("value"), "unit": d.get("unit")}
+    for key in ("ms_per_step", "ms_per_token", "value_cold_l2", "tok_s", "prompts"):
+        if key in d:
+            out[key] = d[key]
+    roof = d.get("roofline") or {}
+    if "frac" in roof or "frac_cold" in roof:
+        out["frac"] = roof.get("frac", roof.get("frac_cold"))
+    if "cpu_reference" in d:
+        c = d["cpu_reference"]
+        out["cpu_reference"] = {k: c[k] for k in ("value", "unit", "cores", "kind") if k in c}
+    return out
+
+
+def run_config5(args, dev, rank, world, barrier):
+    """Headline (config 5): every rank decodes its shard of the sequences
+    (one tle_decode_batch launch per step) straight into its block of the
+    all-gather buffer; the NCCL all-gather of step i runs on its own stream
+    while step i+1 decodes into the other of two buffers.  Returns the
+    max-over-ranks times of the device-timed loop and of the end-to-end loop
+    (pinned host inputs in, the gathered output back to rank 0's host)."""
+    import torch
+    import torch.distributed as dist
+    import shard
+    import tle
+    plan = shard.plan([args.ctx] * args.seqs, world)
+    mine = plan.mine(rank)
+    n = len(mine)
+    max_local = plan.max_local
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    kc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
+    vc = torch.randn((n, 1, args.ctx, KVD), generator=gen, device=dev)
+    caches = [(kc[i], vc[i], args.ctx) for i in range(n)]
+    batch = tle.DecodeBatch(caches, [args.ctx - 1] * n, tle.tinyllama_shape(1))
+    hq = torch.randn((max_local, QD), generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
+    hk = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(8 + rank)).pin_memory()
+    hv = torch.randn((max_local, KVD), generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
+    q = hq.to(dev); k = hk.to(dev); v = hv.to(dev)
+    gathers = [shard.OutputGather(plan, QD, dev) for _ in range(2)]
+    outs = [g.local_slot(rank) if world > 1 else torch.zeros((max_local, QD), device=dev)
+            for g in gathers]
+    stream = torch.cuda.current_stream(dev)
+    gstream = torch.cuda.Stream(dev)
+    dec_done = [torch.cuda.Event() for _ in range(2)]
+    gat_done = [torch.cuda.Event() for _ in range(2)]
+
+    def finish(b):
+        """Issues the gather of buffer b after its decode; returns the
+        event after which buffer b (and the gathered rows) may be reused."""
+        if world == 1:
+            dec_done[b].record(stream)
+            return outs[b], dec_done[b]
+        dec_done[b].record(stream)
+        gstream.wait_event(dec_done[b])
+        with torch.cuda.stream(gstream):
+            res = gathers[b](outs[b])
+        gat_done[b].record(gstream)
+        return res, gat_done[b]
+
+    free = [None, None]
+
+    def step(i, kev=None):
+        b = i & 1
+        if free[b] is not None:
+            stream.wait_event(free[b])
+        if kev is not None:
+            kev[0].record(stream)
+        batch.run(q, k, v, outs[b], 0, rotate=True, stream=stream)
+        if kev is not None:
+            kev[1].record(stream)
+        _, free[b] = finish(b)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    stream.wait_stream(gstream)
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    free[0] = free[1] = None
+    barrier()
+    ev[0].record(stream)
+    for i in range(args.steps):
+        step(i, kev[i])
+    stream.wait_stream(gstream)
+    ev[1].record(stream)
+    barrier()
+    t_ms = ev[0].elapsed_time(ev[1])
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+
+    # ---- end to end through the public API with host buffers ----
+    # Every step copies its q/k/v from pinned host memory (own stream,
+    # double-buffered, so step i+1's inputs move while step i computes),
+    # uploads the per-step descriptor (positions), decodes, gathers, and
+    # rank 0 reads the gathered output of all sequences back to the host.
+    cstream = torch.cuda.Stream(dev)     # host -> device
+    dstream = torch.cuda.Stream(dev)     # device -> host (rank 0)
+    qb = [torch.empty_like(q) for _ in range(2)]
+    kb = [torch.empty_like(k) for _ in range(2)]
+    vb = [torch.empty_like(v) for _ in range(2)]
+    hout = [torch.zeros((args.seqs, QD)).pin_memory() for _ in range(2)]
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
+    in_free = [None, None]
+    out_free = [None, None]
+    barrier()
+    e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    e2[0].record(stream)
+    cstream.wait_event(e2[0])
+    dstream.wait_event(e2[0])
+    for i in range(args.steps):
+        b = i & 1
+        with torch.cuda.stream(cstream):
+            if in_free[b] is not None:
+                cstream.wait_event(in_free[b])        # step i-2 finished reading buffers b
+            qb[b].copy_(hq, non_blocking=True)
+            kb[b].copy_(hk, non_blocking=True)
+            vb[b].copy_(hv, non_blocking=True)
+            h2d_done[b].record(cstream)
+        stream.wait_event(h2d_done[b])
+        batch.upload(stream)                          # per-step descriptor (positions)
+        if out_free[b] is not None:
+            stream.wait_event(out_free[b])            # outs[b] gathered and read back
+        batch.run(qb[b], kb[b], vb[b], outs[b], 0, rotate=True, stream=stream)
+        comp_done[b].record(stream)
+        in_free[b] = comp_done[b]
+        res, ready = finish(b)
+        if rank == 0:
+            with torch.cuda.stream(dstream):
+                dstream.wait_event(ready)
+                hout[b].copy_(res, non_blocking=True)
+                d2h_done[b].record(dstream)
+            out_free[b] = d2h_done[b]
+        else:
+            out_free[b] = ready
+    stream.wait_stream(cstream)
+    stream.wait_stream(gstream)
+    stream.wait_stream(dstream)
+    e2[1].record(stream)
+    barrier()
+    e2e_ms = e2[0].elapsed_time(e2[1])
+    h2d = int(hq[:n].numel() * 4 + hk[:n].numel() * 4 + hv[:n].numel() * 4 + batch.desc_bytes)
+    vals = torch.tensor([t_ms, e2e_ms, k_ms, h2d], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals[:3].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals[3:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, tot])
+    t_ms, e2e_ms, k_ms, h2d_total = [float(x) for x in vals.cpu()]
+    return {"t_ms": t_ms, "e2e_ms": e2e_ms, "kernel_ms": k_ms, "local_bytes": n * args.ctx * ROW_BYTES,
+            "h2d_bytes": int(h2d_total), "d2h_bytes": int(args.seqs * QD * 4)}
+
+
+def run_config4_sharded(dev, rank, world, barrier, peaks, steps=20, warmup=3, n_layers=22):
+    """Config 4 at the job's GPU count: the 64 ragged sequences (lengths
+    U[128, 2048], seeded) LPT-partitioned over the ranks; a step is one decode
+    token for every sequence through all 22 layers (each rank: one CUDA graph
+    of its 22 tle_decode_batch launches, TLE_DECODE_KV_READY) and one NCCL
+    all-gather of every layer's outputs, reordered into sequence order on the
+    gather stream while the next step decodes into the other of two
+    buffers.  Time = max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import shard
+    import tle
+    lengths = np.random.default_rng(4).integers(128, 2049, 64)
+    plan = shard.plan([int(x) for x in lengths], world)
+    mine = plan.mine(rank)
+    n, ml = len(mine), plan.max_local
+    g = torch.Generator(device=dev).manual_seed(44 + rank)
+    caches = [(torch.randn((n_layers, int(lengths[s]), KVD), generator=g, device=dev),
+               torch.randn((n_layers, int(lengths[s]), KVD), generator=g, device=dev), int(lengths[s]))
+              for s in mine]
+    batch = tle.DecodeBatch(caches, [int(lengths[s]) - 1 for s in mine], tle.tinyllama_shape(n_layers))
+    q = torch.randn((n, QD), generator=g, device=dev)
+    k = torch.randn((n, KVD), generator=g, device=dev)
+    v = torch.randn((n, KVD), generator=g, device=dev)
+    outs = [torch.zeros((n_layers, ml, QD), device=dev) for _ in range(2)]
+    gbufs = [torch.zeros((world, n_layers, ml, QD), device=dev) for _ in range(2)]
+    # row of (layer l, sequence s) in a gathered buffer viewed as [world*22*ml][QD]
+    local_idx = {s: i for r in range(world) for i, s in enumerate(plan.local[r])}
+    index = torch.tensor([(plan.owner[s] * n_layers + l) * ml + local_idx[s]
+                          for l in range(n_layers) for s in range(len(lengths))],
+                         dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    gstream = torch.cuda.Stream(dev)
+
+    graphs = []
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    for b in range(2):
+        def layers(st, b=b):
+            for l in range(n_layers):
+                batch.run(q, k, v, outs[b][l], l, True, st, kv_ready=True)
+        with torch.cuda.stream(side):
+            layers(side)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(gr, stream=side):
+                layers(side)
+        graphs.append(gr)
+    torch.cuda.synchronize(dev)
+    dec_done = [torch.cuda.Event() for _ in range(2)]
+    gat_done = [torch.cuda.Event() for _ in range(2)]
+    free = [None, None]
+
+    def step(i):
+        b = i & 1
+        if free[b] is not None:
+            stream.wait_event(free[b])
+        graphs[b].replay()
+        dec_done[b].record(stream)
+        if world == 1:
+            free[b] = dec_done[b]
+            return
+        gstream.wait_event(dec_done[b])
+        with torch.cuda.stream(gstream):
+            dist.all_gather_into_tensor(gbufs[b], outs[b])
+            gbufs[b].view(-1, QD).index_select(0, index)
+        gat_done[b].record(gstream)
+        free[b] = gat_done[b]
+
+    for i in range(warmup):
+        step(i)
+    stream.wait_stream(gstream)
+    barrier()
+    free[0] = free[1] = None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    stream.wait_stream(gstream)
+    e1.record(stream)
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del graphs
+    kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    return {"value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "tok_s": round(64 / (ms / 1e3), 1), "n_gpus": world,
+            "frac_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
 
 
 def _time_steps(fn, steps, warmup, stream):
@@ -468,6 +622,7 @@ def measure_prefill(dev, peaks, steps=10, warmup=3):
     ms = _time_graph(step, steps, warmup, dev)
     flops = n_layers * 4.0 * HD * NH * S * (S + 1) / 2
     tflops = flops / (ms / 1e3) / 1e12
+    cpu = cpu_prefill_reference(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), flops)
     return {"workload": "config3: causal prefill S=2048, 22 layers per step (CUDA graph of the 22 "
                         "tle_prefill calls), bf16 tcgen05 MMA, fp32 softmax, rope+append prep kernel",
             "metric": "prefill attn TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s",
@@ -477,7 +632,47 @@ def measure_prefill(dev, peaks, steps=10, warmup=3):
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tflops / peaks["bf16_tflops"], 4),
                          "peak_source": peaks["source"] + ", burst"},
+            "cpu_reference": cpu,
             "gpu_launches": 2 * n_layers * steps}
+
+
+def _ref_lib():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    kind = "reference" if oracle.have_reference() else "port"
+    return (oracle.reference() if kind == "reference" else oracle.port()), kind
+
+
+def cpu_prefill_reference(q, k, v, flops_22):
+    """Config 3 on the host: the reference's own token-at-a-time prefill
+    (generate.cpp:56-59: rope + attention for pos 0..2047, oracle/_ref) of
+    whole layers, one layer per host thread (ctypes releases the GIL), as
+    many layers at once as there are cores up to 22; the 22-layer time is
+    extrapolated linearly in layers."""
+    import numpy as np
+    lib, kind = _ref_lib()
+    n_layers, S = q.shape[0], q.shape[1]
+    cores = os.cpu_count() or 1
+    run = max(1, min(n_layers, cores))
+    bufs = []
+    for l in range(run):
+        bufs.append((np.zeros((S, QD), np.float32), q[l].copy(), k[l].copy(), v[l].copy(),
+                     np.zeros((1, S, KVD), np.float32), np.zeros((1, S, KVD), np.float32)))
+
+    def one(b):
+        out, qq, kk, vv, kc, vc = b
+        lib.prefill(out, qq, kk, vv, kc, vc, 0, 0, S)
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=one, args=(b,)) for b in bufs]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    dt = (time.perf_counter() - t0) * n_layers / run
+    return {"value": round(flops_22 / dt / 1e12, 6), "unit": "TFLOP/s", "kind": kind, "cores": run,
+            "ms_per_step": round(dt * 1e3, 1),
+            "sample": "%d of 22 layers, one per thread, S=2048 token loop each; x22/%d" % (run, run)}
 
 
 def measure_config4(dev, peaks, steps=20, warmup=3):
@@ -517,6 +712,7 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
     kv_bytes = n_layers * int(lengths.sum()) * ROW_BYTES
     gbs = kv_bytes / (ms / 1e3) / 1e9
     gbs_strict = kv_bytes / (ms_strict / 1e3) / 1e9
+    cpu = cpu_config4_reference(lengths, n_layers)
     return {"workload": "config4: 64 seqs, lengths U[128,2048] (sum %d), 22 layers per step "
                         "(CUDA graph of the 22 tle_decode_batch calls, TLE_DECODE_KV_READY)"
                         % int(lengths.sum()),
@@ -528,7 +724,38 @@ def measure_config4(dev, peaks, steps=20, warmup=3):
             "n_ctas": batch.n_ctas,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+            "cpu_reference": cpu,
             "gpu_launches": n_layers * steps}
+
+
+def cpu_config4_reference(lengths, n_layers, sample_layers=2):
+    """Config 4 on the host: the reference's rope + attention (oracle/_ref)
+    for all 64 sequences, spread over every host thread (independent
+    sequences), for `sample_layers` of the 22 layers (the 3.1 GB of fp32
+    cache for all layers is not built on the host); the 22-layer time is
+    extrapolated linearly in layers."""
+    import numpy as np
+    lib, kind = _ref_lib()
+    cores = os.cpu_count() or 1
+    n = len(lengths)
+    rng = np.random.default_rng(404)
+    kcs = [rng.standard_normal((sample_layers, int(L), KVD), dtype=np.float32) for L in lengths]
+    vcs = [rng.standard_normal((sample_layers, int(L), KVD), dtype=np.float32) for L in lengths]
+    q = rng.standard_normal((n, QD), dtype=np.float32)
+    k = rng.standard_normal((n, KVD), dtype=np.float32)
+    v = rng.standard_normal((n, KVD), dtype=np.float32)
+    out = np.zeros((n, QD), np.float32)
+    lens = [int(L) for L in lengths]
+    pos = [L - 1 for L in lens]
+    t0 = time.perf_counter()
+    for l in range(sample_layers):
+        lib.decode_batch(kcs, vcs, lens, pos, q.copy(), k.copy(), v, out, l, n_threads=min(cores, n))
+    dt = (time.perf_counter() - t0) * n_layers / sample_layers
+    kv_bytes = n_layers * int(np.sum(lengths)) * ROW_BYTES
+    return {"value": round(kv_bytes / dt / 1e9, 3), "unit": "GB/s", "kind": kind, "cores": min(cores, n),
+            "ms_per_step": round(dt * 1e3, 1),
+            "sample": "64 sequences x %d of 22 layers, sequences over %d threads; x22/%d"
+                      % (sample_layers, min(cores, n), sample_layers)}
 
 
 def _paged_setup(dev, lengths, n_layers, page_rows, seed, shuffle=True):
@@ -729,8 +956,8 @@ def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, 
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                          "note": "weight bytes per token x tok/s"},
-            "cpu_reference": {"kind": kind, "cores": cores,
-                              "tok_s": round(1.0 / cpu_s, 3),
+            "cpu_reference": {"kind": kind, "cores": cores, "value": round(1.0 / cpu_s, 3),
+                              "unit": "tok/s",
                               "sample": "%d prompt tokens through the 22-layer model" % cpu_tokens},
             # per generated token: embedding, 22 x (q/k/v, decode, split-K merge,
             # output projection, gate/up, down), LM head, argmax
@@ -773,10 +1000,22 @@ def measure_prompt2(dev, peaks, steps=5, warmup=3, prompts=(128, 2048), seed=2):
                        "fp16_weight_gbs": round(wbytes / (ms / 1e3) / 1e9, 1),
                        "frac_hbm": round(wbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
     per_pass = 1 + 22 * 9 + 1
+    cores = os.cpu_count() or 1
+    cpu_s, kind = cpu_forward_reference(m, np.random.default_rng(seed).integers(0, m.n_vocab, 3), cores)
+    first, last = out[str(prompts[0])], out[str(prompts[-1])]
     return {"workload": "config2 model (TinyLlama-1.1B shapes, random Q4_0) prompt through "
                         "tle_prompt_forward, %s tokens" % "/".join(str(p) for p in prompts),
-            "metric": "prompt tok/s", "value": out[str(prompts[0])]["tok_s"], "unit": "tok/s",
+            "metric": "prompt tok/s", "value": first["tok_s"], "unit": "tok/s",
             "dtype": "f16 products, fp32 accumulation", "prompts": out,
+            "roofline": {"bound": "hbm", "achieved": first["fp16_weight_gbs"], "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": first["frac_hbm"],
+                         "note": "%d tokens: the fp16 weight copy read once per pass" % prompts[0]},
+            "roofline_long": {"bound": "tensor", "achieved": last["tflops"], "peak": peaks["bf16_tflops"],
+                              "unit": "TFLOP/s", "frac": last["frac_tensor"],
+                              "note": "%d tokens: products + causal attention flops" % prompts[-1]},
+            "cpu_reference": {"kind": kind, "cores": cores, "value": round(1.0 / cpu_s, 3), "unit": "tok/s",
+                              "sample": "the reference's prompt loop (one forward() per token, "
+                                        "generate.cpp:56-59), 3 tokens of the 22-layer model"},
             "gpu_launches": per_pass * steps * len(prompts)}
 
 
@@ -863,7 +1102,7 @@ def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
                          "achieved_cold_gbs": round(kv_bytes / (ms_cold / 1e3) / 1e9, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac_cold": round(kv_bytes / (ms_cold / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
-            "cpu_reference": {"kind": kind, "cores": 1, "us_per_token": round(ref_us, 1),
+            "cpu_reference": {"kind": kind, "cores": 1, "value": round(ref_us, 1), "unit": "us",
                               "sample": "22 layers of rope+attention at L=512, one host thread, "
                                         "median of 3 tokens"},
             "gpu_launches": 2 * n_layers * steps}

@@ -327,6 +327,66 @@ void test_norm_add_ffn_argmax() {
     check("top-p with dominant logit picks it consistently", top_count >= 18);
 }
 
+
+// The reference allocates `att` as n_ctx floats (run_state.h:64, 126).  A
+// caller that passes exactly that, followed by a NaN guard region, must get
+// the result of the C ABI call with a full split-K workspace (bit for bit)
+// and find the guard and `att` itself untouched, for single- and multi-CTA
+// splits (L = 512 and 2048 attended rows).
+void test_att_contract() {
+    std::cout << "\n=== att is the reference's n_ctx floats (device) ===\n";
+    const int n_ctx = 2048, kv_dim = 256, n_embd = 2048, guard = 1 << 20;
+    const tle::AttnConfig cfg = tinyllama(1, n_ctx);
+    const tle_shape_t shape = tle::shape_of(cfg);
+    const std::size_t cache = static_cast<std::size_t>(n_ctx) * kv_dim;
+    Dev kc(cache), vc(cache), dq(n_embd), dk(kv_dim), dv(kv_dim), out(n_embd), want(n_embd);
+    std::uint32_t x = 12345u;
+    auto rnd = [&x]() {
+        x = x * 1664525u + 1013904223u;
+        return static_cast<float>(x >> 8) / 16777216.0f - 0.5f;
+    };
+    std::vector<float> h(cache);
+    for (auto& a : h) a = rnd();
+    kc.put(h);
+    for (auto& a : h) a = rnd();
+    vc.put(h);
+    std::vector<float> q(n_embd), k(kv_dim), v(kv_dim);
+    for (auto& a : q) a = rnd();
+    for (auto& a : k) a = rnd();
+    for (auto& a : v) a = rnd();
+    dq.put(q); dk.put(k); dv.put(v);
+    std::vector<float> att_h(static_cast<std::size_t>(n_ctx) + guard, std::nanf(""));
+    for (int i = 0; i < n_ctx; ++i) att_h[i] = 0.25f;
+    Dev att(att_h.size());
+    att.put(att_h);
+    const std::size_t ws_bytes = tle_attention_workspace_bytes(&shape, n_ctx);
+    void* ws = tle::device_alloc_bytes(ws_bytes);
+    bool same = true;
+    for (int L : {512, 2048}) {
+        const int pos = L - 1;
+        for (int fused = 0; fused < 2; ++fused) {
+            if (fused) {
+                tle::rope_attention_gpu(out.p, dq.p, dk.p, dv.p, kc.p, vc.p, att.p, 0, pos, cfg);
+                tle::check(tle_rope_attention(want.p, dq.p, dk.p, dv.p, kc.p, vc.p, 0, pos, n_ctx, &shape, ws,
+                                              ws_bytes, nullptr));
+            } else {
+                tle::attention_gpu(out.p, dq.p, dk.p, dv.p, kc.p, vc.p, att.p, 0, pos, cfg);
+                tle::check(tle_attention(want.p, dq.p, dk.p, dv.p, kc.p, vc.p, 0, pos, n_ctx, &shape, ws, ws_bytes,
+                                         nullptr));
+            }
+            const std::vector<float> a = out.get(), b = want.get();
+            same = same && std::memcmp(a.data(), b.data(), a.size() * sizeof(float)) == 0;
+        }
+    }
+    tle::device_free(ws);
+    check("attention_gpu / rope_attention_gpu == C ABI with a full workspace (L = 512, 2048)", same);
+    const std::vector<float> after = att.get();
+    bool untouched = true;
+    for (std::size_t i = 0; i < after.size(); ++i)
+        untouched = untouched && std::memcmp(&after[i], &att_h[i], sizeof(float)) == 0;
+    check("att (n_ctx floats) and the NaN guard after it untouched", untouched);
+}
+
 }  // namespace
 
 int main() {
@@ -336,6 +396,7 @@ int main() {
         test_errors();
         test_matmul();
         test_norm_add_ffn_argmax();
+        test_att_contract();
         tle::device_sync();
     } catch (const std::exception& e) {
         std::cerr << "error: " << e.what() << "\n";

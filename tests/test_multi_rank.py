@@ -29,9 +29,9 @@ def free_port():
     return p
 
 
-def make_inputs(seed=21, n=7):
+def make_inputs(seed=21, n=7, equal=False):
     rng = np.random.default_rng(seed)
-    lengths = rng.integers(1, 300, n)
+    lengths = np.full(n, 150) if equal else rng.integers(1, 300, n)
     caps = [int(L) + 3 for L in lengths]
     kcs = [rng.standard_normal((1, c, KVD), dtype=np.float32) for c in caps]
     vcs = [rng.standard_normal((1, c, KVD), dtype=np.float32) for c in caps]
@@ -41,7 +41,7 @@ def make_inputs(seed=21, n=7):
     return lengths, caps, kcs, vcs, q, k, v
 
 
-def _worker(rank, world, port, result_path):
+def _worker(rank, world, port, result_path, equal=False):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     sys.path.insert(0, os.path.join(ROOT, "tinyllama-engine_b200"))
     import torch
@@ -50,17 +50,19 @@ def _worker(rank, world, port, result_path):
     import shard
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
-    lengths, caps, kcs, vcs, q, k, v = make_inputs()
+    lengths, caps, kcs, vcs, q, k, v = make_inputs(n=8 if equal else 7, equal=equal)
     p = shard.plan(lengths, world)
     mine = p.mine(rank)
-    out = np.zeros((p.max_local, QD), np.float32)
+    gather = shard.OutputGather(p, QD, "cpu")
+    # equal lengths: decode straight into this rank's slot (in-place gather)
+    out = gather.local_slot(rank).numpy() if equal else np.zeros((p.max_local, QD), np.float32)
     if mine:
         part = np.zeros((len(mine), QD), np.float32)
         oracle.port().decode_batch([kcs[s] for s in mine], [vcs[s] for s in mine],
                                    [caps[s] for s in mine], [int(lengths[s]) - 1 for s in mine],
                                    q[mine].copy(), k[mine].copy(), v[mine].copy(), part, 0)
         out[:len(mine)] = part
-    full = shard.OutputGather(p, QD, "cpu")(torch.from_numpy(out))
+    full = gather(gather.local_slot(rank) if equal else torch.from_numpy(out))
     if rank == 0:
         np.save(result_path, full.numpy())
     dist.barrier()
@@ -84,14 +86,24 @@ def _deserter(rank, world, port, result_path):
         f.write(msg)
 
 
-def test_sharded_decode_gather_matches_single_process(tmp_path):
+@pytest.mark.parametrize("equal", [False, True])
+def test_sharded_decode_gather_matches_single_process(tmp_path, equal):
+    """Ragged lengths: LPT shards, gather + reorder.  Equal lengths (the
+    config-5 shape): contiguous blocks decoded into the gather buffer's own
+    slots, gathered in place and already in sequence order."""
     import torch.multiprocessing as mp
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tinyllama-engine_b200"))
     import oracle
+    import shard
     res = str(tmp_path / "gathered.npy")
-    mp.start_processes(_worker, args=(2, free_port(), res), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(2, free_port(), res, equal), nprocs=2, start_method="spawn")
     got = np.load(res)
-    lengths, caps, kcs, vcs, q, k, v = make_inputs()
+    lengths, caps, kcs, vcs, q, k, v = make_inputs(n=8 if equal else 7, equal=equal)
+    if equal:
+        p = shard.plan(lengths, 2)
+        assert p.local == [[0, 1, 2, 3], [4, 5, 6, 7]]
+        assert shard.OutputGather(p, QD, "cpu").in_order
     want = np.zeros((len(lengths), QD), np.float32)
     oracle.port().decode_batch(kcs, vcs, caps, [int(L) - 1 for L in lengths], q.copy(), k.copy(),
                                v, want, 0)

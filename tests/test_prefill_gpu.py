@@ -51,8 +51,11 @@ def test_golden_prefill(cuda, name):
 
 
 @pytest.mark.parametrize("n_tokens,pos0,n_ctx", [(1, 0, 8), (129, 0, 140), (300, 77, 400),
-                                                 (1024, 0, 1024)])
+                                                 (1024, 0, 1024), (2048, 0, 2048)])
 def test_prefill_matches_oracle(cuda, n_tokens, pos0, n_ctx):
+    """Every output row and cache row against the oracle's token-at-a-time
+    loop (rope + attention per token, bit-exact to the reference's own
+    ops.cpp); (2048, 0, 2048) is config 3's shape (about 6 s of oracle)."""
     import tle
     rng = np.random.default_rng(n_tokens + pos0)
     n_layers, layer = 2, 1
@@ -79,8 +82,8 @@ def test_prefill_matches_oracle(cuda, n_tokens, pos0, n_ctx):
 
 def test_prefill_config3_against_torch_fp32(cuda):
     """North-star config 3 (S=2048, pos0=0) against a torch fp32 causal GQA
-    attention of the same rotated inputs (the oracle's token loop is checked
-    at S=1024 above)."""
+    attention of the same rotated inputs: an independent second check of the
+    shape the oracle test above also covers."""
     import torch
     import tle
     S, n_ctx = 2048, 2048

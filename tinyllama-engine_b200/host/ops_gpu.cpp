@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <map>
+#include <mutex>
 #include <random>
 #include <utility>
 
@@ -15,11 +17,43 @@ void cuda_check(cudaError_t e, const char* what) {
 }
 }  // namespace
 
-std::size_t attention_workspace_floats(const AttnConfig& cfg) {
-    const tle_shape_t s = shape_of(cfg);
-    return (tle_attention_workspace_bytes(&s, static_cast<int>(cfg.n_ctx)) + sizeof(float) - 1) /
-           sizeof(float);
+namespace {
+// Split-K scratch of attention_gpu / rope_attention_gpu, one per (device,
+// stream): the caller's `att` (n_ctx floats in the reference) is smaller
+// than the partials of a split over the SMs, so it is never used.
+struct SplitScratch {
+    void* p = nullptr;
+    std::size_t bytes = 0;
+};
+std::mutex& scratch_mutex() {
+    static std::mutex m;
+    return m;
 }
+std::map<std::pair<int, void*>, SplitScratch>& scratch_map() {
+    static std::map<std::pair<int, void*>, SplitScratch> m;
+    return m;
+}
+void* split_scratch(const tle_shape_t& s, int n_ctx, void* stream, std::size_t* bytes) {
+    const std::size_t need = tle_attention_workspace_bytes(&s, n_ctx);
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(scratch_mutex());
+    SplitScratch& w = scratch_map()[{dev, stream}];
+    if (w.bytes < need) {
+        if (w.p) {
+            // an earlier call may still read it
+            cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            cudaFree(w.p);
+            w = SplitScratch{};
+        }
+        cuda_check(cudaMalloc(&w.p, need), "cudaMalloc split-K scratch");
+        cuda_check(cudaMemset(w.p, 0, need), "cudaMemset split-K scratch");
+        w.bytes = need;
+    }
+    *bytes = w.bytes;
+    return w.p;
+}
+}  // namespace
 
 void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv, float freq_base,
               void* stream) {
@@ -27,20 +61,23 @@ void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_
 }
 
 void attention_gpu(float* out, const float* q, const float* k, const float* v, float* key_cache,
-                   float* value_cache, float* att, int layer, int pos, const AttnConfig& cfg,
+                   float* value_cache, float* /*att*/, int layer, int pos, const AttnConfig& cfg,
                    void* stream) {
     const tle_shape_t s = shape_of(cfg);
+    std::size_t ws_bytes = 0;
+    void* ws = split_scratch(s, static_cast<int>(cfg.n_ctx), stream, &ws_bytes);
     check(tle_attention(out, q, k, v, key_cache, value_cache, layer, pos, static_cast<int>(cfg.n_ctx),
-                        &s, att, attention_workspace_floats(cfg) * sizeof(float), stream));
+                        &s, ws, ws_bytes, stream));
 }
 
 void rope_attention_gpu(float* out, const float* q, const float* k, const float* v,
-                        float* key_cache, float* value_cache, float* att, int layer, int pos,
+                        float* key_cache, float* value_cache, float* /*att*/, int layer, int pos,
                         const AttnConfig& cfg, void* stream) {
     const tle_shape_t s = shape_of(cfg);
+    std::size_t ws_bytes = 0;
+    void* ws = split_scratch(s, static_cast<int>(cfg.n_ctx), stream, &ws_bytes);
     check(tle_rope_attention(out, q, k, v, key_cache, value_cache, layer, pos,
-                             static_cast<int>(cfg.n_ctx), &s, att,
-                             attention_workspace_floats(cfg) * sizeof(float), stream));
+                             static_cast<int>(cfg.n_ctx), &s, ws, ws_bytes, stream));
 }
 
 void matmul_gpu(float* out, const void* W, const float* x, int rows, int cols, int type, void* stream) {
@@ -156,11 +193,12 @@ void DeviceRunState::allocate(const AttnConfig& cfg) {
     q = device_alloc_floats(cfg.n_embd);
     k = device_alloc_floats(kv_dim);
     v = device_alloc_floats(kv_dim);
-    att = device_alloc_floats(attention_workspace_floats(cfg));
+    att = device_alloc_floats(cfg.n_ctx);
     key_cache = device_alloc_floats(cache);
     value_cache = device_alloc_floats(cache);
     for (auto [p, n] : {std::pair{xb2, std::size_t(cfg.n_embd)}, std::pair{q, std::size_t(cfg.n_embd)},
-                        std::pair{k, kv_dim}, std::pair{v, kv_dim}, std::pair{key_cache, cache},
+                        std::pair{k, kv_dim}, std::pair{v, kv_dim}, std::pair{att, std::size_t(cfg.n_ctx)},
+                        std::pair{key_cache, cache},
                         std::pair{value_cache, cache}})
         device_zero(p, n);
     pos = 0;

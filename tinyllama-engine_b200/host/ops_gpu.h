@@ -67,15 +67,20 @@ inline tle_shape_t shape_of(const AttnConfig& c) {
     return s;
 }
 
-// Floats of the `att` buffer attention_gpu needs (its split-K workspace).
-std::size_t attention_workspace_floats(const AttnConfig& cfg);
-
 // ops.h:175-176, in place on device q/k.
 void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv, float freq_base,
               void* stream = nullptr);
 
-// ops.h:204-206 with device pointers; `att` is the device workspace of
-// attention_workspace_floats(cfg) floats (the reference's score scratch).
+// ops.h:204-206 with device pointers.  `att` is the reference's score
+// scratch (run_state.h:64, 126: n_ctx floats); it is accepted so forward.cpp's
+// call sites stay as they are, and it is never read or written (it may be
+// null).  The split-K scratch of the call is owned by this layer instead:
+// one zero-initialised device buffer per (device, stream), made by the first
+// call on that pair (so make that call outside stream capture) and grown,
+// after synchronising the device, when a larger n_ctx needs more; it lives
+// until the process exits.  Calls on one stream are ordered and share it;
+// calls from several host threads on the same stream race, as the
+// reference's shared `att` does.
 void attention_gpu(float* out, const float* q, const float* k, const float* v, float* key_cache,
                    float* value_cache, float* att, int layer, int pos, const AttnConfig& cfg,
                    void* stream = nullptr);
@@ -136,13 +141,14 @@ void device_sync();
 
 // run_state.h:27-182 for the attention block, in HBM: q/k/v/xb2 activations,
 // the [n_layers][n_ctx][kv_dim] fp32 KV cache (zeroed, run_state.h:152-153)
-// and the attention workspace that replaces `att`.
+// and `att`, n_ctx floats as the reference allocates it (run_state.h:126;
+// attention_gpu leaves it untouched).
 struct DeviceRunState {
     float* xb2 = nullptr;  // attention output [n_embd]
     float* q = nullptr;    // [n_embd]
     float* k = nullptr;    // [kv_dim]
     float* v = nullptr;    // [kv_dim]
-    float* att = nullptr;  // workspace [attention_workspace_floats]
+    float* att = nullptr;  // [n_ctx], the reference's score scratch
     float* key_cache = nullptr;
     float* value_cache = nullptr;
     int pos = 0;

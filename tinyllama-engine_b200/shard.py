@@ -35,8 +35,16 @@ class ShardPlan:
 
 
 def plan(lengths: Sequence[int], world: int) -> ShardPlan:
+    """LPT partition of the sequences; a batch of equal lengths that divides
+    evenly is cut into contiguous equal blocks instead (the same balance, and
+    the gathered buffer is then already in sequence order)."""
     import tle
-    owner = tle.partition_lpt(lengths, world)
+    lengths = [int(x) for x in lengths]
+    n = len(lengths)
+    if n and n % world == 0 and len(set(lengths)) == 1:
+        owner = [s // (n // world) for s in range(n)]
+    else:
+        owner = tle.partition_lpt(lengths, world)
     local = [[s for s in range(len(lengths)) if owner[s] == r] for r in range(world)]
     max_local = max(1, max(len(x) for x in local))
     gather_row = [0] * len(lengths)
@@ -47,21 +55,32 @@ def plan(lengths: Sequence[int], world: int) -> ShardPlan:
 
 
 class OutputGather:
-    """All-gathers every rank's [max_local][width] output block and reorders
-    the rows into sequence order (one collective + one device gather)."""
+    """All-gathers every rank's [max_local][width] output block (one NCCL
+    collective) and returns the rows in sequence order: a view of the gather
+    buffer when the plan's blocks are contiguous and full (no copy), else a
+    device gather of the rows.  A rank that decodes straight into
+    ``local_slot(rank)`` makes the collective in place (nothing to copy in)."""
 
     def __init__(self, p: ShardPlan, width: int, device, group=None):
         import torch
         self.p = p
         self.group = group
+        self.n = len(p.gather_row)
         self.buf = torch.zeros((p.world * p.max_local, width), device=device)
+        self.in_order = p.gather_row == list(range(self.n))
         self.index = torch.tensor(p.gather_row, dtype=torch.long, device=device)
+
+    def local_slot(self, rank: int):
+        """This rank's block of the gather buffer: decode into it to gather in place."""
+        return self.buf[rank * self.p.max_local:(rank + 1) * self.p.max_local]
 
     def __call__(self, local_out):
         import torch.distributed as dist
         if self.p.world == 1:
             return local_out  # one rank holds every sequence, already in order
         dist.all_gather_into_tensor(self.buf, local_out, group=self.group)
+        if self.in_order:
+            return self.buf[:self.n]
         return self.buf.index_select(0, self.index)
 
 
