@@ -10,10 +10,9 @@ rope + append + GQA decode-attention call for every sequence
 
 Multi-GPU (torchrun, one process per GPU): the 256 equal sequences are cut
 into contiguous equal blocks (shard.plan), every rank decodes its block from
-its own HBM straight into its slot of the all-gather buffer, and the NCCL
-all-gather of step i (already in sequence order) runs on its own stream while
-step i+1 decodes into a second buffer; the step time is the max over ranks
-(strong scaling: the 256-sequence total is fixed).  The same line carries
+its own HBM straight into its slot of the all-gather buffer, and the in-place
+NCCL all-gather leaves them in sequence order on every rank; the step time is
+the max over ranks (strong scaling: the 256-sequence total is fixed).  The same line carries
 config 4 at the job's GPU count (`decode_config4`: 64 ragged sequences
 LPT-partitioned, 22 layers per step, one all-gather of every layer's
 outputs per step).
@@ -320,10 +319,14 @@ def compact(d):
 def run_config5(args, dev, rank, world, barrier):
     """Headline (config 5): every rank decodes its shard of the sequences
     (one tle_decode_batch launch per step) straight into its block of the
-    all-gather buffer; the NCCL all-gather of step i runs on its own stream
-    while step i+1 decodes into the other of two buffers.  Returns the
-    max-over-ranks times of the device-timed loop and of the end-to-end loop
-    (pinned host inputs in, the gathered output back to rank 0's host)."""
+    all-gather buffer, then the in-place NCCL all-gather leaves every
+    sequence's output in order on every rank.  The gather follows the decode
+    on the same stream: run beside the next step's decode it took SMs from
+    that grid (one CTA per SM, rows split in advance) and made the step
+    slower, not faster.  Two output buffers alternate, so the end-to-end
+    loop can read step i back while step i+1 runs.  Returns the max-over-
+    ranks times of the device-timed loop and of the end-to-end loop (pinned
+    host inputs in, the gathered output back to rank 0's host)."""
     import torch
     import torch.distributed as dist
     import shard
@@ -345,49 +348,34 @@ def run_config5(args, dev, rank, world, barrier):
     outs = [g.local_slot(rank) if world > 1 else torch.zeros((max_local, QD), device=dev)
             for g in gathers]
     stream = torch.cuda.current_stream(dev)
-    gstream = torch.cuda.Stream(dev)
-    dec_done = [torch.cuda.Event() for _ in range(2)]
-    gat_done = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
 
     def finish(b):
-        """Issues the gather of buffer b after its decode; returns the
-        event after which buffer b (and the gathered rows) may be reused."""
-        if world == 1:
-            dec_done[b].record(stream)
-            return outs[b], dec_done[b]
-        dec_done[b].record(stream)
-        gstream.wait_event(dec_done[b])
-        with torch.cuda.stream(gstream):
-            res = gathers[b](outs[b])
-        gat_done[b].record(gstream)
-        return res, gat_done[b]
-
-    free = [None, None]
+        """Gathers buffer b after its decode (same stream); returns the rows
+        in sequence order and the event after which they are complete."""
+        res = gathers[b](outs[b]) if world > 1 else outs[b]
+        done[b].record(stream)
+        return res, done[b]
 
     def step(i, kev=None):
         b = i & 1
-        if free[b] is not None:
-            stream.wait_event(free[b])
         if kev is not None:
             kev[0].record(stream)
         batch.run(q, k, v, outs[b], 0, rotate=True, stream=stream)
         if kev is not None:
             kev[1].record(stream)
-        _, free[b] = finish(b)
+        finish(b)
 
     for i in range(max(3, args.warmup)):
         step(i)
-    stream.wait_stream(gstream)
     barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
-    free[0] = free[1] = None
     barrier()
     ev[0].record(stream)
     for i in range(args.steps):
         step(i, kev[i])
-    stream.wait_stream(gstream)
     ev[1].record(stream)
     barrier()
     t_ms = ev[0].elapsed_time(ev[1])
@@ -440,7 +428,6 @@ def run_config5(args, dev, rank, world, barrier):
         else:
             out_free[b] = ready
     stream.wait_stream(cstream)
-    stream.wait_stream(gstream)
     stream.wait_stream(dstream)
     e2[1].record(stream)
     barrier()
@@ -463,9 +450,8 @@ def run_config4_sharded(dev, rank, world, barrier, peaks, steps=20, warmup=3, n_
     U[128, 2048], seeded) LPT-partitioned over the ranks; a step is one decode
     token for every sequence through all 22 layers (each rank: one CUDA graph
     of its 22 tle_decode_batch launches, TLE_DECODE_KV_READY) and one NCCL
-    all-gather of every layer's outputs, reordered into sequence order on the
-    gather stream while the next step decodes into the other of two
-    buffers.  Time = max over ranks."""
+    all-gather of every layer's outputs, reordered into sequence order.
+    Time = max over ranks."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -491,8 +477,6 @@ def run_config4_sharded(dev, rank, world, barrier, peaks, steps=20, warmup=3, n_
                           for l in range(n_layers) for s in range(len(lengths))],
                          dtype=torch.long, device=dev)
     stream = torch.cuda.current_stream(dev)
-    gstream = torch.cuda.Stream(dev)
-
     graphs = []
     side = torch.cuda.Stream(dev)
     side.wait_stream(stream)
@@ -509,37 +493,22 @@ def run_config4_sharded(dev, rank, world, barrier, peaks, steps=20, warmup=3, n_
                 layers(side)
         graphs.append(gr)
     torch.cuda.synchronize(dev)
-    dec_done = [torch.cuda.Event() for _ in range(2)]
-    gat_done = [torch.cuda.Event() for _ in range(2)]
-    free = [None, None]
 
     def step(i):
         b = i & 1
-        if free[b] is not None:
-            stream.wait_event(free[b])
         graphs[b].replay()
-        dec_done[b].record(stream)
-        if world == 1:
-            free[b] = dec_done[b]
-            return
-        gstream.wait_event(dec_done[b])
-        with torch.cuda.stream(gstream):
+        if world > 1:
             dist.all_gather_into_tensor(gbufs[b], outs[b])
             gbufs[b].view(-1, QD).index_select(0, index)
-        gat_done[b].record(gstream)
-        free[b] = gat_done[b]
 
     for i in range(warmup):
         step(i)
-    stream.wait_stream(gstream)
     barrier()
-    free[0] = free[1] = None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
     for i in range(steps):
         step(i)
-    stream.wait_stream(gstream)
     e1.record(stream)
     barrier()
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
