@@ -213,6 +213,62 @@ def test_single_long_context_matches_oracle(cuda):
     assert maxabs(host(out), want) <= ATOL
 
 
+_SHARED_WS = {}
+
+
+@pytest.mark.parametrize("L", [1, 2, 31, 32, 33, 64, 65, 255, 256, 257, 512, 513, 1000, 2047,
+                               2048, 2049])
+def test_single_sequence_lengths_match_oracle(cuda, L):
+    """rope + attention of one sequence at lengths across the chunk
+    boundaries: up to 2048 rows one launch splits the rows into chunks of 32
+    or 64 per KV head and its last CTA merges them; 2049 takes the SM split.
+    Every case reuses one workspace, so the arrival counters must be back at
+    zero after each call, and the appended row must be the rotated k / v."""
+    import tle
+    rng = np.random.default_rng(1000 + L)
+    n_layers, layer, n_ctx = 2, 1, L + 5
+    kc_h = rng.standard_normal((n_layers, n_ctx, KVD), dtype=np.float32)
+    vc_h = rng.standard_normal((n_layers, n_ctx, KVD), dtype=np.float32)
+    q = rng.standard_normal(QD, dtype=np.float32)
+    k = rng.standard_normal(KVD, dtype=np.float32)
+    v = rng.standard_normal(KVD, dtype=np.float32)
+    shape = tle.tinyllama_shape(n_layers)
+    if "ws" not in _SHARED_WS:
+        _SHARED_WS["ws"] = tle.attention_workspace(shape, 4096)
+    kc, vc = dev(kc_h), dev(vc_h)
+    out, lse = dev(np.full(QD, np.nan, np.float32)), dev(np.zeros(32))
+    pos = L - 1
+    for _ in range(2):   # twice on the same workspace: identical outputs
+        tle.rope_attention(out, dev(q), dev(k), dev(v), kc, vc, layer, pos, n_ctx, shape, _SHARED_WS["ws"])
+        first = host(out).copy()
+    tle.rope_attention(out, dev(q), dev(k), dev(v), kc, vc, layer, pos, n_ctx, shape, _SHARED_WS["ws"])
+    assert np.array_equal(host(out), first)
+    want = np.zeros(QD, np.float32)
+    P = oracle.port()
+    q2, k2 = q.copy(), k.copy()
+    P.rope(q2, k2, pos)
+    P.attention(want, q2, k2, v, kc_h, vc_h, layer, pos, n_ctx)   # appends row pos of kc_h / vc_h
+    assert maxabs(first, want) <= ATOL
+    got_kc, got_vc = host(kc), host(vc)
+    assert maxabs(got_kc[layer, pos], kc_h[layer, pos]) <= ROT_ATOL
+    assert np.array_equal(got_vc[layer, pos], v)
+    mask = np.ones((n_layers, n_ctx), bool)
+    mask[layer, pos] = False
+    assert np.array_equal(got_kc[mask], kc_h[mask]) and np.array_equal(got_vc[mask], vc_h[mask])
+    # the log-sum-exp variant (context split) on the same rows: same output
+    # and lse = log sum_p exp(q.K_p / 8) per head
+    out2 = dev(np.full(QD, np.nan, np.float32))
+    tle.attention_lse(out2, lse, dev(q2), dev(k2), dev(v), kc, vc, layer, pos, n_ctx, shape, _SHARED_WS["ws"])
+    assert maxabs(host(out2), want) <= ATOL
+    K = kc_h[layer, :L].reshape(L, 4, 64)
+    sc = np.einsum("hd,phd->hp", q2.reshape(32, 64).astype(np.float64) / 8.0,
+                   np.repeat(K.astype(np.float64), 8, axis=1))
+    mx = sc.max(1)
+    want_lse = mx + np.log(np.exp(sc - mx[:, None]).sum(1))
+    assert maxabs(host(lse), want_lse) <= 1e-4
+    assert tle.device_error() == 0
+
+
 def test_config4_shapes_all_sequences(cuda):
     """North-star config 4: 64 sequences, lengths U[128, 2048], 22-layer caches;
     layer 13 checked for every sequence."""

@@ -142,6 +142,40 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
         return set_error(TLE_ERR_INVALID, "need 0 <= pos < n_ctx (pos=%d, n_ctx=%d)", pos, n_ctx);
     if (layer < 0 || layer >= shape->n_layers)
         return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
+    const int L = pos + 1;
+    if (L <= tle::kSeqMaxRows) {
+        // short sequence: one launch, chunks of 32 or 64 rows per KV head
+        tle::SeqArgs s{};
+        s.chunk_rows = L <= 256 ? 32 : tle::kSeqMaxChunkRows;
+        s.n_chunks = (L + s.chunk_rows - 1) / s.chunk_rows;
+        if (s.n_chunks > 1) {
+            const size_t need = tle::seq_counter_offset() + tle::kSeqCounterBytes;
+            if (!workspace) return set_error(TLE_ERR_WORKSPACE, "workspace is NULL");
+            if (workspace_bytes < need)
+                return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, need);
+            if (!aligned16(workspace)) return set_error(TLE_ERR_INVALID, "workspace must be 16-byte aligned");
+            s.partials = static_cast<float*>(workspace);
+            s.counters = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) +
+                                                     tle::seq_counter_offset());
+        }
+        s.q = q;
+        s.k = k;
+        s.v = v;
+        s.out = out;
+        s.lse = lse;
+        s.key_cache = key_cache;
+        s.value_cache = value_cache;
+        s.layer = layer;
+        s.pos = pos;
+        s.n_ctx = n_ctx;
+        s.rotate = rotate;
+        fill_inv_freq(s.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+        cudaError_t e = tle::error_word(&s.err);
+        if (e != cudaSuccess) return cuda_error(e, "device error word");
+        e = tle::launch_seq_decode(s, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_error(e, "decode launch");
+        return ok();
+    }
     tle::DecodeArgs a{};
     a.seqs = nullptr;
     a.cta_start = nullptr;
@@ -207,7 +241,7 @@ int tle_rope(float* q, float* k, int pos, int head_dim, int n_head, int n_head_k
 size_t tle_attention_workspace_bytes(const tle_shape_t* shape, int n_ctx) {
     (void)shape;
     (void)n_ctx;
-    return partial_bytes(tle::kMaxCtas + 1);
+    return tle::seq_counter_offset() + tle::kSeqCounterBytes;
 }
 
 int tle_attention(float* out, const float* q, const float* k, const float* v, float* key_cache,
@@ -769,7 +803,7 @@ int tle_sample_top_p(float* logits, int n_vocab, float temperature, float top_p,
 
 size_t tle_forward_workspace_bytes(const tle_model_t* model) {
     if (!model || model->n_ctx <= 0) return 0;
-    return partial_bytes(tle::kMaxCtas + 1);
+    return tle::seq_counter_offset() + tle::kSeqCounterBytes;
 }
 
 int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token, int pos, void* stream) {

@@ -45,6 +45,7 @@ __device__ uint32_t g_tle_error = 0;
 
 constexpr int HD = kHeadDim;
 constexpr int NH = kNHead;
+constexpr int NKV_HEADS = kNHeadKv;
 constexpr int ROWF = kRowFloats;   // 256 floats per cache row
 constexpr int ROWB = ROWF * 4;     // 1024 bytes
 constexpr int TILE = 32;           // rows per pipeline stage
@@ -968,6 +969,189 @@ __global__ void __launch_bounds__(256) merge_lse_kernel(float* out, const float*
     dst[1] = make_float4(o[4] / wsum, o[5] / wsum, o[6] / wsum, o[7] / wsum);
 }
 
+// ---- short single-sequence decode ------------------------------------------
+// attention() for one sequence with L = pos + 1 <= kSeqMaxRows rows, built for
+// latency: CTA (c, g) takes rows [c R, (c+1) R) of KV head g (R = 32 or 64)
+// into shared memory with 16-byte cp.async copies, warp w computes query head
+// 8 g + w over them (lane = row for the scores, lane = a pair of dimensions
+// for P V), and the chunk's (o, m, l) of each head goes to the workspace.  The
+// CTA whose arrival completes KV head g's count merges the chunks of its
+// eight heads in chunk order (deterministic) and resets the count, so no
+// second launch is needed and the workspace is left as it was found.  The
+// last chunk's CTAs rotate the new k (and q, every CTA for its own heads) and
+// append their KV head's slice of k and v at row pos (ops.cpp:1350-1371).
+constexpr int SEQ_THREADS = 256;
+constexpr int SEQ_KP = HD + 4;   // padded row (floats): lane-per-row float4 reads hit all banks
+
+__global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_constant__ SeqArgs A) {
+    __shared__ __align__(16) float ks[kSeqMaxChunkRows][SEQ_KP];
+    __shared__ __align__(16) float vs[kSeqMaxChunkRows][SEQ_KP];
+    __shared__ __align__(16) float qs[8][HD];
+    __shared__ int last_flag;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, g = blockIdx.y;
+    const int L = A.pos + 1;
+    const int r0 = c * A.chunk_rows;
+    const int nrows = min(A.chunk_rows, L - r0);
+    const bool has_new = (r0 + nrows == L);
+    const size_t layer_base = static_cast<size_t>(A.layer) * A.n_ctx * ROWF;
+    // q, k, v, the cache and the counters may be the previous kernel's output
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // cached rows of this chunk (row pos comes from the new k and v)
+    const int ncached = has_new ? nrows - 1 : nrows;
+    for (int e = tid; e < ncached * 32; e += SEQ_THREADS) {
+        const int r = e >> 5, part = e & 31;           // 16 chunks of K then 16 of V
+        const float* src = (part < 16 ? A.key_cache : A.value_cache) + layer_base +
+                           static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (part & 15);
+        float* dst = (part < 16 ? &ks[r][0] : &vs[r][0]) + 4 * (part & 15);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // q of this CTA's heads (rotated, x 1/8) and, in the last chunk, the new row
+    {
+        const int p = lane;   // rotation pair
+        float sn = 0.f, cs = 1.f;
+        if (A.rotate) sincosf(static_cast<float>(A.pos) * A.inv_freq[p], &sn, &cs);
+        const float2 x = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(8 * g + warp) * HD)[p];
+        float y0 = x.x, y1 = x.y;
+        if (A.rotate) {
+            y0 = x.x * cs - x.y * sn;
+            y1 = x.x * sn + x.y * cs;
+        }
+        *reinterpret_cast<float2*>(&qs[warp][2 * p]) = make_float2(y0 * kScale, y1 * kScale);
+        if (has_new && warp < 2) {
+            const size_t row = layer_base + static_cast<size_t>(A.pos) * ROWF + g * HD;
+            if (warp == 0) {   // k: rotate, keep, append (ops.cpp:1370)
+                const float2 kx = reinterpret_cast<const float2*>(A.k + g * HD)[p];
+                float k0 = kx.x, k1 = kx.y;
+                if (A.rotate) {
+                    k0 = kx.x * cs - kx.y * sn;
+                    k1 = kx.x * sn + kx.y * cs;
+                }
+                *reinterpret_cast<float2*>(&ks[nrows - 1][2 * p]) = make_float2(k0, k1);
+                reinterpret_cast<float2*>(A.key_cache + row)[p] = make_float2(k0, k1);
+            } else {           // v: keep, append (ops.cpp:1371)
+                const float2 vx = reinterpret_cast<const float2*>(A.v + g * HD)[p];
+                *reinterpret_cast<float2*>(&vs[nrows - 1][2 * p]) = vx;
+                reinterpret_cast<float2*>(A.value_cache + row)[p] = vx;
+            }
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+
+    // scores: lane owns rows lane and lane + 32 of the chunk
+    float4 q4[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q4[i] = *reinterpret_cast<const float4*>(&qs[warp][4 * i]);
+    float s[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int r = lane + 32 * u;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        if (r < nrows) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float4 kk = *reinterpret_cast<const float4*>(&ks[r][4 * i]);
+                a0 = fmaf(q4[i].x, kk.x, a0);
+                a1 = fmaf(q4[i].y, kk.y, a1);
+                a2 = fmaf(q4[i].z, kk.z, a2);
+                a3 = fmaf(q4[i].w, kk.w, a3);
+            }
+        }
+        s[u] = (r < nrows) ? (a0 + a1) + (a2 + a3) : -INFINITY;
+    }
+    float m = fmaxf(s[0], s[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float p[2], l = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        p[u] = (s[u] == -INFINITY) ? 0.f : expf(s[u] - m);
+        l += p[u];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    // P V: lane owns dimensions 2 lane, 2 lane + 1
+    float o0 = 0.f, o1 = 0.f;
+    const int n0 = min(nrows, 32);
+    for (int r = 0; r < n0; ++r) {
+        const float pr = __shfl_sync(0xffffffffu, p[0], r);
+        const float2 vv = *reinterpret_cast<const float2*>(&vs[r][2 * lane]);
+        o0 = fmaf(pr, vv.x, o0);
+        o1 = fmaf(pr, vv.y, o1);
+    }
+    for (int r = 32; r < nrows; ++r) {
+        const float pr = __shfl_sync(0xffffffffu, p[1], r - 32);
+        const float2 vv = *reinterpret_cast<const float2*>(&vs[r][2 * lane]);
+        o0 = fmaf(pr, vv.x, o0);
+        o1 = fmaf(pr, vv.y, o1);
+    }
+    const int h = 8 * g + warp;
+    if (A.n_chunks == 1) {
+        const float inv = 1.0f / l;
+        reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(o0 * inv, o1 * inv);
+        if (A.lse && lane == 0) A.lse[h] = m + logf(l);
+        return;
+    }
+    // partial of (chunk c, head h): o[64], m, l
+    float* P = A.partials + (static_cast<size_t>(c) * NH + h) * kSeqPartialFloats;
+    reinterpret_cast<float2*>(P)[lane] = make_float2(o0, o1);
+    if (lane == 0) {
+        P[HD] = m;
+        P[HD + 1] = l;
+    }
+    // the last CTA of KV head g to arrive merges (release: every thread's
+    // partial stores are fenced before the CTA's single arrival)
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t ticket = atomicAdd(&A.counters[g], 1u);
+        const int last = (ticket == static_cast<uint32_t>(A.n_chunks - 1));
+        if (last) {
+            A.counters[g] = 0u;   // left zero for the next call
+            __threadfence();
+        }
+        last_flag = last;
+    }
+    __syncthreads();
+    if (!last_flag) return;
+    // merge: warp w folds head h over the chunks in chunk order
+    float mt = -INFINITY;
+    for (int cc = lane; cc < A.n_chunks; cc += 32)
+        mt = fmaxf(mt, ld_cg(A.partials + (static_cast<size_t>(cc) * NH + h) * kSeqPartialFloats + HD));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+    // chunks in groups of 8, every load of a group issued before any is used
+    float acc0 = 0.f, acc1 = 0.f, lt = 0.f;
+    for (int c0 = 0; c0 < A.n_chunks; c0 += 8) {
+        float mc[8], lc[8], ox[8], oy[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            mc[u] = -INFINITY;
+            lc[u] = ox[u] = oy[u] = 0.f;
+            if (c0 + u < A.n_chunks) {
+                const float* Pc = A.partials + (static_cast<size_t>(c0 + u) * NH + h) * kSeqPartialFloats;
+                mc[u] = ld_cg(Pc + HD);
+                lc[u] = ld_cg(Pc + HD + 1);
+                ox[u] = ld_cg(Pc + 2 * lane);
+                oy[u] = ld_cg(Pc + 2 * lane + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const float f = (mc[u] == -INFINITY) ? 0.f : expf(mc[u] - mt);
+            lt = fmaf(lc[u], f, lt);
+            acc0 = fmaf(ox[u], f, acc0);
+            acc1 = fmaf(oy[u], f, acc1);
+        }
+    }
+    const float inv = 1.0f / lt;
+    reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
+    if (A.lse && lane == 0) A.lse[h] = mt + logf(lt);
+}
+
 // rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
 __global__ void rope_kernel(const __grid_constant__ RopeArgs A) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1042,6 +1226,21 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         e = cudaLaunchKernelEx(&cfg, merge_kernel, a);
     }
     return e;
+}
+
+cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream) {
+    // programmatic dependent of the previous kernel: its CTAs may be
+    // scheduled while that grid drains; griddepcontrol.wait orders the reads
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.n_chunks, NKV_HEADS);
+    cfg.blockDim = dim3(SEQ_THREADS);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, seq_decode_kernel, a);
 }
 
 cudaError_t launch_rope(const RopeArgs& a, cudaStream_t stream) {
