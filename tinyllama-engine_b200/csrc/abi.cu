@@ -1023,6 +1023,15 @@ size_t tle_prompt_scratch_bytes(const tle_model_t* model, int n_tokens, int pos0
     return prompt_scratch(model, n_tokens, pos0).total;
 }
 
+namespace {
+// K splits of one prompt product: enough CTAs for the SMs when the output
+// tiles are few (short prompts).
+int gemm_splits(const tle::GemmLaunch& g) {
+    const int s_pad = (g.n_tokens + tle::kGemmTileTokens - 1) / tle::kGemmTileTokens;
+    return tle::gemm_split_for((g.tile_rows / tle::kGemmTileRows) * s_pad, g.K / tle::kGemmTileK, sm_count());
+}
+}  // namespace
+
 int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state_t* s, const int32_t* tokens,
                        int n_tokens, int pos0, void* scratch, size_t scratch_bytes, void* stream) {
     if (int rc = check_prompt_model(m)) return rc;
@@ -1078,6 +1087,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         g.seg[2] = {e + kv, kv, V};
         g.n_seg = 3;
         g.err = err;
+        g.n_split = gemm_splits(g);
         ce = tle::launch_gemm_f16(tle::kEpiStore, g, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attn_qkv");
         // rope + attention of every token (forward.cpp:198-208), appending rows pos0..
@@ -1111,6 +1121,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         g.seg[0] = {0, e, X};
         g.n_seg = 1;
         g.err = err;
+        g.n_split = gemm_splits(g);
         ce = tle::launch_gemm_f16(tle::kEpiAdd, g, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attn_output");
         // rmsnorm + gate/up + SwiGLU (forward.cpp:216-227)
@@ -1125,6 +1136,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         g.tile_rows = ff;
         g.h_out = H16;
         g.err = err;
+        g.n_split = gemm_splits(g);
         ce = tle::launch_gemm_f16(tle::kEpiSwiGLU, g, st);
         if (ce != cudaSuccess) return cuda_error(ce, "ffn_gate/up");
         // down projection + residual (forward.cpp:227-229)
@@ -1138,6 +1150,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         g.seg[0] = {0, e, X};
         g.n_seg = 1;
         g.err = err;
+        g.n_split = gemm_splits(g);
         ce = tle::launch_gemm_f16(tle::kEpiAdd, g, st);
         if (ce != cudaSuccess) return cuda_error(ce, "ffn_down");
     }

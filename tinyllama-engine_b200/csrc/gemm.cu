@@ -28,10 +28,15 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <math.h>
+#include <stddef.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tle {
 
@@ -108,7 +113,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
     const int lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * GM;
     const int t0 = blockIdx.y * GN;
-    const int nk = A.K / GK;
+    // split z of n_split: K blocks [kb0, kb1)
+    const int n_split = static_cast<int>(gridDim.z), z = static_cast<int>(blockIdx.z);
+    const int nk_all = A.K / GK;
+    const int kb0 = z * nk_all / n_split;
+    const int nk = (z + 1) * nk_all / n_split - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -138,10 +147,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             failed = __any_sync(0xffffffffu, failed);   // the warp stops as one
             if (failed) break;
             if (lane == 0) {
+                const int kx = (kb0 + kb) * GK;
                 mbar_arrive_expect_tx(&S.full[s], (NACC + 1) * kTileBytes);
-                tma_load_2d(S.a[s][0], &A.tm_w, kb * GK, m0, &S.full[s]);
-                if (NACC == 2) tma_load_2d(S.a[s][NACC - 1], &A.tm_w, kb * GK, A.up_row0 + m0, &S.full[s]);
-                tma_load_2d(S.b[s], &A.tm_x, kb * GK, t0, &S.full[s]);
+                tma_load_2d(S.a[s][0], &A.tm_w, kx, m0, &S.full[s]);
+                if (NACC == 2) tma_load_2d(S.a[s][NACC - 1], &A.tm_w, kx, A.up_row0 + m0, &S.full[s]);
+                tma_load_2d(S.b[s], &A.tm_x, kx, t0, &S.full[s]);
             }
             __syncwarp();
         }
@@ -173,7 +183,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
     // ------------------------------ epilogue (all warps) ------------------------------
     wait_or_flag(&S.acc_full, 0, A.err, kErrWaitMma, failed);
     tc_fence_after();
-    const int r = m0 + 32 * warp + lane;   // this thread's weight row
+    const int row_in_tile = 32 * warp + lane;
+    const int r = m0 + row_in_tile;   // this thread's weight row
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
     float* seg_out = nullptr;
     int seg_ld = 0;
@@ -185,28 +196,97 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
         seg_ld = A.seg_rows[si];
         seg_out = A.seg_out[si] + (r - A.seg_row0[si]);
     }
-#pragma unroll 1
-    for (int c = 0; c < GN / 32; ++c) {
-        float v[32];
-        float u[32];
-        tmem_ld32(trow + 32 * c, v);
-        if (NACC == 2) tmem_ld32(trow + GN + 32 * c, u);
-        tmem_wait_ld();
+    // The epilogue of tokens [tb, te) of this thread's row from v (and u):
+    // store, residual add (all loads of the chunk before its stores, so
+    // they overlap), or SwiGLU (ops.cpp:1107-1113 then 1129-1146).
+    auto finish = [&](int tb, int n, const float (&v)[32], const float (&u)[32]) {
+        if (EPI == kEpiStore) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int t = t0 + 32 * c + j;
-            if (t >= A.n_tokens) break;
-            if (EPI == kEpiStore) {
-                seg_out[static_cast<size_t>(t) * seg_ld] = v[j];
-            } else if (EPI == kEpiAdd) {
-                float* p = seg_out + static_cast<size_t>(t) * seg_ld;
-                *p = *p + v[j];
-            } else {
-                // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
-                const float g = v[j];
-                A.h_out[static_cast<size_t>(t) * A.up_row0 + r] = f2h((g * (1.0f / (1.0f + expf(-g)))) * u[j]);
+            for (int j = 0; j < 32; ++j)
+                if (j < n && tb + j < A.n_tokens) seg_out[static_cast<size_t>(tb + j) * seg_ld] = v[j];
+        } else if (EPI == kEpiAdd) {
+            float x[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                x[j] = (j < n && tb + j < A.n_tokens) ? seg_out[static_cast<size_t>(tb + j) * seg_ld] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < n && tb + j < A.n_tokens) seg_out[static_cast<size_t>(tb + j) * seg_ld] = x[j] + v[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                if (j < n && tb + j < A.n_tokens) {
+                    const float g = v[j];
+                    A.h_out[static_cast<size_t>(tb + j) * A.up_row0 + r] =
+                        f2h((g * (1.0f / (1.0f + expf(-g)))) * u[j]);
+                }
             }
         }
+    };
+    if (n_split == 1) {
+#pragma unroll 1
+        for (int c = 0; c < GN / 32; ++c) {
+            float v[32];
+            float u[32];
+            tmem_ld32(trow + 32 * c, v);
+            if (NACC == 2) tmem_ld32(trow + GN + 32 * c, u);
+            tmem_wait_ld();
+            finish(t0 + 32 * c, 32, v, u);
+        }
+    } else {
+        // Split K over the CTAs of a cluster (one per split): each stages its
+        // fp32 accumulators in its own shared memory (row-major, rows padded
+        // to RP floats so a warp's 16-byte stores and loads hit distinct bank
+        // groups), and after a cluster barrier split z adds up tokens
+        // [z GN/n, (z+1) GN/n) of every split, in split order
+        // (deterministic), through distributed shared memory (all loads of a
+        // slice issued before the sums) and runs their epilogue.  A second
+        // barrier keeps every CTA's shared memory alive until its peers have
+        // read it.
+        constexpr int RP = GN + 4;
+        float* red = reinterpret_cast<float*>(&S.a[0][0][0]);   // the stages (a, then b) are idle now
+        static_assert(offsetof(typename C::Smem, b) == sizeof(S.a) &&
+                          sizeof(S.a) + sizeof(S.b) >= sizeof(float) * NACC * GM * RP,
+                      "staging fits the stage ring");
+#pragma unroll 1
+        for (int acc = 0; acc < NACC; ++acc) {
+#pragma unroll 1
+            for (int c = 0; c < GN / 32; ++c) {
+                float v[32];
+                tmem_ld32(trow + acc * GN + 32 * c, v);
+                tmem_wait_ld();
+                float4* dst = reinterpret_cast<float4*>(red + (acc * GM + row_in_tile) * RP + 32 * c);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+        }
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        const int per = GN / n_split;   // 16, 32 or 64 tokens
+        for (int tb = z * per; tb < (z + 1) * per; tb += 16) {
+            float v[32];
+            float u[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = u[j] = 0.f;
+            for (int zz = 0; zz < n_split; ++zz) {
+                const float* peer = cl.map_shared_rank(red, zz);
+                float4 a4[4], b4[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    a4[q] = *reinterpret_cast<const float4*>(peer + row_in_tile * RP + tb + 4 * q);
+                    if (NACC == 2) b4[q] = *reinterpret_cast<const float4*>(peer + (GM + row_in_tile) * RP + tb + 4 * q);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v[4 * q] += a4[q].x; v[4 * q + 1] += a4[q].y; v[4 * q + 2] += a4[q].z; v[4 * q + 3] += a4[q].w;
+                    if (NACC == 2) {
+                        u[4 * q] += b4[q].x; u[4 * q + 1] += b4[q].y; u[4 * q + 2] += b4[q].z; u[4 * q + 3] += b4[q].w;
+                    }
+                }
+            }
+            finish(t0 + tb, 16, v, u);
+        }
+        cl.sync();
     }
     tc_fence_before();
     __syncthreads();
@@ -328,12 +408,27 @@ cudaError_t launch_gemm_e(const GemmArgs& a, dim3 grid, cudaStream_t stream) {
     using C = GemmCfg<EPI>;
     static PerDeviceOnce once;
     cudaError_t e = once.run([&](int) {
-        return cudaFuncSetAttribute(gemm_f16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::kSmemBytes);
+        cudaError_t r = cudaFuncSetAttribute(gemm_f16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::kSmemBytes);
+        if (r != cudaSuccess) return r;
+        return cudaFuncSetAttribute(gemm_f16_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     });
     if (e != cudaSuccess) return e;
-    gemm_f16_kernel<EPI><<<grid, kGemmThreads, C::kSmemBytes, stream>>>(a);
-    return cudaGetLastError();
+    // the K splits of a tile form one cluster (z): they are co-scheduled and
+    // reduce through distributed shared memory
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(C::kSmemBytes);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = grid.z;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<EPI>, a);
 }
 
 inline int grid_for(size_t n) {
@@ -361,6 +456,8 @@ cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream) {
     a.up_row0 = g.tile_rows;
     a.h_out = g.h_out;
     a.err = g.err;
+    const int n_split = g.n_split > 1 ? g.n_split : 1;
+    if (n_split > 8 || (n_split & (n_split - 1)) || n_split > g.K / GK) return cudaErrorInvalidValue;
     if (epi != kEpiSwiGLU) {
         // segments: in row order, tile-aligned, covering [0, w_rows)
         if (g.n_seg < 1 || g.n_seg > 3) return cudaErrorInvalidValue;
@@ -376,7 +473,7 @@ cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream) {
         if (next != g.w_rows) return cudaErrorInvalidValue;
         a.n_seg = g.n_seg;
     }
-    const dim3 grid(g.tile_rows / GM, s_pad / GN);
+    const dim3 grid(g.tile_rows / GM, s_pad / GN, n_split);
     switch (epi) {
         case kEpiStore: return launch_gemm_e<kEpiStore>(a, grid, stream);
         case kEpiAdd: return launch_gemm_e<kEpiAdd>(a, grid, stream);

@@ -236,7 +236,20 @@ struct GemmLaunch {
     int n_seg;
     uint16_t* h_out;     // SwiGLU: fp16 [round_up(n_tokens, 128)][tile_rows]
     uint32_t* err;
+    // Split of K over the CTAs of a cluster when the output tiles alone leave
+    // SMs idle (few tokens): 1, 2, 4 or 8 splits.
+    int n_split;
 };
+// Number of K splits (clusters of 1, 2 or 4 CTAs) for a product of `tiles`
+// output tiles and `nk` 64-wide K blocks on `sms` SMs: the most that keeps
+// every cluster resident in one wave (at most 7/8 of the SMs busy, as whole
+// clusters must fit in a GPC) with at least 4 K blocks per split.  (Clusters
+// of 8 of these 197 KB CTAs measured slower than 4.)
+inline int gemm_split_for(int tiles, int nk, int sms) {
+    int s = 1;
+    while (s < 4 && tiles * 2 * s * 8 <= sms * 7 && nk / (2 * s) >= 4) s *= 2;
+    return s;
+}
 cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream);
 // fp16 copy of a GGUF weight (rows x cols of `type`): dst[r][c] = the
 // reference's dequantised value, rounded to nearest fp16.
