@@ -68,21 +68,21 @@ const char* tle_version(void);
 int tle_rope(float* q, float* k, int pos, int head_dim, int n_head, int n_head_kv,
              float freq_base, void* stream);
 
-/* Workspace for tle_attention / tle_rope_attention / tle_attention_lse:
- * split-K partials plus four arrival counters.  Zero-fill it once before its
- * first use (cudaMemset); every call that completes leaves the counters at
- * zero again, so it is reused as it is.  Calls that share a workspace must
- * not overlap on the GPU (calls on one stream never do). */
+/* Workspace for tle_attention / tle_rope_attention / tle_attention_lse
+ * (split-K partials of sequences longer than 2048 rows; no initialisation
+ * needed).  Calls that share a workspace must not overlap on the GPU (calls
+ * on one stream never do). */
 size_t tle_attention_workspace_bytes(const tle_shape_t* shape, int n_ctx);
 
 /* Replaces attention() (reference src/ops.h:204-206, src/ops.cpp:1317-1515)
  * for one sequence: appends k, v at row pos of layer `layer`, then writes
  * out [n_head*head_dim] = softmax(q.K^T/sqrt(hd)) V over rows 0..pos.  q and
  * k are already rotated, as in the reference.  The reference's `att` scratch
- * is replaced by `workspace` (device, tle_attention_workspace_bytes(),
- * zero-filled before its first use).  Up to 2048 attended rows one launch
- * splits the rows into chunks per KV head and its last CTA merges them;
- * longer sequences are split over the SMs and merged by a second launch. */
+ * is replaced by `workspace` (device, tle_attention_workspace_bytes()).  Up
+ * to 2048 attended rows one launch splits the rows into chunks of one
+ * thread-block cluster per KV head, merged in distributed shared memory (the
+ * workspace is not touched); longer sequences are split over the SMs and
+ * merged by a second launch. */
 int tle_attention(float* out, const float* q, const float* k, const float* v, float* key_cache,
                   float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
                   void* workspace, size_t workspace_bytes, void* stream);

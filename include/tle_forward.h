@@ -112,7 +112,7 @@ typedef struct {
 typedef struct {
     float *x, *xb, *xb2, *q, *k, *v, *hb, *hb2, *logits;
     float *key_cache, *value_cache; /* [n_layers][n_ctx][n_head_kv*head_dim] */
-    void* workspace;                /* attention scratch, tle_forward_workspace_bytes, zero-filled once */
+    void* workspace;                /* attention scratch, tle_forward_workspace_bytes */
     size_t workspace_bytes;
 } tle_state_t;
 

@@ -220,10 +220,11 @@ _SHARED_WS = {}
                                2048, 2049])
 def test_single_sequence_lengths_match_oracle(cuda, L):
     """rope + attention of one sequence at lengths across the chunk
-    boundaries: up to 2048 rows one launch splits the rows into chunks of 32
-    or 64 per KV head and its last CTA merges them; 2049 takes the SM split.
-    Every case reuses one workspace, so the arrival counters must be back at
-    zero after each call, and the appended row must be the rotated k / v."""
+    boundaries: up to 2048 rows one launch splits the rows over a cluster of
+    up to 8 CTAs per KV head (32 to 256 rows each) merged in distributed
+    shared memory; 2049 takes the SM split and its second launch.  Three
+    calls on one workspace give identical outputs, and the appended row is
+    the rotated k / v."""
     import tle
     rng = np.random.default_rng(1000 + L)
     n_layers, layer, n_ctx = 2, 1, L + 5

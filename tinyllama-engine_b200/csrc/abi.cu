@@ -144,20 +144,14 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
         return set_error(TLE_ERR_INVALID, "layer %d outside [0, %d)", layer, shape->n_layers);
     const int L = pos + 1;
     if (L <= tle::kSeqMaxRows) {
-        // short sequence: one launch, chunks of 32 or 64 rows per KV head
+        // short sequence: one launch, a cluster of up to 8 CTAs per KV head
+        // taking chunks of 32 .. 256 rows (a multiple of 32)
         tle::SeqArgs s{};
-        s.chunk_rows = L <= 256 ? 32 : tle::kSeqMaxChunkRows;
+        const int chunks = std::min(tle::kSeqMaxChunks, (L + 31) / 32);
+        s.chunk_rows = ((L + chunks - 1) / chunks + 31) / 32 * 32;
         s.n_chunks = (L + s.chunk_rows - 1) / s.chunk_rows;
-        if (s.n_chunks > 1) {
-            const size_t need = tle::seq_counter_offset() + tle::kSeqCounterBytes;
-            if (!workspace) return set_error(TLE_ERR_WORKSPACE, "workspace is NULL");
-            if (workspace_bytes < need)
-                return set_error(TLE_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, need);
-            if (!aligned16(workspace)) return set_error(TLE_ERR_INVALID, "workspace must be 16-byte aligned");
-            s.partials = static_cast<float*>(workspace);
-            s.counters = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) +
-                                                     tle::seq_counter_offset());
-        }
+        (void)workspace;
+        (void)workspace_bytes;
         s.q = q;
         s.k = k;
         s.v = v;
@@ -241,7 +235,7 @@ int tle_rope(float* q, float* k, int pos, int head_dim, int n_head, int n_head_k
 size_t tle_attention_workspace_bytes(const tle_shape_t* shape, int n_ctx) {
     (void)shape;
     (void)n_ctx;
-    return tle::seq_counter_offset() + tle::kSeqCounterBytes;
+    return partial_bytes(tle::kMaxCtas + 1);
 }
 
 int tle_attention(float* out, const float* q, const float* k, const float* v, float* key_cache,
@@ -803,7 +797,7 @@ int tle_sample_top_p(float* logits, int n_vocab, float temperature, float top_p,
 
 size_t tle_forward_workspace_bytes(const tle_model_t* model) {
     if (!model || model->n_ctx <= 0) return 0;
-    return tle::seq_counter_offset() + tle::kSeqCounterBytes;
+    return partial_bytes(tle::kMaxCtas + 1);
 }
 
 int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token, int pos, void* stream) {

@@ -32,9 +32,13 @@
 // entry points).
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tle {
 
@@ -971,44 +975,50 @@ __global__ void __launch_bounds__(256) merge_lse_kernel(float* out, const float*
 
 // ---- short single-sequence decode ------------------------------------------
 // attention() for one sequence with L = pos + 1 <= kSeqMaxRows rows, built for
-// latency: CTA (c, g) takes rows [c R, (c+1) R) of KV head g (R = 32 or 64)
-// into shared memory with 16-byte cp.async copies, warp w computes query head
-// 8 g + w over them (lane = row for the scores, lane = a pair of dimensions
-// for P V), and the chunk's (o, m, l) of each head goes to the workspace.  The
-// CTA whose arrival completes KV head g's count merges the chunks of its
-// eight heads in chunk order (deterministic) and resets the count, so no
-// second launch is needed and the workspace is left as it was found.  The
-// last chunk's CTAs rotate the new k (and q, every CTA for its own heads) and
-// append their KV head's slice of k and v at row pos (ops.cpp:1350-1371).
+// latency: one thread-block cluster per KV head g, its C CTAs (C <= 8) taking
+// consecutive chunks of R rows (R a multiple of 32, C R >= L).  CTA (c, g)
+// copies its rows of KV head g into shared memory with 16-byte cp.async, warp
+// w computes query head 8 g + w over them (lane = row for the scores, lane = a
+// pair of dimensions for P V) and keeps the chunk's (o, m, l) of its eight
+// heads in shared memory.  After a cluster barrier CTA c folds head 8 g + c
+// (and + C, + 2C, ... when C < 8) over the C chunks in chunk order
+// (deterministic) through distributed shared memory and writes the output: no
+// workspace, no global atomics, one launch.  A second barrier keeps every
+// CTA's shared memory alive until its peers have read it.  The last chunk's
+// CTAs rotate the new k (every CTA rotates q for its own heads) and append
+// their KV head's slice of k and v at row pos (ops.cpp:1350-1371).
 constexpr int SEQ_THREADS = 256;
 constexpr int SEQ_KP = HD + 4;   // padded row (floats): lane-per-row float4 reads hit all banks
+constexpr int SEQ_PF = HD + 4;   // one head's partial in shared memory: o[64], m, l (+ pad)
 
 __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_constant__ SeqArgs A) {
-    __shared__ __align__(16) float ks[kSeqMaxChunkRows][SEQ_KP];
-    __shared__ __align__(16) float vs[kSeqMaxChunkRows][SEQ_KP];
-    __shared__ __align__(16) float qs[8][HD];
-    __shared__ int last_flag;
+    extern __shared__ __align__(16) float seq_smem[];
+    float* ks = seq_smem;                                    // [R][SEQ_KP]
+    float* vs = ks + A.chunk_rows * SEQ_KP;                  // [R][SEQ_KP]
+    float* qs = vs + A.chunk_rows * SEQ_KP;                  // [8][64]
+    float* part = qs + 8 * HD;                               // [8][SEQ_PF]
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    cg::cluster_group cl = cg::this_cluster();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c = blockIdx.x, g = blockIdx.y;
+    const int c = blockIdx.x, g = blockIdx.y;   // cluster = the n_chunks CTAs of KV head g
     const int L = A.pos + 1;
     const int r0 = c * A.chunk_rows;
-    const int nrows = min(A.chunk_rows, L - r0);
-    const bool has_new = (r0 + nrows == L);
+    const int nrows = max(0, min(A.chunk_rows, L - r0));
+    const bool has_new = nrows > 0 && (r0 + nrows == L);
     const size_t layer_base = static_cast<size_t>(A.layer) * A.n_ctx * ROWF;
-    // q, k, v, the cache and the counters may be the previous kernel's output
+    // q, k, v and the cache may be the previous kernel's output
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // cached rows of this chunk (row pos comes from the new k and v)
     const int ncached = has_new ? nrows - 1 : nrows;
     for (int e = tid; e < ncached * 32; e += SEQ_THREADS) {
-        const int r = e >> 5, part = e & 31;           // 16 chunks of K then 16 of V
-        const float* src = (part < 16 ? A.key_cache : A.value_cache) + layer_base +
-                           static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (part & 15);
-        float* dst = (part < 16 ? &ks[r][0] : &vs[r][0]) + 4 * (part & 15);
+        const int r = e >> 5, piece = e & 31;           // 16 pieces of K then 16 of V
+        const float* src = (piece < 16 ? A.key_cache : A.value_cache) + layer_base +
+                           static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (piece & 15);
+        float* dst = (piece < 16 ? ks : vs) + r * SEQ_KP + 4 * (piece & 15);
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    // q of this CTA's heads (rotated, x 1/8) and, in the last chunk, the new row
+    // q of this cluster's heads (rotated, x 1/8) and, in the last chunk, the new row
     {
         const int p = lane;   // rotation pair
         float sn = 0.f, cs = 1.f;
@@ -1019,7 +1029,7 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
             y0 = x.x * cs - x.y * sn;
             y1 = x.x * sn + x.y * cs;
         }
-        *reinterpret_cast<float2*>(&qs[warp][2 * p]) = make_float2(y0 * kScale, y1 * kScale);
+        *reinterpret_cast<float2*>(&qs[warp * HD + 2 * p]) = make_float2(y0 * kScale, y1 * kScale);
         if (has_new && warp < 2) {
             const size_t row = layer_base + static_cast<size_t>(A.pos) * ROWF + g * HD;
             if (warp == 0) {   // k: rotate, keep, append (ops.cpp:1370)
@@ -1029,11 +1039,11 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
                     k0 = kx.x * cs - kx.y * sn;
                     k1 = kx.x * sn + kx.y * cs;
                 }
-                *reinterpret_cast<float2*>(&ks[nrows - 1][2 * p]) = make_float2(k0, k1);
+                *reinterpret_cast<float2*>(&ks[(nrows - 1) * SEQ_KP + 2 * p]) = make_float2(k0, k1);
                 reinterpret_cast<float2*>(A.key_cache + row)[p] = make_float2(k0, k1);
             } else {           // v: keep, append (ops.cpp:1371)
                 const float2 vx = reinterpret_cast<const float2*>(A.v + g * HD)[p];
-                *reinterpret_cast<float2*>(&vs[nrows - 1][2 * p]) = vx;
+                *reinterpret_cast<float2*>(&vs[(nrows - 1) * SEQ_KP + 2 * p]) = vx;
                 reinterpret_cast<float2*>(A.value_cache + row)[p] = vx;
             }
         }
@@ -1041,115 +1051,78 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 
-    // scores: lane owns rows lane and lane + 32 of the chunk
+    // scores in row blocks of 32 (lane = row), online softmax across blocks,
+    // P V with lane = dimensions 2 lane, 2 lane + 1
     float4 q4[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) q4[i] = *reinterpret_cast<const float4*>(&qs[warp][4 * i]);
-    float s[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int r = lane + 32 * u;
+    for (int i = 0; i < 16; ++i) q4[i] = *reinterpret_cast<const float4*>(&qs[warp * HD + 4 * i]);
+    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int rb = 0; rb < nrows; rb += 32) {
+        const int r = rb + lane;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
         if (r < nrows) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const float4 kk = *reinterpret_cast<const float4*>(&ks[r][4 * i]);
+                const float4 kk = *reinterpret_cast<const float4*>(&ks[r * SEQ_KP + 4 * i]);
                 a0 = fmaf(q4[i].x, kk.x, a0);
                 a1 = fmaf(q4[i].y, kk.y, a1);
                 a2 = fmaf(q4[i].z, kk.z, a2);
                 a3 = fmaf(q4[i].w, kk.w, a3);
             }
         }
-        s[u] = (r < nrows) ? (a0 + a1) + (a2 + a3) : -INFINITY;
-    }
-    float m = fmaxf(s[0], s[1]);
+        const float sc = (r < nrows) ? (a0 + a1) + (a2 + a3) : -INFINITY;
+        float mb = sc;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float p[2], l = 0.f;
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(m, mb);
+        const float f = (m == -INFINITY) ? 0.f : expf(m - mn);
+        const float pr = (sc == -INFINITY) ? 0.f : expf(sc - mn);
+        float lb = pr;
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        p[u] = (s[u] == -INFINITY) ? 0.f : expf(s[u] - m);
-        l += p[u];
+        for (int o = 16; o > 0; o >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, o);
+        l = fmaf(l, f, lb);
+        o0 *= f;
+        o1 *= f;
+        m = mn;
+        const int nb = min(32, nrows - rb);
+        for (int j = 0; j < nb; ++j) {
+            const float pj = __shfl_sync(0xffffffffu, pr, j);
+            const float2 vv = *reinterpret_cast<const float2*>(&vs[(rb + j) * SEQ_KP + 2 * lane]);
+            o0 = fmaf(pj, vv.x, o0);
+            o1 = fmaf(pj, vv.y, o1);
+        }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    // P V: lane owns dimensions 2 lane, 2 lane + 1
-    float o0 = 0.f, o1 = 0.f;
-    const int n0 = min(nrows, 32);
-    for (int r = 0; r < n0; ++r) {
-        const float pr = __shfl_sync(0xffffffffu, p[0], r);
-        const float2 vv = *reinterpret_cast<const float2*>(&vs[r][2 * lane]);
-        o0 = fmaf(pr, vv.x, o0);
-        o1 = fmaf(pr, vv.y, o1);
-    }
-    for (int r = 32; r < nrows; ++r) {
-        const float pr = __shfl_sync(0xffffffffu, p[1], r - 32);
-        const float2 vv = *reinterpret_cast<const float2*>(&vs[r][2 * lane]);
-        o0 = fmaf(pr, vv.x, o0);
-        o1 = fmaf(pr, vv.y, o1);
-    }
-    const int h = 8 * g + warp;
-    if (A.n_chunks == 1) {
-        const float inv = 1.0f / l;
-        reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(o0 * inv, o1 * inv);
-        if (A.lse && lane == 0) A.lse[h] = m + logf(l);
-        return;
-    }
-    // partial of (chunk c, head h): o[64], m, l
-    float* P = A.partials + (static_cast<size_t>(c) * NH + h) * kSeqPartialFloats;
-    reinterpret_cast<float2*>(P)[lane] = make_float2(o0, o1);
+    // this chunk's partial of head 8 g + warp (an empty chunk: m = -inf, l = 0)
+    reinterpret_cast<float2*>(&part[warp * SEQ_PF])[lane] = make_float2(o0, o1);
     if (lane == 0) {
-        P[HD] = m;
-        P[HD + 1] = l;
+        part[warp * SEQ_PF + HD] = m;
+        part[warp * SEQ_PF + HD + 1] = l;
     }
-    // the last CTA of KV head g to arrive merges (release: every thread's
-    // partial stores are fenced before the CTA's single arrival)
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t ticket = atomicAdd(&A.counters[g], 1u);
-        const int last = (ticket == static_cast<uint32_t>(A.n_chunks - 1));
-        if (last) {
-            A.counters[g] = 0u;   // left zero for the next call
-            __threadfence();
+    cl.sync();
+    // fold: CTA c takes heads c, c + C, ... of this KV head, one warp each
+    const int C = A.n_chunks;
+    for (int hl = c + C * warp; warp < 8 && hl < 8; hl += C * 8) {
+        float mt = -INFINITY;
+        for (int cc = 0; cc < C; ++cc) {
+            const float* pp = cl.map_shared_rank(part, cc);
+            mt = fmaxf(mt, pp[hl * SEQ_PF + HD]);
         }
-        last_flag = last;
+        float acc0 = 0.f, acc1 = 0.f, lt = 0.f;
+        for (int cc = 0; cc < C; ++cc) {
+            const float* pp = cl.map_shared_rank(part, cc) + hl * SEQ_PF;
+            const float mc = pp[HD], lc = pp[HD + 1];
+            const float2 oc = reinterpret_cast<const float2*>(pp)[lane];
+            const float f = (mc == -INFINITY) ? 0.f : expf(mc - mt);
+            lt = fmaf(lc, f, lt);
+            acc0 = fmaf(oc.x, f, acc0);
+            acc1 = fmaf(oc.y, f, acc1);
+        }
+        const int h = 8 * g + hl;
+        const float inv = 1.0f / lt;
+        reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
+        if (A.lse && lane == 0) A.lse[h] = mt + logf(lt);
     }
-    __syncthreads();
-    if (!last_flag) return;
-    // merge: warp w folds head h over the chunks in chunk order
-    float mt = -INFINITY;
-    for (int cc = lane; cc < A.n_chunks; cc += 32)
-        mt = fmaxf(mt, ld_cg(A.partials + (static_cast<size_t>(cc) * NH + h) * kSeqPartialFloats + HD));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-    // chunks in groups of 8, every load of a group issued before any is used
-    float acc0 = 0.f, acc1 = 0.f, lt = 0.f;
-    for (int c0 = 0; c0 < A.n_chunks; c0 += 8) {
-        float mc[8], lc[8], ox[8], oy[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            mc[u] = -INFINITY;
-            lc[u] = ox[u] = oy[u] = 0.f;
-            if (c0 + u < A.n_chunks) {
-                const float* Pc = A.partials + (static_cast<size_t>(c0 + u) * NH + h) * kSeqPartialFloats;
-                mc[u] = ld_cg(Pc + HD);
-                lc[u] = ld_cg(Pc + HD + 1);
-                ox[u] = ld_cg(Pc + 2 * lane);
-                oy[u] = ld_cg(Pc + 2 * lane + 1);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const float f = (mc[u] == -INFINITY) ? 0.f : expf(mc[u] - mt);
-            lt = fmaf(lc[u], f, lt);
-            acc0 = fmaf(ox[u], f, acc0);
-            acc1 = fmaf(oy[u], f, acc1);
-        }
-    }
-    const float inv = 1.0f / lt;
-    reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
-    if (A.lse && lane == 0) A.lse[h] = mt + logf(lt);
+    cl.sync();
 }
 
 // rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
@@ -1229,17 +1202,31 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream) {
-    // programmatic dependent of the previous kernel: its CTAs may be
-    // scheduled while that grid drains; griddepcontrol.wait orders the reads
+    const size_t smem = static_cast<size_t>(2 * a.chunk_rows * SEQ_KP + 8 * HD + 8 * SEQ_PF) * sizeof(float);
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([&](int) {
+        return cudaFuncSetAttribute(seq_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(2 * kSeqMaxChunkRows * SEQ_KP * sizeof(float) +
+                                                     (8 * HD + 8 * SEQ_PF) * sizeof(float)));
+    });
+    if (e != cudaSuccess) return e;
+    // one cluster of n_chunks CTAs per KV head; a programmatic dependent of
+    // the previous kernel (its CTAs may be scheduled while that grid drains;
+    // griddepcontrol.wait orders the reads)
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(a.n_chunks, NKV_HEADS);
     cfg.blockDim = dim3(SEQ_THREADS);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.n_chunks;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, seq_decode_kernel, a);
 }
 

@@ -98,19 +98,13 @@ struct DecodeArgs {
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
 
 // Short single-sequence decode (tle_attention, tle_rope_attention,
-// tle_attention_lse with at most kSeqMaxRows attended rows): one CTA per
-// (chunk of rows, KV head), one warp per query head; the last CTA of each KV
-// head to finish merges the chunks' partials (no second launch).
-constexpr int kSeqMaxChunkRows = 64;
-constexpr int kSeqMaxChunks = 32;
+// tle_attention_lse with at most kSeqMaxRows attended rows): one cluster of
+// n_chunks (<= 8) CTAs per KV head, one warp per query head, the chunks'
+// partials folded through distributed shared memory (no workspace, one
+// launch).
+constexpr int kSeqMaxChunks = 8;
+constexpr int kSeqMaxChunkRows = 256;
 constexpr int kSeqMaxRows = kSeqMaxChunkRows * kSeqMaxChunks;            // 2048
-constexpr int kSeqPartialFloats = kHeadDim + 2;                         // o[64], m, l of one head
-// Byte offset of the four arrival counters in a single-sequence workspace:
-// after every partial slot either decode path writes, so neither clobbers them.
-inline size_t seq_counter_offset() {
-    return static_cast<size_t>(kMaxCtas + 1) * kPartialFloats * sizeof(float);
-}
-constexpr size_t kSeqCounterBytes = 256;
 struct SeqArgs {
     const float* q;              // [32*64]
     const float* k;              // [4*64]
@@ -119,11 +113,9 @@ struct SeqArgs {
     float* lse;                  // optional [32]
     float* key_cache;            // [n_layers][n_ctx][256]
     float* value_cache;
-    float* partials;             // [n_chunks][4][8][kSeqPartialFloats]
-    uint32_t* counters;          // [4], zero between calls
     uint32_t* err;
     int layer, pos, n_ctx, rotate;
-    int chunk_rows, n_chunks;
+    int chunk_rows, n_chunks;    // n_chunks * chunk_rows >= pos + 1, chunk_rows a multiple of 32
     float inv_freq[kHeadDim / 2];
 };
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);

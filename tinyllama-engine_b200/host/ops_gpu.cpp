@@ -47,7 +47,6 @@ void* split_scratch(const tle_shape_t& s, int n_ctx, void* stream, std::size_t* 
             w = SplitScratch{};
         }
         cuda_check(cudaMalloc(&w.p, need), "cudaMalloc split-K scratch");
-        cuda_check(cudaMemset(w.p, 0, need), "cudaMemset split-K scratch");
         w.bytes = need;
     }
     *bytes = w.bytes;

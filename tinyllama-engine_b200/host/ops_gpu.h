@@ -75,7 +75,7 @@ void rope_gpu(float* q, float* k, int pos, int head_dim, int n_head, int n_head_
 // scratch (run_state.h:64, 126: n_ctx floats); it is accepted so forward.cpp's
 // call sites stay as they are, and it is never read or written (it may be
 // null).  The split-K scratch of the call is owned by this layer instead:
-// one zero-initialised device buffer per (device, stream), made by the first
+// one device buffer per (device, stream), made by the first
 // call on that pair (so make that call outside stream capture) and grown,
 // after synchronising the device, when a larger n_ctx needs more; it lives
 // until the process exits.  Calls on one stream are ordered and share it;

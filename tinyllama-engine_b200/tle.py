@@ -207,11 +207,9 @@ def rope(q, k, pos: int, head_dim: int = 64, n_head: int = 32, n_head_kv: int = 
 
 
 def attention_workspace(shape: Shape, n_ctx: int):
-    """Zero-filled workspace of tle_attention / tle_rope_attention (its
-    arrival counters must start at zero; every call leaves them there)."""
     import torch
     n = lib().tle_attention_workspace_bytes(ctypes.byref(shape), n_ctx)
-    return torch.zeros((n + 3) // 4, dtype=torch.float32, device="cuda")
+    return torch.empty((n + 3) // 4, dtype=torch.float32, device="cuda")
 
 
 def _single(fn, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace, stream):
@@ -609,7 +607,7 @@ class DeviceState:
                   "logits": z(m.n_vocab), "key_cache": z(m.n_layers * m.n_ctx * kv),
                   "value_cache": z(m.n_layers * m.n_ctx * kv)}
         nbytes = lib().tle_forward_workspace_bytes(ctypes.byref(dm.desc))
-        self.workspace = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
         self.desc = State(**{k: v.data_ptr() for k, v in self.t.items()},
                           workspace=self.workspace.data_ptr(), workspace_bytes=nbytes)
 
