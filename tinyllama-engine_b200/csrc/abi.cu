@@ -795,9 +795,86 @@ int tle_sample_top_p(float* logits, int n_vocab, float temperature, float top_p,
     return sample_common(logits, n_vocab, temperature, top_p, r, true, token, stream);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Every layer of the token in one persistent cooperative launch, when the
+// model allows it: all linear weights Q4_0 (16-byte aligned), at most
+// kPersistMaxLayers layers, widths that are multiples of 256, the attention
+// of pos + 1 rows in at most SMs / 4 chunks of 64 rows per KV head, the
+// workspace large enough, cooperative launch supported.  Otherwise *used
+// stays false and the caller launches product by product.
+int forward_layers_persistent(const tle_model_t* m, const tle_state_t* s, int pos, uint32_t* err,
+                              cudaStream_t st, bool* used) {
+    *used = false;
+    if (m->n_layers > tle::kPersistMaxLayers) return 0;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& L = m->layers[l];
+        const tle_weight_t* w[7] = {&L.attn_q, &L.attn_k, &L.attn_v, &L.attn_output, &L.ffn_gate, &L.ffn_up,
+                                    &L.ffn_down};
+        for (const tle_weight_t* x : w)
+            if (x->type != TLE_W_Q4_0 || !x->data || !aligned16(x->data)) return 0;
+        if (!L.attn_norm || !L.ffn_norm) return 0;
+    }
+    int dev = 0, coop = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop)
+        return 0;
+    const int grid = sm_count();
+    tle::PersistArgs a{};
+    const size_t smem = tle::persist_smem_bytes(m->n_embd, m->n_ff, grid, &a);
+    if (!smem) return 0;
+    const int chunks = (pos + 1 + tle::kPersistAttRows - 1) / tle::kPersistAttRows;
+    if (chunks > tle::persist_max_chunks(grid)) return 0;
+    if (!s->workspace || s->workspace_bytes < tle::persist_workspace_bytes(grid) ||
+        (reinterpret_cast<uintptr_t>(s->workspace) & 255u) != 0)
+        return 0;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const tle_layer_t& Ly = m->layers[l];
+        const tle_weight_t* w[7] = {&Ly.attn_q, &Ly.attn_k, &Ly.attn_v, &Ly.attn_output, &Ly.ffn_gate, &Ly.ffn_up,
+                                    &Ly.ffn_down};
+        for (int i = 0; i < 7; ++i) a.layer[l].w[i] = static_cast<const uint8_t*>(w[i]->data);
+        a.layer[l].attn_norm = Ly.attn_norm;
+        a.layer[l].ffn_norm = Ly.ffn_norm;
+    }
+    a.n_layers = m->n_layers;
+    a.n_embd = m->n_embd;
+    a.n_ff = m->n_ff;
+    a.n_ctx = m->n_ctx;
+    a.pos = pos;
+    a.eps = m->rms_norm_eps;
+    a.x = s->x;
+    a.q = s->q;
+    a.k = s->k;
+    a.v = s->v;
+    a.hb = s->hb;
+    a.key_cache = s->key_cache;
+    a.value_cache = s->value_cache;
+    a.sync = static_cast<uint32_t*>(s->workspace);
+    a.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(s->workspace) + 256);
+    a.err = err;
+    a.att_chunks = chunks;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, m->rope_freq_base);
+    cudaError_t e = cudaMemsetAsync(a.sync, 0, sizeof(uint32_t), st);   // the barrier count
+    if (e != cudaSuccess) return cuda_error(e, "persistent forward: barrier count");
+    e = tle::launch_forward_persistent(a, grid, smem, st);
+    if (e == cudaErrorCooperativeLaunchTooLarge) {   // SMs held elsewhere: product by product
+        (void)cudaGetLastError();
+        return 0;
+    }
+    if (e != cudaSuccess) return cuda_error(e, "persistent forward launch");
+    *used = true;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
 size_t tle_forward_workspace_bytes(const tle_model_t* model) {
     if (!model || model->n_ctx <= 0) return 0;
-    return partial_bytes(tle::kMaxCtas + 1);
+    return std::max(partial_bytes(tle::kMaxCtas + 1), tle::persist_workspace_bytes(tle::kMaxCtas));
 }
 
 int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token, int pos, void* stream) {
@@ -825,7 +902,9 @@ int tle_forward(const tle_model_t* m, const tle_state_t* s, const int32_t* token
 
     e = tle::launch_embed(m->token_embd.type, s->x, m->token_embd.data, token, m->n_vocab, n_embd, err, st);
     if (e != cudaSuccess) return cuda_error(e, "embedding");
-    for (int l = 0; l < m->n_layers; ++l) {
+    bool persistent = false;
+    if (int rc = forward_layers_persistent(m, s, pos, err, st, &persistent)) return rc;
+    for (int l = 0; !persistent && l < m->n_layers; ++l) {
         const tle_layer_t& L = m->layers[l];
         if (!L.attn_norm || !L.ffn_norm) return set_error(TLE_ERR_INVALID, "layer %d: null norm weight", l);
         // rmsnorm + q, k, v (forward.cpp:184-196): one launch when the three share a format

@@ -19,6 +19,7 @@ enum : uint32_t {
     kErrDrain = 0x104,      // exit-time wait for in-flight copies gave up
     kErrBadPage = 0x105,    // paged decode: a page id outside the pool (access skipped)
     kErrBadToken = 0x106,   // forward: a token id outside the vocabulary (zero embedding used)
+    kErrGridWait = 0x108,   // persistent forward: a grid barrier wait gave up
     kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 

@@ -25,6 +25,8 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -278,22 +280,23 @@ __device__ __forceinline__ void prefetch_l2(const uint8_t* p, size_t bytes) {
 }
 
 // Stages the input vector into xs with ordered L2 loads (it is the previous
-// kernel's output), eight 16-byte loads in flight per thread before any is
-// stored; returns this thread's share of sum(x^2).
+// kernel's output), D 16-byte loads in flight per thread (NT threads) before
+// any is stored; returns this thread's share of sum(x^2).
+template <int NT = GT, int D = 8>
 __device__ __forceinline__ float stage_x(float* xs, const float* x, int cols, int tid) {
     float ss = 0.f;
     if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const int n4 = cols >> 2;
-        for (int base = tid; base < n4; base += GT * 8) {
-            float4 v[8];
+        for (int base = tid; base < n4; base += NT * D) {
+            float4 v[D];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * GT;
+            for (int j = 0; j < D; ++j) {
+                const int i = base + j * NT;
                 if (i < n4) v[j] = ld_cg4(reinterpret_cast<const float4*>(x) + i);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * GT;
+            for (int j = 0; j < D; ++j) {
+                const int i = base + j * NT;
                 if (i < n4) {
                     reinterpret_cast<float4*>(xs)[i] = v[j];
                     ss = fmaf(v[j].x, v[j].x, ss);
@@ -304,16 +307,16 @@ __device__ __forceinline__ float stage_x(float* xs, const float* x, int cols, in
             }
         }
     } else {
-        for (int base = tid; base < cols; base += GT * 8) {
-            float v[8];
+        for (int base = tid; base < cols; base += NT * D) {
+            float v[D];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * GT;
+            for (int j = 0; j < D; ++j) {
+                const int i = base + j * NT;
                 if (i < cols) v[j] = ld_cg(x + i);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * GT;
+            for (int j = 0; j < D; ++j) {
+                const int i = base + j * NT;
                 if (i < cols) {
                     xs[i] = v[j];
                     ss = fmaf(v[j], v[j], ss);
@@ -811,6 +814,521 @@ __global__ void __launch_bounds__(256) vec_add_kernel(float* out, const float* x
         out[i] = ld_cg(out + i) + ld_cg(x + i);
 }
 
+// ---- persistent forward of one token (all-Q4_0 layers) ---------------------
+// One cooperative launch of one CTA per SM runs every layer of a token:
+//   P1 RMSNorm(x) + q/k/v rows   P2 rope + attention + append (row pos)
+//   P3 x += Wo attn              P4 RMSNorm(x) + gate/up rows + SwiGLU -> hb
+//   P5 x += Wdown hb
+// with a grid barrier after each phase (every product reads the whole
+// output of the one before).  CTA b owns rows [b R, (b+1) R) of every
+// product (R = ceil(rows / grid)); its rows of the products to come are
+// bulk-copied (TMA engine), one copy per row into a padded row stride, into
+// one of two shared-memory buffers before the barrier of the phase that
+// precedes their use (weights are never written, so the copies run ahead
+// freely): Wo at P1, gate/up at P2, Wdown at P4, the next layer's q/k/v at
+// P5.  Buffer A holds q/k/v and gate/up, buffer B Wo and Wdown.
+//
+// Products: a thread takes one (row, unit) pair, a unit being 8 Q4_0 blocks
+// (256 weights, 144 bytes = nine 16-byte shared loads), and writes its
+// partial; the partials of a row are then summed in unit order.  Threads of
+// a warp hold consecutive rows of one unit (at most two units per warp), so
+// the input vector is read as a broadcast, and the odd 16-byte row stride
+// puts eight consecutive rows' loads in distinct banks.  The input vector
+// is staged with its 16-byte chunks rotated by the unit index inside each
+// block (two units read by one warp hit distinct banks).  RMSNorm: x * w is
+// staged while sum(x^2) is reduced; the row sums are scaled by 1/rms.
+//
+// Attention (P2) splits the L = pos + 1 rows of each KV head over C = L / 64
+// CTAs (rounded up); their cached K/V rows are copied into shared memory at
+// P1, so P2 waits only for q, k, v.  Warp w takes query head 8 g + (w & 7)
+// over half (w >> 3) of the chunk's rows; the halves are folded in shared
+// memory and each CTA writes one (o, max, sum) record per head.  The records
+// are folded (chunk order) by every CTA while it stages P3's input.  Every
+// read of an activation another CTA wrote goes through L2 (ld.cg), after an
+// acquire at the barrier.
+constexpr int PT = 512;   // 16 warps
+constexpr int PW = PT / 32;
+constexpr int PKP = 68;   // padded K/V row of the attention phase (floats)
+constexpr int kUnit = 256;            // weights per unit
+constexpr int kUnitBytes = 144;       // Q4_0 bytes per unit
+constexpr int kRec = 68;              // floats per attention record: o[64], max, sum, 2 pad
+constexpr int kAttRows = kPersistAttRows;
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier over gridDim.x CTAs (all resident: cooperative launch).  The
+// count only grows within a launch; barrier k waits for (k + 1) * grid
+// arrivals.  A wait that gives up (2 s) records 0x108 and the CTA stops
+// waiting at later barriers, so the launch always ends.
+__device__ __forceinline__ void grid_barrier(uint32_t* ctr, uint32_t target, uint32_t* err, int* failed) {
+    __syncthreads();
+    if (threadIdx.x == 0 && !*failed) {
+        // release: the CTA's writes (ordered before this thread by the
+        // barrier above) before the arrival; acquire on the count
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+        if (ld_acquire_u32(ctr) < target) {
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_u32(ctr) < target) {
+                if (globaltimer() - t0 > kWaitTimeoutNs) {
+                    record_error(err, kErrGridWait);
+                    *failed = 1;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ int cta_rows(int rows, int b, int G, int& r0) {
+    const int R = (rows + G - 1) / G;
+    r0 = min(rows, b * R);
+    return max(0, min(rows, r0 + R) - r0);
+}
+
+// Float index of input element f in the staged (rotated) layout: chunk i of
+// block k of unit u sits at chunk (i + u) mod 8 of the block.
+__device__ __forceinline__ int xs_phys(int f) {
+    return (f & ~31) | (((((f >> 2) + (f >> 8)) & 7)) << 2) | (f & 3);
+}
+
+// Stages x (times w when w is given) into xs in the rotated layout; returns
+// this thread's share of sum(x^2).  cols % 256 == 0.
+__device__ __forceinline__ float stage_rot(float* xs, const float* x, const float* w, int cols) {
+    float ss = 0.f;
+    const int n4 = cols >> 2;
+    for (int base = threadIdx.x; base < n4; base += 2 * PT) {
+        float4 v[2], g[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = base + j * PT;
+            if (i < n4) {
+                v[j] = ld_cg4(reinterpret_cast<const float4*>(x) + i);
+                if (w) g[j] = __ldg(reinterpret_cast<const float4*>(w) + i);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = base + j * PT;
+            if (i < n4) {
+                float4 t = v[j];
+                ss = fmaf(t.x, t.x, ss);
+                ss = fmaf(t.y, t.y, ss);
+                ss = fmaf(t.z, t.z, ss);
+                ss = fmaf(t.w, t.w, ss);
+                if (w) t = make_float4(t.x * g[j].x, t.y * g[j].y, t.z * g[j].z, t.w * g[j].w);
+                *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) = t;
+            }
+        }
+    }
+    return ss;
+}
+
+// The attention output (32 heads x 64) folded from the chunk records, in
+// chunk order (max first, then the rescaled sums), staged rotated into xs.
+__device__ __forceinline__ void stage_attention(float* xs, const float* rec, int n_chunks, int n_embd) {
+    for (int i = threadIdx.x; i < (n_embd >> 2); i += PT) {
+        const int h = i >> 4, d0 = 4 * (i & 15);
+        float mt = -INFINITY;
+        for (int c = 0; c < n_chunks; ++c) mt = fmaxf(mt, ld_cg(rec + (c * kNHead + h) * kRec + kHeadDim));
+        float lt = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int c = 0;
+        for (; c + 4 <= n_chunks; c += 4) {
+            float mc[4], lc[4];
+            float4 oc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float* R = rec + ((c + u) * kNHead + h) * kRec;
+                mc[u] = ld_cg(R + kHeadDim);
+                lc[u] = ld_cg(R + kHeadDim + 1);
+                oc[u] = ld_cg4(reinterpret_cast<const float4*>(R + d0));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float f = expf(mc[u] - mt);
+                lt = fmaf(lc[u], f, lt);
+                acc.x = fmaf(oc[u].x, f, acc.x);
+                acc.y = fmaf(oc[u].y, f, acc.y);
+                acc.z = fmaf(oc[u].z, f, acc.z);
+                acc.w = fmaf(oc[u].w, f, acc.w);
+            }
+        }
+        for (; c < n_chunks; ++c) {
+            const float* R = rec + (c * kNHead + h) * kRec;
+            const float f = expf(ld_cg(R + kHeadDim) - mt);
+            const float4 o = ld_cg4(reinterpret_cast<const float4*>(R + d0));
+            lt = fmaf(ld_cg(R + kHeadDim + 1), f, lt);
+            acc.x = fmaf(o.x, f, acc.x);
+            acc.y = fmaf(o.y, f, acc.y);
+            acc.z = fmaf(o.z, f, acc.z);
+            acc.w = fmaf(o.w, f, acc.w);
+        }
+        const float inv = 1.0f / lt;
+        *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+}
+
+// One unit (8 Q4_0 blocks) of M rows against the staged input: w[m] is the
+// unit's first byte in row m (16-byte aligned), xu the unit's 256 inputs,
+// rot = unit index mod 8.  A 32-byte window (chunks k, k + 1) holds block k
+// at window byte 2k.  Per block: the 32 products as packed f32x2 FMAs (the
+// byte permute builds 2^23 + n exactly, one packed subtract removes
+// 2^23 + 8), the block sum scaled by d as the reference does per block
+// (ops.cpp:495 matmul_q4_0).
+template <int M>
+__device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const float* xu, int rot,
+                                            float (&out)[M]) {
+    uint32_t win[M][8];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const uint4 c0 = *reinterpret_cast<const uint4*>(w[m]);
+        win[m][0] = c0.x;
+        win[m][1] = c0.y;
+        win[m][2] = c0.z;
+        win[m][3] = c0.w;
+        out[m] = 0.f;
+    }
+    const uint64_t magic = pk2(-8388616.0f, -8388616.0f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const uint4 c1 = *reinterpret_cast<const uint4*>(w[m] + 16 * (k + 1));
+            win[m][4] = c1.x;
+            win[m][5] = c1.y;
+            win[m][6] = c1.z;
+            win[m][7] = c1.w;
+        }
+        const int r0 = 2 * k;             // block k's first window byte
+        const int w0 = (r0 + 2) >> 2;     // first window word holding its nibbles
+        float d[M];
+        uint32_t lo[M][5], hi[M][5];
+        uint64_t s2a[M], s2b[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const uint32_t dw = win[m][r0 >> 2];
+            d[m] = h2f(static_cast<uint16_t>((r0 & 2) ? (dw >> 16) : (dw & 0xFFFFu)));
+#pragma unroll
+            for (int j = 0; j < 5; ++j) {
+                const uint32_t v = (w0 + j < 8) ? win[m][w0 + j] : 0u;
+                lo[m][j] = v & 0x0F0F0F0Fu;
+                hi[m][j] = (v >> 4) & 0x0F0F0F0Fu;
+            }
+            s2a[m] = s2b[m] = 0ull;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {   // inputs 4i..4i+3 of the block
+            const float4 xv = *reinterpret_cast<const float4*>(xu + 32 * k + 4 * ((i + rot) & 7));
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+#pragma unroll
+                for (int e = 0; e < 4; e += 2) {
+                    const int p0 = r0 + 2 + (i & 3) * 4 + e, p1 = p0 + 1;   // window bytes of the two weights
+                    const uint32_t* src = (i < 4) ? lo[m] : hi[m];
+                    const float a = __int_as_float(__byte_perm(src[(p0 >> 2) - w0], 0x4B000000u, 0x7540u | (p0 & 3)));
+                    const float b = __int_as_float(__byte_perm(src[(p1 >> 2) - w0], 0x4B000000u, 0x7540u | (p1 & 3)));
+                    const uint64_t nn = add2(pk2(a, b), magic);
+                    const uint64_t xx = e == 0 ? pk2(xv.x, xv.y) : pk2(xv.z, xv.w);
+                    if (i & 1) s2b[m] = fma2(nn, xx, s2b[m]);
+                    else s2a[m] = fma2(nn, xx, s2a[m]);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float2 sa = up2(s2a[m]), sb = up2(s2b[m]);
+            out[m] = fmaf(d[m], (sa.x + sa.y) + (sb.x + sb.y), out[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            win[m][0] = win[m][4];
+            win[m][1] = win[m][5];
+            win[m][2] = win[m][6];
+            win[m][3] = win[m][7];
+        }
+    }
+}
+
+// Every (row, unit) pair of an nr-row product over `units` units, one per
+// thread (nr * units <= PT): row r of matrix m at buf + (r + m * mstride) * stride.  Partials
+// of matrix m go to part[m * PT + u * nr + r].
+template <int M>
+__device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int mstride, int nr, int units,
+                                           const float* xs, float* part) {
+    const int p = threadIdx.x;   // nr * units <= PT (checked on the host)
+    if (p < nr * units) {
+        const int u = p / nr, r = p - u * nr;
+        const uint8_t* w[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+            w[m] = buf + static_cast<size_t>(r + m * mstride) * stride + u * kUnitBytes;
+        float y[M];
+        unit_dot_q4<M>(w, xs + u * kUnit, u & 7, y);
+#pragma unroll
+        for (int m = 0; m < M; ++m) part[m * PT + p] = y[m];
+    }
+}
+
+__device__ __forceinline__ float row_total(const float* part, int r, int nr, int units) {
+    float y = 0.f;
+    for (int u = 0; u < units; ++u) y += part[u * nr + r];
+    return y;
+}
+
+__global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_constant__ PersistArgs A) {
+    extern __shared__ __align__(128) unsigned char psm[];
+    float* xs = reinterpret_cast<float*>(psm);
+    uint8_t* bufA = psm + A.off_a;
+    uint8_t* bufB = psm + A.off_b;
+    float* ks = reinterpret_cast<float*>(psm + A.off_kv);
+    float* vs = ks + kAttRows * PKP;
+    float* qs = vs + kAttRows * PKP;          // 8 heads x 64
+    float* comb = qs + 8 * kHeadDim;          // 8 heads x kRec: the second half's (o, max, sum)
+    float* part = reinterpret_cast<float*>(psm + A.off_part);   // 2 x PT
+    __shared__ __align__(8) uint64_t wbar[2];
+    __shared__ float red[PW];
+    __shared__ int failed;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+    const int E = A.n_embd, KV = kNHeadKv * kHeadDim, FF = A.n_ff;
+    const int rbE = E / 32 * 18, rbF = FF / 32 * 18;   // Q4_0 row bytes (n_embd, n_ff columns)
+    const int uE = E / kUnit, uF = FF / kUnit;
+    const int sE = A.stride_e, sF = A.stride_f;
+    if (tid == 0) {
+        mbar_init(&wbar[0], 1);
+        mbar_init(&wbar[1], 1);
+        fence_barrier_init();
+        failed = 0;
+    }
+    __syncthreads();
+    uint32_t useA = 0, useB = 0, nbar = 0;
+    int r0q, r0e, r0f;
+    const int nq = cta_rows(E + 2 * KV, b, G, r0q);
+    const int ne = cta_rows(E, b, G, r0e);
+    const int nf = cta_rows(FF, b, G, r0f);
+    const int Rf = (FF + G - 1) / G;   // gate rows then up rows in buffer A, this many rows apart
+    // attention chunk of this CTA (P2)
+    const int L = A.pos + 1, C = A.att_chunks;
+    const bool att = b < kNHeadKv * C;
+    const int g = att ? b / C : 0, c = att ? b % C : 0;
+    const int rr0 = c * kAttRows;
+    const int nrows = att ? max(0, min(kAttRows, L - rr0)) : 0;
+    const bool has_new = nrows > 0 && rr0 + nrows == L;
+    const int ncached = has_new ? nrows - 1 : nrows;
+
+    // warp 0: one bulk copy per row (row i of the span to dst + i * stride)
+    auto fill_rows = [&](uint8_t* dst, int stride, int n, int rb, uint64_t* bar, auto src_of) {
+        for (int i = lane; i < n; i += 32) bulk_g2s_plain(dst + static_cast<size_t>(i) * stride, src_of(i), rb, bar);
+    };
+    auto fill_qkv = [&](int l) {
+        const PersistLayer& Ly = A.layer[l];
+        if (lane == 0) mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(nq * rbE));
+        __syncwarp();
+        fill_rows(bufA, sE, nq, rbE, &wbar[0], [&](int i) {
+            const int r = r0q + i;
+            const int m = r < E ? 0 : (r < E + KV ? 1 : 2);
+            const int base = m == 0 ? 0 : (m == 1 ? E : E + KV);
+            return Ly.w[m] + static_cast<size_t>(r - base) * rbE;
+        });
+    };
+    auto fill_o = [&](int l) {
+        if (lane == 0) mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbE));
+        __syncwarp();
+        const uint8_t* W = A.layer[l].w[3] + static_cast<size_t>(r0e) * rbE;
+        fill_rows(bufB, sE, ne, rbE, &wbar[1], [&](int i) { return W + static_cast<size_t>(i) * rbE; });
+    };
+    auto fill_gu = [&](int l) {
+        if (lane == 0) mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(2 * nf * rbE));
+        __syncwarp();
+        const uint8_t* Wg = A.layer[l].w[4] + static_cast<size_t>(r0f) * rbE;
+        const uint8_t* Wu = A.layer[l].w[5] + static_cast<size_t>(r0f) * rbE;
+        fill_rows(bufA, sE, nf, rbE, &wbar[0], [&](int i) { return Wg + static_cast<size_t>(i) * rbE; });
+        fill_rows(bufA + static_cast<size_t>(Rf) * sE, sE, nf, rbE, &wbar[0],
+                  [&](int i) { return Wu + static_cast<size_t>(i) * rbE; });
+    };
+    auto fill_down = [&](int l) {
+        if (lane == 0) mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbF));
+        __syncwarp();
+        const uint8_t* W = A.layer[l].w[6] + static_cast<size_t>(r0e) * rbF;
+        fill_rows(bufB, sF, ne, rbF, &wbar[1], [&](int i) { return W + static_cast<size_t>(i) * rbF; });
+    };
+    auto wait_buf = [&](int which) {
+        uint32_t& u = which ? useB : useA;
+        if (!failed && !mbar_wait(&wbar[which], u & 1)) {
+            if (tid == 0) record_error(A.err, kErrWaitFull);
+            // the copies may still land: wait once more before the buffer is reused or the CTA exits
+            mbar_wait(&wbar[which], u & 1);
+        }
+        ++u;
+    };
+    auto barrier = [&]() {
+        ++nbar;
+        grid_barrier(A.sync, nbar * static_cast<uint32_t>(G), A.err, &failed);
+    };
+    auto block_sum = [&](float v) {   // every thread gets the CTA total (one barrier inside)
+        v = warp_sum(v);
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < PW; ++i) t += red[i];
+        return t;
+    };
+    if (warp == 0) fill_qkv(0);
+
+    for (int l = 0; l < A.n_layers; ++l) {
+        const PersistLayer& Ly = A.layer[l];
+        const size_t lbase = static_cast<size_t>(l) * A.n_ctx * KV;
+        // ---- P1: rmsnorm + q/k/v (forward.cpp:184-196) ----
+        if (warp == 0) fill_o(l);
+        if (att) {   // this chunk's cached K/V rows of head g, for P2
+            for (int e = tid; e < ncached * 32; e += PT) {
+                const int r = e >> 5, piece = e & 31;
+                const float* src = (piece < 16 ? A.key_cache : A.value_cache) + lbase +
+                                   static_cast<size_t>(rr0 + r) * KV + g * kHeadDim + 4 * (piece & 15);
+                float* dst = (piece < 16 ? ks : vs) + r * PKP + 4 * (piece & 15);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+        const float ss1 = stage_rot(xs, A.x, Ly.attn_norm, E);
+        const float rms1 = 1.0f / sqrtf(block_sum(ss1) / static_cast<float>(E) + A.eps);
+        wait_buf(0);
+        rows_units<1>(bufA, sE, 0, nq, uE, xs, part);
+        __syncthreads();
+        if (tid < nq) {
+            const float y = row_total(part, tid, nq, uE) * rms1;
+            const int r = r0q + tid;
+            if (r < E) A.q[r] = y;
+            else if (r < E + KV) A.k[r - E] = y;
+            else A.v[r - E - KV] = y;
+        }
+        barrier();
+        // ---- P2: rope + attention + append (forward.cpp:198-208, ops.cpp:1223/1317) ----
+        if (warp == 0) fill_gu(l);   // buffer A's reads ended before the barrier
+        if (att) {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            if (warp < 8) {   // warp w: rotate query head 8 g + w
+                const int p = lane;
+                float sn, cs;
+                sincosf(static_cast<float>(A.pos) * A.inv_freq[p], &sn, &cs);
+                const int h = 8 * g + warp;
+                const float x0 = ld_cg(A.q + h * kHeadDim + 2 * p), x1 = ld_cg(A.q + h * kHeadDim + 2 * p + 1);
+                qs[warp * kHeadDim + 2 * p] = (x0 * cs - x1 * sn) * 0.125f;
+                qs[warp * kHeadDim + 2 * p + 1] = (x0 * sn + x1 * cs) * 0.125f;
+                if (has_new && warp < 2) {
+                    const size_t row = lbase + static_cast<size_t>(A.pos) * KV + g * kHeadDim;
+                    if (warp == 0) {   // k: rotate, keep, append (ops.cpp:1370)
+                        const float k0 = ld_cg(A.k + g * kHeadDim + 2 * p), k1 = ld_cg(A.k + g * kHeadDim + 2 * p + 1);
+                        const float y0 = k0 * cs - k1 * sn, y1 = k0 * sn + k1 * cs;
+                        ks[(nrows - 1) * PKP + 2 * p] = y0;
+                        ks[(nrows - 1) * PKP + 2 * p + 1] = y1;
+                        A.key_cache[row + 2 * p] = y0;
+                        A.key_cache[row + 2 * p + 1] = y1;
+                    } else {           // v (ops.cpp:1371)
+                        const float v0 = ld_cg(A.v + g * kHeadDim + 2 * p), v1 = ld_cg(A.v + g * kHeadDim + 2 * p + 1);
+                        vs[(nrows - 1) * PKP + 2 * p] = v0;
+                        vs[(nrows - 1) * PKP + 2 * p + 1] = v1;
+                        A.value_cache[row + 2 * p] = v0;
+                        A.value_cache[row + 2 * p + 1] = v1;
+                    }
+                }
+            }
+            __syncthreads();
+            // warp w: head 8 g + (w & 7) over rows [32 half, 32 half + 32) of the chunk
+            const int hw = warp & 7, half = warp >> 3;
+            const float4* q4 = reinterpret_cast<const float4*>(qs + hw * kHeadDim);   // broadcast reads
+            const int r = 32 * half + lane;
+            float sc = -INFINITY;
+            if (r < nrows) {
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float4 kk = *reinterpret_cast<const float4*>(&ks[r * PKP + 4 * i]);
+                    const float4 qq = q4[i];
+                    a0 = fmaf(qq.x, kk.x, a0);
+                    a1 = fmaf(qq.y, kk.y, a1);
+                    a2 = fmaf(qq.z, kk.z, a2);
+                    a3 = fmaf(qq.w, kk.w, a3);
+                }
+                sc = (a0 + a1) + (a2 + a3);
+            }
+            float m = sc;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float pr = (sc == -INFINITY) ? 0.f : expf(sc - m);
+            float lsum = pr;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            float o0 = 0.f, o1 = 0.f;
+            const int nb = max(0, min(32, nrows - 32 * half));
+            for (int j = 0; j < nb; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, pr, j);
+                const float2 vv = *reinterpret_cast<const float2*>(&vs[(32 * half + j) * PKP + 2 * lane]);
+                o0 = fmaf(pj, vv.x, o0);
+                o1 = fmaf(pj, vv.y, o1);
+            }
+            if (half == 1) {
+                reinterpret_cast<float2*>(comb + hw * kRec)[lane] = make_float2(o0, o1);
+                if (lane == 0) {
+                    comb[hw * kRec + kHeadDim] = m;
+                    comb[hw * kRec + kHeadDim + 1] = lsum;
+                }
+            }
+            __syncthreads();
+            if (half == 0) {   // fold the second half (max -inf and sum 0 when it has no rows)
+                const float m1 = comb[hw * kRec + kHeadDim], l1 = comb[hw * kRec + kHeadDim + 1];
+                const float2 p1 = reinterpret_cast<const float2*>(comb + hw * kRec)[lane];
+                const float mt = fmaxf(m, m1);
+                const float f0 = expf(m - mt), f1 = expf(m1 - mt);
+                float* R = A.partials + (static_cast<size_t>(c) * kNHead + 8 * g + hw) * kRec;
+                reinterpret_cast<float2*>(R)[lane] = make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
+                if (lane == 0) {
+                    R[kHeadDim] = mt;
+                    R[kHeadDim + 1] = lsum * f0 + l1 * f1;
+                }
+            }
+        }
+        barrier();
+        // ---- P3: x += Wo attn (forward.cpp:210-214) ----
+        stage_attention(xs, A.partials, C, E);
+        wait_buf(1);
+        __syncthreads();
+        rows_units<1>(bufB, sE, 0, ne, uE, xs, part);
+        __syncthreads();
+        if (tid < ne) A.x[r0e + tid] = ld_cg(A.x + r0e + tid) + row_total(part, tid, ne, uE);
+        barrier();
+        // ---- P4: rmsnorm + gate/up + SwiGLU (forward.cpp:216-227) ----
+        if (warp == 0) fill_down(l);   // buffer B's reads ended before the barrier
+        const float ss4 = stage_rot(xs, A.x, Ly.ffn_norm, E);
+        const float rms4 = 1.0f / sqrtf(block_sum(ss4) / static_cast<float>(E) + A.eps);
+        wait_buf(0);
+        rows_units<2>(bufA, sE, Rf, nf, uE, xs, part);
+        __syncthreads();
+        if (tid < nf) {
+            const float gg = row_total(part, tid, nf, uE) * rms4, uu = row_total(part + PT, tid, nf, uE) * rms4;
+            // silu(g) * u (ops.cpp:1107-1113 then 1129-1146)
+            A.hb[r0f + tid] = (gg * (1.0f / (1.0f + expf(-gg)))) * uu;
+        }
+        barrier();
+        // ---- P5: x += Wdown hb (forward.cpp:227-229) ----
+        if (warp == 0 && l + 1 < A.n_layers) fill_qkv(l + 1);   // buffer A's reads ended before the barrier
+        stage_rot(xs, A.hb, nullptr, FF);
+        wait_buf(1);
+        __syncthreads();
+        rows_units<1>(bufB, sF, 0, ne, uF, xs, part);
+        __syncthreads();
+        if (tid < ne) A.x[r0e + tid] = ld_cg(A.x + r0e + tid) + row_total(part, tid, ne, uF);
+        if (l + 1 < A.n_layers) barrier();
+    }
+}
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        void** args) {
     cudaLaunchConfig_t cfg{};
@@ -870,6 +1388,61 @@ int weight_row_bytes(int type, int cols) {
     case kWQ6_K: return cols % 256 ? -1 : cols / 256 * 210;
     default: return -1;
     }
+}
+
+size_t persist_smem_bytes(int n_embd, int n_ff, int grid, PersistArgs* a) {
+    if (grid <= 0 || n_embd % kUnit || n_ff % kUnit || n_embd != kNHead * kHeadDim) return 0;
+    // odd multiples of 16 bytes: eight consecutive rows' 16-byte loads fall in distinct banks
+    auto stride = [](size_t rb) { return (rb / 16) % 2 ? rb : rb + 16; };
+    const size_t rbE = n_embd / 32 * 18, rbF = n_ff / 32 * 18;
+    const size_t sE = stride(rbE), sF = stride(rbF);
+    const size_t Rq = (n_embd + 2 * kNHeadKv * kHeadDim + grid - 1) / grid;
+    const size_t Re = (n_embd + grid - 1) / grid, Rf = (n_ff + grid - 1) / grid;
+    // one (row, unit) pair per thread: every product's pairs fit one pass of the CTA
+    const size_t uE = n_embd / kUnit, uF = n_ff / kUnit;
+    if (std::max({Rq * uE, Rf * uE, Re * uE, Re * uF}) > static_cast<size_t>(PT)) return 0;
+    auto up128 = [](size_t v) { return (v + 127) / 128 * 128; };
+    const size_t xs = up128(static_cast<size_t>(std::max(n_embd, n_ff)) * sizeof(float));
+    const size_t bufA = up128(std::max(Rq, 2 * Rf) * sE);
+    const size_t bufB = up128(std::max(Re * sE, Re * sF));
+    const size_t kv = up128((2 * kAttRows * PKP + 8 * kHeadDim + 8 * kRec) * sizeof(float));
+    const size_t part = 2 * PT * sizeof(float);
+    const size_t total = xs + bufA + bufB + kv + part;
+    if (total > 220 * 1024) return 0;
+    a->stride_e = static_cast<int>(sE);
+    a->stride_f = static_cast<int>(sF);
+    a->off_a = static_cast<int>(xs);
+    a->off_b = static_cast<int>(xs + bufA);
+    a->off_kv = static_cast<int>(xs + bufA + bufB);
+    a->off_part = static_cast<int>(xs + bufA + bufB + kv);
+    return total;
+}
+
+int persist_max_chunks(int grid) { return grid / kNHeadKv; }
+
+size_t persist_workspace_bytes(int grid) {
+    return 256 + static_cast<size_t>(persist_max_chunks(grid)) * kNHead * kRec * sizeof(float);
+}
+
+cudaError_t launch_forward_persistent(const PersistArgs& a, int grid, size_t smem, cudaStream_t stream) {
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([&](int) {
+        return cudaFuncSetAttribute(forward_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    220 * 1024);
+    });
+    if (e != cudaSuccess) return e;
+    // every CTA must be resident at once (the grid barriers): a cooperative launch
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(PT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, forward_persistent_kernel, a);
 }
 
 cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream) {

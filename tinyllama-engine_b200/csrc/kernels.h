@@ -193,6 +193,48 @@ struct GemvArgs {
 };
 // Bytes of one row of `cols` weights of format `type`; -1 if unsupported.
 int weight_row_bytes(int type, int cols);
+
+// The layers of one token in one persistent cooperative launch (models
+// whose linear weights are all Q4_0): per layer five phases separated by
+// grid barriers -- RMSNorm + q/k/v, rope + attention + append, output
+// projection + residual, RMSNorm + gate/up + SwiGLU, down + residual -- with
+// each CTA's weight rows of the next products bulk-copied into shared
+// memory ahead of the barrier before the phase that reads them.
+constexpr int kPersistMaxLayers = 32;
+constexpr int kPersistAttRows = 64;   // attention rows per chunk
+struct PersistLayer {
+    const uint8_t* w[7];         // q, k, v, output, gate, up, down (Q4_0, 16-byte aligned)
+    const float* attn_norm;
+    const float* ffn_norm;
+};
+struct PersistArgs {
+    PersistLayer layer[kPersistMaxLayers];
+    int n_layers, n_embd, n_ff, n_ctx, pos;
+    float eps;
+    float* x;                    // [n_embd] residual stream
+    float* q;                    // [n_embd]
+    float* k;                    // [256]
+    float* v;                    // [256]
+    float* hb;                   // [n_ff]
+    float* key_cache;            // [n_layers][n_ctx][256]
+    float* value_cache;
+    float* partials;             // [att_chunks][32][68] attention records (o[64], max, sum)
+    uint32_t* sync;              // grid barrier count, zero at launch
+    uint32_t* err;
+    int att_chunks;              // chunks of 64 rows per KV head (ceil((pos + 1) / 64))
+    int stride_e, stride_f;      // shared-memory row strides of n_embd- and n_ff-column rows (bytes)
+    int off_a, off_b, off_kv, off_part;   // shared-memory offsets (bytes): buffers A, B, K/V, partials
+    float inv_freq[kHeadDim / 2];
+};
+// Shared memory a persistent launch over `grid` CTAs needs (fills the
+// strides and offsets of *a); 0 when the shape does not fit (then the
+// per-product launches are used).
+size_t persist_smem_bytes(int n_embd, int n_ff, int grid, PersistArgs* a);
+// Most attention chunks per KV head, and the workspace (barrier count and
+// attention records) a launch over `grid` CTAs needs.
+int persist_max_chunks(int grid);
+size_t persist_workspace_bytes(int grid);
+cudaError_t launch_forward_persistent(const PersistArgs& a, int grid, size_t smem, cudaStream_t stream);
 cudaError_t launch_gemv(int type, int epi, GemvArgs a, cudaStream_t stream);
 cudaError_t launch_embed(int type, float* x, const void* table, const int32_t* token, int n_vocab,
                          int n_embd, uint32_t* err, cudaStream_t stream);

@@ -607,7 +607,7 @@ class DeviceState:
                   "logits": z(m.n_vocab), "key_cache": z(m.n_layers * m.n_ctx * kv),
                   "value_cache": z(m.n_layers * m.n_ctx * kv)}
         nbytes = lib().tle_forward_workspace_bytes(ctypes.byref(dm.desc))
-        self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        self.workspace = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=device)
         self.desc = State(**{k: v.data_ptr() for k, v in self.t.items()},
                           workspace=self.workspace.data_ptr(), workspace_bytes=nbytes)
 
