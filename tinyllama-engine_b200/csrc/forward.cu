@@ -822,20 +822,19 @@ __global__ void __launch_bounds__(256) vec_add_kernel(float* out, const float* x
 // with a grid barrier after each phase (every product reads the whole
 // output of the one before).  CTA b owns rows [b R, (b+1) R) of every
 // product (R = ceil(rows / grid)); its rows of the products to come are
-// bulk-copied (TMA engine), one copy per row into a padded row stride, into
-// one of two shared-memory buffers before the barrier of the phase that
+// bulk-copied (TMA engine, one copy per contiguous span) into one of two shared-memory buffers before the barrier of the phase that
 // precedes their use (weights are never written, so the copies run ahead
 // freely): Wo at P1, gate/up at P2, Wdown at P4, the next layer's q/k/v at
 // P5.  Buffer A holds q/k/v and gate/up, buffer B Wo and Wdown.
 //
 // Products: a thread takes one (row, unit) pair, a unit being 8 Q4_0 blocks
 // (256 weights, 144 bytes = nine 16-byte shared loads), and writes its
-// partial; the partials of a row are then summed in unit order.  Threads of
-// a warp hold consecutive rows of one unit (at most two units per warp), so
-// the input vector is read as a broadcast, and the odd 16-byte row stride
-// puts eight consecutive rows' loads in distinct banks.  The input vector
-// is staged with its 16-byte chunks rotated by the unit index inside each
-// block (two units read by one warp hit distinct banks).  RMSNorm: x * w is
+// partial; the partials of a row are then summed in unit order.  Adjacent
+// threads hold adjacent units of a row: their 16-byte weight loads are 144
+// bytes apart (nine chunks, so eight threads cover all banks), and the input
+// vector is staged with its 16-byte chunks rotated by the unit index inside
+// each block, so eight units' reads of the same input chunk hit distinct
+// banks too.  RMSNorm: x * w is
 // staged while sum(x^2) is reduced; the row sums are scaled by 1/rms.
 //
 // Attention (P2) splits the L = pos + 1 rows of each KV head over C = L / 64
@@ -1057,13 +1056,13 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
 
 // Every (row, unit) pair of an nr-row product over `units` units, one per
 // thread (nr * units <= PT): row r of matrix m at buf + (r + m * mstride) * stride.  Partials
-// of matrix m go to part[m * PT + u * nr + r].
+// of matrix m go to part[m * PT + r * units + u] (the units of a row in adjacent threads).
 template <int M>
 __device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int mstride, int nr, int units,
                                            const float* xs, float* part) {
     const int p = threadIdx.x;   // nr * units <= PT (checked on the host)
     if (p < nr * units) {
-        const int u = p / nr, r = p - u * nr;
+        const int r = p / units, u = p - r * units;
         const uint8_t* w[M];
 #pragma unroll
         for (int m = 0; m < M; ++m)
@@ -1077,7 +1076,7 @@ __device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int m
 
 __device__ __forceinline__ float row_total(const float* part, int r, int nr, int units) {
     float y = 0.f;
-    for (int u = 0; u < units; ++u) y += part[u * nr + r];
+    for (int u = 0; u < units; ++u) y += part[r * units + u];
     return y;
 }
 
@@ -1122,41 +1121,38 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
     const bool has_new = nrows > 0 && rr0 + nrows == L;
     const int ncached = has_new ? nrows - 1 : nrows;
 
-    // warp 0: one bulk copy per row (row i of the span to dst + i * stride)
-    auto fill_rows = [&](uint8_t* dst, int stride, int n, int rb, uint64_t* bar, auto src_of) {
-        for (int i = lane; i < n; i += 32) bulk_g2s_plain(dst + static_cast<size_t>(i) * stride, src_of(i), rb, bar);
+    // lane 0 of warp 0: the CTA's rows of a product, one bulk copy per contiguous span
+    auto span = [&](uint8_t* dst, const uint8_t* src, int bytes, uint64_t* bar) {
+        if (bytes > 0) bulk_g2s_plain(dst, src, static_cast<uint32_t>(bytes), bar);
     };
     auto fill_qkv = [&](int l) {
+        if (lane) return;
         const PersistLayer& Ly = A.layer[l];
-        if (lane == 0) mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(nq * rbE));
-        __syncwarp();
-        fill_rows(bufA, sE, nq, rbE, &wbar[0], [&](int i) {
-            const int r = r0q + i;
-            const int m = r < E ? 0 : (r < E + KV ? 1 : 2);
-            const int base = m == 0 ? 0 : (m == 1 ? E : E + KV);
-            return Ly.w[m] + static_cast<size_t>(r - base) * rbE;
-        });
+        mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(nq * rbE));
+        const int a0 = r0q, a1 = r0q + nq;            // rows of [q; k; v]
+        const int q1 = min(a1, E), k0 = max(a0, E), k1 = min(a1, E + KV), v0 = max(a0, E + KV);
+        span(bufA, Ly.w[0] + static_cast<size_t>(a0) * rbE, (q1 - a0) * rbE, &wbar[0]);
+        span(bufA + static_cast<size_t>(k0 - a0) * rbE, Ly.w[1] + static_cast<size_t>(k0 - E) * rbE,
+             (k1 - k0) * rbE, &wbar[0]);
+        span(bufA + static_cast<size_t>(v0 - a0) * rbE, Ly.w[2] + static_cast<size_t>(v0 - E - KV) * rbE,
+             (a1 - v0) * rbE, &wbar[0]);
     };
     auto fill_o = [&](int l) {
-        if (lane == 0) mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbE));
-        __syncwarp();
-        const uint8_t* W = A.layer[l].w[3] + static_cast<size_t>(r0e) * rbE;
-        fill_rows(bufB, sE, ne, rbE, &wbar[1], [&](int i) { return W + static_cast<size_t>(i) * rbE; });
+        if (lane) return;
+        mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbE));
+        span(bufB, A.layer[l].w[3] + static_cast<size_t>(r0e) * rbE, ne * rbE, &wbar[1]);
     };
-    auto fill_gu = [&](int l) {
-        if (lane == 0) mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(2 * nf * rbE));
-        __syncwarp();
-        const uint8_t* Wg = A.layer[l].w[4] + static_cast<size_t>(r0f) * rbE;
-        const uint8_t* Wu = A.layer[l].w[5] + static_cast<size_t>(r0f) * rbE;
-        fill_rows(bufA, sE, nf, rbE, &wbar[0], [&](int i) { return Wg + static_cast<size_t>(i) * rbE; });
-        fill_rows(bufA + static_cast<size_t>(Rf) * sE, sE, nf, rbE, &wbar[0],
-                  [&](int i) { return Wu + static_cast<size_t>(i) * rbE; });
+    auto fill_gu = [&](int l) {   // gate rows at 0, up rows Rf rows further
+        if (lane) return;
+        mbar_arrive_expect_tx(&wbar[0], static_cast<uint32_t>(2 * nf * rbE));
+        span(bufA, A.layer[l].w[4] + static_cast<size_t>(r0f) * rbE, nf * rbE, &wbar[0]);
+        span(bufA + static_cast<size_t>(Rf) * sE, A.layer[l].w[5] + static_cast<size_t>(r0f) * rbE, nf * rbE,
+             &wbar[0]);
     };
     auto fill_down = [&](int l) {
-        if (lane == 0) mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbF));
-        __syncwarp();
-        const uint8_t* W = A.layer[l].w[6] + static_cast<size_t>(r0e) * rbF;
-        fill_rows(bufB, sF, ne, rbF, &wbar[1], [&](int i) { return W + static_cast<size_t>(i) * rbF; });
+        if (lane) return;
+        mbar_arrive_expect_tx(&wbar[1], static_cast<uint32_t>(ne * rbF));
+        span(bufB, A.layer[l].w[6] + static_cast<size_t>(r0e) * rbF, ne * rbF, &wbar[1]);
     };
     auto wait_buf = [&](int which) {
         uint32_t& u = which ? useB : useA;
@@ -1392,8 +1388,7 @@ int weight_row_bytes(int type, int cols) {
 
 size_t persist_smem_bytes(int n_embd, int n_ff, int grid, PersistArgs* a) {
     if (grid <= 0 || n_embd % kUnit || n_ff % kUnit || n_embd != kNHead * kHeadDim) return 0;
-    // odd multiples of 16 bytes: eight consecutive rows' 16-byte loads fall in distinct banks
-    auto stride = [](size_t rb) { return (rb / 16) % 2 ? rb : rb + 16; };
+    auto stride = [](size_t rb) { return rb; };   // rows back to back (one bulk copy per span)
     const size_t rbE = n_embd / 32 * 18, rbF = n_ff / 32 * 18;
     const size_t sE = stride(rbE), sF = stride(rbF);
     const size_t Rq = (n_embd + 2 * kNHeadKv * kHeadDim + grid - 1) / grid;
