@@ -853,6 +853,10 @@ constexpr int kUnitBytes = 144;       // Q4_0 bytes per unit
 constexpr int kRec = 68;              // floats per attention record: o[64], max, sum, 2 pad
 constexpr int kAttRows = kPersistAttRows;
 
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -932,6 +936,42 @@ __device__ __forceinline__ float stage_rot(float* xs, const float* x, const floa
 __device__ __forceinline__ void stage_attention(float* xs, const float* rec, int n_chunks, int n_embd) {
     for (int i = threadIdx.x; i < (n_embd >> 2); i += PT) {
         const int h = i >> 4, d0 = 4 * (i & 15);
+        if (n_chunks <= 8) {   // every record load in flight at once (one L2 round trip)
+            float mc[8], lc[8];
+            float4 oc[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                mc[c] = -INFINITY;
+                lc[c] = 0.f;
+                oc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c < n_chunks) {
+                    const float* R = rec + (c * kNHead + h) * kRec;
+                    mc[c] = ld_cg(R + kHeadDim);
+                    lc[c] = ld_cg(R + kHeadDim + 1);
+                    oc[c] = ld_cg4(reinterpret_cast<const float4*>(R + d0));
+                }
+            }
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) mt = fmaxf(mt, mc[c]);
+            float lt = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if (c < n_chunks) {
+                    const float f = expf(mc[c] - mt);
+                    lt = fmaf(lc[c], f, lt);
+                    acc.x = fmaf(oc[c].x, f, acc.x);
+                    acc.y = fmaf(oc[c].y, f, acc.y);
+                    acc.z = fmaf(oc[c].z, f, acc.z);
+                    acc.w = fmaf(oc[c].w, f, acc.w);
+                }
+            }
+            const float inv = 1.0f / lt;
+            *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            continue;
+        }
         float mt = -INFINITY;
         for (int c = 0; c < n_chunks; ++c) mt = fmaxf(mt, ld_cg(rec + (c * kNHead + h) * kRec + kHeadDim));
         float lt = 0.f;
@@ -1198,96 +1238,136 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
         wait_buf(0);
         rows_units<1>(bufA, sE, 0, nq, uE, xs, part);
         __syncthreads();
-        if (tid < nq) {
-            const float y = row_total(part, tid, nq, uE) * rms1;
+        {
+            // rope on the q and k rows here (ops.cpp:1223): a pair (2i, 2i + 1)
+            // sits in adjacent threads (r0q is even); q also takes 1 / sqrt(64)
+            float y = tid < nq ? row_total(part, tid, nq, uE) * rms1 : 0.f;
             const int r = r0q + tid;
-            if (r < E) A.q[r] = y;
-            else if (r < E + KV) A.k[r - E] = y;
-            else A.v[r - E - KV] = y;
+            float partner = 0.f;
+            if (warp < (nq + 31) / 32) partner = __shfl_xor_sync(0xffffffffu, y, 1);
+            if (tid < nq) {
+                if (r < E + KV) {
+                    float sn, cs;
+                    sincosf(static_cast<float>(A.pos) * A.inv_freq[(r & (kHeadDim - 1)) >> 1], &sn, &cs);
+                    const float x0 = (r & 1) ? partner : y, x1 = (r & 1) ? y : partner;
+                    y = (r & 1) ? x0 * sn + x1 * cs : x0 * cs - x1 * sn;
+                }
+                if (r < E) A.q[r] = y * 0.125f;
+                else if (r < E + KV) A.k[r - E] = y;
+                else A.v[r - E - KV] = y;
+            }
         }
         barrier();
         // ---- P2: rope + attention + append (forward.cpp:198-208, ops.cpp:1223/1317) ----
         if (warp == 0) fill_gu(l);   // buffer A's reads ended before the barrier
         if (att) {
             asm volatile("cp.async.wait_all;" ::: "memory");
-            if (warp < 8) {   // warp w: rotate query head 8 g + w
+            if (warp < 8) {   // warp w: query head 8 g + w (rotated and scaled in P1)
                 const int p = lane;
-                float sn, cs;
-                sincosf(static_cast<float>(A.pos) * A.inv_freq[p], &sn, &cs);
-                const int h = 8 * g + warp;
-                const float x0 = ld_cg(A.q + h * kHeadDim + 2 * p), x1 = ld_cg(A.q + h * kHeadDim + 2 * p + 1);
-                qs[warp * kHeadDim + 2 * p] = (x0 * cs - x1 * sn) * 0.125f;
-                qs[warp * kHeadDim + 2 * p + 1] = (x0 * sn + x1 * cs) * 0.125f;
-                if (has_new && warp < 2) {
+                const bool kv_row = has_new && warp < 2;   // warp 0 appends k, warp 1 v (rotated in P1)
+                const float* qsrc = A.q + (8 * g + warp) * kHeadDim + 2 * p;
+                const float* nsrc = (warp == 0 ? A.k : A.v) + g * kHeadDim + 2 * p;
+                const float x0 = ld_cg(qsrc), x1 = ld_cg(qsrc + 1);
+                const float n0 = kv_row ? ld_cg(nsrc) : 0.f, n1 = kv_row ? ld_cg(nsrc + 1) : 0.f;
+                qs[warp * kHeadDim + 2 * p] = x0;
+                qs[warp * kHeadDim + 2 * p + 1] = x1;
+                if (kv_row) {   // keep, append (ops.cpp:1370-1371)
                     const size_t row = lbase + static_cast<size_t>(A.pos) * KV + g * kHeadDim;
-                    if (warp == 0) {   // k: rotate, keep, append (ops.cpp:1370)
-                        const float k0 = ld_cg(A.k + g * kHeadDim + 2 * p), k1 = ld_cg(A.k + g * kHeadDim + 2 * p + 1);
-                        const float y0 = k0 * cs - k1 * sn, y1 = k0 * sn + k1 * cs;
-                        ks[(nrows - 1) * PKP + 2 * p] = y0;
-                        ks[(nrows - 1) * PKP + 2 * p + 1] = y1;
-                        A.key_cache[row + 2 * p] = y0;
-                        A.key_cache[row + 2 * p + 1] = y1;
-                    } else {           // v (ops.cpp:1371)
-                        const float v0 = ld_cg(A.v + g * kHeadDim + 2 * p), v1 = ld_cg(A.v + g * kHeadDim + 2 * p + 1);
-                        vs[(nrows - 1) * PKP + 2 * p] = v0;
-                        vs[(nrows - 1) * PKP + 2 * p + 1] = v1;
-                        A.value_cache[row + 2 * p] = v0;
-                        A.value_cache[row + 2 * p + 1] = v1;
+                    float* sm = (warp == 0 ? ks : vs) + (nrows - 1) * PKP + 2 * p;
+                    float* gl = (warp == 0 ? A.key_cache : A.value_cache) + row + 2 * p;
+                    sm[0] = n0;
+                    sm[1] = n1;
+                    gl[0] = n0;
+                    gl[1] = n1;
+                }
+            }
+            __syncthreads();
+            // warps 0-7: query heads 2 hp, 2 hp + 1 (hp = w & 3) over rows
+            // [32 half, 32 half + 32) of the chunk (half = w >> 2); each K/V row
+            // read from shared memory serves both heads
+            if (warp < 8) {
+                const int hp = warp & 3, half = warp >> 2;
+                const float4* qa = reinterpret_cast<const float4*>(qs + (2 * hp) * kHeadDim);   // broadcast reads
+                const float4* qb = reinterpret_cast<const float4*>(qs + (2 * hp + 1) * kHeadDim);
+                const int r = 32 * half + lane;
+                float sa = -INFINITY, sb = -INFINITY;
+                if (r < nrows) {
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float4 kk = *reinterpret_cast<const float4*>(&ks[r * PKP + 4 * i]);
+                        const float4 x = qa[i], y = qb[i];
+                        a0 = fmaf(x.x, kk.x, a0);
+                        a1 = fmaf(x.y, kk.y, a1);
+                        a2 = fmaf(x.z, kk.z, a2);
+                        a3 = fmaf(x.w, kk.w, a3);
+                        b0 = fmaf(y.x, kk.x, b0);
+                        b1 = fmaf(y.y, kk.y, b1);
+                        b2 = fmaf(y.z, kk.z, b2);
+                        b3 = fmaf(y.w, kk.w, b3);
+                    }
+                    sa = (a0 + a1) + (a2 + a3);
+                    sb = (b0 + b1) + (b2 + b3);
+                }
+                float ma = sa, mb = sb;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+                    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+                }
+                const float pa = (sa == -INFINITY) ? 0.f : expf(sa - ma);
+                const float pb = (sb == -INFINITY) ? 0.f : expf(sb - mb);
+                float la = pa, lb = pb;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    la += __shfl_xor_sync(0xffffffffu, la, o);
+                    lb += __shfl_xor_sync(0xffffffffu, lb, o);
+                }
+                float oa0 = 0.f, oa1 = 0.f, ob0 = 0.f, ob1 = 0.f;
+                const int nb = max(0, min(32, nrows - 32 * half));
+                for (int j0 = 0; j0 < nb; j0 += 8) {   // eight rows' shuffles and loads in flight
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int j = j0 + jj;   // < 32
+                        const float wa = __shfl_sync(0xffffffffu, pa, j), wb = __shfl_sync(0xffffffffu, pb, j);
+                        const float2 vv = *reinterpret_cast<const float2*>(&vs[(32 * half + j) * PKP + 2 * lane]);
+                        if (j < nb) {
+                            oa0 = fmaf(wa, vv.x, oa0);
+                            oa1 = fmaf(wa, vv.y, oa1);
+                            ob0 = fmaf(wb, vv.x, ob0);
+                            ob1 = fmaf(wb, vv.y, ob1);
+                        }
                     }
                 }
-            }
-            __syncthreads();
-            // warp w: head 8 g + (w & 7) over rows [32 half, 32 half + 32) of the chunk
-            const int hw = warp & 7, half = warp >> 3;
-            const float4* q4 = reinterpret_cast<const float4*>(qs + hw * kHeadDim);   // broadcast reads
-            const int r = 32 * half + lane;
-            float sc = -INFINITY;
-            if (r < nrows) {
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float4 kk = *reinterpret_cast<const float4*>(&ks[r * PKP + 4 * i]);
-                    const float4 qq = q4[i];
-                    a0 = fmaf(qq.x, kk.x, a0);
-                    a1 = fmaf(qq.y, kk.y, a1);
-                    a2 = fmaf(qq.z, kk.z, a2);
-                    a3 = fmaf(qq.w, kk.w, a3);
+                float* ca = comb + (2 * hp) * kRec;
+                float* cb = comb + (2 * hp + 1) * kRec;
+                if (half == 1) {
+                    reinterpret_cast<float2*>(ca)[lane] = make_float2(oa0, oa1);
+                    reinterpret_cast<float2*>(cb)[lane] = make_float2(ob0, ob1);
+                    if (lane == 0) {
+                        ca[kHeadDim] = ma;
+                        ca[kHeadDim + 1] = la;
+                        cb[kHeadDim] = mb;
+                        cb[kHeadDim + 1] = lb;
+                    }
                 }
-                sc = (a0 + a1) + (a2 + a3);
-            }
-            float m = sc;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float pr = (sc == -INFINITY) ? 0.f : expf(sc - m);
-            float lsum = pr;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-            float o0 = 0.f, o1 = 0.f;
-            const int nb = max(0, min(32, nrows - 32 * half));
-            for (int j = 0; j < nb; ++j) {
-                const float pj = __shfl_sync(0xffffffffu, pr, j);
-                const float2 vv = *reinterpret_cast<const float2*>(&vs[(32 * half + j) * PKP + 2 * lane]);
-                o0 = fmaf(pj, vv.x, o0);
-                o1 = fmaf(pj, vv.y, o1);
-            }
-            if (half == 1) {
-                reinterpret_cast<float2*>(comb + hw * kRec)[lane] = make_float2(o0, o1);
-                if (lane == 0) {
-                    comb[hw * kRec + kHeadDim] = m;
-                    comb[hw * kRec + kHeadDim + 1] = lsum;
-                }
-            }
-            __syncthreads();
-            if (half == 0) {   // fold the second half (max -inf and sum 0 when it has no rows)
-                const float m1 = comb[hw * kRec + kHeadDim], l1 = comb[hw * kRec + kHeadDim + 1];
-                const float2 p1 = reinterpret_cast<const float2*>(comb + hw * kRec)[lane];
-                const float mt = fmaxf(m, m1);
-                const float f0 = expf(m - mt), f1 = expf(m1 - mt);
-                float* R = A.partials + (static_cast<size_t>(c) * kNHead + 8 * g + hw) * kRec;
-                reinterpret_cast<float2*>(R)[lane] = make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
-                if (lane == 0) {
-                    R[kHeadDim] = mt;
-                    R[kHeadDim + 1] = lsum * f0 + l1 * f1;
+                __syncwarp();
+                named_barrier_sync(1, 256);   // warps 0-7
+                if (half == 0) {   // fold the second half (max -inf and sum 0 when it has no rows)
+                    auto fold = [&](const float* cc, float m, float lsum, float o0, float o1, int hl) {
+                        const float m1 = cc[kHeadDim], l1 = cc[kHeadDim + 1];
+                        const float2 p1 = reinterpret_cast<const float2*>(cc)[lane];
+                        const float mt = fmaxf(m, m1);
+                        const float f0 = expf(m - mt), f1 = expf(m1 - mt);
+                        float* R = A.partials + (static_cast<size_t>(c) * kNHead + 8 * g + hl) * kRec;
+                        reinterpret_cast<float2*>(R)[lane] = make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
+                        if (lane == 0) {
+                            R[kHeadDim] = mt;
+                            R[kHeadDim + 1] = lsum * f0 + l1 * f1;
+                        }
+                    };
+                    fold(ca, ma, la, oa0, oa1, 2 * hp);
+                    fold(cb, mb, lb, ob0, ob1, 2 * hp + 1);
                 }
             }
         }
@@ -1396,6 +1476,7 @@ size_t persist_smem_bytes(int n_embd, int n_ff, int grid, PersistArgs* a) {
     // one (row, unit) pair per thread: every product's pairs fit one pass of the CTA
     const size_t uE = n_embd / kUnit, uF = n_ff / kUnit;
     if (std::max({Rq * uE, Rf * uE, Re * uE, Re * uF}) > static_cast<size_t>(PT)) return 0;
+    if (Rq % 2) return 0;   // rope pairs must not straddle two CTAs
     auto up128 = [](size_t v) { return (v + 127) / 128 * 128; };
     const size_t xs = up128(static_cast<size_t>(std::max(n_embd, n_ff)) * sizeof(float));
     const size_t bufA = up128(std::max(Rq, 2 * Rf) * sE);
