@@ -837,9 +837,9 @@ def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, 
     RMSNorm weights 1.0): a 128-token prompt of random ids fed token by token
     (as generate.cpp:56-59 does), then 256 tokens, each the argmax of the
     previous logits, sampled on the device.  Every position runs as one
-    CUDA graph (embedding, 22 x [RMSNorm+q/k/v, rope+attention, output
-    projection+residual, RMSNorm+SwiGLU, down projection+residual], RMSNorm+LM
-    head, argmax) captured once; the token of step t+1 never leaves the
+    CUDA graph (embedding, the 22 layers [RMSNorm+q/k/v, rope+attention,
+    output projection+residual, RMSNorm+SwiGLU, down projection+residual] in
+    one persistent launch, RMSNorm+LM head, argmax) captured once; the token of step t+1 never leaves the
     device.  Timed with CUDA events over whole generations."""
     import numpy as np
     import torch
@@ -854,6 +854,7 @@ def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, 
     toks = torch.zeros(n_ctx + 1, dtype=torch.int32, device=dev)
     toks[:prompt] = torch.from_numpy(ids.astype(np.int32)).to(dev)
     side = torch.cuda.Stream(dev)
+    one_launch = lambda p: tle.forward_layers_one_launch(dm, ds, p)  # noqa: E731
 
     def step(pos, st):
         tle.forward(dm, ds, toks[pos:pos + 1], pos, st)
@@ -928,9 +929,10 @@ def measure_config2(dev, peaks, steps=1, warmup=1, prompt=128, gen=256, seed=2, 
             "cpu_reference": {"kind": kind, "cores": cores, "value": round(1.0 / cpu_s, 3),
                               "unit": "tok/s",
                               "sample": "%d prompt tokens through the 22-layer model" % cpu_tokens},
-            # per generated token: embedding, 22 x (q/k/v, decode, split-K merge,
-            # output projection, gate/up, down), LM head, argmax
-            "gpu_launches": (3 + 22 * 6) * gen * runs}
+            # per generated token: embedding, the layers (one persistent launch,
+            # else 22 x (q/k/v, decode, split-K merge, output projection,
+            # gate/up, down)), LM head, argmax
+            "gpu_launches": sum(3 + (1 if one_launch(p) else 22 * 6) for p in range(prompt, n_ctx)) * runs}
 
 
 def measure_prompt2(dev, peaks, steps=5, warmup=3, prompts=(128, 2048), seed=2):

@@ -119,6 +119,13 @@ typedef struct {
 /* Scratch tle_forward needs (the attention split-K partials). */
 size_t tle_forward_workspace_bytes(const tle_model_t* model);
 
+/* 1 when tle_forward(model, state, token, pos) on the current device runs
+ * all layers in one persistent launch (every linear weight Q4_0, widths
+ * multiples of 256, the pos + 1 cached rows within the launch's attention
+ * split, cooperative launch supported), 0 when it launches product by
+ * product.  Either way the results agree with forward() (forward.cpp:172). */
+int tle_forward_layers_one_launch(const tle_model_t* model, const tle_state_t* state, int pos);
+
 /* forward(model, state, token, pos) forward.h:16 for the token *token
  * (device int32, so a device-side sampler can feed the next step) at
  * position pos: appends row pos of every layer's cache and leaves the

@@ -805,31 +805,37 @@ namespace {
 // of pos + 1 rows in at most SMs / 4 chunks of 64 rows per KV head, the
 // workspace large enough, cooperative launch supported.  Otherwise *used
 // stays false and the caller launches product by product.
-int forward_layers_persistent(const tle_model_t* m, const tle_state_t* s, int pos, uint32_t* err,
-                              cudaStream_t st, bool* used) {
-    *used = false;
-    if (m->n_layers > tle::kPersistMaxLayers) return 0;
+bool persist_plan(const tle_model_t* m, const tle_state_t* s, int pos, int* grid, size_t* smem, int* chunks,
+                  tle::PersistArgs* a) {
+    if (m->n_layers > tle::kPersistMaxLayers) return false;
     for (int l = 0; l < m->n_layers; ++l) {
         const tle_layer_t& L = m->layers[l];
         const tle_weight_t* w[7] = {&L.attn_q, &L.attn_k, &L.attn_v, &L.attn_output, &L.ffn_gate, &L.ffn_up,
                                     &L.ffn_down};
         for (const tle_weight_t* x : w)
-            if (x->type != TLE_W_Q4_0 || !x->data || !aligned16(x->data)) return 0;
-        if (!L.attn_norm || !L.ffn_norm) return 0;
+            if (x->type != TLE_W_Q4_0 || !x->data || !aligned16(x->data)) return false;
+        if (!L.attn_norm || !L.ffn_norm) return false;
     }
     int dev = 0, coop = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop)
-        return 0;
-    const int grid = sm_count();
+        return false;
+    *grid = sm_count();
+    *smem = tle::persist_smem_bytes(m->n_embd, m->n_ff, *grid, a);
+    if (!*smem) return false;
+    *chunks = (pos + 1 + tle::kPersistAttRows - 1) / tle::kPersistAttRows;
+    if (*chunks > tle::persist_max_chunks(*grid)) return false;
+    return s->workspace && s->workspace_bytes >= tle::persist_workspace_bytes(*grid) &&
+           (reinterpret_cast<uintptr_t>(s->workspace) & 255u) == 0;
+}
+
+int forward_layers_persistent(const tle_model_t* m, const tle_state_t* s, int pos, uint32_t* err,
+                              cudaStream_t st, bool* used) {
+    *used = false;
+    int grid = 0, chunks = 0;
+    size_t smem = 0;
     tle::PersistArgs a{};
-    const size_t smem = tle::persist_smem_bytes(m->n_embd, m->n_ff, grid, &a);
-    if (!smem) return 0;
-    const int chunks = (pos + 1 + tle::kPersistAttRows - 1) / tle::kPersistAttRows;
-    if (chunks > tle::persist_max_chunks(grid)) return 0;
-    if (!s->workspace || s->workspace_bytes < tle::persist_workspace_bytes(grid) ||
-        (reinterpret_cast<uintptr_t>(s->workspace) & 255u) != 0)
-        return 0;
+    if (!persist_plan(m, s, pos, &grid, &smem, &chunks, &a)) return 0;
     for (int l = 0; l < m->n_layers; ++l) {
         const tle_layer_t& Ly = m->layers[l];
         const tle_weight_t* w[7] = {&Ly.attn_q, &Ly.attn_k, &Ly.attn_v, &Ly.attn_output, &Ly.ffn_gate, &Ly.ffn_up,
@@ -871,6 +877,14 @@ int forward_layers_persistent(const tle_model_t* m, const tle_state_t* s, int po
 }  // namespace
 
 extern "C" {
+
+int tle_forward_layers_one_launch(const tle_model_t* m, const tle_state_t* s, int pos) {
+    if (!m || !s || pos < 0 || pos >= m->n_ctx) return 0;
+    int grid = 0, chunks = 0;
+    size_t smem = 0;
+    tle::PersistArgs a{};
+    return persist_plan(m, s, pos, &grid, &smem, &chunks, &a) ? 1 : 0;
+}
 
 size_t tle_forward_workspace_bytes(const tle_model_t* model) {
     if (!model || model->n_ctx <= 0) return 0;

@@ -43,7 +43,7 @@ EXPORTED = (
     "tle_decode_desc_paged", "tle_decode_batch_paged",
     # include/tle_forward.h
     "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
-    "tle_forward_workspace_bytes", "tle_forward", "tle_sample_temperature", "tle_sample_top_p",
+    "tle_forward_workspace_bytes", "tle_forward", "tle_forward_layers_one_launch", "tle_sample_temperature", "tle_sample_top_p",
     "tle_prompt_weights_bytes", "tle_prompt_pack_weights", "tle_prompt_scratch_bytes",
     "tle_prompt_forward",
 )
@@ -152,6 +152,8 @@ def lib() -> ctypes.CDLL:
         L.tle_sample_argmax.argtypes = [vp, i, vp, vp]
         L.tle_forward_workspace_bytes.argtypes = [P(Model)]
         L.tle_forward_workspace_bytes.restype = sz
+        L.tle_forward_layers_one_launch.argtypes = [P(Model), P(State), i]
+        L.tle_forward_layers_one_launch.restype = i
         L.tle_forward.argtypes = [P(Model), P(State), vp, i, vp]
         L.tle_sample_temperature.argtypes = [vp, i, f, f, vp, vp]
         L.tle_sample_top_p.argtypes = [vp, i, f, f, f, vp, vp]
@@ -658,6 +660,12 @@ def prompt_forward(dm: DeviceModel, ds: DeviceState, pw: PromptWeights, tokens, 
     _check(lib().tle_prompt_forward(ctypes.byref(dm.desc), _ptr(pw.buf), ctypes.byref(ds.desc),
                                     _ptr(tokens), n, pos0, _ptr(scratch),
                                     scratch.numel() * scratch.element_size(), _stream(stream)))
+
+
+def forward_layers_one_launch(dm: DeviceModel, ds: DeviceState, pos: int) -> bool:
+    """Whether forward() at this position runs every layer in one persistent
+    launch (else one launch per product)."""
+    return bool(lib().tle_forward_layers_one_launch(ctypes.byref(dm.desc), ctypes.byref(ds.desc), pos))
 
 
 def forward(dm: DeviceModel, ds: DeviceState, token, pos: int, stream=None) -> None:
