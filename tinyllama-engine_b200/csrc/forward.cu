@@ -899,9 +899,31 @@ __device__ __forceinline__ int xs_phys(int f) {
     return (f & ~31) | (((((f >> 2) + (f >> 8)) & 7)) << 2) | (f & 3);
 }
 
-// Stages x (times w when w is given) into xs in the rotated layout; returns
-// this thread's share of sum(x^2).  cols % 256 == 0.
-__device__ __forceinline__ float stage_rot(float* xs, const float* x, const float* w, int cols) {
+// The products read the staged input scaled by 2^100 and each weight as the
+// subnormal float n * 2^-149 (one byte permute, exact): a product is then
+// n x 2^-49, a normal float for any |x| in [2^-77, 2^27], and the Q4_0
+// offset is taken per block, sum((n - 8) x) = sum(n x) - 8 sum(x), with
+// 8 sum(x) 2^-49 precomputed here (bs).  Row sums are scaled back by 2^49.
+constexpr float kXScale = 0x1p100f;
+constexpr float kBlockSumScale = 0x1p-146f;   // 8 * 2^-149
+constexpr float kRowScale = 0x1p49f;
+
+// Lanes 8k..8k+7 stage the eight float4 of one 32-input block (i is
+// warp-uniform in range): t scaled into xs, the block's 8 sum(x) 2^-49 into
+// bs[i / 8].
+__device__ __forceinline__ void stage_store(float* xs, float* bs, int i, float4 t) {
+    t = make_float4(t.x * kXScale, t.y * kXScale, t.z * kXScale, t.w * kXScale);
+    *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) = t;
+    float sum = (t.x + t.y) + (t.z + t.w);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if ((i & 7) == 0) bs[i >> 3] = sum * kBlockSumScale;
+}
+
+// Stages x (times w when w is given) into xs in the rotated layout, with
+// the block sums; returns this thread's share of sum(x^2).  cols % 256 == 0.
+__device__ __forceinline__ float stage_rot(float* xs, float* bs, const float* x, const float* w, int cols) {
     float ss = 0.f;
     const int n4 = cols >> 2;
     for (int base = threadIdx.x; base < n4; base += 2 * PT) {
@@ -924,7 +946,7 @@ __device__ __forceinline__ float stage_rot(float* xs, const float* x, const floa
                 ss = fmaf(t.z, t.z, ss);
                 ss = fmaf(t.w, t.w, ss);
                 if (w) t = make_float4(t.x * g[j].x, t.y * g[j].y, t.z * g[j].z, t.w * g[j].w);
-                *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) = t;
+                stage_store(xs, bs, i, t);
             }
         }
     }
@@ -933,7 +955,7 @@ __device__ __forceinline__ float stage_rot(float* xs, const float* x, const floa
 
 // The attention output (32 heads x 64) folded from the chunk records, in
 // chunk order (max first, then the rescaled sums), staged rotated into xs.
-__device__ __forceinline__ void stage_attention(float* xs, const float* rec, int n_chunks, int n_embd) {
+__device__ __forceinline__ void stage_attention(float* xs, float* bs, const float* rec, int n_chunks, int n_embd) {
     for (int i = threadIdx.x; i < (n_embd >> 2); i += PT) {
         const int h = i >> 4, d0 = 4 * (i & 15);
         if (n_chunks <= 8) {   // every record load in flight at once (one L2 round trip)
@@ -968,8 +990,7 @@ __device__ __forceinline__ void stage_attention(float* xs, const float* rec, int
                 }
             }
             const float inv = 1.0f / lt;
-            *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            stage_store(xs, bs, i, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
             continue;
         }
         float mt = -INFINITY;
@@ -1008,20 +1029,21 @@ __device__ __forceinline__ void stage_attention(float* xs, const float* rec, int
             acc.w = fmaf(o.w, f, acc.w);
         }
         const float inv = 1.0f / lt;
-        *reinterpret_cast<float4*>(xs + xs_phys(4 * i)) =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        stage_store(xs, bs, i, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
     }
 }
 
 // One unit (8 Q4_0 blocks) of M rows against the staged input: w[m] is the
-// unit's first byte in row m (16-byte aligned), xu the unit's 256 inputs,
-// rot = unit index mod 8.  A 32-byte window (chunks k, k + 1) holds block k
-// at window byte 2k.  Per block: the 32 products as packed f32x2 FMAs (the
-// byte permute builds 2^23 + n exactly, one packed subtract removes
-// 2^23 + 8), the block sum scaled by d as the reference does per block
-// (ops.cpp:495 matmul_q4_0).
+// unit's first byte in row m (16-byte aligned), xu the unit's 256 staged
+// inputs, bu its 8 block sums, rot = unit index mod 8.  A 32-byte window
+// (chunks k, k + 1) holds block k at window byte 2k.  Per block: low
+// nibbles masked in place (0x0F), high nibbles masked in place (0xF0, so
+// 16 n: their sum is scaled by 1/16), each byte moved into an otherwise
+// zero word (the subnormal n 2^-149), products as packed f32x2 FMAs; the
+// block sum less the precomputed offset term, scaled by d as the reference
+// does per block (ops.cpp:495 matmul_q4_0).  The result carries 2^-49.
 template <int M>
-__device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const float* xu, int rot,
+__device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const float* xu, const float* bu, int rot,
                                             float (&out)[M]) {
     uint32_t win[M][8];
 #pragma unroll
@@ -1033,7 +1055,6 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
         win[m][3] = c0.w;
         out[m] = 0.f;
     }
-    const uint64_t magic = pk2(-8388616.0f, -8388616.0f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
 #pragma unroll
@@ -1046,9 +1067,10 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
         }
         const int r0 = 2 * k;             // block k's first window byte
         const int w0 = (r0 + 2) >> 2;     // first window word holding its nibbles
+        const float off = bu[k];
         float d[M];
         uint32_t lo[M][5], hi[M][5];
-        uint64_t s2a[M], s2b[M];
+        uint64_t sl[M], sh[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) {
             const uint32_t dw = win[m][r0 >> 2];
@@ -1057,9 +1079,9 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
             for (int j = 0; j < 5; ++j) {
                 const uint32_t v = (w0 + j < 8) ? win[m][w0 + j] : 0u;
                 lo[m][j] = v & 0x0F0F0F0Fu;
-                hi[m][j] = (v >> 4) & 0x0F0F0F0Fu;
+                hi[m][j] = v & 0xF0F0F0F0u;
             }
-            s2a[m] = s2b[m] = 0ull;
+            sl[m] = sh[m] = 0ull;
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {   // inputs 4i..4i+3 of the block
@@ -1070,19 +1092,18 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
                 for (int e = 0; e < 4; e += 2) {
                     const int p0 = r0 + 2 + (i & 3) * 4 + e, p1 = p0 + 1;   // window bytes of the two weights
                     const uint32_t* src = (i < 4) ? lo[m] : hi[m];
-                    const float a = __int_as_float(__byte_perm(src[(p0 >> 2) - w0], 0x4B000000u, 0x7540u | (p0 & 3)));
-                    const float b = __int_as_float(__byte_perm(src[(p1 >> 2) - w0], 0x4B000000u, 0x7540u | (p1 & 3)));
-                    const uint64_t nn = add2(pk2(a, b), magic);
+                    const float a = __int_as_float(__byte_perm(src[(p0 >> 2) - w0], 0u, 0x4440u | (p0 & 3)));
+                    const float b = __int_as_float(__byte_perm(src[(p1 >> 2) - w0], 0u, 0x4440u | (p1 & 3)));
                     const uint64_t xx = e == 0 ? pk2(xv.x, xv.y) : pk2(xv.z, xv.w);
-                    if (i & 1) s2b[m] = fma2(nn, xx, s2b[m]);
-                    else s2a[m] = fma2(nn, xx, s2a[m]);
+                    if (i < 4) sl[m] = fma2(pk2(a, b), xx, sl[m]);
+                    else sh[m] = fma2(pk2(a, b), xx, sh[m]);
                 }
             }
         }
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-            const float2 sa = up2(s2a[m]), sb = up2(s2b[m]);
-            out[m] = fmaf(d[m], (sa.x + sa.y) + (sb.x + sb.y), out[m]);
+            const float2 a = up2(sl[m]), b = up2(sh[m]);
+            out[m] = fmaf(d[m], fmaf(b.x + b.y, 0.0625f, a.x + a.y) - off, out[m]);
         }
 #pragma unroll
         for (int m = 0; m < M; ++m) {
@@ -1099,7 +1120,7 @@ __device__ __forceinline__ void unit_dot_q4(const uint8_t* const (&w)[M], const 
 // of matrix m go to part[m * PT + r * units + u] (the units of a row in adjacent threads).
 template <int M>
 __device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int mstride, int nr, int units,
-                                           const float* xs, float* part) {
+                                           const float* xs, const float* bs, float* part) {
     const int p = threadIdx.x;   // nr * units <= PT (checked on the host)
     if (p < nr * units) {
         const int r = p / units, u = p - r * units;
@@ -1108,7 +1129,7 @@ __device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int m
         for (int m = 0; m < M; ++m)
             w[m] = buf + static_cast<size_t>(r + m * mstride) * stride + u * kUnitBytes;
         float y[M];
-        unit_dot_q4<M>(w, xs + u * kUnit, u & 7, y);
+        unit_dot_q4<M>(w, xs + u * kUnit, bs + 8 * u, u & 7, y);
 #pragma unroll
         for (int m = 0; m < M; ++m) part[m * PT + p] = y[m];
     }
@@ -1117,7 +1138,7 @@ __device__ __forceinline__ void rows_units(const uint8_t* buf, int stride, int m
 __device__ __forceinline__ float row_total(const float* part, int r, int nr, int units) {
     float y = 0.f;
     for (int u = 0; u < units; ++u) y += part[r * units + u];
-    return y;
+    return y * kRowScale;
 }
 
 __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_constant__ PersistArgs A) {
@@ -1132,6 +1153,7 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
     float* part = reinterpret_cast<float*>(psm + A.off_part);   // 2 x PT
     __shared__ __align__(8) uint64_t wbar[2];
     __shared__ float red[PW];
+    __shared__ float bsum[kPersistMaxBlocks];   // per 32-input block: 8 sum(x) 2^-49 of the staged input
     __shared__ int failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
@@ -1233,10 +1255,10 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
         }
-        const float ss1 = stage_rot(xs, A.x, Ly.attn_norm, E);
+        const float ss1 = stage_rot(xs, bsum, A.x, Ly.attn_norm, E);
         const float rms1 = 1.0f / sqrtf(block_sum(ss1) / static_cast<float>(E) + A.eps);
         wait_buf(0);
-        rows_units<1>(bufA, sE, 0, nq, uE, xs, part);
+        rows_units<1>(bufA, sE, 0, nq, uE, xs, bsum, part);
         __syncthreads();
         {
             // rope on the q and k rows here (ops.cpp:1223): a pair (2i, 2i + 1)
@@ -1373,19 +1395,19 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
         }
         barrier();
         // ---- P3: x += Wo attn (forward.cpp:210-214) ----
-        stage_attention(xs, A.partials, C, E);
+        stage_attention(xs, bsum, A.partials, C, E);
         wait_buf(1);
         __syncthreads();
-        rows_units<1>(bufB, sE, 0, ne, uE, xs, part);
+        rows_units<1>(bufB, sE, 0, ne, uE, xs, bsum, part);
         __syncthreads();
         if (tid < ne) A.x[r0e + tid] = ld_cg(A.x + r0e + tid) + row_total(part, tid, ne, uE);
         barrier();
         // ---- P4: rmsnorm + gate/up + SwiGLU (forward.cpp:216-227) ----
         if (warp == 0) fill_down(l);   // buffer B's reads ended before the barrier
-        const float ss4 = stage_rot(xs, A.x, Ly.ffn_norm, E);
+        const float ss4 = stage_rot(xs, bsum, A.x, Ly.ffn_norm, E);
         const float rms4 = 1.0f / sqrtf(block_sum(ss4) / static_cast<float>(E) + A.eps);
         wait_buf(0);
-        rows_units<2>(bufA, sE, Rf, nf, uE, xs, part);
+        rows_units<2>(bufA, sE, Rf, nf, uE, xs, bsum, part);
         __syncthreads();
         if (tid < nf) {
             const float gg = row_total(part, tid, nf, uE) * rms4, uu = row_total(part + PT, tid, nf, uE) * rms4;
@@ -1395,10 +1417,10 @@ __global__ void __launch_bounds__(PT, 1) forward_persistent_kernel(const __grid_
         barrier();
         // ---- P5: x += Wdown hb (forward.cpp:227-229) ----
         if (warp == 0 && l + 1 < A.n_layers) fill_qkv(l + 1);   // buffer A's reads ended before the barrier
-        stage_rot(xs, A.hb, nullptr, FF);
+        stage_rot(xs, bsum, A.hb, nullptr, FF);
         wait_buf(1);
         __syncthreads();
-        rows_units<1>(bufB, sF, 0, ne, uF, xs, part);
+        rows_units<1>(bufB, sF, 0, ne, uF, xs, bsum, part);
         __syncthreads();
         if (tid < ne) A.x[r0e + tid] = ld_cg(A.x + r0e + tid) + row_total(part, tid, ne, uF);
         if (l + 1 < A.n_layers) barrier();
@@ -1477,6 +1499,7 @@ size_t persist_smem_bytes(int n_embd, int n_ff, int grid, PersistArgs* a) {
     const size_t uE = n_embd / kUnit, uF = n_ff / kUnit;
     if (std::max({Rq * uE, Rf * uE, Re * uE, Re * uF}) > static_cast<size_t>(PT)) return 0;
     if (Rq % 2) return 0;   // rope pairs must not straddle two CTAs
+    if (std::max(n_embd, n_ff) / 32 > kPersistMaxBlocks) return 0;
     auto up128 = [](size_t v) { return (v + 127) / 128 * 128; };
     const size_t xs = up128(static_cast<size_t>(std::max(n_embd, n_ff)) * sizeof(float));
     const size_t bufA = up128(std::max(Rq, 2 * Rf) * sE);

@@ -202,6 +202,7 @@ int weight_row_bytes(int type, int cols);
 // memory ahead of the barrier before the phase that reads them.
 constexpr int kPersistMaxLayers = 32;
 constexpr int kPersistAttRows = 64;   // attention rows per chunk
+constexpr int kPersistMaxBlocks = 256;   // 32-input blocks of the widest input (n_ff <= 8192)
 struct PersistLayer {
     const uint8_t* w[7];         // q, k, v, output, gate, up, down (Q4_0, 16-byte aligned)
     const float* attn_norm;
