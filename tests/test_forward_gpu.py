@@ -184,6 +184,8 @@ def test_forward_matches_oracle(cuda, wtype, out_type, n_layers, vocab):
     P = oracle.port()
     tokens = [1, vocab - 1, 17, 17, 300 % vocab, 2]
     tok_dev = torch.tensor(tokens, dtype=torch.int32, device="cuda")
+    # Q4_0 models run every layer in one persistent launch, the others per product
+    assert tle.forward_layers_one_launch(dm, ds, 0) == (wtype == Q4_0)
     for pos, tok in enumerate(tokens):
         tle.forward(dm, ds, tok_dev[pos:pos + 1], pos)
         want = P.forward(hf, tok, pos)
@@ -197,6 +199,33 @@ def test_forward_matches_oracle(cuda, wtype, out_type, n_layers, vocab):
     kc = host(ds.t["key_cache"]).reshape(n_layers, 64, -1)[:, :len(tokens)]
     kw = hf.bufs["key_cache"].reshape(n_layers, 64, -1)[:, :len(tokens)]
     assert float(np.max(np.abs(kc - kw))) <= 2e-3 * float(np.max(np.abs(kw)))
+    assert tle.device_error() == 0
+
+
+def test_forward_persistent_attention_chunks_match_oracle(cuda):
+    """The one-launch forward over 576 positions: the attention split grows
+    from 1 to 9 chunks of 64 rows per KV head (the record fold takes its
+    one-pass form up to 8 chunks, its two-pass form at 9), checked against
+    the oracle's forward() at chunk edges."""
+    import torch
+    import tle
+    n = 576
+    m = synth.make_model(seed=21, n_layers=1, n_vocab=512, n_ctx=n)
+    dm = tle.DeviceModel(m)
+    ds = tle.DeviceState(dm)
+    hf = oracle.HostForward(m)
+    P = oracle.port()
+    tokens = np.random.default_rng(21).integers(0, 512, n)
+    tok_dev = torch.tensor(tokens.astype(np.int32), device="cuda")
+    checks = {0, 63, 64, 127, 200, 511, 512, 575}
+    for pos in range(n):
+        assert tle.forward_layers_one_launch(dm, ds, pos)
+        tle.forward(dm, ds, tok_dev[pos:pos + 1], pos)
+        want = P.forward(hf, int(tokens[pos]), pos)
+        if pos in checks:
+            got = host(ds.logits)
+            tol = 2e-3 * float(np.max(np.abs(want)))
+            assert float(np.max(np.abs(got - want))) <= tol, (pos, float(np.max(np.abs(got - want))), tol)
     assert tle.device_error() == 0
 
 
