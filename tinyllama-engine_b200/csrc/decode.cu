@@ -997,6 +997,7 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     float* vs = ks + A.chunk_rows * SEQ_KP;                  // [R][SEQ_KP]
     float* qs = vs + A.chunk_rows * SEQ_KP;                  // [8][64]
     float* part = qs + 8 * HD;                               // [8][SEQ_PF]
+    float* comb = part + 8 * SEQ_PF;                         // [8][SEQ_PF]: the second row half's
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     cg::cluster_group cl = cg::this_cluster();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1051,52 +1052,110 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 
-    // scores in row blocks of 32 (lane = row), online softmax across blocks,
-    // P V with lane = dimensions 2 lane, 2 lane + 1
-    float4 q4[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q4[i] = *reinterpret_cast<const float4*>(&qs[warp * HD + 4 * i]);
-    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-    for (int rb = 0; rb < nrows; rb += 32) {
+    // warp w: query heads 2 hp, 2 hp + 1 of the cluster's eight (hp = w & 3)
+    // over the row blocks 32 half, 32 half + 64, ... (half = w >> 2): scores
+    // lane = row, online softmax across blocks, P V with lane = dimensions
+    // 2 lane, 2 lane + 1; each K/V row read from shared memory serves both
+    // heads.  The halves are folded in shared memory below.
+    const int hp = warp & 3, half = warp >> 2;
+    const float4* qa = reinterpret_cast<const float4*>(&qs[(2 * hp) * HD]);   // broadcast reads
+    const float4* qb = reinterpret_cast<const float4*>(&qs[(2 * hp + 1) * HD]);
+    float ma = -INFINITY, la = 0.f, oa0 = 0.f, oa1 = 0.f;
+    float mb = -INFINITY, lb = 0.f, ob0 = 0.f, ob1 = 0.f;
+    for (int rb = 32 * half; rb < nrows; rb += 64) {
         const int r = rb + lane;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
         if (r < nrows) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const float4 kk = *reinterpret_cast<const float4*>(&ks[r * SEQ_KP + 4 * i]);
-                a0 = fmaf(q4[i].x, kk.x, a0);
-                a1 = fmaf(q4[i].y, kk.y, a1);
-                a2 = fmaf(q4[i].z, kk.z, a2);
-                a3 = fmaf(q4[i].w, kk.w, a3);
+                const float4 x = qa[i], y = qb[i];
+                a0 = fmaf(x.x, kk.x, a0);
+                a1 = fmaf(x.y, kk.y, a1);
+                a2 = fmaf(x.z, kk.z, a2);
+                a3 = fmaf(x.w, kk.w, a3);
+                b0 = fmaf(y.x, kk.x, b0);
+                b1 = fmaf(y.y, kk.y, b1);
+                b2 = fmaf(y.z, kk.z, b2);
+                b3 = fmaf(y.w, kk.w, b3);
             }
         }
-        const float sc = (r < nrows) ? (a0 + a1) + (a2 + a3) : -INFINITY;
-        float mb = sc;
+        const float sa = (r < nrows) ? (a0 + a1) + (a2 + a3) : -INFINITY;
+        const float sb = (r < nrows) ? (b0 + b1) + (b2 + b3) : -INFINITY;
+        float xa = sa, xb = sb;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        const float mn = fmaxf(m, mb);
-        const float f = (m == -INFINITY) ? 0.f : expf(m - mn);
-        const float pr = (sc == -INFINITY) ? 0.f : expf(sc - mn);
-        float lb = pr;
+        for (int o = 16; o > 0; o >>= 1) {
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, o));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, o));
+        }
+        const float na = fmaxf(ma, xa), nb_ = fmaxf(mb, xb);
+        const float fa = (ma == -INFINITY) ? 0.f : expf(ma - na);
+        const float fb = (mb == -INFINITY) ? 0.f : expf(mb - nb_);
+        const float pa = (sa == -INFINITY) ? 0.f : expf(sa - na);
+        const float pb = (sb == -INFINITY) ? 0.f : expf(sb - nb_);
+        float ta = pa, tb = pb;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, o);
-        l = fmaf(l, f, lb);
-        o0 *= f;
-        o1 *= f;
-        m = mn;
+        for (int o = 16; o > 0; o >>= 1) {
+            ta += __shfl_xor_sync(0xffffffffu, ta, o);
+            tb += __shfl_xor_sync(0xffffffffu, tb, o);
+        }
+        la = fmaf(la, fa, ta);
+        lb = fmaf(lb, fb, tb);
+        oa0 *= fa;
+        oa1 *= fa;
+        ob0 *= fb;
+        ob1 *= fb;
+        ma = na;
+        mb = nb_;
         const int nb = min(32, nrows - rb);
-        for (int j = 0; j < nb; ++j) {
-            const float pj = __shfl_sync(0xffffffffu, pr, j);
-            const float2 vv = *reinterpret_cast<const float2*>(&vs[(rb + j) * SEQ_KP + 2 * lane]);
-            o0 = fmaf(pj, vv.x, o0);
-            o1 = fmaf(pj, vv.y, o1);
+        for (int j0 = 0; j0 < nb; j0 += 8) {   // eight rows' shuffles and loads in flight
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const int j = j0 + jj;   // < 32
+                const float wa = __shfl_sync(0xffffffffu, pa, j), wb = __shfl_sync(0xffffffffu, pb, j);
+                const float2 vv = *reinterpret_cast<const float2*>(&vs[(rb + j) * SEQ_KP + 2 * lane]);
+                if (j < nb) {
+                    oa0 = fmaf(wa, vv.x, oa0);
+                    oa1 = fmaf(wa, vv.y, oa1);
+                    ob0 = fmaf(wb, vv.x, ob0);
+                    ob1 = fmaf(wb, vv.y, ob1);
+                }
+            }
         }
     }
-    // this chunk's partial of head 8 g + warp (an empty chunk: m = -inf, l = 0)
-    reinterpret_cast<float2*>(&part[warp * SEQ_PF])[lane] = make_float2(o0, o1);
-    if (lane == 0) {
-        part[warp * SEQ_PF + HD] = m;
-        part[warp * SEQ_PF + HD + 1] = l;
+    // the second half's (o, m, l) to comb; the first folds it (a half
+    // without rows: m = -inf, l = 0) and writes this chunk's partial of its
+    // two heads (an empty chunk: m = -inf, l = 0)
+    if (half == 1) {
+        float* ca = comb + (2 * hp) * SEQ_PF;
+        float* cb = comb + (2 * hp + 1) * SEQ_PF;
+        reinterpret_cast<float2*>(ca)[lane] = make_float2(oa0, oa1);
+        reinterpret_cast<float2*>(cb)[lane] = make_float2(ob0, ob1);
+        if (lane == 0) {
+            ca[HD] = ma;
+            ca[HD + 1] = la;
+            cb[HD] = mb;
+            cb[HD + 1] = lb;
+        }
+    }
+    __syncthreads();
+    if (half == 0) {
+        auto fold = [&](int hl, float m0, float l0, float o0, float o1) {
+            const float* cc = comb + hl * SEQ_PF;
+            const float m1 = cc[HD], l1 = cc[HD + 1];
+            const float2 p1 = reinterpret_cast<const float2*>(cc)[lane];
+            const float mt = fmaxf(m0, m1);
+            const float f0 = (m0 == -INFINITY) ? 0.f : expf(m0 - mt);
+            const float f1 = (m1 == -INFINITY) ? 0.f : expf(m1 - mt);
+            reinterpret_cast<float2*>(&part[hl * SEQ_PF])[lane] =
+                make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
+            if (lane == 0) {
+                part[hl * SEQ_PF + HD] = mt;
+                part[hl * SEQ_PF + HD + 1] = l0 * f0 + l1 * f1;
+            }
+        };
+        fold(2 * hp, ma, la, oa0, oa1);
+        fold(2 * hp + 1, mb, lb, ob0, ob1);
     }
     cl.sync();
     // fold: CTA c takes heads c, c + C, ... of this KV head, one warp each
@@ -1202,12 +1261,12 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(2 * a.chunk_rows * SEQ_KP + 8 * HD + 8 * SEQ_PF) * sizeof(float);
+    const size_t smem = static_cast<size_t>(2 * a.chunk_rows * SEQ_KP + 8 * HD + 16 * SEQ_PF) * sizeof(float);
     static PerDeviceOnce once;
     cudaError_t e = once.run([&](int) {
         return cudaFuncSetAttribute(seq_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(2 * kSeqMaxChunkRows * SEQ_KP * sizeof(float) +
-                                                     (8 * HD + 8 * SEQ_PF) * sizeof(float)));
+                                                     (8 * HD + 16 * SEQ_PF) * sizeof(float)));
     });
     if (e != cudaSuccess) return e;
     // one cluster of n_chunks CTAs per KV head; a programmatic dependent of
