@@ -163,7 +163,15 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
         s.pos = pos;
         s.n_ctx = n_ctx;
         s.rotate = rotate;
-        fill_inv_freq(s.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+        // the rotation angles as the reference computes them (ops.cpp:1233-1238:
+        // float angle, std::cos / std::sin), once per call on the host
+        float inv_freq[tle::kHeadDim / 2];
+        fill_inv_freq(inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+        for (int i = 0; i < tle::kHeadDim / 2; ++i) {
+            const float angle = static_cast<float>(pos) * inv_freq[i];
+            s.rope_cos[i] = std::cos(angle);
+            s.rope_sin[i] = std::sin(angle);
+        }
         cudaError_t e = tle::error_word(&s.err);
         if (e != cudaSuccess) return cuda_error(e, "device error word");
         e = tle::launch_seq_decode(s, static_cast<cudaStream_t>(stream));

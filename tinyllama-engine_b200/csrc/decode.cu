@@ -1022,8 +1022,7 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     // q of this cluster's heads (rotated, x 1/8) and, in the last chunk, the new row
     {
         const int p = lane;   // rotation pair
-        float sn = 0.f, cs = 1.f;
-        if (A.rotate) sincosf(static_cast<float>(A.pos) * A.inv_freq[p], &sn, &cs);
+        const float sn = A.rope_sin[p], cs = A.rope_cos[p];
         const float2 x = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(8 * g + warp) * HD)[p];
         float y0 = x.x, y1 = x.y;
         if (A.rotate) {
@@ -1161,20 +1160,33 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     // fold: CTA c takes heads c, c + C, ... of this KV head, one warp each
     const int C = A.n_chunks;
     for (int hl = c + C * warp; warp < 8 && hl < 8; hl += C * 8) {
-        float mt = -INFINITY;
-        for (int cc = 0; cc < C; ++cc) {
-            const float* pp = cl.map_shared_rank(part, cc);
-            mt = fmaxf(mt, pp[hl * SEQ_PF + HD]);
+        // every chunk's record in flight at once (C <= 8), then the fold in chunk order
+        float mc[kSeqMaxChunks], lc[kSeqMaxChunks];
+        float2 oc[kSeqMaxChunks];
+#pragma unroll
+        for (int cc = 0; cc < kSeqMaxChunks; ++cc) {
+            mc[cc] = -INFINITY;
+            lc[cc] = 0.f;
+            oc[cc] = make_float2(0.f, 0.f);
+            if (cc < C) {
+                const float* pp = cl.map_shared_rank(part, cc) + hl * SEQ_PF;
+                mc[cc] = pp[HD];
+                lc[cc] = pp[HD + 1];
+                oc[cc] = reinterpret_cast<const float2*>(pp)[lane];
+            }
         }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int cc = 0; cc < kSeqMaxChunks; ++cc) mt = fmaxf(mt, mc[cc]);
         float acc0 = 0.f, acc1 = 0.f, lt = 0.f;
-        for (int cc = 0; cc < C; ++cc) {
-            const float* pp = cl.map_shared_rank(part, cc) + hl * SEQ_PF;
-            const float mc = pp[HD], lc = pp[HD + 1];
-            const float2 oc = reinterpret_cast<const float2*>(pp)[lane];
-            const float f = (mc == -INFINITY) ? 0.f : expf(mc - mt);
-            lt = fmaf(lc, f, lt);
-            acc0 = fmaf(oc.x, f, acc0);
-            acc1 = fmaf(oc.y, f, acc1);
+#pragma unroll
+        for (int cc = 0; cc < kSeqMaxChunks; ++cc) {
+            if (cc < C) {
+                const float f = (mc[cc] == -INFINITY) ? 0.f : expf(mc[cc] - mt);
+                lt = fmaf(lc[cc], f, lt);
+                acc0 = fmaf(oc[cc].x, f, acc0);
+                acc1 = fmaf(oc[cc].y, f, acc1);
+            }
         }
         const int h = 8 * g + hl;
         const float inv = 1.0f / lt;

@@ -116,7 +116,7 @@ struct SeqArgs {
     uint32_t* err;
     int layer, pos, n_ctx, rotate;
     int chunk_rows, n_chunks;    // n_chunks * chunk_rows >= pos + 1, chunk_rows a multiple of 32
-    float inv_freq[kHeadDim / 2];
+    float rope_cos[kHeadDim / 2], rope_sin[kHeadDim / 2];   // of pos * inv_freq[i], from the host
 };
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);
 // out[32*64] = sum_r w_r parts[r] with w_r = exp(lses[r][h] - LSE_h),
