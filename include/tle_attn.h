@@ -257,7 +257,9 @@ int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* 
  * 0 = no error.  Codes: 0x101-0x104 a bounded wait expired (0x101 a stage
  * never filled, 0x102 never drained, 0x103 a tensor-core commit never
  * arrived, 0x104 the exit-time drain), 0x105 a paged decode met a page id
- * outside the pool, 0x1ff the self-test below.  The first code recorded
+ * outside the pool, 0x106 a token id outside the vocabulary, 0x108 a grid
+ * barrier wait of the one-launch forward expired, 0x109 a finite activation
+ * of the batched prompt overflowed fp16, 0x1ff the self-test below.  The first code recorded
  * stays until cleared.  Synchronises the device. */
 int tle_device_error(int clear, uint32_t* code);
 

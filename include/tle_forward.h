@@ -164,7 +164,9 @@ size_t tle_prompt_scratch_bytes(const tle_model_t* model, int n_tokens, int pos0
  * leaves the last token's logits in state->logits and its final residual
  * in state->x, as the reference's prompt loop does.  scratch: device,
  * 1024-byte aligned, tle_prompt_scratch_bytes.  Tokens outside [0, n_vocab)
- * are reported through tle_device_error (0x106) and embed as zeros. */
+ * are reported through tle_device_error (0x106) and embed as zeros.  The
+ * products take fp16 operands: an activation whose fp16 rounding overflows
+ * (|x| >= 65520) is reported (0x109) rather than passed on silently. */
 int tle_prompt_forward(const tle_model_t* model, const void* packed, const tle_state_t* state,
                        const int32_t* tokens, int n_tokens, int pos0, void* scratch,
                        size_t scratch_bytes, void* stream);

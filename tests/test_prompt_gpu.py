@@ -157,3 +157,25 @@ def test_prompt_single_token_and_bad_token(cuda):
     assert tle.device_error() == 0x106
     assert np.all(np.isfinite(host(ds.logits)))
     assert tle.device_error() == 0
+
+
+def test_fp16_overflow_is_reported():
+    """An activation beyond fp16's range (RMSNorm weights of 1e5 push the
+    normalised rows to ~1e5 > 65504) is reported as 0x109 instead of
+    entering the fp16 products silently as inf; a model in range reports
+    nothing."""
+    import torch
+    import tle
+    tle.device_error(clear=True)
+    m = synth.make_model(seed=9, n_layers=1, n_vocab=512, n_ctx=160, n_ff=512)
+    m.layers[0]["attn_norm"] = np.full(m.n_embd, 1e5, np.float32)
+    dm = tle.DeviceModel(m)
+    ds = tle.DeviceState(dm)
+    tok = torch.tensor(np.arange(40, dtype=np.int32), device="cuda")
+    tle.prompt_forward(dm, ds, tle.PromptWeights(dm), tok, 0)
+    assert tle.device_error(clear=True) == 0x109
+    m2 = synth.make_model(seed=9, n_layers=1, n_vocab=512, n_ctx=160, n_ff=512)
+    dm2 = tle.DeviceModel(m2)
+    ds2 = tle.DeviceState(dm2)
+    tle.prompt_forward(dm2, ds2, tle.PromptWeights(dm2), tok, 0)
+    assert tle.device_error(clear=True) == 0

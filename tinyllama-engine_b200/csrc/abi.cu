@@ -1168,7 +1168,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         const tle_layer_t& L = m->layers[l];
         const uint16_t* Wl = static_cast<const uint16_t*>(packed) + P.total * static_cast<size_t>(l);
         // rmsnorm + q/k/v for all tokens (forward.cpp:184-196)
-        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.attn_norm, e, eps, S, st);
+        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.attn_norm, e, eps, S, err, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attn_norm");
         tle::GemmLaunch g{};
         g.W = Wl + P.qkv;
@@ -1204,7 +1204,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         ce = tle::launch_prefill(a, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attention");
         // output projection + residual (forward.cpp:210-214)
-        ce = tle::launch_to_f16(ATT16, ATT, static_cast<size_t>(S) * e, st);
+        ce = tle::launch_to_f16(ATT16, ATT, static_cast<size_t>(S) * e, err, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attention output");
         g = tle::GemmLaunch{};
         g.W = Wl + P.o;
@@ -1220,7 +1220,7 @@ int tle_prompt_forward(const tle_model_t* m, const void* packed, const tle_state
         ce = tle::launch_gemm_f16(tle::kEpiAdd, g, st);
         if (ce != cudaSuccess) return cuda_error(ce, "attn_output");
         // rmsnorm + gate/up + SwiGLU (forward.cpp:216-227)
-        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.ffn_norm, e, eps, S, st);
+        ce = tle::launch_rmsnorm_rows_f16(XB16, X, L.ffn_norm, e, eps, S, err, st);
         if (ce != cudaSuccess) return cuda_error(ce, "ffn_norm");
         g = tle::GemmLaunch{};
         g.W = Wl + P.gu;

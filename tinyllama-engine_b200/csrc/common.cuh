@@ -20,6 +20,7 @@ enum : uint32_t {
     kErrBadPage = 0x105,    // paged decode: a page id outside the pool (access skipped)
     kErrBadToken = 0x106,   // forward: a token id outside the vocabulary (zero embedding used)
     kErrGridWait = 0x108,   // persistent forward: a grid barrier wait gave up
+    kErrF16Range = 0x109,   // batched prompt: a finite value beyond fp16's range became inf
     kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 

@@ -52,6 +52,14 @@ constexpr uint32_t kIdesc = idesc_f16_f32(GM, GN);
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+// f2h for activations: a finite value whose fp16 rounding overflows (|f| >=
+// 65520) is reported (0x109) instead of silently entering the next product
+// as inf.
+__device__ __forceinline__ uint16_t f2h_checked(float f, uint32_t* err) {
+    const uint16_t h = f2h(f);
+    if ((h & 0x7FFFu) == 0x7C00u && fabsf(f) < INFINITY) record_error(err, kErrF16Range);
+    return h;
+}
 
 // Bounded wait; after the first expiry in a thread every later wait of that
 // thread returns at once.
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
                 if (j < n && tb + j < A.n_tokens) {
                     const float g = v[j];
                     A.h_out[static_cast<size_t>(tb + j) * A.up_row0 + r] =
-                        f2h((g * (1.0f / (1.0f + expf(-g)))) * u[j]);
+                        f2h_checked((g * (1.0f / (1.0f + expf(-g)))) * u[j], A.err);
                 }
             }
         }
@@ -353,7 +361,8 @@ __global__ void __launch_bounds__(256) pack_f16_kernel(uint16_t* __restrict__ ds
 
 // ---- RMSNorm of S rows into the fp16 operand (ops.cpp:1040-1054 per row) ----
 __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
-                                                               const float* __restrict__ w, int n, float eps) {
+                                                               const float* __restrict__ w, int n, float eps,
+                                                               uint32_t* err) {
     __shared__ float red[8];
     __shared__ float rms;
     const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
@@ -371,14 +380,14 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* __restr
     }
     __syncthreads();
     const float s = rms;
-    for (int i = threadIdx.x; i < n; i += 256) orow[i] = f2h(xr[i] * s * w[i]);
+    for (int i = threadIdx.x; i < n; i += 256) orow[i] = f2h_checked(xr[i] * s * w[i], err);
 }
 
 __global__ void __launch_bounds__(256) to_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
-                                                     size_t n) {
+                                                     size_t n, uint32_t* err) {
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
-        out[i] = f2h(x[i]);
+        out[i] = f2h_checked(x[i], err);
 }
 
 // embed_token (forward.cpp:35-60) for S tokens: block (x, t) writes a slice
@@ -499,15 +508,15 @@ cudaError_t launch_pack_f16(int type, uint16_t* dst, const void* W, int rows, in
 }
 
 cudaError_t launch_rmsnorm_rows_f16(uint16_t* out, const float* x, const float* w, int n, float eps,
-                                    int n_tokens, cudaStream_t stream) {
+                                    int n_tokens, uint32_t* err, cudaStream_t stream) {
     if (n <= 0 || n_tokens <= 0) return cudaErrorInvalidValue;
-    rmsnorm_rows_f16_kernel<<<n_tokens, 256, 0, stream>>>(out, x, w, n, eps);
+    rmsnorm_rows_f16_kernel<<<n_tokens, 256, 0, stream>>>(out, x, w, n, eps, err);
     return cudaGetLastError();
 }
 
-cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, cudaStream_t stream) {
+cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, uint32_t* err, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    to_f16_kernel<<<grid_for(n), 256, 0, stream>>>(out, x, n);
+    to_f16_kernel<<<grid_for(n), 256, 0, stream>>>(out, x, n, err);
     return cudaGetLastError();
 }
 

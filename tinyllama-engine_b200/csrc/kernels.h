@@ -291,9 +291,9 @@ cudaError_t launch_gemm_f16(int epi, const GemmLaunch& g, cudaStream_t stream);
 cudaError_t launch_pack_f16(int type, uint16_t* dst, const void* W, int rows, int cols, cudaStream_t stream);
 // out[t][:] = fp16(rmsnorm(x[t][:]) * w) for t < n_tokens.
 cudaError_t launch_rmsnorm_rows_f16(uint16_t* out, const float* x, const float* w, int n, float eps,
-                                    int n_tokens, cudaStream_t stream);
+                                    int n_tokens, uint32_t* err, cudaStream_t stream);
 // out[i] = fp16(x[i]), i < n.
-cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, cudaStream_t stream);
+cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, uint32_t* err, cudaStream_t stream);
 // x[t][:] = row tokens[t] of the table (F16 or F32), t < n_tokens.
 cudaError_t launch_embed_rows(int type, float* x, const void* table, const int32_t* tokens, int n_tokens,
                              int n_vocab, int n_embd, uint32_t* err, cudaStream_t stream);
