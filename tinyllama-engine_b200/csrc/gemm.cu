@@ -79,6 +79,8 @@ struct GemmSmem {
     uint64_t full[STAGES];               // the stage's copies landed
     uint64_t empty[STAGES];              // the stage's MMAs completed
     uint64_t acc_full;                   // the last MMA completed
+    uint64_t drain;                      // failure path: every MMA issued so far completed
+    int issued, consumed;                // failure path: K blocks copied / taken by the MMAs
     uint32_t tmem_base;
 };
 template <int EPI>
@@ -133,6 +135,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             mbar_init(&S.empty[s], 1);
         }
         mbar_init(&S.acc_full, 1);
+        mbar_init(&S.drain, 1);
+        S.issued = 0;
+        S.consumed = 0;
         fence_barrier_init();
         prefetch_tmap(&A.tm_w);
         prefetch_tmap(&A.tm_x);
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
                 tma_load_2d(S.a[s][0], &A.tm_w, kx, m0, &S.full[s]);
                 if (NACC == 2) tma_load_2d(S.a[s][NACC - 1], &A.tm_w, kx, A.up_row0 + m0, &S.full[s]);
                 tma_load_2d(S.b[s], &A.tm_x, kx, t0, &S.full[s]);
+                S.issued = kb + 1;
             }
             __syncwarp();
         }
@@ -170,6 +176,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             wait_or_flag(&S.full[s], (kb / ST) & 1, A.err, kErrWaitFull, failed);
             failed = __any_sync(0xffffffffu, failed);
             if (failed) break;
+            if (lane == 0) S.consumed = kb + 1;
             tc_fence_after();
             if (elect_one()) {
                 const uint64_t db = sw128_desc(smem_u32(S.b[s]));
@@ -296,8 +303,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
         }
         cl.sync();
     }
+    // Failure path (a bounded wait expired somewhere in the CTA): nothing the
+    // CTA issued may still write shared or tensor memory when the memory is
+    // freed, so wait (bounded) for the copies no MMA took and for a final
+    // commit of the MMA thread's work; a drain that expires is reported too.
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(failed ? 1 : 0)) {
+        bool drained = true;
+        if (warp == 1 && elect_one()) {
+            umma_commit(&S.drain);
+            drained = mbar_wait(&S.drain, 0);
+        }
+        if (threadIdx.x == 0)
+            for (int kb = S.consumed; kb < S.issued; ++kb)
+                if (!mbar_wait(&S.full[kb % ST], (kb / ST) & 1)) {
+                    drained = false;
+                    break;
+                }
+        if (!drained) record_error(A.err, kErrDrain);
+        __syncthreads();
+    }
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, C::kCols);
