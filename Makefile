@@ -16,7 +16,8 @@ REF ?= $(abspath $(CURDIR)/../reference)
 ARCH := -gencode arch=compute_100a,code=sm_100a
 NVFLAGS := -std=c++20 -O3 $(ARCH) -lineinfo -Xcompiler -fPIC -Xcompiler -Wall \
            --expt-relaxed-constexpr -Iinclude -I$(CSRC)
-CU_SRCS := $(CSRC)/decode.cu $(CSRC)/prefill.cu $(CSRC)/forward.cu $(CSRC)/gemm.cu $(CSRC)/abi.cu
+CU_SRCS := $(CSRC)/decode.cu $(CSRC)/decode_bf16.cu $(CSRC)/prefill.cu $(CSRC)/forward.cu $(CSRC)/gemm.cu \
+           $(CSRC)/abi.cu
 HOST_SRCS := $(HOST)/ops_gpu.cpp
 CU_OBJS := $(patsubst $(CSRC)/%.cu,_build/%.o,$(CU_SRCS))
 HOST_OBJS := $(patsubst $(HOST)/%.cpp,_build/host_%.o,$(HOST_SRCS))

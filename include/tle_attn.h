@@ -158,6 +158,36 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
                      const float* q, const float* k, const float* v, float* out, int layer,
                      int flags, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- batched decode over a bf16 KV cache ----
+ * No counterpart in the reference (its cache is fp32, run_state.h:134-138):
+ * the same decode step with cache rows stored as bf16 (round to nearest
+ * even), half the bytes per row.  The query and the softmax weights enter
+ * the tensor cores as bf16 with fp32 accumulation, so outputs agree with
+ * the fp32 reference to bf16 precision (the prefill contract, 2e-2), not
+ * to the fp32 decode's 1e-4. */
+typedef struct {
+    void* key_cache;    /* device bf16 [n_layers][n_ctx][n_head_kv*head_dim] */
+    void* value_cache;  /* device bf16, same layout                          */
+    int32_t n_ctx;
+    int32_t pos;
+} tle_seq_bf16_t;
+
+/* Scratch of tle_decode_batch_bf16 for n_seqs sequences of at most max_rows
+ * rows (pos + 1). */
+size_t tle_decode_bf16_workspace_bytes(int n_seqs, int max_rows);
+
+/* One decode step of layer `layer` for sequences seqs_dev[0..n_seqs) (a
+ * device array): per sequence s, if flags & TLE_DECODE_ROTATE, rope(q_s,
+ * k_s, pos_s) (not written back); append bf16(k_s), bf16(v_s) at row pos_s;
+ * out_s = attention over rows 0..pos_s.  q [n_seqs][n_head*hd], k/v
+ * [n_seqs][n_head_kv*hd] fp32; max_rows >= every pos_s + 1 (a record with
+ * pos outside [0, n_ctx) or beyond max_rows is skipped and reported through
+ * tle_device_error as 0x10a).  Other flag bits are rejected with
+ * TLE_ERR_INVALID. */
+int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_dev, int n_seqs,
+                          int max_rows, const float* q, const float* k, const float* v, float* out,
+                          int layer, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- batched decode over a paged KV cache ----
  * No counterpart in the reference: run_state.h:20-25 sizes one contiguous
  * [n_layers][n_ctx][256] cache per sequence and names PagedAttention as the
@@ -259,7 +289,8 @@ int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* 
  * arrived, 0x104 the exit-time drain), 0x105 a paged decode met a page id
  * outside the pool, 0x106 a token id outside the vocabulary, 0x108 a grid
  * barrier wait of the one-launch forward expired, 0x109 a finite activation
- * of the batched prompt overflowed fp16, 0x1ff the self-test below.  The first code recorded
+ * of the batched prompt overflowed fp16, 0x10a a bf16 decode record outside
+ * its cache, 0x1ff the self-test below.  The first code recorded
  * stays until cleared.  Synchronises the device. */
 int tle_device_error(int clear, uint32_t* code);
 

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def header_functions():
     text = "".join(open(os.path.join(ROOT, "include", h)).read()
                    for h in ("tle_attn.h", "tle_forward.h"))
-    return sorted(set(re.findall(r"\b(tle_[a-z_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(tle_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_library_exports_every_header_symbol():

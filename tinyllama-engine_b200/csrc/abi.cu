@@ -438,6 +438,43 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
     return ok();
 }
 
+size_t tle_decode_bf16_workspace_bytes(int n_seqs, int max_rows) {
+    if (n_seqs <= 0 || max_rows <= 0) return 0;
+    return tle::decode_bf16_workspace_bytes(n_seqs, max_rows);
+}
+
+int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_dev, int n_seqs,
+                          int max_rows, const float* q, const float* k, const float* v, float* out,
+                          int layer, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!seqs_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer");
+    if (n_seqs <= 0 || n_seqs > 65535 || max_rows <= 0 || layer < 0 || layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "n_seqs %d, max_rows %d, layer %d", n_seqs, max_rows, layer);
+    if (flags & ~TLE_DECODE_ROTATE) return set_error(TLE_ERR_INVALID, "unknown flags 0x%x", flags);
+    const size_t need = tle::decode_bf16_workspace_bytes(n_seqs, max_rows);
+    const int max_chunks = (max_rows + tle::kBfChunk - 1) / tle::kBfChunk;
+    if (max_chunks > 1 && (!workspace || workspace_bytes < need))
+        return set_error(TLE_ERR_INVALID, "workspace %zu bytes, need %zu", workspace_bytes, need);
+    tle::BfArgs a{};
+    a.seqs = seqs_dev;
+    a.n_seqs = n_seqs;
+    a.max_chunks = max_chunks;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.parts = static_cast<float*>(workspace);
+    a.lses = a.parts ? a.parts + static_cast<size_t>(n_seqs) * max_chunks * tle::kNHead * tle::kHeadDim : nullptr;
+    a.layer = layer;
+    a.rotate = (flags & TLE_DECODE_ROTATE) != 0;
+    fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    cudaError_t e = tle::error_word(&a.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_decode_bf16(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "bf16 decode launch");
+    return ok();
+}
+
 int tle_decode_batch_paged(const tle_shape_t* shape, const tle_page_pool_t* pool,
                            const void* desc_dev, int n_seqs, int n_ctas, const float* q,
                            const float* k, const float* v, float* out, int layer, int flags,

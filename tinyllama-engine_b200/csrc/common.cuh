@@ -21,6 +21,7 @@ enum : uint32_t {
     kErrBadToken = 0x106,   // forward: a token id outside the vocabulary (zero embedding used)
     kErrGridWait = 0x108,   // persistent forward: a grid barrier wait gave up
     kErrF16Range = 0x109,   // batched prompt: a finite value beyond fp16's range became inf
+    kErrBadSeq = 0x10a,     // bf16 decode: a sequence record outside its cache or max_rows (skipped)
     kErrSelfTest = 0x1ff,   // tle_selftest_wait_timeout: the planted wait expired
 };
 

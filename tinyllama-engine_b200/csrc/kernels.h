@@ -119,6 +119,27 @@ struct SeqArgs {
     float rope_cos[kHeadDim / 2], rope_sin[kHeadDim / 2];   // of pos * inv_freq[i], from the host
 };
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);
+
+// Decode over bf16 caches (decode_bf16.cu): CTA (c, s) takes rows
+// [c kBfChunk, (c + 1) kBfChunk) of sequence s; chunk partials (o / l and
+// the log-sum-exp) of sequences with more than one chunk are merged by a
+// second launch.
+constexpr int kBfChunk = 2048;
+struct BfArgs {
+    const tle_seq_bf16_t* seqs;  // device [n_seqs]
+    int n_seqs, max_chunks;      // max_chunks = ceil(max_rows / kBfChunk)
+    const float* q;              // [n_seqs][32*64]
+    const float* k;              // [n_seqs][256]
+    const float* v;
+    float* out;                  // [n_seqs][32*64]
+    float* parts;                // [n_seqs][max_chunks][32][64]
+    float* lses;                 // [n_seqs][max_chunks][32]
+    int layer, rotate;
+    uint32_t* err;
+    float inv_freq[kHeadDim / 2];
+};
+size_t decode_bf16_workspace_bytes(int n_seqs, int max_rows);
+cudaError_t launch_decode_bf16(const BfArgs& a, cudaStream_t stream);
 // out[32*64] = sum_r w_r parts[r] with w_r = exp(lses[r][h] - LSE_h),
 // LSE_h = log sum_r exp(lses[r][h]): the attention over the union of the
 // parts' key sets, each part normalised over its own keys.

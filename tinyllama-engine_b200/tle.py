@@ -40,7 +40,8 @@ EXPORTED = (
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
     "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
-    "tle_decode_desc_paged", "tle_decode_batch_paged",
+    "tle_decode_desc_paged", "tle_decode_batch_paged", "tle_decode_bf16_workspace_bytes",
+    "tle_decode_batch_bf16",
     # include/tle_forward.h
     "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
     "tle_forward_workspace_bytes", "tle_forward", "tle_forward_layers_one_launch", "tle_sample_temperature", "tle_sample_top_p",
@@ -64,6 +65,12 @@ class Shape(ctypes.Structure):
 
 class Seq(ctypes.Structure):
     """tle_seq_t: one sequence's device KV cache and decode position."""
+    _fields_ = [("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
+                ("n_ctx", ctypes.c_int32), ("pos", ctypes.c_int32)]
+
+
+class SeqBf16(ctypes.Structure):
+    """tle_seq_bf16_t: the same record for a bf16 cache."""
     _fields_ = [("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
                 ("n_ctx", ctypes.c_int32), ("pos", ctypes.c_int32)]
 
@@ -136,6 +143,9 @@ def lib() -> ctypes.CDLL:
         L.tle_decode_workspace_bytes.argtypes = [P(Shape), i, i]
         L.tle_decode_workspace_bytes.restype = sz
         L.tle_decode_batch.argtypes = [P(Shape), vp, i, i, vp, vp, vp, vp, i, i, vp, sz, vp]
+        L.tle_decode_bf16_workspace_bytes.argtypes = [i, i]
+        L.tle_decode_bf16_workspace_bytes.restype = sz
+        L.tle_decode_batch_bf16.argtypes = [P(Shape), vp, i, i, vp, vp, vp, vp, i, i, vp, sz, vp]
         L.tle_prefill_workspace_bytes.argtypes = [P(Shape), i, i]
         L.tle_prefill_workspace_bytes.restype = sz
         L.tle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, P(Shape), vp, sz, vp]
@@ -266,6 +276,52 @@ def merge_lse(out, parts, lses, stream=None) -> None:
 
 
 # ----------------------------------------------------------- batched decode
+class DecodeBatchBf16:
+    """The decode step over bf16 caches (tle_decode_batch_bf16).
+
+    ``caches`` is a list of (key_cache, value_cache, n_ctx) device tensors of
+    dtype torch.bfloat16, each [n_layers][n_ctx][256].  The sequence records
+    live in device memory; ``set_positions`` rewrites them (one H2D copy).
+    """
+
+    def __init__(self, caches: Sequence, positions: Sequence[int], shape: Optional[Shape] = None):
+        import torch
+        self.shape = shape or tinyllama_shape()
+        self.caches = list(caches)
+        self.n = len(self.caches)
+        for kc, vc, _ in self.caches:
+            if kc.dtype != torch.bfloat16 or vc.dtype != torch.bfloat16 or not kc.is_cuda:
+                raise ValueError("bf16 CUDA caches expected")
+        self._seqs_dev = torch.empty(self.n * ctypes.sizeof(SeqBf16), dtype=torch.uint8, device="cuda")
+        self.workspace = None
+        self.set_positions(positions)
+
+    def set_positions(self, positions: Sequence[int]) -> None:
+        import torch
+        if len(positions) != self.n:
+            raise ValueError("one position per sequence")
+        self.positions = [int(p) for p in positions]
+        self.max_rows = max(self.positions) + 1
+        seqs = (SeqBf16 * self.n)()
+        for i, (kc, vc, n_ctx) in enumerate(self.caches):
+            seqs[i] = SeqBf16(_ptr(kc), _ptr(vc), int(n_ctx), self.positions[i])
+        host = torch.frombuffer(bytearray(bytes(seqs)), dtype=torch.uint8)
+        self._seqs_dev.copy_(host)
+        nbytes = lib().tle_decode_bf16_workspace_bytes(self.n, self.max_rows)
+        if self.workspace is None or self.workspace.numel() * 4 < nbytes:
+            self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device="cuda")
+
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+        """q [n][2048], k/v [n][256], out [n][2048]: fp32 CUDA tensors."""
+        for t, n, name in ((q, self.n * 2048, "q"), (k, self.n * 256, "k"), (v, self.n * 256, "v"),
+                           (out, self.n * 2048, "out")):
+            _want(t, n, name)
+        _check(lib().tle_decode_batch_bf16(ctypes.byref(self.shape), self._seqs_dev.data_ptr(), self.n,
+                                           self.max_rows, _ptr(q), _ptr(k), _ptr(v), _ptr(out), layer,
+                                           1 if rotate else 0, _ptr(self.workspace),
+                                           self.workspace.numel() * 4, _stream(stream)))
+
+
 class DecodeBatch:
     """attention() for many independent sequences in one launch per layer.
 
