@@ -228,7 +228,8 @@ def main():
         fn = {"prefill3": measure_prefill, "decode4": measure_config4, "decode1": measure_config1,
               "decode5paged": measure_paged5, "decode4paged": measure_paged4, "decode5bf16": measure_bf16_5,
               "generate2": measure_config2, "prompt2": measure_prompt2}[args.only]
-        res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup))
+        kw = {"n_seqs": args.seqs, "ctx": args.ctx} if args.only == "decode5bf16" else {}
+        res = fn(dev, load_peaks(), steps=args.steps, warmup=max(3, args.warmup), **kw)
         print(json.dumps(dict(res, impl="tle", n_gpus=1, steps=args.steps,
                               warmup=max(3, args.warmup))), flush=True)
         return
@@ -772,7 +773,7 @@ def measure_paged5(dev, peaks, steps=10, warmup=3, page_rows=256, shuffle=True):
             "gpu_launches": steps}
 
 
-def measure_bf16_5(dev, peaks, steps=10, warmup=3):
+def measure_bf16_5(dev, peaks, steps=10, warmup=3, n_seqs=N_SEQS, ctx=CTX):
     """Config 5's shape over bf16 caches: 256 sequences x 32768 rows, one
     tle_decode_batch_bf16 call per step (8.6 GB of K+V, > L2).  The KV bytes
     are the bf16 bytes read; tok/s counts 22 layers per token as the fp32
@@ -781,25 +782,25 @@ def measure_bf16_5(dev, peaks, steps=10, warmup=3):
     import tle
     g = torch.Generator(device=dev).manual_seed(56)
     caches = []
-    for _ in range(N_SEQS):
-        kc = torch.randn((1, CTX, KVD), generator=g, device=dev).to(torch.bfloat16)
-        vc = torch.randn((1, CTX, KVD), generator=g, device=dev).to(torch.bfloat16)
-        caches.append((kc, vc, CTX))
-    batch = tle.DecodeBatchBf16(caches, [CTX - 1] * N_SEQS, tle.tinyllama_shape(1))
-    q = torch.randn((N_SEQS, QD), generator=g, device=dev)
-    k = torch.randn((N_SEQS, KVD), generator=g, device=dev)
-    v = torch.randn((N_SEQS, KVD), generator=g, device=dev)
-    out = torch.zeros((N_SEQS, QD), device=dev)
+    for _ in range(n_seqs):
+        kc = torch.randn((1, ctx, KVD), generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn((1, ctx, KVD), generator=g, device=dev).to(torch.bfloat16)
+        caches.append((kc, vc, ctx))
+    batch = tle.DecodeBatchBf16(caches, [ctx - 1] * n_seqs, tle.tinyllama_shape(1))
+    q = torch.randn((n_seqs, QD), generator=g, device=dev)
+    k = torch.randn((n_seqs, KVD), generator=g, device=dev)
+    v = torch.randn((n_seqs, KVD), generator=g, device=dev)
+    out = torch.zeros((n_seqs, QD), device=dev)
     stream = torch.cuda.current_stream(dev)
     ms = _time_steps(lambda: batch.run(q, k, v, out, 0, True, stream), steps, warmup, stream)
-    kv_bytes = N_SEQS * CTX * KVD * 2 * 2
+    kv_bytes = n_seqs * ctx * KVD * 2 * 2
     gbs = kv_bytes / (ms / 1e3) / 1e9
     assert tle.device_error() == 0
     del caches
-    return {"workload": "config5 shape, bf16 KV: 256 seqs x 32768 rows, 1 layer per step "
-                        "(tle_decode_batch_bf16, mma.sync m16n8k16)",
+    return {"workload": "config5 shape, bf16 KV: %d seqs x %d rows, 1 layer per step "
+                        "(tle_decode_batch_bf16, mma.sync m16n8k16)" % (n_seqs, ctx),
             "metric": "decode-attn KV GB/s", "value": round(gbs, 1), "unit": "GB/s",
-            "ms_per_step": round(ms, 4), "tok_s_attn_22_layers": round(N_SEQS / (22 * ms / 1e3), 1),
+            "ms_per_step": round(ms, 4), "tok_s_attn_22_layers": round(n_seqs / (22 * ms / 1e3), 1),
             "dtype": "bf16 KV, bf16 q and P on the tensor pipe, fp32 accumulation",
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
