@@ -452,12 +452,14 @@ int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_d
         return set_error(TLE_ERR_INVALID, "n_seqs %d, max_rows %d, layer %d", n_seqs, max_rows, layer);
     if (flags & ~TLE_DECODE_ROTATE) return set_error(TLE_ERR_INVALID, "unknown flags 0x%x", flags);
     const size_t need = tle::decode_bf16_workspace_bytes(n_seqs, max_rows);
-    const int max_chunks = (max_rows + tle::kBfChunk - 1) / tle::kBfChunk;
+    const int chunk = tle::bf16_chunk_rows(n_seqs, max_rows);
+    const int max_chunks = (max_rows + chunk - 1) / chunk;
     if (max_chunks > 1 && (!workspace || workspace_bytes < need))
         return set_error(TLE_ERR_INVALID, "workspace %zu bytes, need %zu", workspace_bytes, need);
     tle::BfArgs a{};
     a.seqs = seqs_dev;
     a.n_seqs = n_seqs;
+    a.chunk = chunk;
     a.max_chunks = max_chunks;
     a.q = q;
     a.k = k;

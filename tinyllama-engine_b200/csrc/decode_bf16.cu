@@ -11,7 +11,7 @@
 // precision (2e-2, the prefill contract), not to the fp32 decode's 1e-4.
 //
 // Design: cache rows are 512 bytes (4 KV heads x 64 bf16).  CTA (c, s) takes
-// chunk c (kBfChunk rows) of sequence s and streams it in 64-row tiles of
+// chunk c (A.chunk rows) of sequence s and streams it in 64-row tiles of
 // all four KV heads through a 3-stage shared-memory ring with 16-byte
 // cp.async (16-byte chunks XOR-swizzled by row so the ldmatrix reads are
 // conflict-free; rows past the chunk are zero-filled).  Warp w takes KV head
@@ -101,16 +101,16 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
     const int c = blockIdx.x, s = blockIdx.y;
     const tle_seq_bf16_t sq = A.seqs[s];
     const int L = sq.pos + 1;
-    const int n_chunks = (L + kBfChunk - 1) / kBfChunk;
+    const int n_chunks = (L + A.chunk - 1) / A.chunk;
     // a record outside its cache, or longer than the launch's max_rows, is
     // reported and skipped (no access)
     if (sq.pos < 0 || sq.pos >= sq.n_ctx || n_chunks > A.max_chunks) {
         if (c == 0 && tid == 0) record_error(A.err, kErrBadSeq);
         return;
     }
-    const int r0 = c * kBfChunk;
+    const int r0 = c * A.chunk;
     if (r0 >= L) return;                                   // past the sequence's last chunk
-    const int nrows = min(kBfChunk, L - r0);
+    const int nrows = min(A.chunk, L - r0);
     const bool has_new = r0 + nrows == L;
     uint16_t* kc = static_cast<uint16_t*>(sq.key_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
     uint16_t* vc = static_cast<uint16_t*>(sq.value_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(256) merge_bf16_kernel(const __grid_constant__
     const int s = blockIdx.x;
     const tle_seq_bf16_t sq = A.seqs[s];
     const int L = sq.pos + 1;
-    const int n_chunks = (L + kBfChunk - 1) / kBfChunk;
+    const int n_chunks = (L + A.chunk - 1) / A.chunk;
     if (n_chunks <= 1 || sq.pos >= sq.n_ctx || n_chunks > A.max_chunks) return;   // reported by the decode
     const int h = threadIdx.x >> 3, d0 = 8 * (threadIdx.x & 7);
     const size_t base = static_cast<size_t>(s) * A.max_chunks * BNH + h;
@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(256) merge_bf16_kernel(const __grid_constant__
 }  // namespace
 
 size_t decode_bf16_workspace_bytes(int n_seqs, int max_rows) {
-    const size_t chunks = static_cast<size_t>((max_rows + kBfChunk - 1) / kBfChunk);
+    const int chunk = bf16_chunk_rows(n_seqs, max_rows);
+    const size_t chunks = static_cast<size_t>((max_rows + chunk - 1) / chunk);
     return static_cast<size_t>(n_seqs) * chunks * BNH * (BHD + 1) * sizeof(float);
 }
 

@@ -121,13 +121,20 @@ struct SeqArgs {
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);
 
 // Decode over bf16 caches (decode_bf16.cu): CTA (c, s) takes rows
-// [c kBfChunk, (c + 1) kBfChunk) of sequence s; chunk partials (o / l and
-// the log-sum-exp) of sequences with more than one chunk are merged by a
-// second launch.
-constexpr int kBfChunk = 2048;
+// [c chunk, (c + 1) chunk) of sequence s; chunk partials (o / l and the
+// log-sum-exp) of sequences with more than one chunk are merged by a second
+// launch.  The chunk (a multiple of 64 rows, at most kBfMaxChunk) is chosen
+// from the batch shape so that a launch has about kBfTargetCtas CTAs.
+constexpr int kBfMaxChunk = 2048;
+constexpr int kBfTargetCtas = 2 * 148;
+inline int bf16_chunk_rows(int n_seqs, int max_rows) {
+    const long long per = (static_cast<long long>(n_seqs) * max_rows + kBfTargetCtas - 1) / kBfTargetCtas;
+    const long long c = (per + 63) / 64 * 64;
+    return static_cast<int>(c < 64 ? 64 : (c > kBfMaxChunk ? kBfMaxChunk : c));
+}
 struct BfArgs {
     const tle_seq_bf16_t* seqs;  // device [n_seqs]
-    int n_seqs, max_chunks;      // max_chunks = ceil(max_rows / kBfChunk)
+    int n_seqs, chunk, max_chunks;   // max_chunks = ceil(max_rows / chunk)
     const float* q;              // [n_seqs][32*64]
     const float* k;              // [n_seqs][256]
     const float* v;
