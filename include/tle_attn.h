@@ -188,6 +188,21 @@ int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_d
                           int max_rows, const float* q, const float* k, const float* v, float* out,
                           int layer, int flags, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The bf16 decode over page pools (the paged layout below, rows stored as
+ * bf16): row r of page p of layer l is at
+ *   pool + ((l * n_pages + p) * page_rows + r) * n_head_kv * head_dim
+ * bf16 elements; page_rows a power of two in [64, 65536].  seqs_dev is a
+ * device array of tle_paged_seq_t records, their page tables on the device too.
+ * A record with pos outside its table is skipped (0x10a), a page id
+ * outside the pool is not dereferenced (0x105).  Same results as
+ * tle_decode_batch_bf16 on the same rows. */
+typedef struct {
+    void* key_pool;     /* device bf16 [n_layers][n_pages][page_rows][n_head_kv*head_dim] */
+    void* value_pool;
+    int32_t n_pages;
+    int32_t page_rows;
+} tle_page_pool_bf16_t;
+
 /* ---- batched decode over a paged KV cache ----
  * No counterpart in the reference: run_state.h:20-25 sizes one contiguous
  * [n_layers][n_ctx][256] cache per sequence and names PagedAttention as the
@@ -213,6 +228,13 @@ typedef struct {
     int32_t n_pages;      /* entries in pages; need n_pages * page_rows > pos       */
     int32_t pos;          /* position of the token being decoded (appended at row pos) */
 } tle_paged_seq_t;
+
+/* tle_decode_batch_bf16 over bf16 page pools (see tle_page_pool_bf16_t);
+ * workspace as tle_decode_bf16_workspace_bytes. */
+int tle_decode_batch_bf16_paged(const tle_shape_t* shape, const tle_page_pool_bf16_t* pool,
+                                const tle_paged_seq_t* seqs_dev, int n_seqs, int max_rows, const float* q,
+                                const float* k, const float* v, float* out, int layer, int flags,
+                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* tle_decode_desc for a paged batch (same tle_decode_desc_bytes size, same
  * split of rows over CTAs).  The page tables stay on the device and are

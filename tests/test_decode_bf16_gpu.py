@@ -113,3 +113,63 @@ def test_bf16_decode_reports_bad_record():
     assert tle.device_error(clear=True) == 0x10a
     assert torch.isfinite(out[0]).all() and bool((out[1] == 0).all())
     assert torch.equal(kc2, kc2_before)   # the bad record's cache was not touched
+
+
+@pytest.mark.parametrize("page_rows", [64, 256])
+def test_bf16_paged_matches_contiguous(page_rows):
+    """The same rows in shuffled bf16 page pools give bit-identical outputs
+    and appended rows to the contiguous bf16 caches."""
+    import torch
+    import tle
+    rng = np.random.default_rng(page_rows)
+    lengths = [70, 2100, 300, 1]
+    n = len(lengths)
+    shape = tle.tinyllama_shape(2)
+    layer = 1
+    cont, tables = [], []
+    pc = tle.PagedKVCache(sum(-(-L // page_rows) for L in lengths) + 5, page_rows, shape, dtype=torch.bfloat16)
+    pc._free = [int(i) for i in rng.permutation(pc.n_pages)]
+    for L in lengths:
+        kc = torch.randn(2, L, 256).to(torch.bfloat16).cuda()
+        vc = torch.randn(2, L, 256).to(torch.bfloat16).cuda()
+        cont.append((kc, vc, L))
+        ids = pc.alloc(-(-L // page_rows))
+        for j, pid in enumerate(ids):
+            r0, r1 = page_rows * j, min(page_rows * (j + 1), L)
+            pc.key_pool[:, pid, :r1 - r0] = kc[:, r0:r1]
+            pc.value_pool[:, pid, :r1 - r0] = vc[:, r0:r1]
+        tables.append(pc.table(ids))
+    pos = [L - 1 for L in lengths]
+    q = torch.randn(n, 2048, device="cuda")
+    k = torch.randn(n, 256, device="cuda")
+    v = torch.randn(n, 256, device="cuda")
+    o1 = torch.full((n, 2048), float("nan"), device="cuda")
+    o2 = torch.full((n, 2048), float("nan"), device="cuda")
+    tle.DecodeBatchBf16(cont, pos, shape).run(q, k, v, o1, layer)
+    tle.PagedDecodeBatchBf16(pc, tables, pos).run(q, k, v, o2, layer)
+    torch.cuda.synchronize()
+    assert tle.device_error() == 0
+    assert torch.isfinite(o1).all() and torch.equal(o1, o2)
+    for (kc, vc, L), t in zip(cont, tables):
+        p = L - 1
+        pid = int(t[p // page_rows])
+        assert torch.equal(pc.key_pool[layer, pid, p % page_rows], kc[layer, p])
+        assert torch.equal(pc.value_pool[layer, pid, p % page_rows], vc[layer, p])
+
+
+def test_bf16_paged_bad_page_is_reported():
+    """A page id outside the pool is never dereferenced: 0x105."""
+    import torch
+    import tle
+    shape = tle.tinyllama_shape(1)
+    pc = tle.PagedKVCache(4, 64, shape, dtype=torch.bfloat16)
+    pc.key_pool.normal_()
+    pc.value_pool.normal_()
+    tables = [pc.table([0, 1]), pc.table([2, 1000])]   # the second table's page 1 is out of the pool
+    out = torch.zeros(2, 2048, device="cuda")
+    tle.device_error(clear=True)
+    tle.PagedDecodeBatchBf16(pc, tables, [100, 100]).run(
+        torch.randn(2, 2048, device="cuda"), torch.randn(2, 256, device="cuda"),
+        torch.randn(2, 256, device="cuda"), out, 0)
+    assert tle.device_error(clear=True) == 0x105
+    assert torch.isfinite(out[0]).all()

@@ -443,9 +443,14 @@ size_t tle_decode_bf16_workspace_bytes(int n_seqs, int max_rows) {
     return tle::decode_bf16_workspace_bytes(n_seqs, max_rows);
 }
 
-int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_dev, int n_seqs,
-                          int max_rows, const float* q, const float* k, const float* v, float* out,
-                          int layer, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Checks and fills the arguments shared by the contiguous and paged bf16 calls.
+int bf16_args(const tle_shape_t* shape, const void* seqs_dev, int n_seqs, int max_rows, const float* q,
+              const float* k, const float* v, float* out, int layer, int flags, void* workspace,
+              size_t workspace_bytes, tle::BfArgs& a) {
     if (int rc = check_shape(shape)) return rc;
     if (!seqs_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer");
     if (n_seqs <= 0 || n_seqs > 65535 || max_rows <= 0 || layer < 0 || layer >= shape->n_layers)
@@ -456,8 +461,7 @@ int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_d
     const int max_chunks = (max_rows + chunk - 1) / chunk;
     if (max_chunks > 1 && (!workspace || workspace_bytes < need))
         return set_error(TLE_ERR_INVALID, "workspace %zu bytes, need %zu", workspace_bytes, need);
-    tle::BfArgs a{};
-    a.seqs = seqs_dev;
+    a = tle::BfArgs{};
     a.n_seqs = n_seqs;
     a.chunk = chunk;
     a.max_chunks = max_chunks;
@@ -472,8 +476,51 @@ int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_d
     fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
     cudaError_t e = tle::error_word(&a.err);
     if (e != cudaSuccess) return cuda_error(e, "device error word");
-    e = tle::launch_decode_bf16(a, static_cast<cudaStream_t>(stream));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tle_decode_batch_bf16(const tle_shape_t* shape, const tle_seq_bf16_t* seqs_dev, int n_seqs,
+                          int max_rows, const float* q, const float* k, const float* v, float* out,
+                          int layer, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+    tle::BfArgs a;
+    if (int rc = bf16_args(shape, seqs_dev, n_seqs, max_rows, q, k, v, out, layer, flags, workspace,
+                           workspace_bytes, a))
+        return rc;
+    a.seqs = seqs_dev;
+    cudaError_t e = tle::launch_decode_bf16(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, "bf16 decode launch");
+    return ok();
+}
+
+int tle_decode_batch_bf16_paged(const tle_shape_t* shape, const tle_page_pool_bf16_t* pool,
+                                const tle_paged_seq_t* seqs_dev, int n_seqs, int max_rows, const float* q,
+                                const float* k, const float* v, float* out, int layer, int flags,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    tle::BfArgs a;
+    if (int rc = bf16_args(shape, seqs_dev, n_seqs, max_rows, q, k, v, out, layer, flags, workspace,
+                           workspace_bytes, a))
+        return rc;
+    if (!pool || !pool->key_pool || !pool->value_pool)
+        return set_error(TLE_ERR_INVALID, "page pool and both pools must be non-null");
+    if (!aligned16(pool->key_pool) || !aligned16(pool->value_pool))
+        return set_error(TLE_ERR_INVALID, "page pools must be 16-byte aligned");
+    const int pr = pool->page_rows;
+    if (pr < 64 || pr > 65536 || (pr & (pr - 1)) != 0)
+        return set_error(TLE_ERR_INVALID, "page_rows %d is not a power of two in [64, 65536]", pr);
+    if (pool->n_pages <= 0) return set_error(TLE_ERR_INVALID, "pool n_pages %d <= 0", pool->n_pages);
+    int shift = 0;
+    while ((1 << shift) < pr) ++shift;
+    a.pseqs = seqs_dev;
+    a.key_pool = pool->key_pool;
+    a.value_pool = pool->value_pool;
+    a.pool_pages = pool->n_pages;
+    a.page_shift = shift;
+    cudaError_t e = tle::launch_decode_bf16(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "paged bf16 decode launch");
     return ok();
 }
 

@@ -94,17 +94,67 @@ __device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) 
                  : "memory");
 }
 
+// A sequence as the kernel sees it: its position and where its rows are.
+// Contiguous: row r of the layer at kc/vc + 256 r.  Paged: row r at page
+// pages[r >> page_shift] of the pools (an id outside the pool is reported
+// as 0x105 and its rows are neither read nor written).
+template <bool PAGED>
+struct BfSeqView {
+    int pos;
+    bool ok;
+    uint16_t* kc;
+    uint16_t* vc;
+    const int32_t* pages;
+};
+template <bool PAGED>
+__device__ __forceinline__ BfSeqView<PAGED> bf_seq(const BfArgs& A, int s) {
+    BfSeqView<PAGED> v{};
+    if (PAGED) {
+        const tle_paged_seq_t ps = A.pseqs[s];
+        v.pos = ps.pos;
+        v.ok = ps.pos >= 0 && (static_cast<long long>(ps.n_pages) << A.page_shift) > ps.pos;
+        v.pages = ps.pages;
+        const size_t layer = static_cast<size_t>(A.layer) * A.pool_pages << A.page_shift;
+        v.kc = static_cast<uint16_t*>(A.key_pool) + layer * BROW;
+        v.vc = static_cast<uint16_t*>(A.value_pool) + layer * BROW;
+    } else {
+        const tle_seq_bf16_t sq = A.seqs[s];
+        v.pos = sq.pos;
+        v.ok = sq.pos >= 0 && sq.pos < sq.n_ctx;
+        v.kc = static_cast<uint16_t*>(sq.key_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
+        v.vc = static_cast<uint16_t*>(sq.value_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
+        v.pages = nullptr;
+    }
+    return v;
+}
+// Element offset of row r from kc / vc; false (reported) for a bad page id.
+template <bool PAGED>
+__device__ __forceinline__ bool bf_row(const BfArgs& A, const BfSeqView<PAGED>& v, int r, size_t& off) {
+    if (!PAGED) {
+        off = static_cast<size_t>(r) * BROW;
+        return true;
+    }
+    const int id = __ldg(v.pages + (r >> A.page_shift));
+    if (static_cast<unsigned>(id) >= static_cast<unsigned>(A.pool_pages)) {
+        record_error(A.err, kErrBadPage);
+        return false;
+    }
+    off = ((static_cast<size_t>(id) << A.page_shift) | static_cast<size_t>(r & ((1 << A.page_shift) - 1))) * BROW;
+    return true;
+}
+
+template <bool PAGED>
 __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_constant__ BfArgs A) {
     extern __shared__ __align__(128) unsigned char bf_raw[];
     BfSmem& S = *reinterpret_cast<BfSmem*>(bf_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, s = blockIdx.y;
-    const tle_seq_bf16_t sq = A.seqs[s];
+    const BfSeqView<PAGED> sq = bf_seq<PAGED>(A, s);
     const int L = sq.pos + 1;
     const int n_chunks = (L + A.chunk - 1) / A.chunk;
-    // a record outside its cache, or longer than the launch's max_rows, is
-    // reported and skipped (no access)
-    if (sq.pos < 0 || sq.pos >= sq.n_ctx || n_chunks > A.max_chunks) {
+    // a record outside its cache (or page table), or longer than the
+    // launch's max_rows, is reported and skipped (no access)
+    if (!sq.ok || n_chunks > A.max_chunks) {
         if (c == 0 && tid == 0) record_error(A.err, kErrBadSeq);
         return;
     }
@@ -112,8 +162,8 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
     if (r0 >= L) return;                                   // past the sequence's last chunk
     const int nrows = min(A.chunk, L - r0);
     const bool has_new = r0 + nrows == L;
-    uint16_t* kc = static_cast<uint16_t*>(sq.key_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
-    uint16_t* vc = static_cast<uint16_t*>(sq.value_cache) + static_cast<size_t>(A.layer) * sq.n_ctx * BROW;
+    uint16_t* kc = sq.kc;
+    uint16_t* vc = sq.vc;
 
     // q of sequence s: rotate (ops.cpp:1229-1260), x 1/8 (exact), bf16.
     // Thread t: pair t & 31 of heads t / 32 + 8 i.
@@ -135,8 +185,8 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
         }
         // The chunk holding row pos appends bf16(rotated k) and bf16(v)
         // (ops.cpp:1370-1371) before its tiles are read.
-        if (has_new) {
-            const size_t row = static_cast<size_t>(sq.pos) * BROW;
+        size_t row = 0;
+        if (has_new && bf_row<PAGED>(A, sq, sq.pos, row)) {
             if (tid < BROW / 2) {   // k pairs: head tid / 32, pair tid & 31 (= lane)
                 const float2 x = reinterpret_cast<const float2*>(A.k + static_cast<size_t>(s) * BROW)[tid];
                 float y0 = x.x, y1 = x.y;
@@ -158,16 +208,19 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
     // Tile t of the chunk into stage t % BSTAGES: 64 rows x 32 chunks of K
     // and of V, 16 pieces per thread; rows past the chunk are zero-filled.
     const int n_tiles = (nrows + BTILE - 1) / BTILE;
+    // (A tile's 64 rows lie in one page: chunks start at multiples of 64 and
+    // pages hold a power-of-two multiple of 64 rows.)
     auto issue = [&](int t) {
         const int st = t % BSTAGES;
         const uint32_t kb = smem_u32(S.k[st]), vb = smem_u32(S.v[st]);
+        size_t tb = 0;
+        const bool tok = bf_row<PAGED>(A, sq, r0 + t * BTILE, tb);
 #pragma unroll
         for (int j = 0; j < (BTILE * 32) / BTHREADS; ++j) {
             const int e = tid + j * BTHREADS;
             const int r = e >> 5, ch = e & 31;
-            const int row = t * BTILE + r;
-            const bool ok = row < nrows;
-            const size_t src = static_cast<size_t>(r0 + (ok ? row : 0)) * BROW + ch * 8;
+            const bool ok = tok && t * BTILE + r < nrows;
+            const size_t src = ok ? tb + static_cast<size_t>(r) * BROW + ch * 8 : 0;
             cp16(kb + tile_off(r, ch), kc + src, ok);
             cp16(vb + tile_off(r, ch), vc + src, ok);
         }
@@ -309,12 +362,13 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
 // Sequences of more than one chunk: out = sum_c w_c o_c, w_c = exp(lse_c -
 // LSE), LSE = log sum_c exp(lse_c), in chunk order.  Thread t: head t / 8,
 // dims 8 (t % 8) ...
+template <bool PAGED>
 __global__ void __launch_bounds__(256) merge_bf16_kernel(const __grid_constant__ BfArgs A) {
     const int s = blockIdx.x;
-    const tle_seq_bf16_t sq = A.seqs[s];
+    const BfSeqView<PAGED> sq = bf_seq<PAGED>(A, s);
     const int L = sq.pos + 1;
     const int n_chunks = (L + A.chunk - 1) / A.chunk;
-    if (n_chunks <= 1 || sq.pos >= sq.n_ctx || n_chunks > A.max_chunks) return;   // reported by the decode
+    if (n_chunks <= 1 || !sq.ok || n_chunks > A.max_chunks) return;   // reported by the decode
     const int h = threadIdx.x >> 3, d0 = 8 * (threadIdx.x & 7);
     const size_t base = static_cast<size_t>(s) * A.max_chunks * BNH + h;
     float mx = -INFINITY;
@@ -353,14 +407,20 @@ size_t decode_bf16_workspace_bytes(int n_seqs, int max_rows) {
 cudaError_t launch_decode_bf16(const BfArgs& a, cudaStream_t stream) {
     static PerDeviceOnce once;
     cudaError_t e = once.run([&](int) {
-        return cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t r = cudaFuncSetAttribute(decode_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(BfSmem)));
+        if (r != cudaSuccess) return r;
+        return cudaFuncSetAttribute(decode_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(sizeof(BfSmem)));
     });
     if (e != cudaSuccess) return e;
-    decode_bf16_kernel<<<dim3(a.max_chunks, a.n_seqs), BTHREADS, sizeof(BfSmem), stream>>>(a);
+    const dim3 grid(a.max_chunks, a.n_seqs);
+    if (a.pseqs) decode_bf16_kernel<true><<<grid, BTHREADS, sizeof(BfSmem), stream>>>(a);
+    else decode_bf16_kernel<false><<<grid, BTHREADS, sizeof(BfSmem), stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess || a.max_chunks <= 1) return e;
-    merge_bf16_kernel<<<a.n_seqs, 256, 0, stream>>>(a);
+    if (a.pseqs) merge_bf16_kernel<true><<<a.n_seqs, 256, 0, stream>>>(a);
+    else merge_bf16_kernel<false><<<a.n_seqs, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -133,7 +133,11 @@ inline int bf16_chunk_rows(int n_seqs, int max_rows) {
     return static_cast<int>(c < 64 ? 64 : (c > kBfMaxChunk ? kBfMaxChunk : c));
 }
 struct BfArgs {
-    const tle_seq_bf16_t* seqs;  // device [n_seqs]
+    const tle_seq_bf16_t* seqs;  // device [n_seqs] (contiguous caches), or
+    const tle_paged_seq_t* pseqs;   // device [n_seqs] (paged: rows in the pools below)
+    void* key_pool;              // paged: bf16 [n_layers][pool_pages][1 << page_shift][256]
+    void* value_pool;
+    int pool_pages, page_shift;
     int n_seqs, chunk, max_chunks;   // max_chunks = ceil(max_rows / chunk)
     const float* q;              // [n_seqs][32*64]
     const float* k;              // [n_seqs][256]

@@ -41,7 +41,7 @@ EXPORTED = (
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
     "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
     "tle_decode_desc_paged", "tle_decode_batch_paged", "tle_decode_bf16_workspace_bytes",
-    "tle_decode_batch_bf16",
+    "tle_decode_batch_bf16", "tle_decode_batch_bf16_paged",
     # include/tle_forward.h
     "tle_matmul", "tle_rmsnorm", "tle_vec_add", "tle_ffn_swiglu", "tle_sample_argmax",
     "tle_forward_workspace_bytes", "tle_forward", "tle_forward_layers_one_launch", "tle_sample_temperature", "tle_sample_top_p",
@@ -67,6 +67,12 @@ class Seq(ctypes.Structure):
     """tle_seq_t: one sequence's device KV cache and decode position."""
     _fields_ = [("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
                 ("n_ctx", ctypes.c_int32), ("pos", ctypes.c_int32)]
+
+
+class PagePoolBf16(ctypes.Structure):
+    """tle_page_pool_bf16_t: bf16 page pools."""
+    _fields_ = [("key_pool", ctypes.c_void_p), ("value_pool", ctypes.c_void_p),
+                ("n_pages", ctypes.c_int32), ("page_rows", ctypes.c_int32)]
 
 
 class SeqBf16(ctypes.Structure):
@@ -146,6 +152,7 @@ def lib() -> ctypes.CDLL:
         L.tle_decode_bf16_workspace_bytes.argtypes = [i, i]
         L.tle_decode_bf16_workspace_bytes.restype = sz
         L.tle_decode_batch_bf16.argtypes = [P(Shape), vp, i, i, vp, vp, vp, vp, i, i, vp, sz, vp]
+        L.tle_decode_batch_bf16_paged.argtypes = [P(Shape), vp, vp, i, i, vp, vp, vp, vp, i, i, vp, sz, vp]
         L.tle_prefill_workspace_bytes.argtypes = [P(Shape), i, i]
         L.tle_prefill_workspace_bytes.restype = sz
         L.tle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, P(Shape), vp, sz, vp]
@@ -322,6 +329,49 @@ class DecodeBatchBf16:
                                            self.workspace.numel() * 4, _stream(stream)))
 
 
+class PagedDecodeBatchBf16:
+    """DecodeBatchBf16 over a bf16 PagedKVCache (tle_decode_batch_bf16_paged):
+    one device page table per sequence; the sequence records (page table,
+    entries, pos) live in device memory and ``set_positions`` rewrites them."""
+
+    def __init__(self, cache: "PagedKVCache", tables: Sequence, positions: Sequence[int]):
+        import torch
+        if cache.dtype != torch.bfloat16:
+            raise ValueError("a bfloat16 PagedKVCache expected")
+        self.cache = cache
+        self.tables = list(tables)
+        self.n = len(self.tables)
+        self.shape = cache.shape
+        self._seqs_dev = torch.empty(self.n * ctypes.sizeof(PagedSeq), dtype=torch.uint8, device="cuda")
+        self.workspace = None
+        self.set_positions(positions)
+
+    def set_positions(self, positions: Sequence[int]) -> None:
+        import torch
+        if len(positions) != self.n:
+            raise ValueError("one position per sequence")
+        self.positions = [int(p) for p in positions]
+        self.max_rows = max(self.positions) + 1
+        seqs = (PagedSeq * self.n)()
+        for i, t in enumerate(self.tables):
+            seqs[i] = PagedSeq(_ptr(t), int(t.numel()), self.positions[i])
+        self._seqs_dev.copy_(torch.frombuffer(bytearray(bytes(seqs)), dtype=torch.uint8))
+        nbytes = lib().tle_decode_bf16_workspace_bytes(self.n, self.max_rows)
+        if self.workspace is None or self.workspace.numel() * 4 < nbytes:
+            self.workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device="cuda")
+
+    def run(self, q, k, v, out, layer: int, rotate: bool = True, stream=None) -> None:
+        for t, n, name in ((q, self.n * 2048, "q"), (k, self.n * 256, "k"), (v, self.n * 256, "v"),
+                           (out, self.n * 2048, "out")):
+            _want(t, n, name)
+        pool = self.cache.pool()
+        _check(lib().tle_decode_batch_bf16_paged(ctypes.byref(self.shape), ctypes.byref(pool),
+                                                 self._seqs_dev.data_ptr(), self.n, self.max_rows, _ptr(q),
+                                                 _ptr(k), _ptr(v), _ptr(out), layer, 1 if rotate else 0,
+                                                 _ptr(self.workspace), self.workspace.numel() * 4,
+                                                 _stream(stream)))
+
+
 class DecodeBatch:
     """attention() for many independent sequences in one launch per layer.
 
@@ -399,17 +449,20 @@ class PagedKVCache:
     """
 
     def __init__(self, n_pages: int, page_rows: int = 256, shape: Optional[Shape] = None,
-                 device="cuda"):
+                 device="cuda", dtype=None):
         import torch
         self.shape = shape or tinyllama_shape()
         self.n_pages = int(n_pages)
         self.page_rows = int(page_rows)
+        self.dtype = dtype or torch.float32   # torch.bfloat16: pools for PagedDecodeBatchBf16
         dims = (self.shape.n_layers, self.n_pages, self.page_rows, 256)
-        self.key_pool = torch.zeros(dims, dtype=torch.float32, device=device)
-        self.value_pool = torch.zeros(dims, dtype=torch.float32, device=device)
+        self.key_pool = torch.zeros(dims, dtype=self.dtype, device=device)
+        self.value_pool = torch.zeros(dims, dtype=self.dtype, device=device)
         self._free = list(range(self.n_pages - 1, -1, -1))
 
-    def pool(self) -> PagePool:
+    def pool(self):
+        if self.dtype != __import__("torch").float32:
+            return PagePoolBf16(_ptr(self.key_pool), _ptr(self.value_pool), self.n_pages, self.page_rows)
         return PagePool(_ptr(self.key_pool), _ptr(self.value_pool), self.n_pages, self.page_rows)
 
     def pages_for(self, n_rows: int) -> int:
