@@ -147,6 +147,10 @@ template <bool PAGED>
 __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_constant__ BfArgs A) {
     extern __shared__ __align__(128) unsigned char bf_raw[];
     BfSmem& S = *reinterpret_cast<BfSmem*>(bf_raw);
+    // a programmatic dependent of the previous kernel (scheduled as it
+    // drains); everything this kernel reads may be that kernel's output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, s = blockIdx.y;
     const BfSeqView<PAGED> sq = bf_seq<PAGED>(A, s);
@@ -364,6 +368,7 @@ __global__ void __launch_bounds__(BTHREADS, 1) decode_bf16_kernel(const __grid_c
 // dims 8 (t % 8) ...
 template <bool PAGED>
 __global__ void __launch_bounds__(256) merge_bf16_kernel(const __grid_constant__ BfArgs A) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the decode's partials
     const int s = blockIdx.x;
     const BfSeqView<PAGED> sq = bf_seq<PAGED>(A, s);
     const int L = sq.pos + 1;
@@ -414,14 +419,25 @@ cudaError_t launch_decode_bf16(const BfArgs& a, cudaStream_t stream) {
                                     static_cast<int>(sizeof(BfSmem)));
     });
     if (e != cudaSuccess) return e;
-    const dim3 grid(a.max_chunks, a.n_seqs);
-    if (a.pseqs) decode_bf16_kernel<true><<<grid, BTHREADS, sizeof(BfSmem), stream>>>(a);
-    else decode_bf16_kernel<false><<<grid, BTHREADS, sizeof(BfSmem), stream>>>(a);
-    e = cudaGetLastError();
+    // both launches are programmatic dependents of the kernel before them
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.max_chunks, a.n_seqs);
+    cfg.blockDim = dim3(BTHREADS);
+    cfg.dynamicSmemBytes = sizeof(BfSmem);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = a.pseqs ? cudaLaunchKernelEx(&cfg, decode_bf16_kernel<true>, a)
+                : cudaLaunchKernelEx(&cfg, decode_bf16_kernel<false>, a);
     if (e != cudaSuccess || a.max_chunks <= 1) return e;
-    if (a.pseqs) merge_bf16_kernel<true><<<a.n_seqs, 256, 0, stream>>>(a);
-    else merge_bf16_kernel<false><<<a.n_seqs, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    cfg.gridDim = dim3(a.n_seqs);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    return a.pseqs ? cudaLaunchKernelEx(&cfg, merge_bf16_kernel<true>, a)
+                   : cudaLaunchKernelEx(&cfg, merge_bf16_kernel<false>, a);
 }
 
 }  // namespace tle
