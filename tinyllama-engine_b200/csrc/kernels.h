@@ -18,7 +18,7 @@ constexpr int kNHeadKv = 4;
 constexpr int kRowFloats = kNHeadKv * kHeadDim;          // one cache row, all kv heads
 constexpr int kPartialFloats = kNHead * (kHeadDim + 2);  // o[32][64], m[32], l[32]
 constexpr int kMaxCtas = 1024;                            // upper bound on decode CTAs
-constexpr int kMinRowsPerCta = 32;                        // smallest split worth a CTA
+constexpr int kMinRowsPerCta = 128;                       // smallest split worth a CTA
 
 // Batch descriptor (built on the host by tle_decode_desc, read by the kernels):
 //   DescHeader | tle_seq_t seqs[n_seqs] | CtaStart cta_start[n_ctas+1] | SeqCtas seq_ctas[n_seqs]
