@@ -158,6 +158,18 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
                      const float* q, const float* k, const float* v, float* out, int layer,
                      int flags, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tle_decode_batch for a batch whose every sequence attends to at most 2048
+ * rows (pos + 1 <= max_rows <= 2048), built for latency: one thread-block
+ * cluster of up to 8 CTAs per (sequence, KV head), the chunk partials folded
+ * in distributed shared memory (no workspace, no atomics, one launch).
+ * desc_dev as for tle_decode_batch (a contiguous-cache descriptor); only its
+ * sequence records are read.  Same contract and tolerance as
+ * tle_decode_batch; faster when the batch's rows leave the SMs short of work
+ * (for example one rank's share of a sequence-partitioned batch). */
+int tle_decode_batch_short(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int max_rows,
+                           const float* q, const float* k, const float* v, float* out, int layer,
+                           int flags, void* stream);
+
 /* ---- batched decode over a bf16 KV cache ----
  * No counterpart in the reference (its cache is fp32, run_state.h:134-138):
  * the same decode step with cache rows stored as bf16 (round to nearest

@@ -451,3 +451,36 @@ def test_kv_ready_flag_gives_identical_results(cuda):
     assert np.all(np.isfinite(base[0])) and np.all(np.isfinite(base[1]))
     for got in res[True] + res[False][1:]:
         assert np.array_equal(got[0], base[0]) and np.array_equal(got[1], base[1])
+
+
+def test_short_batch_matches_split_and_oracle(cuda):
+    """tle_decode_batch_short (one cluster per sequence and KV head, every
+    sequence <= 2048 rows) agrees with the split-K batch decode to fp32
+    rounding and with the oracle to 1e-4, appended rows included."""
+    import torch
+    import oracle
+    import tle
+    rng = np.random.default_rng(77)
+    lengths = [1, 33, 640, 2048, 1500]
+    n = len(lengths)
+    hk = [rng.standard_normal((2, L + 2, KVD), dtype=np.float32) for L in lengths]
+    hv = [rng.standard_normal((2, L + 2, KVD), dtype=np.float32) for L in lengths]
+    q = rng.standard_normal((n, QD), dtype=np.float32)
+    k = rng.standard_normal((n, KVD), dtype=np.float32)
+    v = rng.standard_normal((n, KVD), dtype=np.float32)
+    outs = []
+    for short in (False, True):
+        caches = [(dev(a), dev(b), L + 2) for a, b, L in zip(hk, hv, lengths)]
+        batch = tle.DecodeBatch(caches, [L - 1 for L in lengths], tle.tinyllama_shape(2))
+        o = dev(np.full((n, QD), np.nan, np.float32))
+        batch.run(dev(q), dev(k), dev(v), o, 1, True, short=short)
+        outs.append((host(o), [(host(a), host(b)) for a, b, _ in caches]))
+    assert tle.device_error() == 0
+    assert float(np.max(np.abs(outs[0][0] - outs[1][0]))) <= 1e-5
+    for (ka, va), (kb, vb) in zip(outs[0][1], outs[1][1]):
+        assert np.array_equal(va, vb) and float(np.max(np.abs(ka - kb))) <= 1e-6
+    P = oracle.port()
+    want = np.zeros((n, QD), np.float32)
+    P.decode_batch([a.copy() for a in hk], [b.copy() for b in hv], [L + 2 for L in lengths],
+                   [L - 1 for L in lengths], q.copy(), k.copy(), v, want, 1)
+    assert float(np.max(np.abs(outs[1][0] - want))) <= ATOL

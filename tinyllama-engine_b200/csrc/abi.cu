@@ -438,6 +438,38 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
     return ok();
 }
 
+int tle_decode_batch_short(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int max_rows,
+                           const float* q, const float* k, const float* v, float* out, int layer,
+                           int flags, void* stream) {
+    if (int rc = check_shape(shape)) return rc;
+    if (!desc_dev || !q || !k || !v || !out) return set_error(TLE_ERR_INVALID, "null pointer");
+    if (n_seqs <= 0 || n_seqs > 65535 || max_rows <= 0 || max_rows > tle::kSeqMaxRows || layer < 0 ||
+        layer >= shape->n_layers)
+        return set_error(TLE_ERR_INVALID, "n_seqs %d, max_rows %d (<= %d), layer %d", n_seqs, max_rows,
+                         tle::kSeqMaxRows, layer);
+    if (flags & ~(TLE_DECODE_ROTATE | TLE_DECODE_KV_READY))
+        return set_error(TLE_ERR_INVALID, "unknown flags 0x%x", flags);
+    tle::SeqArgs s{};
+    const int chunks = std::min(tle::kSeqMaxChunks, (max_rows + 31) / 32);
+    s.chunk_rows = ((max_rows + chunks - 1) / chunks + 31) / 32 * 32;
+    s.n_chunks = (max_rows + s.chunk_rows - 1) / s.chunk_rows;
+    s.seqs = reinterpret_cast<const tle_seq_t*>(static_cast<const unsigned char*>(desc_dev) +
+                                                sizeof(tle::DescHeader));
+    s.n_seqs = n_seqs;
+    s.q = q;
+    s.k = k;
+    s.v = v;
+    s.out = out;
+    s.layer = layer;
+    s.rotate = (flags & TLE_DECODE_ROTATE) != 0;
+    fill_inv_freq(s.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
+    cudaError_t e = tle::error_word(&s.err);
+    if (e != cudaSuccess) return cuda_error(e, "device error word");
+    e = tle::launch_seq_decode(s, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "short batch decode launch");
+    return ok();
+}
+
 size_t tle_decode_bf16_workspace_bytes(int n_seqs, int max_rows) {
     if (n_seqs <= 0 || max_rows <= 0) return 0;
     return tle::decode_bf16_workspace_bytes(n_seqs, max_rows);

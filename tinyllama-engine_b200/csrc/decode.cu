@@ -1002,18 +1002,30 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     cg::cluster_group cl = cg::this_cluster();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, g = blockIdx.y;   // cluster = the n_chunks CTAs of KV head g
-    const int L = A.pos + 1;
+    // this cluster's sequence (batch mode: record blockIdx.z, written by the
+    // host before the launch)
+    const int sz = blockIdx.z;
+    const bool batch = A.seqs != nullptr;
+    const tle_seq_t sq = batch ? A.seqs[sz] : tle_seq_t{A.key_cache, A.value_cache, A.n_ctx, A.pos};
+    const float* qin = A.q + (batch ? static_cast<size_t>(sz) * NH * HD : 0);
+    const float* kin = A.k + (batch ? static_cast<size_t>(sz) * ROWF : 0);
+    const float* vin = A.v + (batch ? static_cast<size_t>(sz) * ROWF : 0);
+    float* outp = A.out + (batch ? static_cast<size_t>(sz) * NH * HD : 0);
+    float* const key_cache = sq.key_cache;
+    float* const value_cache = sq.value_cache;
+    const int L = sq.pos + 1;
+    const int C = (L + A.chunk_rows - 1) / A.chunk_rows;   // this sequence's chunks (<= n_chunks)
     const int r0 = c * A.chunk_rows;
     const int nrows = max(0, min(A.chunk_rows, L - r0));
     const bool has_new = nrows > 0 && (r0 + nrows == L);
-    const size_t layer_base = static_cast<size_t>(A.layer) * A.n_ctx * ROWF;
+    const size_t layer_base = static_cast<size_t>(A.layer) * sq.n_ctx * ROWF;
     // q, k, v and the cache may be the previous kernel's output
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // cached rows of this chunk (row pos comes from the new k and v)
     const int ncached = has_new ? nrows - 1 : nrows;
     for (int e = tid; e < ncached * 32; e += SEQ_THREADS) {
         const int r = e >> 5, piece = e & 31;           // 16 pieces of K then 16 of V
-        const float* src = (piece < 16 ? A.key_cache : A.value_cache) + layer_base +
+        const float* src = (piece < 16 ? key_cache : value_cache) + layer_base +
                            static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (piece & 15);
         float* dst = (piece < 16 ? ks : vs) + r * SEQ_KP + 4 * (piece & 15);
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -1022,8 +1034,9 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     // q of this cluster's heads (rotated, x 1/8) and, in the last chunk, the new row
     {
         const int p = lane;   // rotation pair
-        const float sn = A.rope_sin[p], cs = A.rope_cos[p];
-        const float2 x = reinterpret_cast<const float2*>(A.q + static_cast<size_t>(8 * g + warp) * HD)[p];
+        float sn = A.rope_sin[p], cs = A.rope_cos[p];
+        if (batch && A.rotate) sincosf(static_cast<float>(sq.pos) * A.inv_freq[p], &sn, &cs);
+        const float2 x = reinterpret_cast<const float2*>(qin + static_cast<size_t>(8 * g + warp) * HD)[p];
         float y0 = x.x, y1 = x.y;
         if (A.rotate) {
             y0 = x.x * cs - x.y * sn;
@@ -1031,20 +1044,20 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
         }
         *reinterpret_cast<float2*>(&qs[warp * HD + 2 * p]) = make_float2(y0 * kScale, y1 * kScale);
         if (has_new && warp < 2) {
-            const size_t row = layer_base + static_cast<size_t>(A.pos) * ROWF + g * HD;
+            const size_t row = layer_base + static_cast<size_t>(sq.pos) * ROWF + g * HD;
             if (warp == 0) {   // k: rotate, keep, append (ops.cpp:1370)
-                const float2 kx = reinterpret_cast<const float2*>(A.k + g * HD)[p];
+                const float2 kx = reinterpret_cast<const float2*>(kin + g * HD)[p];
                 float k0 = kx.x, k1 = kx.y;
                 if (A.rotate) {
                     k0 = kx.x * cs - kx.y * sn;
                     k1 = kx.x * sn + kx.y * cs;
                 }
                 *reinterpret_cast<float2*>(&ks[(nrows - 1) * SEQ_KP + 2 * p]) = make_float2(k0, k1);
-                reinterpret_cast<float2*>(A.key_cache + row)[p] = make_float2(k0, k1);
+                reinterpret_cast<float2*>(key_cache + row)[p] = make_float2(k0, k1);
             } else {           // v: keep, append (ops.cpp:1371)
-                const float2 vx = reinterpret_cast<const float2*>(A.v + g * HD)[p];
+                const float2 vx = reinterpret_cast<const float2*>(vin + g * HD)[p];
                 *reinterpret_cast<float2*>(&vs[(nrows - 1) * SEQ_KP + 2 * p]) = vx;
-                reinterpret_cast<float2*>(A.value_cache + row)[p] = vx;
+                reinterpret_cast<float2*>(value_cache + row)[p] = vx;
             }
         }
     }
@@ -1158,8 +1171,8 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     }
     cl.sync();
     // fold: CTA c takes heads c, c + C, ... of this KV head, one warp each
-    const int C = A.n_chunks;
-    for (int hl = c + C * warp; warp < 8 && hl < 8; hl += C * 8) {
+    // (the sequence's C chunks: CTAs c >= C of a shorter sequence of the batch fold nothing)
+    for (int hl = c + C * warp; c < C && warp < 8 && hl < 8; hl += C * 8) {
         // every chunk's record in flight at once (C <= 8), then the fold in chunk order
         float mc[kSeqMaxChunks], lc[kSeqMaxChunks];
         float2 oc[kSeqMaxChunks];
@@ -1190,8 +1203,8 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
         }
         const int h = 8 * g + hl;
         const float inv = 1.0f / lt;
-        reinterpret_cast<float2*>(A.out + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
-        if (A.lse && lane == 0) A.lse[h] = mt + logf(lt);
+        reinterpret_cast<float2*>(outp + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
+        if (!batch && A.lse && lane == 0) A.lse[h] = mt + logf(lt);
     }
     cl.sync();
 }
@@ -1285,7 +1298,7 @@ cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream) {
     // the previous kernel (its CTAs may be scheduled while that grid drains;
     // griddepcontrol.wait orders the reads)
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(a.n_chunks, NKV_HEADS);
+    cfg.gridDim = dim3(a.n_chunks, NKV_HEADS, a.seqs ? a.n_seqs : 1);
     cfg.blockDim = dim3(SEQ_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

@@ -117,6 +117,13 @@ struct SeqArgs {
     int layer, pos, n_ctx, rotate;
     int chunk_rows, n_chunks;    // n_chunks * chunk_rows >= pos + 1, chunk_rows a multiple of 32
     float rope_cos[kHeadDim / 2], rope_sin[kHeadDim / 2];   // of pos * inv_freq[i], from the host
+    // Batch mode (seqs != nullptr): grid z = sequence s of seqs[0..n_seqs)
+    // (device records; pos + 1 <= n_chunks * chunk_rows for every s), q/k/v/out
+    // [n_seqs][...], angles from inv_freq on the device; the fields above
+    // that describe one sequence (pos, n_ctx, caches, lse, angles) are unused.
+    const tle_seq_t* seqs;
+    int n_seqs;
+    float inv_freq[kHeadDim / 2];
 };
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);
 
