@@ -1045,13 +1045,19 @@ def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
     out = torch.zeros(QD, device=dev)
     ws = tle.attention_workspace(shape, n_ctx)
 
-    def step_on(c):
+    def step_on(c, kv_ready=True):
+        # kv_ready (TLE_DECODE_KV_READY): each call's previous kernel is the
+        # previous layer's call, which writes only that layer's row pos, so
+        # this layer's cached rows stream while it finishes (in a forward
+        # pass the previous kernel is the q/k/v projection, same contract)
         def step(st):
             kc, vc = caches[c]
             for l in range(n_layers):
-                tle.rope_attention(out, q, k, v, kc, vc, l, pos, n_ctx, shape, ws, st)
+                tle.rope_attention(out, q, k, v, kc, vc, l, pos, n_ctx, shape, ws, st,
+                                   kv_ready=kv_ready)
         return step
 
+    ms_strict = _time_graph(step_on(0, kv_ready=False), steps, warmup, dev)
     ms_warm = _time_graph(step_on(0), steps, warmup, dev)
     # cold: one captured graph per cache copy, replayed in rotation
     side = torch.cuda.Stream(dev)
@@ -1102,6 +1108,9 @@ def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
                         "the 22 tle_rope_attention calls of one token (CUDA graph)",
             "metric": "decode token latency (22 layers)", "unit": "us", "higher_is_better": False,
             "value": round(ms_warm * 1e3, 2), "value_cold_l2": round(ms_cold * 1e3, 2),
+            "value_strict_order": round(ms_strict * 1e3, 2),
+            "kv_ready": "value and value_cold_l2 use TLE_DECODE_KV_READY (rows stream before the "
+                        "wait on the previous kernel); value_strict_order waits first",
             "kv_gbs_warm": round(kv_bytes / (ms_warm / 1e3) / 1e9, 1),
             "kv_gbs_cold": round(kv_bytes / (ms_cold / 1e3) / 1e9, 1),
             "cold_l2": "%d cache copies rotated (%.0f MB > 126 MB L2)" % (copies, copies * 2 * n_layers * n_ctx * KVD * 4 / 1e6),
@@ -1112,7 +1121,7 @@ def measure_config1(dev, peaks, steps=50, warmup=5, copies=8):
             "cpu_reference": {"kind": kind, "cores": 1, "value": round(ref_us, 1), "unit": "us",
                               "sample": "22 layers of rope+attention at L=512, one host thread, "
                                         "median of 3 tokens"},
-            "gpu_launches": 2 * n_layers * steps}
+            "gpu_launches": 3 * n_layers * steps}
 
 
 def measure_ctxsplit(args, dev, rank, world, local):

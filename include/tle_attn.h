@@ -114,6 +114,16 @@ int tle_rope_attention(float* out, const float* q, const float* k, const float* 
                        const tle_shape_t* shape, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* tle_rope_attention with flags: TLE_DECODE_KV_READY (defined below; the
+ * same contract as for tle_decode_batch, for this call's layer and rows <
+ * pos) lets the kernel stream the cached rows while the kernel launched
+ * before it on the stream finishes.  0 gives tle_rope_attention; unknown
+ * bits are rejected with TLE_ERR_INVALID. */
+int tle_rope_attention_flags(float* out, const float* q, const float* k, const float* v,
+                             float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                             const tle_shape_t* shape, int flags, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* ---- batched multi-sequence decode (no reference counterpart: the
  * reference decodes one sequence; this runs its attention() for many
  * independent sequences in one launch, ops.cpp:1317 per sequence) ---- */

@@ -453,6 +453,43 @@ def test_kv_ready_flag_gives_identical_results(cuda):
         assert np.array_equal(got[0], base[0]) and np.array_equal(got[1], base[1])
 
 
+@pytest.mark.parametrize("L", [1, 65, 512, 2048, 3000])
+def test_single_kv_ready_gives_identical_results(cuda, L):
+    """tle_rope_attention_flags with TLE_DECODE_KV_READY over a chain of
+    layers (each call's previous kernel writes another layer's row) gives
+    bit-identical outputs and cache contents to tle_rope_attention, on the
+    cluster path (L <= 2048) and the SM split (3000); unknown flag bits are
+    rejected."""
+    import ctypes
+    import torch
+    import tle
+    rng = np.random.default_rng(77 + L)
+    n_layers, n_ctx = 3, L + 2
+    pos = L - 1
+    shape = tle.tinyllama_shape(n_layers)
+    kc_h = rng.standard_normal((n_layers, n_ctx, KVD), dtype=np.float32)
+    vc_h = rng.standard_normal((n_layers, n_ctx, KVD), dtype=np.float32)
+    q, k, v = (dev(rng.standard_normal((n_layers, n), dtype=np.float32)) for n in (QD, KVD, KVD))
+    ws = tle.attention_workspace(shape, n_ctx)
+    res = []
+    for kvr in (False, True):
+        kc, vc = dev(kc_h), dev(vc_h)
+        outs = torch.full((n_layers, QD), float("nan"), device="cuda")
+        for layer in range(n_layers):
+            tle.rope_attention(outs[layer], q[layer], k[layer], v[layer], kc, vc, layer, pos, n_ctx,
+                               shape, ws, kv_ready=kvr)
+        res.append((host(outs), host(kc), host(vc)))
+    assert tle.device_error() == 0
+    assert np.all(np.isfinite(res[0][0]))
+    for a, b in zip(res[0], res[1]):
+        assert np.array_equal(a, b)
+    rc = tle.lib().tle_rope_attention_flags(
+        ctypes.c_void_p(outs.data_ptr()), ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+        ctypes.c_void_p(v.data_ptr()), ctypes.c_void_p(kc.data_ptr()), ctypes.c_void_p(vc.data_ptr()),
+        0, pos, n_ctx, ctypes.byref(shape), 4, ctypes.c_void_p(ws.data_ptr()), ws.numel() * 4, None)
+    assert rc != 0
+
+
 def test_short_batch_matches_split_and_oracle(cuda):
     """tle_decode_batch_short (one cluster per sequence and KV head, every
     sequence <= 2048 rows) agrees with the split-K batch decode to fp32

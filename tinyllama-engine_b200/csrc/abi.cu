@@ -131,7 +131,7 @@ size_t partial_bytes(int n_slots) {
 int single_decode(float* out, const float* q, const float* k, const float* v, float* key_cache,
                   float* value_cache, int layer, int pos, int n_ctx, const tle_shape_t* shape,
                   void* workspace, size_t workspace_bytes, void* stream, int rotate,
-                  float* lse = nullptr) {
+                  float* lse = nullptr, int kv_ready = 0) {
     if (int rc = check_shape(shape)) return rc;
     if (!out || !q || !k || !v || !key_cache || !value_cache)
         return set_error(TLE_ERR_INVALID, "null buffer pointer");
@@ -163,6 +163,7 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
         s.pos = pos;
         s.n_ctx = n_ctx;
         s.rotate = rotate;
+        s.kv_ready = kv_ready;
         // the rotation angles as the reference computes them (ops.cpp:1233-1238:
         // float angle, std::cos / std::sin), once per call on the host
         float inv_freq[tle::kHeadDim / 2];
@@ -204,6 +205,7 @@ int single_decode(float* out, const float* q, const float* k, const float* v, fl
     a.lse = lse;
     a.layer = layer;
     a.rotate = rotate;
+    a.kv_ready = kv_ready;
     fill_inv_freq(a.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
     cudaError_t e = tle::error_word(&a.err);
     if (e != cudaSuccess) return cuda_error(e, "device error word");
@@ -277,6 +279,15 @@ int tle_rope_attention(float* out, const float* q, const float* k, const float* 
                        void* stream) {
     return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
                          workspace_bytes, stream, 1);
+}
+
+int tle_rope_attention_flags(float* out, const float* q, const float* k, const float* v,
+                             float* key_cache, float* value_cache, int layer, int pos, int n_ctx,
+                             const tle_shape_t* shape, int flags, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+    if (flags & ~TLE_DECODE_KV_READY) return set_error(TLE_ERR_INVALID, "unknown flags 0x%x", flags);
+    return single_decode(out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
+                         workspace_bytes, stream, 1, nullptr, (flags & TLE_DECODE_KV_READY) ? 1 : 0);
 }
 
 size_t tle_decode_desc_bytes(int n_seqs, int max_ctas) {
@@ -462,6 +473,7 @@ int tle_decode_batch_short(const tle_shape_t* shape, const void* desc_dev, int n
     s.out = out;
     s.layer = layer;
     s.rotate = (flags & TLE_DECODE_ROTATE) != 0;
+    s.kv_ready = (flags & TLE_DECODE_KV_READY) != 0;
     fill_inv_freq(s.inv_freq, tle::kHeadDim / 2, shape->rope_freq_base);
     cudaError_t e = tle::error_word(&s.err);
     if (e != cudaSuccess) return cuda_error(e, "device error word");

@@ -1019,18 +1019,29 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     const int nrows = max(0, min(A.chunk_rows, L - r0));
     const bool has_new = nrows > 0 && (r0 + nrows == L);
     const size_t layer_base = static_cast<size_t>(A.layer) * sq.n_ctx * ROWF;
-    // q, k, v and the cache may be the previous kernel's output
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     // cached rows of this chunk (row pos comes from the new k and v)
     const int ncached = has_new ? nrows - 1 : nrows;
-    for (int e = tid; e < ncached * 32; e += SEQ_THREADS) {
-        const int r = e >> 5, piece = e & 31;           // 16 pieces of K then 16 of V
-        const float* src = (piece < 16 ? key_cache : value_cache) + layer_base +
-                           static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (piece & 15);
-        float* dst = (piece < 16 ? ks : vs) + r * SEQ_KP + 4 * (piece & 15);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    auto load_rows = [&]() {
+        for (int e = tid; e < ncached * 32; e += SEQ_THREADS) {
+            const int r = e >> 5, piece = e & 31;           // 16 pieces of K then 16 of V
+            const float* src = (piece < 16 ? key_cache : value_cache) + layer_base +
+                               static_cast<size_t>(r0 + r) * ROWF + g * HD + 4 * (piece & 15);
+            float* dst = (piece < 16 ? ks : vs) + r * SEQ_KP + 4 * (piece & 15);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // q, k, v and the cache may be the previous kernel's output; with
+    // kv_ready the caller guarantees that kernel wrote none of the cached
+    // rows read here (in a forward pass it is the q/k/v projection), so they
+    // stream while it drains
+    if (A.kv_ready) {
+        load_rows();
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        load_rows();
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     // q of this cluster's heads (rotated, x 1/8) and, in the last chunk, the new row
     {
         const int p = lane;   // rotation pair

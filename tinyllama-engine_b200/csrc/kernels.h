@@ -123,6 +123,7 @@ struct SeqArgs {
     // that describe one sequence (pos, n_ctx, caches, lse, angles) are unused.
     const tle_seq_t* seqs;
     int n_seqs;
+    int kv_ready;                // TLE_DECODE_KV_READY: the cached rows are read before the wait
     float inv_freq[kHeadDim / 2];
 };
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream);

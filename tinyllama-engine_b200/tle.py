@@ -36,7 +36,7 @@ def _decode_flags(rotate: bool, kv_ready: bool) -> int:
 # Every symbol include/tle_attn.h declares (tests check the .so exports them).
 EXPORTED = (
     "tle_last_error", "tle_version", "tle_rope", "tle_attention_workspace_bytes",
-    "tle_attention", "tle_rope_attention", "tle_decode_desc_bytes", "tle_decode_desc",
+    "tle_attention", "tle_rope_attention", "tle_rope_attention_flags", "tle_decode_desc_bytes", "tle_decode_desc",
     "tle_decode_workspace_bytes", "tle_decode_batch", "tle_prefill_workspace_bytes",
     "tle_prefill", "tle_partition_lpt", "tle_device_error", "tle_decode_batch_noalloc",
     "tle_selftest_wait_timeout", "tle_attention_lse", "tle_merge_lse",
@@ -150,6 +150,7 @@ def lib() -> ctypes.CDLL:
         L.tle_attention_workspace_bytes.restype = sz
         for name in ("tle_attention", "tle_rope_attention"):
             getattr(L, name).argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), vp, sz, vp]
+        L.tle_rope_attention_flags.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, P(Shape), i, vp, sz, vp]
         L.tle_decode_desc_bytes.argtypes = [i, i]
         L.tle_decode_desc_bytes.restype = sz
         L.tle_decode_desc.argtypes = [P(Shape), P(Seq), i, i, vp, sz, P(i)]
@@ -260,11 +261,20 @@ def attention(out, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx:
 
 
 def rope_attention(out, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx: int,
-                   shape: Optional[Shape] = None, workspace=None, stream=None) -> None:
-    """rope()+attention() (forward.cpp:192-208) in one launch; q, k unrotated."""
+                   shape: Optional[Shape] = None, workspace=None, stream=None,
+                   kv_ready: bool = False) -> None:
+    """rope()+attention() (forward.cpp:192-208) in one launch; q, k unrotated.
+    kv_ready: TLE_DECODE_KV_READY (the kernels still in flight on the stream
+    write none of this layer's rows < pos), so the cached rows stream while
+    the previous kernel finishes."""
     shape = shape or tinyllama_shape()
-    _single(lib().tle_rope_attention, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx,
-            shape, workspace, stream)
+    if not kv_ready:
+        _single(lib().tle_rope_attention, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx,
+                shape, workspace, stream)
+        return
+    flagged = lambda *a: lib().tle_rope_attention_flags(*a[:10], TLE_DECODE_KV_READY, *a[10:])  # noqa: E731
+    _single(flagged, out, q, k, v, key_cache, value_cache, layer, pos, n_ctx, shape, workspace,
+            stream)
 
 
 def attention_lse(out, lse, q, k, v, key_cache, value_cache, layer: int, pos: int, n_ctx: int,
