@@ -175,7 +175,9 @@ int tle_decode_batch(const tle_shape_t* shape, const void* desc_dev, int n_seqs,
  * desc_dev as for tle_decode_batch (a contiguous-cache descriptor); only its
  * sequence records are read.  Same contract and tolerance as
  * tle_decode_batch; faster when the batch's rows leave the SMs short of work
- * (for example one rank's share of a sequence-partitioned batch). */
+ * (for example one rank's share of a sequence-partitioned batch).  A record
+ * with pos outside [0, n_ctx), pos + 1 beyond max_rows or a null cache is
+ * skipped and reported through tle_device_error as 0x10a. */
 int tle_decode_batch_short(const tle_shape_t* shape, const void* desc_dev, int n_seqs, int max_rows,
                            const float* q, const float* k, const float* v, float* out, int layer,
                            int flags, void* stream);
@@ -333,8 +335,8 @@ int tle_partition_lpt(const int32_t* lengths, int n_seqs, int n_ranks, int32_t* 
  * arrived, 0x104 the exit-time drain), 0x105 a paged decode met a page id
  * outside the pool, 0x106 a token id outside the vocabulary, 0x108 a grid
  * barrier wait of the one-launch forward expired, 0x109 a finite activation
- * of the batched prompt overflowed fp16, 0x10a a bf16 decode record outside
- * its cache, 0x1ff the self-test below.  The first code recorded
+ * of the batched prompt overflowed fp16, 0x10a a bf16 or short-batch decode
+ * record outside its cache or max_rows, 0x1ff the self-test below.  The first code recorded
  * stays until cleared.  Synchronises the device. */
 int tle_device_error(int clear, uint32_t* code);
 

@@ -521,3 +521,38 @@ def test_short_batch_matches_split_and_oracle(cuda):
     P.decode_batch([a.copy() for a in hk], [b.copy() for b in hv], [L + 2 for L in lengths],
                    [L - 1 for L in lengths], q.copy(), k.copy(), v, want, 1)
     assert float(np.max(np.abs(outs[1][0] - want))) <= ATOL
+
+
+def test_short_batch_record_beyond_max_rows_is_reported(cuda):
+    """A record longer than the launch's max_rows (more chunks than the
+    cluster has CTAs) is skipped and reported as 0x10a: its output and cache
+    are untouched, the other sequences decode as with a correct max_rows
+    (to fp32 rounding)."""
+    import ctypes
+    import torch
+    import tle
+    rng = np.random.default_rng(78)
+    lengths = [100, 700, 300]
+    n = len(lengths)
+    shape = tle.tinyllama_shape(1)
+    hk = [rng.standard_normal((1, L, KVD), dtype=np.float32) for L in lengths]
+    hv = [rng.standard_normal((1, L, KVD), dtype=np.float32) for L in lengths]
+    q, k, v = (dev(rng.standard_normal((n, d), dtype=np.float32)) for d in (QD, KVD, KVD))
+    res = []
+    for max_rows in (700, 512):   # 512 rows: 8 chunks of 64, short of the second record
+        caches = [(dev(a), dev(b), L) for a, b, L in zip(hk, hv, lengths)]
+        batch = tle.DecodeBatch(caches, [L - 1 for L in lengths], shape)
+        out = torch.zeros((n, QD), device="cuda")
+        tle.device_error(clear=True)
+        rc = tle.lib().tle_decode_batch_short(ctypes.byref(shape), batch._desc_dev.data_ptr(), n, max_rows,
+                                              ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+                                              ctypes.c_void_p(v.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                              0, 1, None)
+        assert rc == 0
+        res.append((tle.device_error(clear=True), host(out), [host(c[0]) for c in caches]))
+    assert res[0][0] == 0 and res[1][0] == 0x10a
+    good, bad = res[0][1], res[1][1]
+    # (another max_rows gives other chunk sizes, so a different fold order)
+    assert maxabs(bad[0], good[0]) <= 1e-5 and maxabs(bad[2], good[2]) <= 1e-5
+    assert np.all(bad[1] == 0)
+    assert np.array_equal(res[1][2][1], hk[1])   # the skipped record's cache was not touched

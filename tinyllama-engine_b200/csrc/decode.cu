@@ -1014,6 +1014,14 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     float* const key_cache = sq.key_cache;
     float* const value_cache = sq.value_cache;
     const int L = sq.pos + 1;
+    // batch mode: a record outside its cache, or longer than the launch's
+    // max_rows (more chunks than the cluster has CTAs), is reported and
+    // skipped by every CTA of its cluster alike (no access, no cluster sync)
+    if (batch && (sq.pos < 0 || sq.pos >= sq.n_ctx || L > static_cast<int>(gridDim.x) * A.chunk_rows ||
+                  !key_cache || !value_cache)) {
+        if (c == 0 && g == 0 && tid == 0) record_error(A.err, kErrBadSeq);
+        return;
+    }
     const int C = (L + A.chunk_rows - 1) / A.chunk_rows;   // this sequence's chunks (<= n_chunks)
     const int r0 = c * A.chunk_rows;
     const int nrows = max(0, min(A.chunk_rows, L - r0));
