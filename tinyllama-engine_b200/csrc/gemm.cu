@@ -129,6 +129,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
     const int kb0 = z * nk_all / n_split;
     const int nk = (z + 1) * nk_all / n_split - kb0;
 
+    // Programmatic dependent launch: the next kernel on the stream may be
+    // scheduled now; it waits for this grid before touching its outputs.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
             mbar_init(&S.full[s], 1);
@@ -154,9 +157,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
-        for (int kb = 0; kb < nk; ++kb) {
+        // No kernel writes the weights, so the first stages' weight slices
+        // stream while the previous kernel on the stream (the producer of the
+        // token operand) finishes; the token slices, and everything else
+        // this grid reads or writes, wait for it (griddepcontrol.wait).
+        const int pre = nk < ST ? nk : ST;
+        if (lane == 0) {
+            for (int kb = 0; kb < pre; ++kb) {
+                const int kx = (kb0 + kb) * GK;
+                mbar_arrive_expect_tx(&S.full[kb], (NACC + 1) * kTileBytes);
+                tma_load_2d(S.a[kb][0], &A.tm_w, kx, m0, &S.full[kb]);
+                if (NACC == 2) tma_load_2d(S.a[kb][NACC - 1], &A.tm_w, kx, A.up_row0 + m0, &S.full[kb]);
+            }
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (lane == 0) {
+            for (int kb = 0; kb < pre; ++kb) tma_load_2d(S.b[kb], &A.tm_x, (kb0 + kb) * GK, t0, &S.full[kb]);
+            S.issued = pre;
+        }
+        __syncwarp();
+        for (int kb = pre; kb < nk; ++kb) {
             const int s = kb % ST;
-            if (kb >= ST) wait_or_flag(&S.empty[s], ((kb / ST) - 1) & 1, A.err, kErrWaitEmpty, failed);
+            wait_or_flag(&S.empty[s], ((kb / ST) - 1) & 1, A.err, kErrWaitEmpty, failed);
             failed = __any_sync(0xffffffffu, failed);   // the warp stops as one
             if (failed) break;
             if (lane == 0) {
@@ -170,6 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             __syncwarp();
         }
     } else if (warp == 1) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         // ------------------------------ MMA issuer --------------------------------
         for (int kb = 0; kb < nk; ++kb) {
             const int s = kb % ST;
@@ -196,6 +219,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
     }
 
     // ------------------------------ epilogue (all warps) ------------------------------
+    if (warp >= 2) asm volatile("griddepcontrol.wait;" ::: "memory");   // the epilogue reads / writes outputs
     wait_or_flag(&S.acc_full, 0, A.err, kErrWaitMma, failed);
     tc_fence_after();
     const int row_in_tile = 32 * warp + lane;
@@ -385,11 +409,20 @@ __global__ void __launch_bounds__(256) pack_f16_kernel(uint16_t* __restrict__ ds
 }
 
 // ---- RMSNorm of S rows into the fp16 operand (ops.cpp:1040-1054 per row) ----
-__global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
-                                                               const float* __restrict__ w, int n, float eps,
-                                                               uint32_t* err) {
+// The row kernels below run as programmatic dependents: they trigger the
+// next launch and wait for the previous kernel before their first load.  Data
+// the previous kernel wrote is read through plain pointers, which the
+// compiler may not hoist above the wait.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* out, const float* x, const float* w, int n,
+                                                               float eps, uint32_t* err) {
     __shared__ float red[8];
     __shared__ float rms;
+    pdl_enter();
     const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
     uint16_t* orow = out + static_cast<size_t>(blockIdx.x) * n;
     float ss = 0.f;
@@ -408,8 +441,8 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(uint16_t* __restr
     for (int i = threadIdx.x; i < n; i += 256) orow[i] = f2h_checked(xr[i] * s * w[i], err);
 }
 
-__global__ void __launch_bounds__(256) to_f16_kernel(uint16_t* __restrict__ out, const float* __restrict__ x,
-                                                     size_t n, uint32_t* err) {
+__global__ void __launch_bounds__(256) to_f16_kernel(uint16_t* out, const float* x, size_t n, uint32_t* err) {
+    pdl_enter();
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
         out[i] = f2h_checked(x[i], err);
@@ -418,9 +451,9 @@ __global__ void __launch_bounds__(256) to_f16_kernel(uint16_t* __restrict__ out,
 // embed_token (forward.cpp:35-60) for S tokens: block (x, t) writes a slice
 // of row t.  A token outside [0, n_vocab) is reported (0x106) and gives zeros.
 template <int T>
-__global__ void __launch_bounds__(256) embed_rows_kernel(float* __restrict__ x, const uint8_t* __restrict__ table,
-                                                         const int32_t* __restrict__ tokens, int n_vocab,
-                                                         int n_embd, uint32_t* err) {
+__global__ void __launch_bounds__(256) embed_rows_kernel(float* x, const uint8_t* table, const int32_t* tokens,
+                                                         int n_vocab, int n_embd, uint32_t* err) {
+    pdl_enter();
     const int t = blockIdx.y;
     const int tok = tokens[t];
     const bool ok = tok >= 0 && tok < n_vocab;
@@ -455,19 +488,40 @@ cudaError_t launch_gemm_e(const GemmArgs& a, dim3 grid, cudaStream_t stream) {
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = static_cast<size_t>(C::kSmemBytes);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    // and a programmatic dependent of the previous kernel on the stream
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = grid.z;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<EPI>, a);
 }
 
 inline int grid_for(size_t n) {
     const size_t b = (n + 255) / 256;
     return static_cast<int>(b < 148 * 16 ? (b ? b : 1) : 148 * 16);
+}
+
+// A row kernel of the prompt pass as a programmatic dependent of the
+// previous kernel on the stream (the kernels wait with griddepcontrol.wait
+// before their first load).
+template <typename... P, typename... Arg>
+cudaError_t launch_row_kernel(void (*fn)(P...), dim3 grid, cudaStream_t stream, Arg... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, static_cast<P>(args)...);
 }
 
 }  // namespace
@@ -535,14 +589,12 @@ cudaError_t launch_pack_f16(int type, uint16_t* dst, const void* W, int rows, in
 cudaError_t launch_rmsnorm_rows_f16(uint16_t* out, const float* x, const float* w, int n, float eps,
                                     int n_tokens, uint32_t* err, cudaStream_t stream) {
     if (n <= 0 || n_tokens <= 0) return cudaErrorInvalidValue;
-    rmsnorm_rows_f16_kernel<<<n_tokens, 256, 0, stream>>>(out, x, w, n, eps, err);
-    return cudaGetLastError();
+    return launch_row_kernel(rmsnorm_rows_f16_kernel, dim3(n_tokens), stream, out, x, w, n, eps, err);
 }
 
 cudaError_t launch_to_f16(uint16_t* out, const float* x, size_t n, uint32_t* err, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    to_f16_kernel<<<grid_for(n), 256, 0, stream>>>(out, x, n, err);
-    return cudaGetLastError();
+    return launch_row_kernel(to_f16_kernel, dim3(grid_for(n)), stream, out, x, n, err);
 }
 
 cudaError_t launch_embed_rows(int type, float* x, const void* table, const int32_t* tokens, int n_tokens,
@@ -550,13 +602,9 @@ cudaError_t launch_embed_rows(int type, float* x, const void* table, const int32
     if (n_tokens <= 0 || n_embd <= 0 || n_tokens > 65535) return cudaErrorInvalidValue;
     const dim3 grid((n_embd + 255) / 256, n_tokens);
     const uint8_t* tb = static_cast<const uint8_t*>(table);
-    if (type == kWF16)
-        embed_rows_kernel<kWF16><<<grid, 256, 0, stream>>>(x, tb, tokens, n_vocab, n_embd, err);
-    else if (type == kWF32)
-        embed_rows_kernel<kWF32><<<grid, 256, 0, stream>>>(x, tb, tokens, n_vocab, n_embd, err);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (type == kWF16) return launch_row_kernel(embed_rows_kernel<kWF16>, grid, stream, x, tb, tokens, n_vocab, n_embd, err);
+    if (type == kWF32) return launch_row_kernel(embed_rows_kernel<kWF32>, grid, stream, x, tb, tokens, n_vocab, n_embd, err);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace tle

@@ -124,6 +124,9 @@ __global__ void __launch_bounds__(kPrepThreads, 3) prefill_prep_kernel(const __g
     // sets up its barriers and TMEM while this grid runs, and its TMA
     // producer waits for this grid to complete before loading the operands.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // This grid is itself a programmatic dependent of the previous kernel on
+    // the stream (the producer of q, k and v): nothing is read before it ends.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (blockIdx.y == 0) {
@@ -745,12 +748,20 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     p.R_pad = L.R_pad;
     for (int i = 0; i < HD / 2; ++i) p.inv_freq[i] = a.inv_freq[i];
     {
+        // a programmatic dependent of the previous kernel (it waits for it
+        // before its first load), so its launch overlaps that kernel's tail
         const int gx = std::max((L.S_pad + kPrepTokensPerBlock - 1) / kPrepTokensPerBlock, L.R_pad / kVtRows);
-        if (a.f16)
-            prefill_prep_kernel<true><<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
-        else
-            prefill_prep_kernel<false><<<dim3(gx, 2), kPrepThreads, 0, stream>>>(p);
-        cudaError_t e = cudaGetLastError();
+        cudaLaunchConfig_t pc{};
+        pc.gridDim = dim3(gx, 2);
+        pc.blockDim = dim3(kPrepThreads);
+        pc.stream = stream;
+        cudaLaunchAttribute pa[1];
+        pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pa[0].val.programmaticStreamSerializationAllowed = 1;
+        pc.attrs = pa;
+        pc.numAttrs = 1;
+        cudaError_t e = a.f16 ? cudaLaunchKernelEx(&pc, prefill_prep_kernel<true>, p)
+                              : cudaLaunchKernelEx(&pc, prefill_prep_kernel<false>, p);
         if (e != cudaSuccess) return e;
     }
     AttnArgs t{};
