@@ -45,7 +45,7 @@ namespace {
 constexpr int GM = kGemmTileRows;     // 128 weight rows: TMEM lanes
 constexpr int GN = kGemmTileTokens;   // 128 tokens: TMEM columns per accumulator
 constexpr int GK = kGemmTileK;        // 64 fp16 = one 128-byte swizzle row
-constexpr int kGemmThreads = 128;
+constexpr int kGemmThreads = 256;
 constexpr uint32_t kTileBytes = GM * GK * 2;   // 16 KB, the same for a token tile
 static_assert(GM == GN, "weight and token tiles share one tensor-map box");
 constexpr uint32_t kIdesc = idesc_f16_f32(GM, GN);
@@ -106,10 +106,11 @@ struct GemmArgs {
     uint32_t* err;
 };
 
-// Warp roles (128 threads, one CTA per SM by shared memory):
+// Warp roles (256 threads, one CTA per SM by shared memory):
 //   warp 0: TMA producer (one lane issues), warp 1: MMA issuer (one elected
-//   lane); then all four warps run the epilogue, warp w on TMEM lanes
-//   32w..32w+31 (the lanes a warp may access are fixed by its rank mod 4).
+//   lane); then all eight warps run the epilogue, warp w on TMEM lanes
+//   32 (w % 4) .. +31 (the lanes a warp may access are fixed by its rank mod
+//   4) and token half w / 4 of the tile.
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_constant__ GemmArgs A) {
     using C = GemmCfg<EPI>;
@@ -222,9 +223,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
     if (warp >= 2) asm volatile("griddepcontrol.wait;" ::: "memory");   // the epilogue reads / writes outputs
     wait_or_flag(&S.acc_full, 0, A.err, kErrWaitMma, failed);
     tc_fence_after();
-    const int row_in_tile = 32 * warp + lane;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row_in_tile = 32 * quad + lane;
     const int r = m0 + row_in_tile;   // this thread's weight row
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quad) << 16);
     float* seg_out = nullptr;
     int seg_ld = 0;
     if (EPI != kEpiSwiGLU) {
@@ -252,19 +254,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             for (int j = 0; j < 32; ++j)
                 if (j < n && tb + j < A.n_tokens) seg_out[static_cast<size_t>(tb + j) * seg_ld] = x[j] + v[j];
         } else {
+            // silu(g) u with the fast exponential and division: the result
+            // is rounded to fp16 (11 bits), far coarser than their error
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 if (j < n && tb + j < A.n_tokens) {
                     const float g = v[j];
                     A.h_out[static_cast<size_t>(tb + j) * A.up_row0 + r] =
-                        f2h_checked((g * (1.0f / (1.0f + expf(-g)))) * u[j], A.err);
+                        f2h_checked(__fdividef(g, 1.0f + __expf(-g)) * u[j], A.err);
                 }
             }
         }
     };
     if (n_split == 1) {
 #pragma unroll 1
-        for (int c = 0; c < GN / 32; ++c) {
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
             float v[32];
             float u[32];
             tmem_ld32(trow + 32 * c, v);
@@ -273,59 +277,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_f16_kernel(const __grid_
             finish(t0 + 32 * c, 32, v, u);
         }
     } else {
-        // Split K over the CTAs of a cluster (one per split): each stages its
-        // fp32 accumulators in its own shared memory (row-major, rows padded
-        // to RP floats so a warp's 16-byte stores and loads hit distinct bank
-        // groups), and after a cluster barrier split z adds up tokens
-        // [z GN/n, (z+1) GN/n) of every split, in split order
-        // (deterministic), through distributed shared memory (all loads of a
-        // slice issued before the sums) and runs their epilogue.  A second
-        // barrier keeps every CTA's shared memory alive until its peers have
-        // read it.
-        constexpr int RP = GN + 4;
-        float* red = reinterpret_cast<float*>(&S.a[0][0][0]);   // the stages (a, then b) are idle now
+        // Split K over the CTAs of a cluster (one per split).  Split z owns
+        // tokens [z per, (z+1) per) of the output.  Once every split's MMAs
+        // have completed (first cluster barrier: the stage memory of every
+        // CTA is idle), each split pushes its fp32 accumulators, token slice
+        // by token slice, into the owning CTA's shared memory with remote
+        // stores (slot (acc, split) of a row padded to per + 4 floats, so
+        // 16-byte accesses hit distinct bank groups); after the second
+        // barrier each CTA adds up its slots in split order (deterministic)
+        // from its own memory and runs the epilogue.  Remote stores expose no
+        // round trip, where remote loads cost one per slice and split.
+        float* red = reinterpret_cast<float*>(&S.a[0][0][0]);
         static_assert(offsetof(typename C::Smem, b) == sizeof(S.a) &&
-                          sizeof(S.a) + sizeof(S.b) >= sizeof(float) * NACC * GM * RP,
-                      "staging fits the stage ring");
+                          sizeof(S.a) + sizeof(S.b) >= sizeof(float) * NACC * GM * (GN + 4 * 8),
+                      "the slots of up to 8 splits fit the stage ring");
+        const int per = GN / n_split;   // 16, 32, 64 or 128 tokens
+        const int rps = per + 4;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
 #pragma unroll 1
         for (int acc = 0; acc < NACC; ++acc) {
 #pragma unroll 1
-            for (int c = 0; c < GN / 32; ++c) {
+            for (int c = 2 * half; c < 2 * half + 2; ++c) {
                 float v[32];
                 tmem_ld32(trow + acc * GN + 32 * c, v);
                 tmem_wait_ld();
-                float4* dst = reinterpret_cast<float4*>(red + (acc * GM + row_in_tile) * RP + 32 * c);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                for (int j = 0; j < 8; ++j) {
+                    const int tk = 32 * c + 4 * j;   // a 4-token group never straddles two owners
+                    const int dst = tk / per;
+                    float* peer = cl.map_shared_rank(red, dst);
+                    *reinterpret_cast<float4*>(peer + ((acc * n_split + z) * GM + row_in_tile) * rps + (tk - dst * per)) =
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
             }
         }
-        cg::cluster_group cl = cg::this_cluster();
         cl.sync();
-        const int per = GN / n_split;   // 16, 32 or 64 tokens
-        for (int tb = z * per; tb < (z + 1) * per; tb += 16) {
+        const int hb = per / 2;   // this warp's half of the CTA's tokens
+        for (int tb = half * hb; tb < (half + 1) * hb; tb += 32) {
+            const int n = (half + 1) * hb - tb < 32 ? (half + 1) * hb - tb : 32;
             float v[32];
             float u[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = u[j] = 0.f;
             for (int zz = 0; zz < n_split; ++zz) {
-                const float* peer = cl.map_shared_rank(red, zz);
-                float4 a4[4], b4[4];
+                const float* sa = red + (zz * GM + row_in_tile) * rps + tb;
+                const float* sb = red + ((n_split + zz) * GM + row_in_tile) * rps + tb;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    a4[q] = *reinterpret_cast<const float4*>(peer + row_in_tile * RP + tb + 4 * q);
-                    if (NACC == 2) b4[q] = *reinterpret_cast<const float4*>(peer + (GM + row_in_tile) * RP + tb + 4 * q);
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    v[4 * q] += a4[q].x; v[4 * q + 1] += a4[q].y; v[4 * q + 2] += a4[q].z; v[4 * q + 3] += a4[q].w;
-                    if (NACC == 2) {
-                        u[4 * q] += b4[q].x; u[4 * q + 1] += b4[q].y; u[4 * q + 2] += b4[q].z; u[4 * q + 3] += b4[q].w;
+                for (int q = 0; q < 8; ++q) {
+                    if (4 * q < n) {
+                        const float4 a4 = *reinterpret_cast<const float4*>(sa + 4 * q);
+                        v[4 * q] += a4.x; v[4 * q + 1] += a4.y; v[4 * q + 2] += a4.z; v[4 * q + 3] += a4.w;
+                        if (NACC == 2) {
+                            const float4 b4 = *reinterpret_cast<const float4*>(sb + 4 * q);
+                            u[4 * q] += b4.x; u[4 * q + 1] += b4.y; u[4 * q + 2] += b4.z; u[4 * q + 3] += b4.w;
+                        }
                     }
                 }
             }
-            finish(t0 + tb, 16, v, u);
+            finish(t0 + z * per + tb, n, v, u);
         }
-        cl.sync();
     }
     // Failure path (a bounded wait expired somewhere in the CTA): nothing the
     // CTA issued may still write shared or tensor memory when the memory is
