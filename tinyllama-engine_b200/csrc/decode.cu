@@ -996,8 +996,9 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
     float* ks = seq_smem;                                    // [R][SEQ_KP]
     float* vs = ks + A.chunk_rows * SEQ_KP;                  // [R][SEQ_KP]
     float* qs = vs + A.chunk_rows * SEQ_KP;                  // [8][64]
-    float* part = qs + 8 * HD;                               // [8][SEQ_PF]
-    float* comb = part + 8 * SEQ_PF;                         // [8][SEQ_PF]: the second row half's
+    float* comb = qs + 8 * HD;                               // [8][SEQ_PF]: the second row half's
+    float* recv = comb + 8 * SEQ_PF;                         // [n_chunks][8][SEQ_PF]: the chunk records
+                                                             // of the heads this CTA folds
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     cg::cluster_group cl = cg::this_cluster();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1022,6 +1023,9 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
         if (c == 0 && g == 0 && tid == 0) record_error(A.err, kErrBadSeq);
         return;
     }
+    // this CTA has started: the cluster's CTAs wait for it (below) before
+    // they store into its shared memory
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     const int C = (L + A.chunk_rows - 1) / A.chunk_rows;   // this sequence's chunks (<= n_chunks)
     const int r0 = c * A.chunk_rows;
     const int nrows = max(0, min(A.chunk_rows, L - r0));
@@ -1170,7 +1174,12 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
         }
     }
     __syncthreads();
-    if (half == 0) {
+    // Records of this chunk, pushed into the folding CTA of each head (head
+    // hl: CTA hl mod C, warp hl / C) with remote stores, slot (chunk, head);
+    // after the cluster barrier every fold reads its own shared memory, and
+    // no CTA touches another's afterwards (no second barrier).
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // every CTA of the cluster has started
+    if (half == 0 && c < C) {
         auto fold = [&](int hl, float m0, float l0, float o0, float o1) {
             const float* cc = comb + hl * SEQ_PF;
             const float m1 = cc[HD], l1 = cc[HD + 1];
@@ -1178,11 +1187,11 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
             const float mt = fmaxf(m0, m1);
             const float f0 = (m0 == -INFINITY) ? 0.f : expf(m0 - mt);
             const float f1 = (m1 == -INFINITY) ? 0.f : expf(m1 - mt);
-            reinterpret_cast<float2*>(&part[hl * SEQ_PF])[lane] =
-                make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
+            float* dst = cl.map_shared_rank(recv, hl % C) + (c * 8 + hl) * SEQ_PF;
+            reinterpret_cast<float2*>(dst)[lane] = make_float2(o0 * f0 + p1.x * f1, o1 * f0 + p1.y * f1);
             if (lane == 0) {
-                part[hl * SEQ_PF + HD] = mt;
-                part[hl * SEQ_PF + HD + 1] = l0 * f0 + l1 * f1;
+                dst[HD] = mt;
+                dst[HD + 1] = l0 * f0 + l1 * f1;
             }
         };
         fold(2 * hp, ma, la, oa0, oa1);
@@ -1201,7 +1210,7 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
             lc[cc] = 0.f;
             oc[cc] = make_float2(0.f, 0.f);
             if (cc < C) {
-                const float* pp = cl.map_shared_rank(part, cc) + hl * SEQ_PF;
+                const float* pp = recv + (cc * 8 + hl) * SEQ_PF;
                 mc[cc] = pp[HD];
                 lc[cc] = pp[HD + 1];
                 oc[cc] = reinterpret_cast<const float2*>(pp)[lane];
@@ -1225,7 +1234,6 @@ __global__ void __launch_bounds__(SEQ_THREADS) seq_decode_kernel(const __grid_co
         reinterpret_cast<float2*>(outp + h * HD)[lane] = make_float2(acc0 * inv, acc1 * inv);
         if (!batch && A.lse && lane == 0) A.lse[h] = mt + logf(lt);
     }
-    cl.sync();
 }
 
 // rope() (ops.cpp:1223-1281): one thread per (head, pair); q heads then k heads.
@@ -1305,12 +1313,13 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_seq_decode(const SeqArgs& a, cudaStream_t stream) {
-    const size_t smem = static_cast<size_t>(2 * a.chunk_rows * SEQ_KP + 8 * HD + 16 * SEQ_PF) * sizeof(float);
+    const size_t smem =
+        static_cast<size_t>(2 * a.chunk_rows * SEQ_KP + 8 * HD + (8 + 8 * a.n_chunks) * SEQ_PF) * sizeof(float);
     static PerDeviceOnce once;
     cudaError_t e = once.run([&](int) {
         return cudaFuncSetAttribute(seq_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(2 * kSeqMaxChunkRows * SEQ_KP * sizeof(float) +
-                                                     (8 * HD + 16 * SEQ_PF) * sizeof(float)));
+                                                     (8 * HD + (8 + 8 * kSeqMaxChunks) * SEQ_PF) * sizeof(float)));
     });
     if (e != cudaSuccess) return e;
     // one cluster of n_chunks CTAs per KV head; a programmatic dependent of
