@@ -85,9 +85,14 @@ int choose_ctas(int64_t rows, int max_ctas) {
 // measured best on a 64-sequence ragged batch against 32 .. 256), so a
 // CTA that holds several short segments gets fewer rows.  CTA boundaries are
 // cost positions mapped to (sequence, row); a boundary inside a sequence's
-// overhead lands on its first row.  seq_ctas[t] = first and last CTA owning a
-// row of t.  No allocation (shared by the no-allocation entry point).
+// overhead lands on its first row, and a boundary inside a sequence is
+// rounded down to a multiple of kStartAlignRows, the decode kernel's
+// pipeline tile, so no CTA starts or ends a segment with a partial tile
+// (config 4: 1.1 % faster contiguous, 1.7 % paged).  seq_ctas[t] = first and
+// last CTA owning a row of t.  No allocation (shared by the no-allocation
+// entry point).
 constexpr int64_t kSegCostRows = 128;
+constexpr int64_t kStartAlignRows = 32;
 
 void plan_ctas(const tle_seq_t* seqs, int n, int G, tle::CtaStart* cs, tle::SeqCtas* sc) {
     int64_t T = 0;
@@ -107,7 +112,7 @@ void plan_ctas(const tle_seq_t* seqs, int n, int G, tle::CtaStart* cs, tle::SeqC
         }
         const int64_t r = x - X - kSegCostRows;
         cs[c].seq = s;
-        cs[c].off = r > 0 ? static_cast<int32_t>(r) : 0;
+        cs[c].off = r > 0 ? static_cast<int32_t>(r / kStartAlignRows * kStartAlignRows) : 0;
     }
     for (int t = 0; t < n; ++t) {
         sc[t].lo = G;
