@@ -93,10 +93,12 @@ __device__ __forceinline__ void cta_range(const DecodeArgs& A, int c, int& s0, i
         const CtaStart b = A.cta_start[c], e = A.cta_start[c + 1];
         s0 = b.seq; o0 = b.off; s1 = e.seq; o1 = e.off;
     } else {
+        // boundaries rounded down to the pipeline tile (the planner gives
+        // each CTA >= 128 rows, so no range becomes empty)
         const int L = A.single.pos + 1;
         s0 = 0;
-        o0 = static_cast<int>(static_cast<int64_t>(c) * L / A.n_ctas);
-        const int e = static_cast<int>(static_cast<int64_t>(c + 1) * L / A.n_ctas);
+        o0 = static_cast<int>(static_cast<int64_t>(c) * L / A.n_ctas) / TILE * TILE;
+        const int e = c + 1 == A.n_ctas ? L : static_cast<int>(static_cast<int64_t>(c + 1) * L / A.n_ctas) / TILE * TILE;
         if (e >= L) { s1 = 1; o1 = 0; } else { s1 = 0; o1 = e; }
     }
 }
