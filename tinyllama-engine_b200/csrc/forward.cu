@@ -504,15 +504,15 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int n
     const int tid = threadIdx.x;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int base = tid; base < n; base += 1024 * 8) {
-        float vs[8];                         // eight loads in flight, then the scan
+    for (int base = tid; base < n; base += 1024 * 32) {
+        float vs[32];                        // 32 loads in flight (a 32 K vocabulary in one round trip), then the scan
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 32; ++j) {
             const int i = base + j * 1024;
             vs[j] = i < n ? ld_cg(logits + i) : -INFINITY;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 32; ++j) {
             const int i = base + j * 1024;
             float v = vs[j];
             if (i >= n) break;
