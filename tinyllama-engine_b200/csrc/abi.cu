@@ -82,7 +82,8 @@ int choose_ctas(int64_t rows, int max_ctas) {
 // Splits a batch over G CTAs in "cost" units: every sequence costs its rows
 // plus kSegCostRows (the per-segment setup of the decode kernel: q rotation,
 // warp merge, output write: about three microseconds of streaming time; 128
-// measured best on a 64-sequence ragged batch against 32 .. 256), so a
+// measured best on a 64-sequence ragged batch against 32 .. 256, and again
+// against 96 and 160 with the tile-aligned starts below), so a
 // CTA that holds several short segments gets fewer rows.  CTA boundaries are
 // cost positions mapped to (sequence, row); a boundary inside a sequence's
 // overhead lands on its first row, and a boundary inside a sequence is
