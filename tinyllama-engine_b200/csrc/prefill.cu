@@ -374,6 +374,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) prefill_attn_kernel(const __g
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int wg = warp >> 2;
+    // the next kernel on the stream may be scheduled as this grid's CTAs
+    // leave their SMs (it waits for this grid before reading its output)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int n_items = A.n_qt * (NH / 2);
     const int G = static_cast<int>(gridDim.x);
     const int cta = static_cast<int>(blockIdx.x);
