@@ -1,5 +1,5 @@
-// decode_bf16.cu -- decode step over a bf16 KV cache (the
-// reduced-precision cache variant), fused RoPE + append + attention for a
+// decode_bf16.cu -- decode step over a bf16 KV cache (the reduced-precision
+// cache variant of run_state.h:20-25), fused RoPE + append + attention for a
 // batch of sequences.
 //
 // Reference semantics: rope() src/ops.cpp:1223-1281 then attention()
