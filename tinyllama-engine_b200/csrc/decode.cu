@@ -84,6 +84,7 @@ struct __align__(128) DecodeSmem {
     uint64_t empty[NSTAGE];
     uint64_t qfull[2];
     uint64_t csync;             // all-warp barrier (bounded waits)
+    int merge_last;             // wide merge: this CTA arrived last for the segment's sequence
 };
 
 // CTA c's row range as (start seq, start off) .. (end seq, end off), exclusive end.
@@ -470,6 +471,59 @@ __device__ __forceinline__ void merge_partials(const DecodeArgs& A, int s, int l
     }
 }
 
+// A sequence split over at least kWideMergeParts CTAs is folded by all eight
+// warps of its last CTA: warp w takes heads 4w .. 4w+3, lane = (head 4w +
+// lane / 8, dimensions 8 (lane % 8) .. +7), and the partials are folded in
+// CTA order, eight per round with all their loads in flight (one warp alone
+// needs a round trip per two partials).  Deterministic like merge_partials;
+// the fold order, and so the last bits, differ from it.
+constexpr int kWideMergeParts = 4;
+__device__ __forceinline__ void merge_partials_wide(const DecodeArgs& A, int s, int warp, int lane, SeqCtas sc) {
+    const int hh = 4 * warp + (lane >> 3), d0 = 8 * (lane & 7);
+    float m = -INFINITY, l = 0.f;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    for (int c0 = sc.lo; c0 <= sc.hi; c0 += 8) {
+        float mc[8], lc[8];
+        float4 o0[8], o1[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            mc[j] = -INFINITY;
+            lc[j] = 0.f;
+            o0[j] = o1[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c0 + j <= sc.hi) {
+                const float* P = A.partials + static_cast<size_t>(s + c0 + j) * kPartialFloats;
+                mc[j] = ld_cg(P + NH * HD + hh);
+                lc[j] = ld_cg(P + NH * HD + NH + hh);
+                o0[j] = ld_cg4(reinterpret_cast<const float4*>(P + hh * HD + d0));
+                o1[j] = ld_cg4(reinterpret_cast<const float4*>(P + hh * HD + d0 + 4));
+            }
+        }
+        float mn = m;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mn = fmaxf(mn, mc[j]);
+        const float fr = (m == -INFINITY) ? 0.f : expf(m - mn);
+        l *= fr;
+        a0 = make_float4(a0.x * fr, a0.y * fr, a0.z * fr, a0.w * fr);
+        a1 = make_float4(a1.x * fr, a1.y * fr, a1.z * fr, a1.w * fr);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (c0 + j <= sc.hi) {   // every partial covers a row, so its m is finite
+                const float f = expf(mc[j] - mn);
+                l = fmaf(lc[j], f, l);
+                a0 = make_float4(fmaf(o0[j].x, f, a0.x), fmaf(o0[j].y, f, a0.y), fmaf(o0[j].z, f, a0.z),
+                                 fmaf(o0[j].w, f, a0.w));
+                a1 = make_float4(fmaf(o1[j].x, f, a1.x), fmaf(o1[j].y, f, a1.y), fmaf(o1[j].z, f, a1.z),
+                                 fmaf(o1[j].w, f, a1.w));
+            }
+        }
+        m = mn;
+    }
+    const float inv = 1.0f / l;
+    float4* dst = reinterpret_cast<float4*>(A.out + static_cast<size_t>(s) * NH * HD + hh * HD + d0);
+    dst[0] = make_float4(a0.x * inv, a0.y * inv, a0.z * inv, a0.w * inv);
+    dst[1] = make_float4(a1.x * inv, a1.y * inv, a1.z * inv, a1.w * inv);
+}
+
 // e^x on the SFU: ex2.approx.ftz(x log2 e), relative error ~2^-22 (far inside
 // the 1e-4 output bound); e^-inf = 0.
 __device__ __forceinline__ float exp_sfu(float x) {
@@ -832,11 +886,12 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             __syncwarp();
             merge_out_a(m_run, l_run, acc, OA, S.mlA, h);
         }
+        // CTAs sharing this sequence (every warp: the wide merge needs them)
+        const bool split = A.arrivals && !(seg_a == 0 && seg_b == L);
+        const SeqCtas sc = split ? A.seq_ctas[s] : SeqCtas{0, 0};
+        const bool wide = split && sc.hi - sc.lo + 1 >= kWideMergeParts;
         if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
         if (warp == 0) {
-            // CTAs sharing this sequence (the load overlaps the stores below).
-            SeqCtas sc{0, 0};
-            if (A.arrivals && !(seg_a == 0 && seg_b == L)) sc = A.seq_ctas[s];
             merge_in_a(m_run, l_run, acc, OA, S.mlA, h);
             // ---- write: whole sequence -> output; otherwise a partial ----
             // Staged through buffer A (only warp 0 touches it from here to
@@ -861,9 +916,18 @@ __global__ void __launch_bounds__(NCT, 1) decode_kernel(const __grid_constant__ 
             if (!whole) {
                 dst[NH * HD + h] = m_run;
                 dst[NH * HD + NH + h] = l_run;
-                if (A.arrivals && arrive_last(A, s, lane, sc)) merge_partials(A, s, lane, sc);
+                if (wide) {
+                    const bool last = arrive_last(A, s, lane, sc);
+                    if (lane == 0) S.merge_last = last ? 1 : 0;
+                } else if (A.arrivals && arrive_last(A, s, lane, sc)) {
+                    merge_partials(A, s, lane, sc);
+                }
             }
             __syncwarp();
+        }
+        if (wide) {   // the same value in every warp
+            if (!cta_sync(S, cphase, lane)) { record_error(A.err, kErrWaitFull); ok = false; break; }
+            if (S.merge_last) merge_partials_wide(A, s, warp, lane, sc);
         }
     }
 
